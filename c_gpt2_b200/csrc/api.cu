@@ -1,0 +1,218 @@
+// extern "C" entry points of include/gpt2_w8a8.h: argument validation and
+// dispatch between the tensor-core and CUDA-core kernels.
+#include "common.cuh"
+#include "kernels.cuh"
+#include "runtime.cuh"
+
+namespace w8a8 {
+
+// Smallest token count that takes the tensor-core path; below it the
+// weight-streaming GEMV wins (the MMA's N dimension cannot go below 16 and
+// the work is pure HBM streaming).
+constexpr int kTcMinM = 16;
+
+static bool tc_ok_i8(const void *X, int64_t ldx, const void *W, int K) {
+  return (K % 16 == 0) && (ldx % 16 == 0) && aligned16(X) && aligned16(W);
+}
+
+static int dispatch_linear(const int8_t *Xq, int64_t ldx, const int8_t *W, const LinearArgs &a,
+                           cudaStream_t s) {
+  if (a.M >= kTcMinM && tc_ok_i8(Xq, ldx, W, a.K)) return gemm_tc_i8(W, Xq, ldx, a, s);
+  return launch_gemv_i8(Xq, ldx, W, a, s);
+}
+
+static LinearArgs make_args(int epi, int M, int N, int K, const float *sX, const float *sW,
+                            const uint16_t *bias, const uint16_t *R, int64_t ldr, void *Y,
+                            int64_t ldy) {
+  LinearArgs a = {};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.epi = epi;
+  a.sX = sX;
+  a.sW = sW;
+  a.bias = bias;
+  a.R = R;
+  a.ldr = ldr;
+  a.Y = Y;
+  a.ldy = ldy;
+  a.T = 1;
+  a.dseg = N;
+  return a;
+}
+
+}  // namespace w8a8
+
+using namespace w8a8;
+
+static int ready(void) {
+  int st;
+  return device_ctx(&st) ? W8A8_OK : st;
+}
+
+extern "C" int w8a8_quant_rows(const gpt2_bf16_t *X, int64_t ldx, int M, int K, int8_t *Xq,
+                               float *sX, void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!X || !Xq || !sX || M < 0 || K <= 0 || ldx < K) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  return launch_quant_rows(X, ldx, M, K, Xq, sX, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_layernorm_quant(const gpt2_bf16_t *X, int64_t ldx, int M, int d,
+                                    const gpt2_bf16_t *gamma, const gpt2_bf16_t *beta, float eps,
+                                    gpt2_bf16_t *Y, int64_t ldy, int8_t *Xq, float *sX,
+                                    void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!X || !gamma || !beta || M < 0 || d <= 0 || d > 8192 || ldx < d) return W8A8_ERR_INVALID;
+  if (!Y && !Xq) return W8A8_ERR_INVALID;
+  if (Y && ldy < d) return W8A8_ERR_INVALID;
+  if ((Xq == nullptr) != (sX == nullptr)) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  return launch_layernorm_quant(X, ldx, M, d, gamma, beta, eps, Y, ldy, Xq, sX,
+                                (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_embed_layernorm_quant(const gpt2_bf16_t *wte, const gpt2_bf16_t *wpe,
+                                          const int32_t *tokens, int M, int T,
+                                          const int32_t *pos0, int d, gpt2_bf16_t *H,
+                                          const gpt2_bf16_t *gamma, const gpt2_bf16_t *beta,
+                                          float eps, gpt2_bf16_t *Y, int8_t *Xq, float *sX,
+                                          void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!wte || !wpe || !tokens || !gamma || !beta || M < 0 || T <= 0 || M % T != 0 || d <= 0 ||
+      d > 8192)
+    return W8A8_ERR_INVALID;
+  if ((Xq == nullptr) != (sX == nullptr)) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  return launch_embed_layernorm_quant(wte, wpe, tokens, M, T, pos0, d, H, gamma, beta, eps, Y, Xq,
+                                      sX, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_gemm_s32(const int8_t *Xq, int M, int K, const int8_t *W, int N, int32_t *Y,
+                             void *stream) {
+  if (M == 0 || N == 0) return W8A8_OK;
+  if (!Xq || !W || !Y || M < 0 || N < 0 || K <= 0) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  LinearArgs a = make_args(EPI_S32, M, N, K, nullptr, nullptr, nullptr, nullptr, 0, Y, N);
+  return dispatch_linear(Xq, K, W, a, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W,
+                           const float *sW, const gpt2_bf16_t *bias, int N, int epilogue,
+                           const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy,
+                           void *stream) {
+  if (M == 0 || N == 0) return W8A8_OK;
+  if (!Xq || !sX || !W || !sW || !Y || M < 0 || N < 0 || K <= 0 || ldy < N)
+    return W8A8_ERR_INVALID;
+  int epi;
+  switch (epilogue) {
+    case W8A8_EPI_DEQUANT: epi = EPI_DEQUANT; break;
+    case W8A8_EPI_BIAS: epi = EPI_BIAS; break;
+    case W8A8_EPI_BIAS_RESID: epi = EPI_RESID; break;
+    case W8A8_EPI_BIAS_GELU: epi = EPI_GELU; break;
+    default: return W8A8_ERR_INVALID;
+  }
+  if (epi != EPI_DEQUANT && !bias) return W8A8_ERR_INVALID;
+  if (epi == EPI_RESID && (!R || ldr < N)) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  LinearArgs a = make_args(epi, M, N, K, sX, sW, bias, R, ldr, Y, ldy);
+  return dispatch_linear(Xq, K, W, a, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_linear_qkv(const int8_t *Xq, const float *sX, int M, int d,
+                               const int8_t *Wqkv, const float *sWqkv, const gpt2_bf16_t *bqkv,
+                               gpt2_bf16_t *Q, int64_t ldq, gpt2_bf16_t *Kc, gpt2_bf16_t *Vc,
+                               int64_t seq_stride, int T, const int32_t *pos0, void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!Xq || !sX || !Wqkv || !sWqkv || !bqkv || !Q || !Kc || !Vc || M < 0 || d <= 0 || T <= 0 ||
+      M % T != 0 || ldq < d)
+    return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  LinearArgs a = make_args(EPI_QKV, M, 3 * d, d, sX, sWqkv, bqkv, nullptr, 0, Q, ldq);
+  a.Kc = Kc;
+  a.Vc = Vc;
+  a.seq_stride = seq_stride;
+  a.T = T;
+  a.pos0 = pos0;
+  a.dseg = d;
+  return dispatch_linear(Xq, d, Wqkv, a, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_attention_prefill(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,
+                                      const gpt2_bf16_t *Vc, int64_t seq_stride, int n_seq, int T,
+                                      int n_head, int head_dim, gpt2_bf16_t *O, int64_t ldo,
+                                      void *stream) {
+  if (n_seq == 0 || T == 0) return W8A8_OK;
+  if (!Q || !Kc || !Vc || !O || n_seq < 0 || T < 0 || n_head <= 0) return W8A8_ERR_INVALID;
+  if (head_dim != 64 || T > 1024) return W8A8_ERR_UNSUPPORTED;
+  if (ldq % 8 || ldo % 2 || seq_stride % 8 || !aligned16(Q) || !aligned16(Kc) || !aligned16(Vc) ||
+      ((uintptr_t)O & 3))
+    return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  return launch_attention_prefill(Q, ldq, Kc, Vc, seq_stride, n_seq, T, n_head, O, ldo,
+                                  (cudaStream_t)stream);
+}
+
+extern "C" size_t w8a8_attention_decode_workspace_size(int n_seq, int n_head, int max_ctx) {
+  // sized for the largest split count the launcher may pick
+  int splits = 1;
+  while (splits * 2 * 64 <= max_ctx) splits *= 2;
+  return decode_workspace_bytes(n_seq, n_head, max_ctx, splits);
+}
+
+extern "C" int w8a8_attention_decode(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,
+                                     const gpt2_bf16_t *Vc, int64_t seq_stride, int n_seq,
+                                     const int32_t *n_ctx, int max_ctx, int n_head, int head_dim,
+                                     gpt2_bf16_t *O, int64_t ldo, void *workspace,
+                                     size_t workspace_bytes, void *stream) {
+  if (n_seq == 0) return W8A8_OK;
+  if (!Q || !Kc || !Vc || !O || !workspace || n_seq < 0 || n_head <= 0 || max_ctx <= 0)
+    return W8A8_ERR_INVALID;
+  if (head_dim != 64 || max_ctx > 1024) return W8A8_ERR_UNSUPPORTED;
+  if (ldq % 8 || seq_stride % 8 || !aligned16(Q) || !aligned16(Kc) || !aligned16(Vc))
+    return W8A8_ERR_INVALID;
+  int st;
+  DeviceCtx *c = device_ctx(&st);
+  if (!c) return st;
+  return launch_attention_decode(Q, ldq, Kc, Vc, seq_stride, n_seq, n_ctx, max_ctx, n_head, O, ldo,
+                                 workspace, workspace_bytes, c->sm_count, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_lm_head(const gpt2_bf16_t *Xf, int64_t ldx, int M, int d,
+                            const gpt2_bf16_t *wte, int V, gpt2_bf16_t *logits, int64_t ldl,
+                            void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!Xf || !wte || !logits || M < 0 || d <= 0 || V <= 0 || ldl < V || ldx < d)
+    return W8A8_ERR_INVALID;
+  if (d % 8 || ldx % 8 || !aligned16(Xf) || !aligned16(wte)) return W8A8_ERR_UNSUPPORTED;
+  int st = ready();
+  if (st) return st;
+  LinearArgs a = make_args(EPI_F32_BF16, M, V, d, nullptr, nullptr, nullptr, nullptr, 0, logits, ldl);
+  return gemm_tc_bf16(wte, Xf, ldx, a, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_sample_greedy(const gpt2_bf16_t *logits, int64_t ldl, int M, int V,
+                                  int32_t *out_tokens, int32_t *append_to, int64_t append_stride,
+                                  int32_t *append_pos, void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!logits || !out_tokens || M < 0 || V <= 0 || ldl < V) return W8A8_ERR_INVALID;
+  if (append_to && !append_pos) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  return launch_greedy_sample(logits, ldl, M, V, out_tokens, append_to, append_stride, append_pos,
+                              (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_advance_positions(int32_t *dst, const int32_t *src, int n, int delta,
+                                      void *stream) {
+  if (n == 0) return W8A8_OK;
+  if (!dst || !src || n < 0) return W8A8_ERR_INVALID;
+  return launch_advance(dst, src, n, delta, (cudaStream_t)stream);
+}

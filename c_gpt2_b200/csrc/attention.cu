@@ -1,0 +1,517 @@
+// Causal multi-head attention over the bf16 KV cache (head_dim 64).
+//
+// Reference dataflow per head (gpt2.c:1182-1219 with cuda/softmax.cu:24-92):
+//   S   = bf16(alpha * q.k)            cuBLAS bf16 GEMM, fp32 accumulate,
+//                                       alpha = 1/sqrt(64) = 0.125 (exact)
+//   m   = max_j S_j                     (j <= query position)
+//   e_j = expf(S_j - m)                 written as bf16; summed unrounded
+//   sum = 256-slot tree of e_j          (thread t of 256 adds j = t, t+256, ..)
+//   P_j = bf16(float(bf16(e_j)) * (1/sum))
+//   O   = bf16(sum_j P_j V_j)           cuBLAS bf16 GEMM, fp32 accumulate
+// These kernels keep every rounding point, and the softmax sum uses the same
+// 256-slot tree, so P is bit-identical to the reference for identical S.
+// The S and O dot products accumulate in a fixed order of ours (the
+// reference's order is cuBLAS's), so S and O agree within rounding.
+//
+// Prefill: one CTA per (sequence, head, 64-query tile). Scores for the whole
+// causal row block live in shared memory as bf16 (<= 128 KB at 1024 keys),
+// so softmax needs no online rescaling and P is formed exactly as above.
+// Q.K^T and P.V run on mma.sync bf16 tensor-core fragments.
+//
+// Decode: per (sequence, head), keys split over CTAs when the batch alone
+// cannot fill the GPU. Kernel 1 writes bf16 scores to the workspace; kernel 2
+// forms P from the full score row (every split recomputes the row's max and
+// tree sum, so no split needs another's result) and accumulates its share of
+// P.V; the last split to finish (ticket counter, no waiting) adds the partials
+// in split order and rounds.
+#include "common.cuh"
+#include "runtime.cuh"
+
+namespace w8a8 {
+
+constexpr int kHD = 64;  // head_dim of every GPT-2 size (model_config.h: d_model / nof_heads)
+
+// ---------------------------------------------------------------------------
+// warp-level helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                        uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                          uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool pred) {
+  const int sz = pred ? 16 : 0;  // zero-fill when out of range
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(sz)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+// Reference softmax sum: 256 partials folded pairwise (s = 128 .. 1). Lane l
+// holds slots l + 32*i, i < 8.
+__device__ __forceinline__ float tree256(float (&v)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] += v[i + 4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) v[i] += v[i + 2];
+  float x = v[0] + v[1];
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) x += __shfl_down_sync(0xffffffffu, x, s);
+  return __shfl_sync(0xffffffffu, x, 0);
+}
+
+// In-place softmax of one causal row held as bf16 in shared memory:
+// entries [0, n) hold S; on return they hold P, entries [n, n_pad) hold 0.
+__device__ __forceinline__ void softmax_row_inplace(uint16_t *row, int n, int n_pad, int lane) {
+  float mx = -INFINITY;
+  for (int j = lane; j < n; j += 32) mx = fmaxf(mx, bf2f(row[j]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float local_sum = 0.0f;
+    for (int j = lane + 32 * i; j < n; j += 256) {
+      float e = expf(bf2f(row[j]) - mx);
+      row[j] = f2bf(e);
+      local_sum += e;
+    }
+    v[i] = local_sum;
+  }
+  const float sum_exp = tree256(v);
+  const float inv_sum = 1.0f / sum_exp;
+  __syncwarp();
+  for (int j = lane; j < n_pad; j += 32)
+    row[j] = j < n ? f2bf(bf2f(row[j]) * inv_sum) : (uint16_t)0;
+  __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// prefill
+// ---------------------------------------------------------------------------
+constexpr int kQT = 64;          // query rows per CTA
+constexpr int kKT = 64;          // keys per K/V tile
+constexpr int kTileStride = 72;  // bf16 elements per smem tile row (64 + 8 pad)
+
+struct PrefillArgs {
+  const uint16_t *Q;
+  int64_t ldq;
+  const uint16_t *Kc, *Vc;
+  int64_t seq_stride;
+  int n_seq, T, n_head, d;
+  uint16_t *O;
+  int64_t ldo;
+  int s_stride;  // bf16 elements per score row in smem
+};
+
+__global__ void __launch_bounds__(128)
+    attention_prefill_kernel(PrefillArgs a) {
+  extern __shared__ __align__(16) uint16_t sm[];
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qt * kQT;
+  if (q0 >= a.T) return;
+  const int nk = min(q0 + kQT, a.T);  // keys visible to this query tile
+  const int n_ktiles = (nk + kKT - 1) / kKT;
+  const int nk_pad = n_ktiles * kKT;
+
+  uint16_t *sQ = sm;                            // [64][72]
+  uint16_t *sKV = sQ + kQT * kTileStride;       // [2][64][72]
+  uint16_t *sS = sKV + 2 * kKT * kTileStride;   // [64][s_stride]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x;
+
+  const uint16_t *Kb = a.Kc + (int64_t)b * a.seq_stride + h * kHD;
+  const uint16_t *Vb = a.Vc + (int64_t)b * a.seq_stride + h * kHD;
+  const uint16_t *Qb = a.Q + ((int64_t)b * a.T) * a.ldq + h * kHD;
+
+  // tile loader: 64 rows x 128 bytes = 512 x 16 B chunks, 4 per thread
+  auto load_tile = [&](uint16_t *dst, const uint16_t *src, int64_t ld, int row0, int nrows) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int c = tid + 128 * i;
+      int r = c >> 3, cc = (c & 7) * 8;
+      bool ok = row0 + r < nrows;
+      const uint16_t *g = src + (int64_t)(ok ? row0 + r : 0) * ld + cc;
+      cp_async16(dst + r * kTileStride + cc, g, ok);
+    }
+  };
+
+  load_tile(sQ, Qb, a.ldq, q0, a.T);
+  load_tile(sKV, Kb, a.d, 0, nk);
+  cp_async_commit();
+
+  // Q fragments (rows 16*warp .. +15), 4 k-steps of 16
+  uint32_t qa[4][4];
+  const int g = lane >> 2, tq = lane & 3;
+
+  // ---- phase A: S = bf16(0.125 * Q K^T) into sS ----
+  for (int kt = 0; kt < n_ktiles; ++kt) {
+    cp_async_wait_all();
+    __syncthreads();
+    if (kt + 1 < n_ktiles) {
+      load_tile(sKV + ((kt + 1) & 1) * kKT * kTileStride, Kb, a.d, (kt + 1) * kKT, nk);
+      cp_async_commit();
+    }
+    if (kt == 0) {
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint16_t *p = sQ + (warp * 16 + (lane & 15)) * kTileStride + ks * 16 + (lane >> 4) * 8;
+        ldsm_x4(smem_u32(p), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+      }
+    }
+    const uint16_t *sK = sKV + (kt & 1) * kKT * kTileStride;
+    float c[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) c[nb][i] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int nb2 = 0; nb2 < 4; ++nb2) {  // pairs of 8-key blocks
+        const int q = lane >> 3;
+        const uint16_t *p =
+            sK + (nb2 * 16 + (q >> 1) * 8 + (lane & 7)) * kTileStride + ks * 16 + (q & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(p), b0, b1, b2, b3);
+        mma_bf16_16816(c[2 * nb2], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+        mma_bf16_16816(c[2 * nb2 + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+      }
+    }
+    // scale, round, store (columns beyond a row's causal limit are never read)
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+      const int col = kt * kKT + nb * 8 + 2 * tq;
+      const int r0 = warp * 16 + g;
+      uint32_t lo = (uint32_t)f2bf(c[nb][0] * 0.125f) | ((uint32_t)f2bf(c[nb][1] * 0.125f) << 16);
+      uint32_t hi = (uint32_t)f2bf(c[nb][2] * 0.125f) | ((uint32_t)f2bf(c[nb][3] * 0.125f) << 16);
+      *reinterpret_cast<uint32_t *>(sS + r0 * a.s_stride + col) = lo;
+      *reinterpret_cast<uint32_t *>(sS + (r0 + 8) * a.s_stride + col) = hi;
+    }
+  }
+  __syncthreads();
+
+  // prefetch V tile 0 while the softmax runs
+  load_tile(sKV, Vb, a.d, 0, nk);
+  cp_async_commit();
+
+  // ---- phase B: causal softmax per row (warp w: rows w, w+4, ...) ----
+  for (int r = warp; r < kQT; r += 4) {
+    const int qpos = q0 + r;
+    const int n = qpos < a.T ? qpos + 1 : 0;
+    softmax_row_inplace(sS + r * a.s_stride, n, nk_pad, lane);
+  }
+
+  // ---- phase C: O = P V ----
+  float o[8][4];
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[nb][i] = 0.f;
+  for (int kt = 0; kt < n_ktiles; ++kt) {
+    cp_async_wait_all();
+    __syncthreads();
+    if (kt + 1 < n_ktiles) {
+      load_tile(sKV + ((kt + 1) & 1) * kKT * kTileStride, Vb, a.d, (kt + 1) * kKT, nk);
+      cp_async_commit();
+    }
+    const uint16_t *sV = sKV + (kt & 1) * kKT * kTileStride;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {  // 16 keys per step
+      uint32_t pa0, pa1, pa2, pa3;
+      const uint16_t *pp =
+          sS + (warp * 16 + (lane & 15)) * a.s_stride + kt * kKT + ks * 16 + (lane >> 4) * 8;
+      ldsm_x4(smem_u32(pp), pa0, pa1, pa2, pa3);
+#pragma unroll
+      for (int nb2 = 0; nb2 < 4; ++nb2) {  // pairs of 8-dim blocks
+        const int q = lane >> 3;
+        const uint16_t *p =
+            sV + (ks * 16 + (q & 1) * 8 + (lane & 7)) * kTileStride + nb2 * 16 + (q >> 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(p), b0, b1, b2, b3);
+        mma_bf16_16816(o[2 * nb2], pa0, pa1, pa2, pa3, b0, b1);
+        mma_bf16_16816(o[2 * nb2 + 1], pa0, pa1, pa2, pa3, b2, b3);
+      }
+    }
+  }
+  // ---- store O ----
+  const int r0 = warp * 16 + g;
+#pragma unroll
+  for (int nb = 0; nb < 8; ++nb) {
+    const int col = h * kHD + nb * 8 + 2 * tq;
+    if (q0 + r0 < a.T) {
+      uint32_t v = (uint32_t)f2bf(o[nb][0]) | ((uint32_t)f2bf(o[nb][1]) << 16);
+      *reinterpret_cast<uint32_t *>(a.O + ((int64_t)b * a.T + q0 + r0) * a.ldo + col) = v;
+    }
+    if (q0 + r0 + 8 < a.T) {
+      uint32_t v = (uint32_t)f2bf(o[nb][2]) | ((uint32_t)f2bf(o[nb][3]) << 16);
+      *reinterpret_cast<uint32_t *>(a.O + ((int64_t)b * a.T + q0 + r0 + 8) * a.ldo + col) = v;
+    }
+  }
+}
+
+int launch_attention_prefill(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
+                             const uint16_t *Vc, int64_t seq_stride, int n_seq, int T, int n_head,
+                             uint16_t *O, int64_t ldo, cudaStream_t s) {
+  PrefillArgs a;
+  a.Q = Q;
+  a.ldq = ldq;
+  a.Kc = Kc;
+  a.Vc = Vc;
+  a.seq_stride = seq_stride;
+  a.n_seq = n_seq;
+  a.T = T;
+  a.n_head = n_head;
+  a.d = n_head * kHD;
+  a.O = O;
+  a.ldo = ldo;
+  const int max_pad = ((T + kKT - 1) / kKT) * kKT;
+  a.s_stride = max_pad + 8;
+  size_t smem = (size_t)(kQT * kTileStride + 2 * kKT * kTileStride + kQT * a.s_stride) * 2;
+  if (smem > 227 * 1024) return W8A8_ERR_UNSUPPORTED;
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    cudaFuncSetAttribute(attention_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         227 * 1024);
+    attr[dev & 63] = true;
+  }
+  dim3 grid((T + kQT - 1) / kQT, n_head, n_seq);
+  attention_prefill_kernel<<<grid, 128, smem, s>>>(a);
+  return check_launch("attention_prefill");
+}
+
+// ---------------------------------------------------------------------------
+// decode
+// ---------------------------------------------------------------------------
+struct DecodeArgs {
+  const uint16_t *Q;
+  int64_t ldq;
+  const uint16_t *Kc, *Vc;
+  int64_t seq_stride;
+  int n_seq, n_head, d, max_ctx, splits, keys_per_split;
+  const int32_t *n_ctx;  // per-sequence key counts, or NULL: every sequence uses max_ctx
+  uint16_t *O;
+  int64_t ldo;
+  uint16_t *scores;   // [n_seq][n_head][max_ctx]
+  float *partials;    // [n_seq][n_head][splits][64]
+  int *tickets;       // [n_seq][n_head]
+};
+
+// Kernel 1: S_j = bf16(0.125 * q.k_j) for this split's keys. 8 lanes cover
+// one 128-byte key row (16 bytes each), a warp 4 keys per step.
+__global__ void __launch_bounds__(256) attention_decode_scores_kernel(DecodeArgs a) {
+  const int bh = blockIdx.x, split = blockIdx.y;
+  const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
+  const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
+  const int j0 = split * a.keys_per_split;
+  const int j1 = min(n, j0 + a.keys_per_split);
+  if (j0 >= j1) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane >> 3, part = lane & 7;  // key within step, 16-byte part
+  const uint4 qv = *reinterpret_cast<const uint4 *>(a.Q + (int64_t)b * a.ldq + h * kHD + part * 8);
+  float q[8];
+  {
+    const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      q[2 * i] = __uint_as_float(w[i] << 16);
+      q[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  const uint16_t *Kb = a.Kc + (int64_t)b * a.seq_stride + h * kHD + part * 8;
+  uint16_t *srow = a.scores + ((int64_t)b * a.n_head + h) * a.max_ctx;
+  // warp w handles keys j0 + 32*step + 4*w + sub: 4 keys per warp step,
+  // 32 keys per block step
+  for (int jb = j0 + warp * 4; jb < j1; jb += 32) {
+    const int j = jb + sub;
+    float s = 0.f;
+    if (j < j1) {
+      const uint4 kv = __ldg(reinterpret_cast<const uint4 *>(Kb + (int64_t)j * a.d));
+      const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        s = fmaf(q[2 * i], __uint_as_float(w[i] << 16), s);
+        s = fmaf(q[2 * i + 1], __uint_as_float(w[i] & 0xffff0000u), s);
+      }
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if (part == 0 && j < j1) srow[j] = f2bf(s * 0.125f);
+  }
+}
+
+// Kernel 2: softmax from the full score row + this split's share of P.V.
+__global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) {
+  __shared__ float s_red[8];
+  __shared__ float s_part[8][kHD];
+  __shared__ float s_p[1024];
+  __shared__ int s_last;
+  const int bh = blockIdx.x, split = blockIdx.y;
+  const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
+  const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
+  const int j0 = split * a.keys_per_split;
+  const int j1 = min(n, j0 + a.keys_per_split);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint16_t *srow = a.scores + ((int64_t)b * a.n_head + h) * a.max_ctx;
+
+  // max over the whole row
+  float mx = -INFINITY;
+  for (int j = tid; j < n; j += 256) mx = fmaxf(mx, bf2f(srow[j]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) s_red[warp] = mx;
+  __syncthreads();
+  mx = s_red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_red[w]);
+  __syncthreads();
+  // reference tree sum: thread t adds j = t, t+256, ... ; then s = 128 .. 1
+  float local_sum = 0.0f;
+  for (int j = tid; j < n; j += 256) local_sum += expf(bf2f(srow[j]) - mx);
+  __shared__ float s_tree[256];
+  s_tree[tid] = local_sum;
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if (tid < s) s_tree[tid] += s_tree[tid + s];
+    __syncthreads();
+  }
+  const float inv_sum = 1.0f / s_tree[0];
+  // P for this split's keys
+  for (int j = j0 + tid; j < j1; j += 256) {
+    float e = expf(bf2f(srow[j]) - mx);
+    s_p[j - j0] = bf2f(f2bf(bf2f(f2bf(e)) * inv_sum));
+  }
+  __syncthreads();
+  // P.V: 8 lanes per 128-byte V row (8 dims each), 4 rows per warp step
+  const int sub = lane >> 3, part = lane & 7;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  const uint16_t *Vb = a.Vc + (int64_t)b * a.seq_stride + h * kHD + part * 8;
+  for (int j = j0 + warp * 4 + sub; j < j1; j += 32) {
+    const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(Vb + (int64_t)j * a.d));
+    const float p = s_p[j - j0];
+    const uint32_t w[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[2 * i] = fmaf(p, __uint_as_float(w[i] << 16), acc[2 * i]);
+      acc[2 * i + 1] = fmaf(p, __uint_as_float(w[i] & 0xffff0000u), acc[2 * i + 1]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 8);
+    acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 16);
+  }
+  if (sub == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s_part[warp][part * 8 + i] = acc[i];
+  }
+  __syncthreads();
+  float o = 0.f;
+  if (tid < kHD) {
+#pragma unroll
+    for (int w = 0; w < 8; ++w) o += s_part[w][tid];
+  }
+  if (a.splits == 1) {
+    if (tid < kHD) a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(o);
+    return;
+  }
+  float *part_out = a.partials + (((int64_t)b * a.n_head + h) * a.splits + split) * kHD;
+  if (tid < kHD) part_out[tid] = o;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    int ticket = atomicAdd(&a.tickets[b * a.n_head + h], 1);
+    s_last = (ticket == a.splits - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid < kHD) {
+    const float *pp = a.partials + ((int64_t)b * a.n_head + h) * a.splits * kHD;
+    float tot = 0.f;
+    for (int sidx = 0; sidx < a.splits; ++sidx) tot += __ldcg(pp + sidx * kHD + tid);
+    a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(tot);
+  }
+  if (tid == 0) a.tickets[b * a.n_head + h] = 0;  // ready for the next call
+}
+
+static int decode_splits(int n_seq, int n_head, int max_ctx, int sm_count) {
+  const int pairs = n_seq * n_head;
+  int splits = 1;
+  while (pairs * splits < 2 * sm_count && splits * 2 * 64 <= max_ctx) splits *= 2;
+  return splits;
+}
+
+size_t decode_workspace_bytes(int n_seq, int n_head, int max_ctx, int splits) {
+  size_t scores = (size_t)n_seq * n_head * max_ctx * 2;
+  scores = (scores + 255) & ~(size_t)255;
+  size_t parts = (size_t)n_seq * n_head * splits * kHD * 4;
+  size_t tick = (size_t)n_seq * n_head * 4;
+  return scores + parts + tick + 256;
+}
+
+int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
+                            const uint16_t *Vc, int64_t seq_stride, int n_seq,
+                            const int32_t *n_ctx, int max_ctx, int n_head, uint16_t *O,
+                            int64_t ldo, void *ws, size_t ws_bytes, int sm_count,
+                            cudaStream_t s) {
+  DecodeArgs a;
+  a.Q = Q;
+  a.ldq = ldq;
+  a.Kc = Kc;
+  a.Vc = Vc;
+  a.seq_stride = seq_stride;
+  a.n_seq = n_seq;
+  a.n_head = n_head;
+  a.d = n_head * kHD;
+  a.max_ctx = max_ctx;
+  a.n_ctx = n_ctx;
+  a.O = O;
+  a.ldo = ldo;
+  a.splits = decode_splits(n_seq, n_head, max_ctx, sm_count);
+  a.keys_per_split = (max_ctx + a.splits - 1) / a.splits;
+  if (decode_workspace_bytes(n_seq, n_head, max_ctx, a.splits) > ws_bytes)
+    return W8A8_ERR_INVALID;
+  uint8_t *w = (uint8_t *)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
+  a.scores = (uint16_t *)w;
+  size_t scores = ((size_t)n_seq * n_head * max_ctx * 2 + 255) & ~(size_t)255;
+  a.partials = (float *)(w + scores);
+  a.tickets = (int *)(w + scores + (size_t)n_seq * n_head * a.splits * kHD * 4);
+  dim3 grid(n_seq * n_head, a.splits);
+  if (a.splits > 1 &&
+      cudaMemsetAsync(a.tickets, 0, (size_t)n_seq * n_head * sizeof(int), s) != cudaSuccess)
+    return W8A8_ERR_CUDA;
+  attention_decode_scores_kernel<<<grid, 256, 0, s>>>(a);
+  int st = check_launch("attention_decode_scores");
+  if (st) return st;
+  attention_decode_pv_kernel<<<grid, 256, 0, s>>>(a);
+  return check_launch("attention_decode_pv");
+}
+
+}  // namespace w8a8

@@ -1,0 +1,175 @@
+// HBM-streaming INT8 GEMV for decode (1..15 tokens) and the CUDA-core
+// fallback for shapes the TMA path cannot take (K % 16 != 0, unaligned rows).
+//
+// One warp owns one output channel n: it streams W[n, :] with 16-byte loads
+// (8 independent loads in flight per lane), multiplies against the token
+// rows held in shared memory with dp4a, and reduces across lanes. A block
+// holds 4 warps; the grid covers N/4 blocks, so even the 768-row projections
+// of GPT-2 small spread over more blocks than the B200 has SMs. Exact integer
+// accumulation: results are identical to the tensor-core path, and the same
+// fused epilogues apply.
+#include "common.cuh"
+#include "epilogue.cuh"
+#include "kernels.cuh"
+#include "runtime.cuh"
+
+namespace w8a8 {
+
+typedef LinearArgs GemvArgs;
+
+constexpr int kGemvWarps = 4;
+
+__device__ __forceinline__ void gemv_store(const GemvArgs &a, int m, int n, int32_t acc) {
+  float sw = (a.epi != 0) ? a.sW[n] : 0.f;
+  float sx = (a.epi != 0) ? a.sX[m] : 0.f;
+  switch (a.epi) {
+    case 0:
+      reinterpret_cast<int32_t *>(a.Y)[(int64_t)m * a.ldy + n] = acc;
+      break;
+    case 1:
+      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(dequant_bf(acc, sw, sx));
+      break;
+    case 2:
+      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] =
+          f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bf2f(a.bias[n])));
+      break;
+    case 3: {
+      float y = add_bf(dequant_bf(acc, sw, sx), bf2f(a.bias[n]));
+      float r = bf2f(a.R[(int64_t)m * a.ldr + n]);
+      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(__fadd_rn(r, y));
+      break;
+    }
+    case 4: {
+      float y = add_bf(dequant_bf(acc, sw, sx), bf2f(a.bias[n]));
+      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(gelu_tanh(y));
+      break;
+    }
+    default: {  // QKV scatter
+      uint16_t v = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bf2f(a.bias[n])));
+      int seg = n / a.dseg, col = n - (n / a.dseg) * a.dseg;
+      if (seg == 0) {
+        reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + col] = v;
+      } else {
+        int b = m / a.T, t = m - (m / a.T) * a.T;
+        int p = (a.pos0 ? a.pos0[b] : 0) + t;
+        uint16_t *base = seg == 1 ? a.Kc : a.Vc;
+        base[(int64_t)b * a.seq_stride + (int64_t)p * a.dseg + col] = v;
+      }
+      break;
+    }
+  }
+}
+
+// Vector path: K % 16 == 0 and 16-byte aligned rows.
+template <int MT>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    gemv_i8_vec_kernel(const int8_t *__restrict__ X, int64_t ldx, const int8_t *__restrict__ W,
+                       GemvArgs a) {
+  extern __shared__ int4 xs4[];  // [MT][K] int8
+  int8_t *xs = reinterpret_cast<int8_t *>(xs4);
+  const int K = a.K;
+  const int kv = K >> 4;  // 16-byte vectors per row
+  for (int i = threadIdx.x; i < MT * kv; i += blockDim.x) {
+    int m = i / kv, v = i - (i / kv) * kv;
+    int4 val = make_int4(0, 0, 0, 0);
+    if (m < a.M) val = __ldg(reinterpret_cast<const int4 *>(X + (int64_t)m * ldx) + v);
+    xs4[i] = val;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * kGemvWarps + warp;
+  if (n >= a.N) return;
+  const int4 *wrow = reinterpret_cast<const int4 *>(W + (int64_t)n * K);
+  int acc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] = 0;
+  constexpr int U = 8;
+  int v = lane;
+  for (; v + 32 * (U - 1) < kv; v += 32 * U) {
+    int4 w[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) w[u] = __ldg(wrow + v + 32 * u);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        int4 x = xs4[m * kv + v + 32 * u];
+        acc[m] = __dp4a(w[u].x, x.x, acc[m]);
+        acc[m] = __dp4a(w[u].y, x.y, acc[m]);
+        acc[m] = __dp4a(w[u].z, x.z, acc[m]);
+        acc[m] = __dp4a(w[u].w, x.w, acc[m]);
+      }
+    }
+  }
+  for (; v < kv; v += 32) {
+    int4 w = __ldg(wrow + v);
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      int4 x = xs4[m * kv + v];
+      acc[m] = __dp4a(w.x, x.x, acc[m]);
+      acc[m] = __dp4a(w.y, x.y, acc[m]);
+      acc[m] = __dp4a(w.z, x.z, acc[m]);
+      acc[m] = __dp4a(w.w, x.w, acc[m]);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+  }
+  // lane m stores token m (spreads the epilogue over the warp)
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+    if (lane == m && m < a.M) gemv_store(a, m, n, acc[m]);
+}
+
+// Scalar fallback for any K / alignment (correctness path, not a hot path).
+__global__ void gemv_i8_scalar_kernel(const int8_t *__restrict__ X, int64_t ldx,
+                                      const int8_t *__restrict__ W, GemvArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * kGemvWarps + warp;
+  const int m = blockIdx.y;
+  if (n >= a.N || m >= a.M) return;
+  int acc = 0;
+  for (int k = lane; k < a.K; k += 32)
+    acc += (int)X[(int64_t)m * ldx + k] * (int)W[(int64_t)n * a.K + k];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) gemv_store(a, m, n, acc);
+}
+
+template <int MT>
+static int launch_vec(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs &a,
+                      cudaStream_t s) {
+  size_t smem = (size_t)MT * a.K;
+  if (smem > 160 * 1024) return W8A8_ERR_UNSUPPORTED;
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    cudaFuncSetAttribute(gemv_i8_vec_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         160 * 1024);
+    attr[dev & 63] = true;
+  }
+  dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps);
+  gemv_i8_vec_kernel<MT><<<grid, kGemvWarps * 32, smem, s>>>(X, ldx, W, a);
+  return check_launch("gemv_i8_vec");
+}
+
+int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs &a,
+                   cudaStream_t s) {
+  const bool vec = (a.K % 16 == 0) && (ldx % 16 == 0) && aligned16(X) && aligned16(W);
+  if (vec && a.M <= 16) {
+    if (a.M <= 1) return launch_vec<1>(X, ldx, W, a, s);
+    if (a.M <= 2) return launch_vec<2>(X, ldx, W, a, s);
+    if (a.M <= 4) return launch_vec<4>(X, ldx, W, a, s);
+    if (a.M <= 8) return launch_vec<8>(X, ldx, W, a, s);
+    return launch_vec<16>(X, ldx, W, a, s);
+  }
+  if (a.M > 65535) return W8A8_ERR_UNSUPPORTED;
+  dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps, a.M);
+  gemv_i8_scalar_kernel<<<grid, kGemvWarps * 32, 0, s>>>(X, ldx, W, a);
+  return check_launch("gemv_i8_scalar");
+}
+
+}  // namespace w8a8

@@ -1,0 +1,76 @@
+// Launcher interfaces shared between the kernel files and the C-ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace w8a8 {
+
+// Epilogue of the INT8 GEMM / GEMV (see epilogue.cuh for the arithmetic).
+enum EpiKind {
+  EPI_S32 = 0,       // raw int32 accumulators
+  EPI_DEQUANT = 1,   // bf16(acc*sW*sX)
+  EPI_BIAS = 2,      // + bias
+  EPI_RESID = 3,     // + bias, + residual
+  EPI_GELU = 4,      // + bias, gelu
+  EPI_QKV = 5,       // + bias, scatter into Q / K cache / V cache
+  EPI_F32_BF16 = 6,  // bf16(acc) for the bf16 LM head
+};
+
+// Arguments of the INT8 linear layer shared by the tensor-core GEMM and the
+// CUDA-core GEMV. M tokens, N output channels, K reduction length.
+struct LinearArgs {
+  int M, N, K;
+  int epi;
+  const float *sX;
+  const float *sW;
+  const uint16_t *bias;
+  const uint16_t *R;
+  int64_t ldr;
+  void *Y;
+  int64_t ldy;
+  // QKV scatter: column n -> segment n / dseg (0 = Q in Y, 1 = K cache,
+  // 2 = V cache); token m = b*T + t lands at cache row pos0[b] + t.
+  uint16_t *Kc, *Vc;
+  int64_t seq_stride;
+  int T;
+  const int32_t *pos0;
+  int dseg;
+};
+
+// gemm_tc.cu
+int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,
+               cudaStream_t stream);
+int gemm_tc_bf16(const uint16_t *W, const uint16_t *X, int64_t ldx, const LinearArgs &a,
+                 cudaStream_t stream);
+// gemv_i8.cu
+int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const LinearArgs &a,
+                   cudaStream_t s);
+// norm_quant.cu
+int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, float *sX,
+                      cudaStream_t s);
+int launch_layernorm_quant(const uint16_t *X, int64_t ldx, int M, int d, const uint16_t *gamma,
+                           const uint16_t *beta, float eps, uint16_t *Y, int64_t ldy, int8_t *Xq,
+                           float *sX, cudaStream_t s);
+int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const int32_t *tokens,
+                                 int M, int T, const int32_t *pos0, int d, uint16_t *H,
+                                 const uint16_t *gamma, const uint16_t *beta, float eps,
+                                 uint16_t *Y, int8_t *Xq, float *sX, cudaStream_t s);
+// attention.cu
+int launch_attention_prefill(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
+                             const uint16_t *Vc, int64_t seq_stride, int n_seq, int T, int n_head,
+                             uint16_t *O, int64_t ldo, cudaStream_t s);
+size_t decode_workspace_bytes(int n_seq, int n_head, int max_ctx, int splits);
+int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
+                            const uint16_t *Vc, int64_t seq_stride, int n_seq,
+                            const int32_t *n_ctx, int max_ctx, int n_head, uint16_t *O,
+                            int64_t ldo, void *ws, size_t ws_bytes, int sm_count,
+                            cudaStream_t s);
+// sample.cu
+int launch_greedy_sample(const uint16_t *logits, int64_t ldl, int M, int V, int32_t *out,
+                         int32_t *append_to, int64_t append_stride, int32_t *append_pos,
+                         cudaStream_t s);
+int launch_advance(int32_t *dst, const int32_t *src, int n, int delta, cudaStream_t s);
+
+}  // namespace w8a8

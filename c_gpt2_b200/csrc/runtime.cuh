@@ -1,0 +1,37 @@
+// Per-device runtime state shared by the kernel launchers: SM count, device
+// error word, TMA descriptor encoder (resolved through the runtime's driver
+// entry-point query, so the library links against libcudart only).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gpt2_w8a8.h"
+
+namespace w8a8 {
+
+struct DeviceCtx {
+  int ready;
+  int sm_count;
+  int *err;  // device error word (in device memory of this device)
+};
+
+// Returns the context of the current device, initialising it on first use
+// (first use must not happen inside stream capture; w8a8_init does it early).
+DeviceCtx *device_ctx(int *status);
+
+// 2-D row-major tensor map: `rows` x `cols` elements, row pitch in bytes,
+// box of box_cols x box_rows, 128-byte swizzle, out-of-bounds reads as zero.
+int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, uint64_t rows,
+                 uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows);
+
+inline int check_launch(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  (void)what;
+  return e == cudaSuccess ? W8A8_OK : W8A8_ERR_CUDA;
+}
+
+__host__ __device__ inline bool aligned16(const void *p) { return (((uintptr_t)p) & 15u) == 0; }
+
+}  // namespace w8a8

@@ -1,0 +1,573 @@
+/*
+ * Batched W8A8 GPT-2 inference host engine (C). See include/gpt2_engine.h.
+ *
+ * Per layer, the reference runs 3 quant+GEMM+dequant triplets for Q/K/V, 3
+ * bias adds, H x (QK^T, softmax, PV), concat, and 5 more launch groups for
+ * the projection / MLP (gpt2.c:1124-1330). Here a layer is 9 launches:
+ *
+ *   LN1+quant -> QKV GEMM (dequant, bias, scatter into Q and the KV cache)
+ *   -> attention -> quant -> proj GEMM (dequant, bias, residual)
+ *   -> LN2+quant -> W1 GEMM (dequant, bias, GELU) -> quant
+ *   -> W2 GEMM (dequant, bias, residual)
+ *
+ * with the first LN1 fused into the embedding gather. Each intermediate is
+ * rounded to bf16 where the reference rounds it, so every output element is
+ * the reference's value for the same inputs (see gpt2_w8a8.h).
+ */
+#include "../../include/gpt2_engine.h"
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define ALIGN_UP(x, a) (((x) + ((size_t)(a)-1)) & ~((size_t)(a)-1))
+
+typedef struct {
+  gpt2_bf16_t *ln1_g, *ln1_b, *bqkv, *bproj, *ln2_g, *ln2_b, *b1, *b2;
+  int8_t *Wqkv, *Wproj, *W1, *W2;
+  float *sWqkv, *sWproj, *sW1, *sW2;
+} layer_w;
+
+struct gpt2_engine {
+  gpt2_engine_config cfg;
+  int device;
+  cudaStream_t stream;
+  char err[256];
+  /* weights */
+  void *wblob;
+  size_t wbytes;
+  gpt2_bf16_t *wte, *wpe, *lnf_g, *lnf_b;
+  layer_w *layers;
+  int loaded;
+  /* KV cache [max_batch][L][ctx][d] */
+  gpt2_bf16_t *Kc, *Vc;
+  /* activations */
+  void *ablob;
+  gpt2_bf16_t *H, *R1, *Q, *ATT, *X1, *Xf, *logits;
+  int8_t *Xq;
+  float *sX;
+  int32_t *len, *nctx, *gen, *next, *tokens_in, *out_default;
+  void *attn_ws;
+  size_t attn_ws_bytes;
+  /* current batch */
+  int B;
+  int32_t *out;
+  int out_stride;
+  /* decode graph */
+  int use_graphs;
+  cudaGraphExec_t graph;
+  int graph_B;
+  int32_t *graph_out;
+};
+
+static int fail(gpt2_engine *e, int st, const char *fmt, ...) {
+  if (e) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(e->err, sizeof e->err, fmt, ap);
+    va_end(ap);
+  }
+  return st;
+}
+
+#define CUDA_TRY(e, call)                                                           \
+  do {                                                                              \
+    cudaError_t err__ = (call);                                                     \
+    if (err__ != cudaSuccess)                                                       \
+      return fail((e), W8A8_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(err__)); \
+  } while (0)
+
+#define W8_TRY(e, call)                                                          \
+  do {                                                                           \
+    int st__ = (call);                                                           \
+    if (st__ != W8A8_OK)                                                         \
+      return fail((e), st__, "%s: %s", #call, w8a8_status_string(st__));         \
+  } while (0)
+
+const char *gpt2_engine_last_error(const gpt2_engine *e) { return e ? e->err : "null engine"; }
+void *gpt2_engine_stream(gpt2_engine *e) { return e ? (void *)e->stream : NULL; }
+
+static int cfg_ok(const gpt2_engine_config *c) {
+  return c && c->d_model > 0 && c->n_layer > 0 && c->n_head > 0 && c->d_model % c->n_head == 0 &&
+         c->d_model / c->n_head == 64 && c->d_model % 16 == 0 && c->vocab > 0 && c->ctx > 0 &&
+         c->ctx <= 1024 && c->max_batch > 0 && c->max_tokens >= c->max_batch;
+}
+
+/* ---- quant8.bin layout (writer.py: every block padded to 16 bytes) ---- */
+static size_t blk(size_t bytes) { return ALIGN_UP(bytes, 16); }
+
+size_t gpt2_engine_quant8_bytes(const gpt2_engine_config *c) {
+  if (!c) return 0;
+  const size_t d = c->d_model, f = 4 * d;
+  size_t n = blk((size_t)c->vocab * d * 4) + blk((size_t)c->ctx * d * 4);
+  size_t per = 0;
+  per += 2 * blk(d * 4);                          /* ln1 */
+  per += blk(3 * d * d) + blk(3 * d * 4);         /* W_qkv + scale */
+  per += blk(3 * d * 4);                          /* b_qkv */
+  per += blk(d * d) + blk(d * 4) + blk(d * 4);    /* attn_proj + scale + bias */
+  per += 2 * blk(d * 4);                          /* ln2 */
+  per += blk(f * d) + blk(f * 4) + blk(f * 4);    /* W1 + scale + b1 */
+  per += blk(d * f) + blk(d * 4) + blk(d * 4);    /* W2 + scale + b2 */
+  n += per * c->n_layer;
+  n += 2 * blk(d * 4); /* lnf */
+  return n;
+}
+
+/* Device weight arena layout: tensors 256-byte aligned. */
+static size_t weight_arena_bytes(const gpt2_engine_config *c) {
+  const size_t d = c->d_model, f = 4 * d;
+  size_t n = 0;
+#define ADD(bytes) n += ALIGN_UP((bytes), 256)
+  ADD((size_t)c->vocab * d * 2);
+  ADD((size_t)c->ctx * d * 2);
+  for (int l = 0; l < c->n_layer; ++l) {
+    ADD(d * 2); ADD(d * 2);
+    ADD(3 * d * d); ADD(3 * d * 4); ADD(3 * d * 2);
+    ADD(d * d); ADD(d * 4); ADD(d * 2);
+    ADD(d * 2); ADD(d * 2);
+    ADD(f * d); ADD(f * 4); ADD(f * 2);
+    ADD(d * f); ADD(d * 4); ADD(d * 2);
+  }
+  ADD(d * 2); ADD(d * 2);
+#undef ADD
+  return n;
+}
+
+static uint16_t f32_to_bf16(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u); /* quiet NaN */
+  u += 0x7fffu + ((u >> 16) & 1u); /* round to nearest, ties to even */
+  return (uint16_t)(u >> 16);
+}
+
+/* Host-side parse of the quant8 image into a host staging copy of the device
+ * arena, then one H2D copy. */
+typedef struct {
+  const uint8_t *p;
+  size_t left;
+} reader;
+
+static int rd_take(reader *r, size_t bytes, const uint8_t **out) {
+  size_t padded = blk(bytes);
+  if (r->left < padded) return 0;
+  *out = r->p;
+  r->p += padded;
+  r->left -= padded;
+  return 1;
+}
+
+int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **out) {
+  if (!out) return W8A8_ERR_INVALID;
+  *out = NULL;
+  if (!cfg_ok(cfg)) return W8A8_ERR_INVALID;
+  gpt2_engine *e = (gpt2_engine *)calloc(1, sizeof *e);
+  if (!e) return W8A8_ERR_NOMEM;
+  e->cfg = *cfg;
+  e->device = device;
+  e->use_graphs = 1;
+  e->layers = (layer_w *)calloc((size_t)cfg->n_layer, sizeof(layer_w));
+  if (!e->layers) {
+    free(e);
+    return W8A8_ERR_NOMEM;
+  }
+  int st = w8a8_init(device);
+  if (st != W8A8_OK) {
+    gpt2_engine_destroy(e);
+    return st;
+  }
+  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    gpt2_engine_destroy(e);
+    return W8A8_ERR_CUDA;
+  }
+  const size_t d = cfg->d_model, L = cfg->n_layer, C = cfg->ctx, Bm = cfg->max_batch;
+  const size_t Mt = cfg->max_tokens;
+  /* KV cache */
+  const size_t kv = Bm * L * C * d * 2;
+  if (cudaMalloc((void **)&e->Kc, kv) != cudaSuccess ||
+      cudaMalloc((void **)&e->Vc, kv) != cudaSuccess) {
+    gpt2_engine_destroy(e);
+    return W8A8_ERR_NOMEM;
+  }
+  /* activations */
+  e->attn_ws_bytes = w8a8_attention_decode_workspace_size((int)Bm, cfg->n_head, (int)C);
+  size_t off = 0, sizes[14];
+  sizes[0] = Mt * d * 2;        /* H */
+  sizes[1] = Mt * d * 2;        /* R1 */
+  sizes[2] = Mt * d * 2;        /* Q */
+  sizes[3] = Mt * d * 2;        /* ATT */
+  sizes[4] = Mt * 4 * d * 2;    /* X1 */
+  sizes[5] = Bm * d * 2;        /* Xf */
+  sizes[6] = Bm * (size_t)cfg->vocab * 2; /* logits */
+  sizes[7] = Mt * 4 * d;        /* Xq */
+  sizes[8] = Mt * 4;            /* sX */
+  sizes[9] = Bm * 4 * 4;        /* len, nctx, gen, next */
+  sizes[10] = Mt * 4;           /* tokens_in */
+  sizes[11] = Bm * 4 * (size_t)C; /* default output buffer */
+  sizes[12] = e->attn_ws_bytes;
+  sizes[13] = 0;
+  size_t offs[14];
+  for (int i = 0; i < 14; ++i) {
+    offs[i] = off;
+    off += ALIGN_UP(sizes[i], 256);
+  }
+  if (cudaMalloc(&e->ablob, off) != cudaSuccess) {
+    gpt2_engine_destroy(e);
+    return W8A8_ERR_NOMEM;
+  }
+  uint8_t *a = (uint8_t *)e->ablob;
+  e->H = (gpt2_bf16_t *)(a + offs[0]);
+  e->R1 = (gpt2_bf16_t *)(a + offs[1]);
+  e->Q = (gpt2_bf16_t *)(a + offs[2]);
+  e->ATT = (gpt2_bf16_t *)(a + offs[3]);
+  e->X1 = (gpt2_bf16_t *)(a + offs[4]);
+  e->Xf = (gpt2_bf16_t *)(a + offs[5]);
+  e->logits = (gpt2_bf16_t *)(a + offs[6]);
+  e->Xq = (int8_t *)(a + offs[7]);
+  e->sX = (float *)(a + offs[8]);
+  e->len = (int32_t *)(a + offs[9]);
+  e->nctx = e->len + Bm;
+  e->gen = e->len + 2 * Bm;
+  e->next = e->len + 3 * Bm;
+  e->tokens_in = (int32_t *)(a + offs[10]);
+  e->out_default = (int32_t *)(a + offs[11]);
+  e->attn_ws = a + offs[12];
+  if (cudaMemset(e->ablob, 0, off) != cudaSuccess) {
+    gpt2_engine_destroy(e);
+    return W8A8_ERR_CUDA;
+  }
+  *out = e;
+  return W8A8_OK;
+}
+
+void gpt2_engine_destroy(gpt2_engine *e) {
+  if (!e) return;
+  if (e->graph) cudaGraphExecDestroy(e->graph);
+  if (e->wblob) cudaFree(e->wblob);
+  if (e->ablob) cudaFree(e->ablob);
+  if (e->Kc) cudaFree(e->Kc);
+  if (e->Vc) cudaFree(e->Vc);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  free(e->layers);
+  free(e);
+}
+
+int gpt2_engine_load_quant8_memory(gpt2_engine *e, const void *data, size_t bytes) {
+  if (!e || !data) return W8A8_ERR_INVALID;
+  const gpt2_engine_config *c = &e->cfg;
+  if (bytes < gpt2_engine_quant8_bytes(c))
+    return fail(e, W8A8_ERR_IO, "quant8 image too short: %zu < %zu bytes", bytes,
+                gpt2_engine_quant8_bytes(c));
+  const size_t d = c->d_model, f = 4 * d;
+  const size_t arena = weight_arena_bytes(c);
+  uint8_t *host = (uint8_t *)malloc(arena);
+  if (!host) return fail(e, W8A8_ERR_NOMEM, "host staging of %zu bytes", arena);
+  memset(host, 0, arena);
+  if (!e->wblob) {
+    if (cudaMalloc(&e->wblob, arena) != cudaSuccess) {
+      free(host);
+      return fail(e, W8A8_ERR_NOMEM, "weights: cudaMalloc %zu", arena);
+    }
+    e->wbytes = arena;
+  }
+  reader r = {(const uint8_t *)data, bytes};
+  size_t off = 0;
+  uint8_t *dev = (uint8_t *)e->wblob;
+  const uint8_t *src;
+  int ok = 1;
+  /* helpers: place `count` elements at the next arena slot */
+#define SLOT(bytes_) (off = ALIGN_UP(off, 256), off += (bytes_), off - (bytes_))
+#define PUT_BF16(dst_ptr, count)                                                   \
+  do {                                                                             \
+    size_t n_ = (count);                                                           \
+    size_t o_ = SLOT(n_ * 2);                                                      \
+    if (!rd_take(&r, n_ * 4, &src)) { ok = 0; break; }                              \
+    uint16_t *h_ = (uint16_t *)(host + o_);                                        \
+    for (size_t i_ = 0; i_ < n_; ++i_) {                                           \
+      float v_;                                                                    \
+      memcpy(&v_, src + 4 * i_, 4);                                                \
+      h_[i_] = f32_to_bf16(v_);                                                    \
+    }                                                                              \
+    (dst_ptr) = (gpt2_bf16_t *)(dev + o_);                                         \
+  } while (0)
+#define PUT_RAW(dst_ptr, type, bytes_)                                             \
+  do {                                                                             \
+    size_t b_ = (bytes_);                                                          \
+    size_t o_ = SLOT(b_);                                                          \
+    if (!rd_take(&r, b_, &src)) { ok = 0; break; }                                  \
+    memcpy(host + o_, src, b_);                                                    \
+    (dst_ptr) = (type *)(dev + o_);                                                \
+  } while (0)
+
+  do {
+    PUT_BF16(e->wte, (size_t)c->vocab * d);
+    if (!ok) break;
+    PUT_BF16(e->wpe, (size_t)c->ctx * d);
+    if (!ok) break;
+    for (int l = 0; l < c->n_layer && ok; ++l) {
+      layer_w *w = &e->layers[l];
+      PUT_BF16(w->ln1_g, d);
+      if (!ok) break;
+      PUT_BF16(w->ln1_b, d);
+      if (!ok) break;
+      PUT_RAW(w->Wqkv, int8_t, 3 * d * d);
+      if (!ok) break;
+      PUT_RAW(w->sWqkv, float, 3 * d * 4);
+      if (!ok) break;
+      PUT_BF16(w->bqkv, 3 * d);
+      if (!ok) break;
+      PUT_RAW(w->Wproj, int8_t, d * d);
+      if (!ok) break;
+      PUT_RAW(w->sWproj, float, d * 4);
+      if (!ok) break;
+      PUT_BF16(w->bproj, d);
+      if (!ok) break;
+      PUT_BF16(w->ln2_g, d);
+      if (!ok) break;
+      PUT_BF16(w->ln2_b, d);
+      if (!ok) break;
+      PUT_RAW(w->W1, int8_t, f * d);
+      if (!ok) break;
+      PUT_RAW(w->sW1, float, f * 4);
+      if (!ok) break;
+      PUT_BF16(w->b1, f);
+      if (!ok) break;
+      PUT_RAW(w->W2, int8_t, d * f);
+      if (!ok) break;
+      PUT_RAW(w->sW2, float, d * 4);
+      if (!ok) break;
+      PUT_BF16(w->b2, d);
+      if (!ok) break;
+    }
+    if (!ok) break;
+    PUT_BF16(e->lnf_g, d);
+    if (!ok) break;
+    PUT_BF16(e->lnf_b, d);
+  } while (0);
+#undef SLOT
+#undef PUT_BF16
+#undef PUT_RAW
+  if (!ok) {
+    free(host);
+    return fail(e, W8A8_ERR_IO, "quant8 image truncated");
+  }
+  cudaError_t ce = cudaMemcpy(e->wblob, host, arena, cudaMemcpyHostToDevice);
+  free(host);
+  if (ce != cudaSuccess) return fail(e, W8A8_ERR_CUDA, "weights H2D: %s", cudaGetErrorString(ce));
+  e->loaded = 1;
+  return W8A8_OK;
+}
+
+int gpt2_engine_load_quant8(gpt2_engine *e, const char *path) {
+  if (!e || !path) return W8A8_ERR_INVALID;
+  FILE *fp = fopen(path, "rb");
+  if (!fp) return fail(e, W8A8_ERR_IO, "cannot open %s", path);
+  size_t need = gpt2_engine_quant8_bytes(&e->cfg);
+  uint8_t *buf = (uint8_t *)malloc(need);
+  if (!buf) {
+    fclose(fp);
+    return fail(e, W8A8_ERR_NOMEM, "host buffer of %zu bytes", need);
+  }
+  size_t got = fread(buf, 1, need, fp);
+  fclose(fp);
+  int st = got == need ? gpt2_engine_load_quant8_memory(e, buf, need)
+                       : fail(e, W8A8_ERR_IO, "%s: read %zu of %zu bytes", path, got, need);
+  free(buf);
+  return st;
+}
+
+/* ---- forward passes ---- */
+
+/* One transformer block over M = B*T rows of H (T tokens per sequence,
+ * written at cache rows pos0[b] + t; pos0 == NULL means prefill from 0). */
+static int block_forward(gpt2_engine *e, int l, int B, int T, const int32_t *pos0, int first) {
+  const gpt2_engine_config *c = &e->cfg;
+  const layer_w *w = &e->layers[l];
+  const int d = c->d_model, f = 4 * d, M = B * T, Hh = c->n_head;
+  const float eps = 1e-5f; /* gpt2.c:627 */
+  const int64_t seq_stride = (int64_t)c->n_layer * c->ctx * d;
+  gpt2_bf16_t *Kl = e->Kc + (int64_t)l * c->ctx * d;
+  gpt2_bf16_t *Vl = e->Vc + (int64_t)l * c->ctx * d;
+  void *s = (void *)e->stream;
+  if (!first)
+    W8_TRY(e, w8a8_layernorm_quant(e->H, d, M, d, w->ln1_g, w->ln1_b, eps, NULL, 0, e->Xq, e->sX, s));
+  W8_TRY(e, w8a8_linear_qkv(e->Xq, e->sX, M, d, w->Wqkv, w->sWqkv, w->bqkv, e->Q, d, Kl, Vl,
+                            seq_stride, T, pos0, s));
+  if (pos0 == NULL)
+    W8_TRY(e, w8a8_attention_prefill(e->Q, d, Kl, Vl, seq_stride, B, T, Hh, 64, e->ATT, d, s));
+  else
+    W8_TRY(e, w8a8_attention_decode(e->Q, d, Kl, Vl, seq_stride, B, e->nctx, c->ctx, Hh, 64,
+                                    e->ATT, d, e->attn_ws, e->attn_ws_bytes, s));
+  W8_TRY(e, w8a8_quant_rows(e->ATT, d, M, d, e->Xq, e->sX, s));
+  W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, d, w->Wproj, w->sWproj, w->bproj, d, W8A8_EPI_BIAS_RESID,
+                        e->H, d, e->R1, d, s));
+  W8_TRY(e, w8a8_layernorm_quant(e->R1, d, M, d, w->ln2_g, w->ln2_b, eps, NULL, 0, e->Xq, e->sX, s));
+  W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, d, w->W1, w->sW1, w->b1, f, W8A8_EPI_BIAS_GELU, NULL, 0,
+                        e->X1, f, s));
+  W8_TRY(e, w8a8_quant_rows(e->X1, f, M, f, e->Xq, e->sX, s));
+  W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, f, w->W2, w->sW2, w->b2, d, W8A8_EPI_BIAS_RESID, e->R1, d,
+                        e->H, d, s));
+  return W8A8_OK;
+}
+
+/* Embedding + all blocks + final LN of the last row of each sequence + LM
+ * head + greedy pick appended to the output buffer. */
+static int model_forward(gpt2_engine *e, const int32_t *tokens_d, int B, int T,
+                         const int32_t *pos0) {
+  const gpt2_engine_config *c = &e->cfg;
+  const int d = c->d_model, M = B * T;
+  const float eps = 1e-5f;
+  void *s = (void *)e->stream;
+  const layer_w *w0 = &e->layers[0];
+  W8_TRY(e, w8a8_embed_layernorm_quant(e->wte, e->wpe, tokens_d, M, T, pos0, d, e->H, w0->ln1_g,
+                                       w0->ln1_b, eps, NULL, e->Xq, e->sX, s));
+  for (int l = 0; l < c->n_layer; ++l) {
+    int st = block_forward(e, l, B, T, pos0, l == 0);
+    if (st) return st;
+  }
+  /* final LayerNorm on the last token of every sequence (gpt2.c:2150-2157) */
+  W8_TRY(e, w8a8_layernorm_quant(e->H + (int64_t)(T - 1) * d, (int64_t)T * d, B, d, e->lnf_g,
+                                 e->lnf_b, eps, e->Xf, d, NULL, NULL, s));
+  W8_TRY(e, w8a8_lm_head(e->Xf, d, B, d, e->wte, c->vocab, e->logits, c->vocab, s));
+  W8_TRY(e, w8a8_sample_greedy(e->logits, c->vocab, B, c->vocab, e->next, e->out,
+                               e->out_stride, e->gen, s));
+  return W8A8_OK;
+}
+
+int gpt2_engine_launches_per_decode_step(const gpt2_engine *e) {
+  /* embed+LN1, 9 per block minus the fused first LN1, nctx, final LN, LM
+   * head, sample, len advance (+ the attention's second kernel and ticket
+   * reset per block) */
+  if (!e) return 0;
+  return 1 + e->cfg.n_layer * 10 - 1 + 1 + 3 + 1;
+}
+
+int gpt2_engine_launches_per_prefill(const gpt2_engine *e) {
+  if (!e) return 0;
+  return 1 + e->cfg.n_layer * 9 - 1 + 3;
+}
+
+int gpt2_engine_prefill(gpt2_engine *e, const int32_t *prompts_d, int B, int T,
+                        int32_t *out_tokens_d, int out_stride) {
+  if (!e || !prompts_d || !out_tokens_d) return W8A8_ERR_INVALID;
+  if (!e->loaded) return fail(e, W8A8_ERR_INVALID, "weights not loaded");
+  const gpt2_engine_config *c = &e->cfg;
+  if (B <= 0 || T <= 0 || B > c->max_batch || (size_t)B * T > (size_t)c->max_tokens ||
+      T > c->ctx)
+    return fail(e, W8A8_ERR_INVALID, "batch %d x %d exceeds engine limits", B, T);
+  e->B = B;
+  e->out = out_tokens_d;
+  e->out_stride = out_stride;
+  /* reset per-sequence state: gen = 0, len = T (after this prefill) */
+  CUDA_TRY(e, cudaMemsetAsync(e->gen, 0, (size_t)B * 4, e->stream));
+  int st = model_forward(e, prompts_d, B, T, NULL);
+  if (st) return st;
+  CUDA_TRY(e, cudaMemsetAsync(e->len, 0, (size_t)B * 4, e->stream));
+  W8_TRY(e, w8a8_advance_positions(e->len, e->len, B, T, (void *)e->stream));
+  return W8A8_OK;
+}
+
+/* One decode step: token next[b] at position len[b]. */
+static int decode_step_launches(gpt2_engine *e) {
+  const int B = e->B;
+  W8_TRY(e, w8a8_advance_positions(e->nctx, e->len, B, 1, (void *)e->stream));
+  int st = model_forward(e, e->next, B, 1, e->len);
+  if (st) return st;
+  W8_TRY(e, w8a8_advance_positions(e->len, e->len, B, 1, (void *)e->stream));
+  return W8A8_OK;
+}
+
+int gpt2_engine_decode_steps(gpt2_engine *e, int steps) {
+  if (!e) return W8A8_ERR_INVALID;
+  if (steps <= 0) return W8A8_OK;
+  if (e->B <= 0) return fail(e, W8A8_ERR_INVALID, "decode before prefill");
+  if (!e->use_graphs) {
+    for (int i = 0; i < steps; ++i) {
+      int st = decode_step_launches(e);
+      if (st) return st;
+    }
+    return W8A8_OK;
+  }
+  if (!e->graph || e->graph_B != e->B || e->graph_out != e->out) {
+    if (e->graph) {
+      cudaGraphExecDestroy(e->graph);
+      e->graph = NULL;
+    }
+    cudaGraph_t g;
+    CUDA_TRY(e, cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    int st = decode_step_launches(e);
+    cudaGraph_t captured = NULL;
+    cudaError_t ce = cudaStreamEndCapture(e->stream, &captured);
+    if (st) {
+      if (captured) cudaGraphDestroy(captured);
+      return st;
+    }
+    if (ce != cudaSuccess) return fail(e, W8A8_ERR_CUDA, "capture: %s", cudaGetErrorString(ce));
+    g = captured;
+    ce = cudaGraphInstantiate(&e->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return fail(e, W8A8_ERR_CUDA, "instantiate: %s", cudaGetErrorString(ce));
+    e->graph_B = e->B;
+    e->graph_out = e->out;
+  }
+  for (int i = 0; i < steps; ++i) CUDA_TRY(e, cudaGraphLaunch(e->graph, e->stream));
+  return W8A8_OK;
+}
+
+int gpt2_engine_generate_device(gpt2_engine *e, const int32_t *prompts_d, int B, int T, int n_gen,
+                                int32_t *out_tokens_d, void *stream) {
+  if (!e || n_gen <= 0) return W8A8_ERR_INVALID;
+  if (T + n_gen - 1 > e->cfg.ctx)
+    return fail(e, W8A8_ERR_INVALID, "prompt %d + %d tokens exceeds ctx %d", T, n_gen, e->cfg.ctx);
+  cudaStream_t user = (cudaStream_t)stream;
+  cudaEvent_t ev = NULL;
+  if (user && user != e->stream) {
+    /* order the engine stream after the caller's work, and back */
+    CUDA_TRY(e, cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    CUDA_TRY(e, cudaEventRecord(ev, user));
+    CUDA_TRY(e, cudaStreamWaitEvent(e->stream, ev, 0));
+  }
+  int st = gpt2_engine_prefill(e, prompts_d, B, T, out_tokens_d, n_gen);
+  if (!st) st = gpt2_engine_decode_steps(e, n_gen - 1);
+  if (ev) {
+    cudaEventRecord(ev, e->stream);
+    cudaStreamWaitEvent(user, ev, 0);
+    cudaEventDestroy(ev);
+  }
+  return st;
+}
+
+int gpt2_engine_generate(gpt2_engine *e, const int32_t *prompts, int B, int T, int n_gen,
+                         int32_t *out_tokens) {
+  if (!e || !prompts || !out_tokens || B <= 0 || T <= 0 || n_gen <= 0) return W8A8_ERR_INVALID;
+  if ((size_t)B * T > (size_t)e->cfg.max_tokens || B > e->cfg.max_batch)
+    return fail(e, W8A8_ERR_INVALID, "batch %d x %d exceeds engine limits", B, T);
+  if ((size_t)B * n_gen > (size_t)e->cfg.max_batch * e->cfg.ctx)
+    return fail(e, W8A8_ERR_INVALID, "output buffer too small");
+  CUDA_TRY(e, cudaMemcpyAsync(e->tokens_in, prompts, (size_t)B * T * 4, cudaMemcpyHostToDevice,
+                              e->stream));
+  int st = gpt2_engine_generate_device(e, e->tokens_in, B, T, n_gen, e->out_default, NULL);
+  if (st) return st;
+  CUDA_TRY(e, cudaMemcpyAsync(out_tokens, e->out_default, (size_t)B * n_gen * 4,
+                              cudaMemcpyDeviceToHost, e->stream));
+  CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+  int derr = w8a8_device_error(1);
+  if (derr) return fail(e, W8A8_ERR_DEVICE, "device error word 0x%x", derr);
+  return W8A8_OK;
+}
+
+int gpt2_engine_copy_logits(gpt2_engine *e, gpt2_bf16_t *host, int rows) {
+  if (!e || !host || rows <= 0 || rows > e->cfg.max_batch) return W8A8_ERR_INVALID;
+  CUDA_TRY(e, cudaMemcpyAsync(host, e->logits, (size_t)rows * e->cfg.vocab * 2,
+                              cudaMemcpyDeviceToHost, e->stream));
+  CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+  return W8A8_OK;
+}
+
+int gpt2_engine_set_graphs(gpt2_engine *e, int enable) {
+  if (!e) return W8A8_ERR_INVALID;
+  e->use_graphs = enable ? 1 : 0;
+  return W8A8_OK;
+}

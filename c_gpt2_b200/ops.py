@@ -1,0 +1,187 @@
+"""Torch-tensor front end of the C ABI (include/gpt2_w8a8.h).
+
+Each function takes CUDA tensors, checks dtypes/shapes on the host, and calls
+the native entry point on the current torch stream. Names follow the
+reference's kernel ABI (include/cuda_kernels.h of roeybenhayun/c_gpt2) where a
+function has a counterpart there.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, core
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("expected a CUDA tensor")
+    return t.data_ptr()
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if t.dtype != dtype:
+        raise TypeError(f"{name}: expected {dtype}, got {t.dtype}")
+    if not t.is_cuda:
+        raise ValueError(f"{name}: expected a CUDA tensor")
+
+
+def init(device: int = 0) -> None:
+    check(core().w8a8_init(device), "w8a8_init")
+
+
+def device_error(reset: bool = True) -> int:
+    return core().w8a8_device_error(1 if reset else 0)
+
+
+def per_token_quant(X: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """activation_quant.cu:37-110 — X [M,K] bf16 -> (Xq int8 [M,K], sX f32 [M])."""
+    _need(X, torch.bfloat16, "X")
+    M, K = X.shape
+    Xq = torch.empty((M, K), dtype=torch.int8, device=X.device)
+    sX = torch.empty((M,), dtype=torch.float32, device=X.device)
+    check(core().w8a8_quant_rows(_ptr(X), X.stride(0), M, K, _ptr(Xq), _ptr(sX), _stream()),
+          "w8a8_quant_rows")
+    return Xq, sX
+
+
+def layernorm_quant(X: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
+                    want_y: bool = True, want_q: bool = True):
+    """layernorm.cu:7-100 (+ per-token quant). Returns (Y, Xq, sX), None where not asked."""
+    _need(X, torch.bfloat16, "X")
+    M, d = X.shape
+    Y = torch.empty((M, d), dtype=torch.bfloat16, device=X.device) if want_y else None
+    Xq = torch.empty((M, d), dtype=torch.int8, device=X.device) if want_q else None
+    sX = torch.empty((M,), dtype=torch.float32, device=X.device) if want_q else None
+    check(core().w8a8_layernorm_quant(_ptr(X), X.stride(0), M, d, _ptr(gamma), _ptr(beta), eps,
+                                      _ptr(Y), d, _ptr(Xq), _ptr(sX), _stream()),
+          "w8a8_layernorm_quant")
+    return Y, Xq, sX
+
+
+def embed_layernorm_quant(wte, wpe, tokens, T, pos0, gamma, beta, eps=1e-5):
+    """embeddings.cu + layernorm.cu + quant for M = B*T new tokens.
+    Returns (H, Y, Xq, sX)."""
+    _need(tokens, torch.int32, "tokens")
+    M = tokens.numel()
+    d = wte.shape[1]
+    dev = wte.device
+    H = torch.empty((M, d), dtype=torch.bfloat16, device=dev)
+    Y = torch.empty((M, d), dtype=torch.bfloat16, device=dev)
+    Xq = torch.empty((M, d), dtype=torch.int8, device=dev)
+    sX = torch.empty((M,), dtype=torch.float32, device=dev)
+    check(core().w8a8_embed_layernorm_quant(_ptr(wte), _ptr(wpe), _ptr(tokens), M, T, _ptr(pos0),
+                                            d, _ptr(H), _ptr(gamma), _ptr(beta), eps, _ptr(Y),
+                                            _ptr(Xq), _ptr(sX), _stream()),
+          "w8a8_embed_layernorm_quant")
+    return H, Y, Xq, sX
+
+
+def gemm_s32(Xq: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
+    """The reference's cublasGemmEx INT8 call: Xq [M,K] · W[N,K]^T -> int32 [M,N]."""
+    _need(Xq, torch.int8, "Xq")
+    _need(W, torch.int8, "W")
+    M, K = Xq.shape
+    N = W.shape[0]
+    Y = torch.empty((M, N), dtype=torch.int32, device=Xq.device)
+    check(core().w8a8_gemm_s32(_ptr(Xq), M, K, _ptr(W), N, _ptr(Y), _stream()), "w8a8_gemm_s32")
+    return Y
+
+
+def linear(Xq, sX, W, sW, bias, epilogue=_lib.EPI_BIAS, R=None, out=None):
+    """Fused W8A8 linear: dequant (+bias) (+residual | +GELU) -> bf16 [M,N]."""
+    _need(Xq, torch.int8, "Xq")
+    M, K = Xq.shape
+    N = W.shape[0]
+    Y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=Xq.device)
+    ldr = R.stride(0) if R is not None else 0
+    check(core().w8a8_linear(_ptr(Xq), _ptr(sX), M, K, _ptr(W), _ptr(sW), _ptr(bias), N, epilogue,
+                             _ptr(R), ldr, _ptr(Y), Y.stride(0), _stream()), "w8a8_linear")
+    return Y
+
+
+def linear_qkv(Xq, sX, Wqkv, sWqkv, bqkv, Q, Kc, Vc, seq_stride, T, pos0=None):
+    M, d = Xq.shape
+    check(core().w8a8_linear_qkv(_ptr(Xq), _ptr(sX), M, d, _ptr(Wqkv), _ptr(sWqkv), _ptr(bqkv),
+                                 _ptr(Q), Q.stride(0), _ptr(Kc), _ptr(Vc), seq_stride, T,
+                                 _ptr(pos0), _stream()), "w8a8_linear_qkv")
+
+
+def attention_prefill(Q, Kc, Vc, seq_stride, n_seq, T, n_head, out=None):
+    d = n_head * 64
+    O = out if out is not None else torch.empty((n_seq * T, d), dtype=torch.bfloat16,
+                                                device=Q.device)
+    check(core().w8a8_attention_prefill(_ptr(Q), Q.stride(0), _ptr(Kc), _ptr(Vc), seq_stride,
+                                        n_seq, T, n_head, 64, _ptr(O), O.stride(0), _stream()),
+          "w8a8_attention_prefill")
+    return O
+
+
+def attention_decode(Q, Kc, Vc, seq_stride, n_ctx, max_ctx, n_head, out=None, workspace=None):
+    n_seq = Q.shape[0]
+    d = n_head * 64
+    O = out if out is not None else torch.empty((n_seq, d), dtype=torch.bfloat16, device=Q.device)
+    need = core().w8a8_attention_decode_workspace_size(n_seq, n_head, max_ctx)
+    if workspace is None:
+        workspace = torch.empty((need,), dtype=torch.uint8, device=Q.device)
+    check(core().w8a8_attention_decode(_ptr(Q), Q.stride(0), _ptr(Kc), _ptr(Vc), seq_stride,
+                                       n_seq, _ptr(n_ctx), max_ctx, n_head, 64, _ptr(O),
+                                       O.stride(0), _ptr(workspace), workspace.numel(),
+                                       _stream()), "w8a8_attention_decode")
+    return O
+
+
+def lm_head(Xf, wte):
+    M, d = Xf.shape
+    V = wte.shape[0]
+    logits = torch.empty((M, V), dtype=torch.bfloat16, device=Xf.device)
+    check(core().w8a8_lm_head(_ptr(Xf), Xf.stride(0), M, d, _ptr(wte), V, _ptr(logits), V,
+                              _stream()), "w8a8_lm_head")
+    return logits
+
+
+def sample_greedy(logits):
+    M, V = logits.shape
+    out = torch.empty((M,), dtype=torch.int32, device=logits.device)
+    check(core().w8a8_sample_greedy(_ptr(logits), logits.stride(0), M, V, _ptr(out), None, 0, None,
+                                    _stream()), "w8a8_sample_greedy")
+    return out
+
+
+# ---- reference-shaped element-wise operations (in place where the reference is) ----
+
+def ref_softmax(a, rows, cols, stride, out, temperature=1.0, causal=0):
+    check(core().w8a8_ref_softmax(_ptr(a), rows, cols, stride, _ptr(out), temperature, causal,
+                                  _stream()), "w8a8_ref_softmax")
+
+
+def ref_gelu(x):
+    rows, cols = x.shape
+    check(core().w8a8_ref_gelu(_ptr(x), cols, rows, _stream()), "w8a8_ref_gelu")
+
+
+def ref_dequant(Y, sW, sX):
+    M, N = Y.shape
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=Y.device)
+    check(core().w8a8_ref_dequant(_ptr(Y), _ptr(sW), _ptr(sX), _ptr(out), M, N, _stream()),
+          "w8a8_ref_dequant")
+    return out
+
+
+def ref_add_bias(a, b):
+    rows, cols = a.shape
+    check(core().w8a8_ref_add_bias(_ptr(a), rows, cols, _ptr(b), _stream()), "w8a8_ref_add_bias")
+
+
+def ref_add_2d(a, b, out=None):
+    rows, cols = a.shape
+    out = a if out is None else out
+    check(core().w8a8_ref_add_2d(_ptr(a), rows, cols, _ptr(b), _ptr(out), _stream()),
+          "w8a8_ref_add_2d")
+    return out

@@ -1,0 +1,88 @@
+/*
+ * gpt2_engine.h — C host engine for batched W8A8 GPT-2 inference on one GPU.
+ *
+ * This is the host side of the reference's INT8 GPU build (gpt2.c:1124-1330
+ * transformer_block_gpu, gpt2.c:2094-2222 token loop) rebuilt around the
+ * kernels of gpt2_w8a8.h: it loads the reference's quant8.bin weight file,
+ * keeps W_qkv packed, holds one reference-layout KV cache ([L][ctx][d] bf16)
+ * per resident sequence, runs prefill for a batch of equal-length prompts,
+ * then greedy decode with one CUDA graph per decode step. Sequences are
+ * independent: each sequence's tokens are those it would produce alone.
+ *
+ * Device memory is allocated once in gpt2_engine_create / load (the
+ * reference's allocate_weights_gpu, gpt2.c:864-942); generation allocates
+ * nothing.
+ */
+#ifndef GPT2_ENGINE_H
+#define GPT2_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "gpt2_w8a8.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct gpt2_engine gpt2_engine;
+
+typedef struct {
+  int d_model;     /* 768 / 1024 / 1280 for small / medium / large (model_config.h:10-36) */
+  int n_layer;     /* 12 / 24 / 36 */
+  int n_head;      /* 12 / 16 / 20; head_dim = d_model / n_head must be 64 */
+  int vocab;       /* 50257 */
+  int ctx;         /* 1024: KV-cache rows per sequence and wpe rows */
+  int max_batch;   /* sequences resident at once */
+  int max_tokens;  /* largest prefill: max_batch * prompt length */
+} gpt2_engine_config;
+
+int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **out);
+void gpt2_engine_destroy(gpt2_engine *e);
+
+/* Load weights in the reference's quant8.bin layout
+ * (tools/offline_quant/src/writer.py:50-69; read by gpt2.c:1703-1800):
+ * FP32 wte, wpe, then per layer ln1 γ/β, INT8 W_qkv [3d,d] + FP32 scales,
+ * FP32 b_qkv, INT8 attn_proj + scales, bias, ln2 γ/β, INT8 W1 + scales, b1,
+ * INT8 W2 + scales, b2; then lnf γ/β. Every block is padded to 16 bytes.
+ * FP32 tensors are rounded to bf16 (round-to-nearest-even) as the
+ * reference's loader does (gpt2.c:1613-1628). */
+int gpt2_engine_load_quant8(gpt2_engine *e, const char *path);
+int gpt2_engine_load_quant8_memory(gpt2_engine *e, const void *data, size_t bytes);
+/* Bytes of a quant8.bin for this configuration. */
+size_t gpt2_engine_quant8_bytes(const gpt2_engine_config *cfg);
+
+/* Greedy generation for B prompts of T tokens each: the first new token comes
+ * from prefill, the other n_gen-1 from decode steps (the reference counts
+ * tokens the same way, gpt2.c:2094-2247). KV caches start empty.
+ * Host-buffer form: prompts [B*T] and out_tokens [B*n_gen] are host memory;
+ * the call copies prompts in and tokens out (synchronous). */
+int gpt2_engine_generate(gpt2_engine *e, const int32_t *prompts, int B, int T, int n_gen,
+                         int32_t *out_tokens);
+/* Device-buffer form, asynchronous on `stream` (NULL = engine stream). */
+int gpt2_engine_generate_device(gpt2_engine *e, const int32_t *prompts_d, int B, int T, int n_gen,
+                                int32_t *out_tokens_d, void *stream);
+
+/* Step-level interface (device buffers, engine stream):
+ * prefill resets the batch, fills the KV caches and writes the first token
+ * of each sequence to out_tokens_d[b*out_stride]; decode_steps runs `steps`
+ * further greedy steps, appending tokens after those already produced. */
+int gpt2_engine_prefill(gpt2_engine *e, const int32_t *prompts_d, int B, int T,
+                        int32_t *out_tokens_d, int out_stride);
+int gpt2_engine_decode_steps(gpt2_engine *e, int steps);
+
+/* Copy the logits of the last step ([B, vocab] bf16) to host memory. */
+int gpt2_engine_copy_logits(gpt2_engine *e, gpt2_bf16_t *host, int rows);
+/* Enable (default) or disable CUDA-graph replay of decode steps. */
+int gpt2_engine_set_graphs(gpt2_engine *e, int enable);
+/* Kernel launches per decode step (for launch accounting). */
+int gpt2_engine_launches_per_decode_step(const gpt2_engine *e);
+int gpt2_engine_launches_per_prefill(const gpt2_engine *e);
+void *gpt2_engine_stream(gpt2_engine *e);
+const char *gpt2_engine_last_error(const gpt2_engine *e);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPT2_ENGINE_H */

@@ -1,0 +1,173 @@
+/*
+ * gpt2_w8a8.h — runtime-dimension C ABI of the sm_100a W8A8 GPT-2 kernels.
+ *
+ * Every pointer argument is device memory owned by the caller; no entry point
+ * allocates (the reference's ownership rule: all buffers belong to the host
+ * program, gpt2.c:864-942). Streams are passed as `void *` (a cudaStream_t;
+ * NULL = legacy default stream, the stream the reference launches on).
+ * bf16 tensors are passed as raw 16-bit patterns (gpt2_bf16_t), bit-compatible
+ * with __nv_bfloat16 / __bf16.
+ *
+ * All matrices are row-major. Weights are stored [OUT, IN] exactly as the
+ * reference's quant8.bin holds them (tools/offline_quant/src/quantizer.py:3-4),
+ * so X[M,K] · W[N,K]^T needs no transpose.
+ *
+ * Every entry point returns W8A8_OK (0) or a negative status; nothing aborts.
+ * The reference-shaped drop-in functions (include/cuda_kernels.h) wrap these
+ * and keep the reference's abort-on-error convention.
+ */
+#ifndef GPT2_W8A8_H
+#define GPT2_W8A8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t gpt2_bf16_t;
+
+/* ---- status codes ---- */
+#define W8A8_OK 0
+#define W8A8_ERR_INVALID (-1)     /* bad shape, null pointer, misaligned buffer */
+#define W8A8_ERR_UNSUPPORTED (-2) /* shape this build does not handle */
+#define W8A8_ERR_CUDA (-3)        /* a CUDA runtime call or launch failed */
+#define W8A8_ERR_DEVICE (-4)      /* a kernel recorded an error (see w8a8_device_error) */
+#define W8A8_ERR_NOMEM (-5)
+#define W8A8_ERR_IO (-6)
+
+/* ---- epilogues of the INT8 linear layer (applied to acc = Xq · W^T) ----
+ * t = bf16(((float)acc * sW[n]) * sX[m])          dequant, activation_quant.cu:129-130
+ * b-step  y = bf16(float(t) + float(bias[n]))     add_bias.cu:13
+ * Each mode stores one bf16 per output element: */
+#define W8A8_EPI_DEQUANT 0    /* Y = t                                        */
+#define W8A8_EPI_BIAS 1       /* Y = y                                        */
+#define W8A8_EPI_BIAS_RESID 2 /* Y = bf16(float(R[m,n]) + float(y))   add_2d.cu:14 */
+#define W8A8_EPI_BIAS_GELU 3  /* Y = bf16(gelu_tanh(float(y)))        gelu.cu:10-16 */
+
+/* Per-device set-up: resolves the device error word and the TMA encoder.
+ * Call once per device (with that device current) before stream capture. */
+int w8a8_init(int device);
+const char *w8a8_status_string(int status);
+/* Returns the first error code a kernel recorded on the current device since
+ * the last reset (0 = none); `reset` != 0 clears it. Synchronises the device. */
+int w8a8_device_error(int reset);
+
+/* ---- per-token INT8 activation quantization (activation_quant.cu:37-110) ----
+ * X [M,K] bf16 (row stride ldx elements) -> Xq [M,K] int8 (row stride K),
+ * sX [M] fp32: scale = amax>0 ? amax/127 : 1 ; q = clamp(rn(x*(1/scale)),±127) */
+int w8a8_quant_rows(const gpt2_bf16_t *X, int64_t ldx, int M, int K, int8_t *Xq, float *sX,
+                    void *stream);
+
+/* ---- LayerNorm (layernorm.cu:7-100) fused with per-token quantization ----
+ * Y = bf16(((x-mean)*rsqrt(var+eps))*gamma + beta), with the reference's
+ * two-pass fp32 statistics. Y (nullable) receives the bf16 rows; Xq/sX
+ * (nullable together) receive the quantized rows of Y. d <= 8192. */
+int w8a8_layernorm_quant(const gpt2_bf16_t *X, int64_t ldx, int M, int d,
+                         const gpt2_bf16_t *gamma, const gpt2_bf16_t *beta, float eps,
+                         gpt2_bf16_t *Y, int64_t ldy, int8_t *Xq, float *sX, void *stream);
+
+/* ---- token + position embedding (embeddings.cu:8-25) fused with LayerNorm
+ * and quantization of the first layer's input ----
+ * Row m = b*T + t (b < M/T sequences of T new tokens): token id tokens[m],
+ * position p = (pos0 ? pos0[b] : 0) + t. H[m] = bf16(wte[id] + wpe[p]) and
+ * LayerNorm/quantization of H[m] as in w8a8_layernorm_quant. */
+int w8a8_embed_layernorm_quant(const gpt2_bf16_t *wte, const gpt2_bf16_t *wpe,
+                               const int32_t *tokens, int M, int T, const int32_t *pos0, int d,
+                               gpt2_bf16_t *H, const gpt2_bf16_t *gamma,
+                               const gpt2_bf16_t *beta, float eps, gpt2_bf16_t *Y,
+                               int8_t *Xq, float *sX, void *stream);
+
+/* ---- INT8 x INT8 -> INT32 GEMM (the reference's cublasGemmEx call,
+ * gpt2.c:404-415): Y[M,N] = Xq[M,K] · W[N,K]^T, exact integer arithmetic.
+ * K % 16 == 0 and 16-byte aligned operands take the tcgen05 tensor-core path;
+ * other shapes take a CUDA-core kernel with the same results. */
+int w8a8_gemm_s32(const int8_t *Xq, int M, int K, const int8_t *W, int N, int32_t *Y,
+                  void *stream);
+
+/* ---- fused W8A8 linear layer: GEMM + dequant + bias (+ residual / GELU) ----
+ * Replaces dot_2d_gpu_int8 + add_bias_cuda (+ add_2d_cuda / gelu_cuda),
+ * gpt2.c:384-428, 1145-1325. R is read only for W8A8_EPI_BIAS_RESID and may
+ * alias Y (in-place residual add). bias may be NULL only for EPI_DEQUANT. */
+int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W,
+                const float *sW, const gpt2_bf16_t *bias, int N, int epilogue,
+                const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy, void *stream);
+
+/* ---- packed QKV projection straight into Q and the KV cache ----
+ * W_qkv [3d, d] stays packed (the reference splits it at load,
+ * gpt2.c:1725-1738; splitting changes no output element). Output column n of
+ * row m: n < d -> Q[m*ldq + n]; d <= n < 2d -> K cache; 2d <= n -> V cache,
+ * each bf16(bf16(acc*sW*sX)+b) as the reference's three calls produce
+ * (gpt2.c:1145-1167). Row m = b*T + t belongs to sequence b at cache position
+ * p = (pos0 ? pos0[b] : 0) + t; its K row is Kc + b*seq_stride + p*d. */
+int w8a8_linear_qkv(const int8_t *Xq, const float *sX, int M, int d, const int8_t *Wqkv,
+                    const float *sWqkv, const gpt2_bf16_t *bqkv, gpt2_bf16_t *Q, int64_t ldq,
+                    gpt2_bf16_t *Kc, gpt2_bf16_t *Vc, int64_t seq_stride, int T,
+                    const int32_t *pos0, void *stream);
+
+/* ---- causal attention over the KV cache, prefill (gpt2.c:1205-1217) ----
+ * n_seq sequences of T tokens each, cached from position 0. Query row
+ * m = b*T + t, head h, reads Q[m*ldq + h*hd ..]; attends keys 0..t of
+ * sequence b. S = bf16(q.k / sqrt(hd)); P = bf16(bf16(exp(S-max)) / sum);
+ * O[m*ldo + h*hd ..] = bf16(P·V). hd == 64, T <= 1024. */
+int w8a8_attention_prefill(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,
+                           const gpt2_bf16_t *Vc, int64_t seq_stride, int n_seq, int T,
+                           int n_head, int hd, gpt2_bf16_t *O, int64_t ldo,
+                           void *stream);
+
+/* ---- attention of one new token per sequence, decode (gpt2.c:1191-1203) ----
+ * Sequence b attends its first n_ctx[b] cache rows (n_ctx includes the new
+ * token, device array). max_ctx bounds every n_ctx[b] (<= 1024); with
+ * n_ctx == NULL every sequence attends exactly max_ctx rows. The
+ * workspace holds scores and split partials; size it with
+ * w8a8_attention_decode_workspace_size(). */
+size_t w8a8_attention_decode_workspace_size(int n_seq, int n_head, int max_ctx);
+int w8a8_attention_decode(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,
+                          const gpt2_bf16_t *Vc, int64_t seq_stride, int n_seq,
+                          const int32_t *n_ctx, int max_ctx, int n_head, int hd,
+                          gpt2_bf16_t *O, int64_t ldo, void *workspace,
+                          size_t workspace_bytes, void *stream);
+
+/* ---- LM head (gpt2.c:2160): logits[M,V] = bf16(Xf[M,d] · wte[V,d]^T), fp32
+ * accumulation. wte is used as stored ([vocab, d], K-major); the reference's
+ * host transpose wte_T (gpt2.c:1915-1918) is not needed. */
+int w8a8_lm_head(const gpt2_bf16_t *Xf, int64_t ldx, int M, int d, const gpt2_bf16_t *wte,
+                 int V, gpt2_bf16_t *logits, int64_t ldl, void *stream);
+
+/* ---- greedy next token (gpt2.c:2180-2222) ----
+ * Per row: probs = softmax(logits) in the reference's bf16 rounding order
+ * (softmax.cu:24-92, temperature 1), token = first index of the largest
+ * bf16 probability. Writes out_tokens[m]; if append_to is non-NULL also
+ * stores the token at append_to[m*append_stride + append_pos[m]] and
+ * increments append_pos[m] (device-side sequence bookkeeping for decode). */
+int w8a8_sample_greedy(const gpt2_bf16_t *logits, int64_t ldl, int M, int V,
+                       int32_t *out_tokens, int32_t *append_to, int64_t append_stride,
+                       int32_t *append_pos, void *stream);
+
+/* dst[i] = src[i] + delta for i < n (device arrays; dst may equal src). */
+int w8a8_advance_positions(int32_t *dst, const int32_t *src, int n, int delta, void *stream);
+
+/* ---- reference-shaped element-wise operations ----
+ * Runtime-dimension forms of the reference's cuda/ kernels with their
+ * exact per-element results; include/cuda_kernels.h maps its drop-in symbols
+ * onto these. */
+int w8a8_ref_embeddings(const gpt2_bf16_t *wte, const gpt2_bf16_t *wpe, const int32_t *tokens,
+                        gpt2_bf16_t *emb, int d, int start_row, int n_rows, void *stream);
+int w8a8_ref_add_bias(gpt2_bf16_t *a, int rows, int cols, const gpt2_bf16_t *b, void *stream);
+int w8a8_ref_add_2d(const gpt2_bf16_t *a, int rows, int cols, const gpt2_bf16_t *b,
+                    gpt2_bf16_t *out, void *stream);
+int w8a8_ref_gelu(gpt2_bf16_t *x, int cols, int rows, void *stream);
+int w8a8_ref_dequant(const int32_t *Y, const float *sW, const float *sX, gpt2_bf16_t *out, int M,
+                     int N, void *stream);
+int w8a8_ref_causal_mask(gpt2_bf16_t *x, int stride, int tokens, void *stream);
+int w8a8_ref_concat_heads(const gpt2_bf16_t *src, gpt2_bf16_t *dest, int token_index, int n_head,
+                          int hd, int ctx, void *stream);
+int w8a8_ref_softmax(const gpt2_bf16_t *a, int rows, int cols, int stride, gpt2_bf16_t *out,
+                     float temperature, int causal_mask, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPT2_W8A8_H */

@@ -1,0 +1,105 @@
+"""End-to-end parity of the C host engine: greedy streams against the CPU
+oracle's restatement of the reference's W8A8 forward, the prefill logits
+against the reference's own FP32 build (tests/golden/ref_fp32_small.npz),
+batching invariance and CUDA-graph replay."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from c_gpt2_b200.engine import Engine
+from c_gpt2_b200.quant8 import DIMS, GPT2Dims
+from c_gpt2_b200.synthetic import prompts, quant8_image
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TINY = GPT2Dims(d_model=128, n_layer=2, n_head=2, vocab=512, ctx=128)
+
+
+@pytest.fixture(scope="module")
+def tiny_image():
+    return quant8_image(TINY, 11)
+
+
+def test_tiny_engine_matches_oracle(cuda, tiny_image):
+    eng = Engine(TINY, max_batch=4, max_tokens=4 * 40)
+    eng.load_quant8(tiny_image)
+    P = prompts(3, 20, TINY.vocab, seed=2)
+    out = eng.generate(P, 24)
+    for b in range(3):
+        want, want_logits = oracle.generate(tiny_image, TINY, P[b], 24)
+        np.testing.assert_array_equal(out[b], want)
+    got_logits = eng.logits(3)
+    d = np.abs(got_logits[2] - oracle.bf16_to_f32(want_logits))
+    assert d.max() < 5e-2 and d.mean() < 5e-3
+    eng.close()
+
+
+def test_batching_and_graphs_invariant(cuda, tiny_image):
+    """A sequence's tokens do not depend on its batch mates, on prompt-length
+    chunking of the batch, or on graph replay vs eager decode."""
+    P = prompts(5, 16, TINY.vocab, seed=9)
+    eng = Engine(TINY, max_batch=8, max_tokens=8 * 16)
+    eng.load_quant8(tiny_image)
+    batch = eng.generate(P, 30)
+    eng.set_graphs(False)
+    eager = eng.generate(P, 30)
+    np.testing.assert_array_equal(batch, eager)
+    eng.set_graphs(True)
+    for b in (0, 4):
+        alone = eng.generate(P[b:b + 1], 30)
+        np.testing.assert_array_equal(alone[0], batch[b])
+    # repeated calls reuse the captured graph and give the same result
+    np.testing.assert_array_equal(eng.generate(P, 30), batch)
+    eng.close()
+
+
+def test_device_api_matches_host_api(cuda, tiny_image):
+    eng = Engine(TINY, max_batch=4, max_tokens=4 * 16)
+    eng.load_quant8(tiny_image)
+    P = prompts(4, 16, TINY.vocab, seed=4)
+    host = eng.generate(P, 12)
+    pd = torch.from_numpy(P).to(cuda)
+    out = torch.empty((4, 12), dtype=torch.int32, device=cuda)
+    s = torch.cuda.current_stream()
+    eng.generate_device(pd, 12, out, stream=s)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), host)
+    eng.close()
+
+
+def test_engine_rejects_oversize(cuda, tiny_image):
+    from c_gpt2_b200._lib import W8A8Error
+    eng = Engine(TINY, max_batch=2, max_tokens=2 * 16)
+    eng.load_quant8(tiny_image)
+    with pytest.raises(W8A8Error):
+        eng.generate(prompts(3, 16, TINY.vocab), 4)       # batch too large
+    with pytest.raises(W8A8Error):
+        eng.generate(prompts(1, 100, TINY.vocab), 40)     # prompt + gen > ctx
+    with pytest.raises(W8A8Error):
+        eng.load_quant8(tiny_image[:1000])                # truncated image
+    eng.close()
+
+
+def test_gpt2_small_config1_stream(cuda):
+    """Config 1: GPT-2 small, seed-0 weights quantized per channel, a
+    32-token seed-0 prompt, 64 greedy tokens. The stream equals the oracle's
+    W8A8 stream; the prefill logits are within the W8A8 quantization error of
+    the reference's own FP32 build and pick the same first token."""
+    z = np.load(GOLDEN / "ref_fp32_small.npz")
+    dims = DIMS["small"]
+    img = quant8_image(dims, 0)
+    eng = Engine(dims, max_batch=1, max_tokens=32)
+    eng.load_quant8(img)
+    first = eng.generate(z["prompt"][None], 1)
+    lg = eng.logits(1)[0]
+    ref = z["prefill_logits"].astype(np.float32)
+    assert first[0, 0] == z["first_token"][0]
+    err = np.abs(lg - ref)
+    assert err.mean() < 2e-2 and err.max() < 0.15, (err.mean(), err.max())
+    out = eng.generate(z["prompt"][None], 64)[0]
+    want, _ = oracle.generate(img, dims, z["prompt"], 64)
+    np.testing.assert_array_equal(out, want)
+    eng.close()

@@ -1,0 +1,215 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle (same seeded
+inputs). Integer and quantization results are bit-exact; bf16 outputs that
+pass through CUDA's tanhf/rsqrtf/expf or through reordered fp32 sums are
+checked within the tolerance written in each test."""
+import numpy as np
+import pytest
+import torch
+
+from c_gpt2_b200 import _lib, ops
+from c_gpt2_b200.synthetic import outlier_activations
+from oracle import oracle
+from tests.gpu_util import bf16_ulp_diff, from_dev_bf16, to_dev, to_dev_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand_bf16(rng, shape, scale=1.0):
+    return oracle.bf16_bits(rng.standard_normal(shape).astype(np.float32) * np.float32(scale))
+
+
+@pytest.mark.parametrize("M,K", [(1, 768), (7, 3072), (64, 5120), (333, 1024), (5, 100),
+                                 (3, 8), (1024, 768)])
+def test_quant_rows_bit_exact(cuda, M, K):
+    rng = np.random.default_rng(M * 7 + K)
+    x = outlier_activations(M, K, seed=M + K)
+    if M > 2:
+        x[1] = 0.0  # zero row
+    xb = oracle.bf16_bits(x)
+    xq, sx = ops.per_token_quant(to_dev_bf16(xb))
+    rq, rs = oracle.quant_rows(xb)
+    np.testing.assert_array_equal(xq.cpu().numpy(), rq)
+    np.testing.assert_array_equal(sx.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+
+
+# (M, N, K): decode GEMV (M < 16), tensor-core tiles with ragged M/N, K not a
+# multiple of 128, and the CUDA-core fallback (K % 16 != 0).
+GEMM_SHAPES = [(1, 768, 768), (4, 2304, 768), (15, 3072, 1024), (16, 768, 768),
+               (33, 200, 768), (64, 5120, 1280), (100, 1280, 5120), (128, 2304, 768),
+               (200, 384, 192), (257, 640, 768), (1024, 1024, 1024), (40, 96, 80),
+               (20, 72, 40), (3, 130, 56)]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm_s32_bit_exact(cuda, M, N, K):
+    rng = np.random.default_rng(M + 3 * N + 7 * K)
+    xq = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    W = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    Y = ops.gemm_s32(to_dev(xq), to_dev(W)).cpu().numpy()
+    np.testing.assert_array_equal(Y, oracle.gemm_s32(xq, W))
+
+
+def test_gemm_s32_extreme_values(cuda):
+    # |acc| up to 127*127*5120 = 8.3e7: still exact int32
+    M, N, K = 32, 256, 5120
+    xq = np.full((M, K), 127, np.int8)
+    W = np.full((N, K), -127, np.int8)
+    W[::2] = 127
+    Y = ops.gemm_s32(to_dev(xq), to_dev(W)).cpu().numpy()
+    np.testing.assert_array_equal(Y, oracle.gemm_s32(xq, W))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 2304, 768), (9, 768, 3072), (16, 2304, 768),
+                                   (128, 3072, 768), (300, 768, 3072), (1024, 2304, 768)])
+@pytest.mark.parametrize("epi", [_lib.EPI_DEQUANT, _lib.EPI_BIAS, _lib.EPI_BIAS_RESID])
+def test_linear_epilogues_bit_exact(cuda, M, N, K, epi):
+    rng = np.random.default_rng(M + N + K + epi)
+    x = oracle.bf16_bits(outlier_activations(M, K, seed=epi + M))
+    xq, sx = oracle.quant_rows(x)
+    W = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    b = _rand_bf16(rng, (N,), 0.02)
+    R = _rand_bf16(rng, (M, N))
+    want = oracle.linear(xq, sx, W, sw, b, epi, R if epi == _lib.EPI_BIAS_RESID else None)
+    out = ops.linear(to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw), to_dev_bf16(b), epi,
+                     R=to_dev_bf16(R) if epi == _lib.EPI_BIAS_RESID else None)
+    np.testing.assert_array_equal(from_dev_bf16(out), want)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 3072, 768), (64, 5120, 1280), (512, 3072, 768)])
+def test_linear_gelu_within_one_ulp(cuda, M, N, K):
+    """GELU uses CUDA's tanhf on the GPU and the C library's on the CPU:
+    at most 1 bf16 ulp apart, almost always identical."""
+    rng = np.random.default_rng(N + K)
+    x = oracle.bf16_bits(outlier_activations(M, K, seed=3))
+    xq, sx = oracle.quant_rows(x)
+    W = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    b = _rand_bf16(rng, (N,), 0.02)
+    want = oracle.linear(xq, sx, W, sw, b, oracle.EPI_BIAS_GELU)
+    got = from_dev_bf16(ops.linear(to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw),
+                                   to_dev_bf16(b), _lib.EPI_BIAS_GELU))
+    ulp = bf16_ulp_diff(got, want)
+    assert ulp.max() <= 1
+    assert (ulp > 0).mean() < 1e-3
+
+
+@pytest.mark.parametrize("M,d", [(1, 768), (37, 1024), (300, 1280), (8, 2000)])
+def test_layernorm_quant(cuda, M, d):
+    """LayerNorm within 1 bf16 ulp of the oracle (GPU rsqrtf vs CPU 1/sqrtf);
+    quantization of the GPU's own LN output bit-exact."""
+    rng = np.random.default_rng(d + M)
+    x = _rand_bf16(rng, (M, d), 2.0)
+    g = oracle.bf16_bits(rng.uniform(0.5, 1.5, d).astype(np.float32))
+    b = _rand_bf16(rng, (d,), 0.1)
+    Y, Xq, sX = ops.layernorm_quant(to_dev_bf16(x), to_dev_bf16(g), to_dev_bf16(b))
+    y = from_dev_bf16(Y)
+    want = oracle.layernorm(x, g, b)
+    ulp = bf16_ulp_diff(y, want)
+    assert ulp.max() <= 1, ulp.max()
+    rq, rs = oracle.quant_rows(y)
+    np.testing.assert_array_equal(Xq.cpu().numpy(), rq)
+    np.testing.assert_array_equal(sX.cpu().numpy(), rs)
+
+
+def test_embed_layernorm_quant(cuda):
+    rng = np.random.default_rng(5)
+    V, C, d, B, T = 300, 64, 768, 3, 5
+    wte = _rand_bf16(rng, (V, d), 0.02)
+    wpe = _rand_bf16(rng, (C, d), 0.02)
+    g = oracle.bf16_bits(np.ones(d, np.float32))
+    b = oracle.bf16_bits(np.zeros(d, np.float32))
+    toks = rng.integers(0, V, B * T).astype(np.int32)
+    pos0 = np.array([0, 7, 40], np.int32)
+    H, Y, Xq, sX = ops.embed_layernorm_quant(to_dev_bf16(wte), to_dev_bf16(wpe), to_dev(toks), T,
+                                             to_dev(pos0), to_dev_bf16(g), to_dev_bf16(b))
+    pos = (pos0[:, None] + np.arange(T)[None]).reshape(-1)
+    h = oracle.bf16_bits(oracle.bf16_to_f32(wte)[toks] + oracle.bf16_to_f32(wpe)[pos])
+    np.testing.assert_array_equal(from_dev_bf16(H), h)
+    assert bf16_ulp_diff(from_dev_bf16(Y), oracle.layernorm(h, g, b)).max() <= 1
+
+
+def _attn_case(rng, n_seq, T_ctx, H):
+    d = 64 * H
+    Q = _rand_bf16(rng, (n_seq, T_ctx, d))
+    K = _rand_bf16(rng, (n_seq, T_ctx, d))
+    V = _rand_bf16(rng, (n_seq, T_ctx, d))
+    return Q, K, V
+
+
+def _attn_tolerance(got, want):
+    """P.V and q.k sums are reordered relative to the oracle: bf16 outputs
+    within 2e-2 absolute (|O| <= max|V|, here ~4) and 99% within 2 ulp."""
+    g, w = oracle.bf16_to_f32(got), oracle.bf16_to_f32(want)
+    assert np.max(np.abs(g - w)) < 2e-2
+    assert (bf16_ulp_diff(got, want) <= 2).mean() > 0.99
+
+
+@pytest.mark.parametrize("n_seq,T,H", [(1, 1, 1), (1, 37, 2), (2, 64, 12), (3, 130, 4),
+                                       (1, 512, 16), (1, 1024, 2)])
+def test_attention_prefill(cuda, n_seq, T, H):
+    rng = np.random.default_rng(T * 13 + H)
+    Q, K, V = _attn_case(rng, n_seq, T, H)
+    d = 64 * H
+    O = ops.attention_prefill(to_dev_bf16(Q.reshape(-1, d)), to_dev_bf16(K), to_dev_bf16(V),
+                              T * d, n_seq, T, H)
+    got = from_dev_bf16(O).reshape(n_seq, T, d)
+    for s in range(n_seq):
+        _attn_tolerance(got[s], oracle.attention(Q[s], K[s], V[s], 0, H))
+
+
+@pytest.mark.parametrize("n_seq,H,lens", [(1, 16, [300]), (1, 12, [1]), (3, 2, [5, 64, 129]),
+                                          (64, 20, None), (2, 20, [1024, 513])])
+def test_attention_decode(cuda, n_seq, H, lens):
+    rng = np.random.default_rng(n_seq * 31 + H)
+    C = 1024
+    lens = lens or list(rng.integers(1, C + 1, n_seq))
+    d = 64 * H
+    K = _rand_bf16(rng, (n_seq, C, d))
+    V = _rand_bf16(rng, (n_seq, C, d))
+    q = _rand_bf16(rng, (n_seq, d))
+    n_ctx = np.array(lens, np.int32)
+    O = ops.attention_decode(to_dev_bf16(q), to_dev_bf16(K), to_dev_bf16(V), C * d,
+                             to_dev(n_ctx), C, H)
+    got = from_dev_bf16(O)
+    for s in range(n_seq):
+        n = lens[s]
+        want = oracle.attention(q[s:s + 1], K[s, :n], V[s, :n], n - 1, H)
+        _attn_tolerance(got[s:s + 1], want)
+
+
+@pytest.mark.parametrize("M", [1, 3, 16, 64])
+def test_lm_head_and_greedy(cuda, M):
+    rng = np.random.default_rng(M)
+    V, d = 50257, 768
+    wte = _rand_bf16(rng, (V, d), 0.02)
+    xf = _rand_bf16(rng, (M, d))
+    logits = ops.lm_head(to_dev_bf16(xf), to_dev_bf16(wte))
+    got = from_dev_bf16(logits)
+    toks = ops.sample_greedy(logits).cpu().numpy()
+    for m in range(M):
+        want = oracle.lm_head(xf[m], wte)
+        g, w = oracle.bf16_to_f32(got[m]), oracle.bf16_to_f32(want)
+        assert np.max(np.abs(g - w)) < 1e-2
+        assert (bf16_ulp_diff(got[m], want) <= 1).mean() > 0.99
+        # greedy on the GPU's own logits equals the oracle's greedy on them
+        assert toks[m] == oracle.greedy(got[m])
+
+
+def test_greedy_tie_break_first_index(cuda):
+    V = 50257
+    x = np.full((2, V), -3.0, np.float32)
+    x[0, [17, 4000, 50000]] = 5.0
+    x[1, [50256, 9]] = 1.0
+    lg = oracle.bf16_bits(x)
+    toks = ops.sample_greedy(to_dev_bf16(lg)).cpu().numpy()
+    assert list(toks) == [17, 9] == [oracle.greedy(lg[0]), oracle.greedy(lg[1])]
+
+
+def test_rejects_bad_arguments(cuda):
+    x = torch.zeros((4, 8), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(_lib.W8A8Error):
+        ops.layernorm_quant(x, x[0], x[0], want_y=False, want_q=False)
+    q = torch.zeros((4, 64), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(_lib.W8A8Error):  # max_ctx beyond the 1024-row cache
+        ops.attention_decode(q, q, q, 0, None, 2048, 1)
