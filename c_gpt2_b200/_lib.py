@@ -36,8 +36,10 @@ SIGNATURES = {
     "w8a8_layernorm_quant": (_i, [_p, _i64, _i, _i, _p, _p, _f, _p, _i64, _p, _p, _p]),
     "w8a8_embed_layernorm_quant": (_i, [_p, _p, _p, _i, _i, _p, _i, _p, _p, _p, _f, _p, _p, _p, _p]),
     "w8a8_gemm_s32": (_i, [_p, _i, _i, _p, _i, _p, _p]),
-    "w8a8_linear": (_i, [_p, _p, _i, _i, _p, _p, _p, _i, _i, _p, _i64, _p, _i64, _p]),
-    "w8a8_linear_qkv": (_i, [_p, _p, _i, _i, _p, _p, _p, _p, _i64, _p, _p, _i64, _i, _p, _p]),
+    "w8a8_linear": (_i, [_p, _p, _i, _i, _p, _p, _p, _i, _i, _p, _i64, _p, _i64, _p, _sz, _p]),
+    "w8a8_linear_workspace_size": (_sz, [_i, _i]),
+    "w8a8_linear_qkv": (_i, [_p, _p, _i, _i, _p, _p, _p, _p, _i64, _p, _p, _i64, _i, _p, _p,
+                             _sz, _p]),
     "w8a8_attention_prefill": (_i, [_p, _i64, _p, _p, _i64, _i, _i, _i, _i, _p, _i64, _p]),
     "w8a8_attention_decode_workspace_size": (_sz, [_i, _i, _i]),
     "w8a8_attention_decode": (_i, [_p, _i64, _p, _p, _i64, _i, _p, _i, _i, _i, _p, _i64, _p, _sz, _p]),

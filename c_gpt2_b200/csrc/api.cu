@@ -104,7 +104,7 @@ extern "C" int w8a8_gemm_s32(const int8_t *Xq, int M, int K, const int8_t *W, in
 extern "C" int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W,
                            const float *sW, const gpt2_bf16_t *bias, int N, int epilogue,
                            const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy,
-                           void *stream) {
+                           void *workspace, size_t workspace_bytes, void *stream) {
   if (M == 0 || N == 0) return W8A8_OK;
   if (!Xq || !sX || !W || !sW || !Y || M < 0 || N < 0 || K <= 0 || ldy < N)
     return W8A8_ERR_INVALID;
@@ -121,13 +121,21 @@ extern "C" int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, cons
   int st = ready();
   if (st) return st;
   LinearArgs a = make_args(epi, M, N, K, sX, sW, bias, R, ldr, Y, ldy);
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
   return dispatch_linear(Xq, K, W, a, (cudaStream_t)stream);
+}
+
+extern "C" size_t w8a8_linear_workspace_size(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  return linear_workspace_bytes(M, N);
 }
 
 extern "C" int w8a8_linear_qkv(const int8_t *Xq, const float *sX, int M, int d,
                                const int8_t *Wqkv, const float *sWqkv, const gpt2_bf16_t *bqkv,
                                gpt2_bf16_t *Q, int64_t ldq, gpt2_bf16_t *Kc, gpt2_bf16_t *Vc,
-                               int64_t seq_stride, int T, const int32_t *pos0, void *stream) {
+                               int64_t seq_stride, int T, const int32_t *pos0,
+                               void *workspace, size_t workspace_bytes, void *stream) {
   if (M == 0) return W8A8_OK;
   if (!Xq || !sX || !Wqkv || !sWqkv || !bqkv || !Q || !Kc || !Vc || M < 0 || d <= 0 || T <= 0 ||
       M % T != 0 || ldq < d)
@@ -141,6 +149,8 @@ extern "C" int w8a8_linear_qkv(const int8_t *Xq, const float *sX, int M, int d,
   a.T = T;
   a.pos0 = pos0;
   a.dseg = d;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
   return dispatch_linear(Xq, d, Wqkv, a, (cudaStream_t)stream);
 }
 

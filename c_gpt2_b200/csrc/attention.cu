@@ -320,67 +320,63 @@ struct DecodeArgs {
   int *tickets;       // [n_seq][n_head]
 };
 
-// Kernel 1: S_j = bf16(0.125 * q.k_j) for this split's keys. 8 lanes cover
-// one 128-byte key row (16 bytes each), a warp 4 keys per step.
-__global__ void __launch_bounds__(256) attention_decode_scores_kernel(DecodeArgs a) {
-  const int bh = blockIdx.x, split = blockIdx.y;
-  const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
-  const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
-  const int j0 = split * a.keys_per_split;
-  const int j1 = min(n, j0 + a.keys_per_split);
-  if (j0 >= j1) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sub = lane >> 3, part = lane & 7;  // key within step, 16-byte part
+// q row of (b, h) in registers: lane part p holds dims 8p .. 8p+7.
+__device__ __forceinline__ void load_q8(const DecodeArgs &a, int b, int h, int part, float (&q)[8]) {
   const uint4 qv = *reinterpret_cast<const uint4 *>(a.Q + (int64_t)b * a.ldq + h * kHD + part * 8);
-  float q[8];
-  {
-    const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+  const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      q[2 * i] = __uint_as_float(w[i] << 16);
-      q[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-    }
+  for (int i = 0; i < 4; ++i) {
+    q[2 * i] = __uint_as_float(w[i] << 16);
+    q[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
   }
+}
+
+// S_j = bf16(0.125 * q.k_j) for keys [j0, j1), written through `emit(j, s)`.
+// 8 lanes cover one 128-byte key row (16 bytes each), a warp 4 keys per
+// step; each lane keeps 4 row loads in flight.
+template <typename Emit>
+__device__ __forceinline__ void score_keys(const DecodeArgs &a, int b, int h, int j0, int j1,
+                                           int warp, int nwarps, int lane, Emit emit) {
+  const int sub = lane >> 3, part = lane & 7;
+  float q[8];
+  load_q8(a, b, h, part, q);
   const uint16_t *Kb = a.Kc + (int64_t)b * a.seq_stride + h * kHD + part * 8;
-  uint16_t *srow = a.scores + ((int64_t)b * a.n_head + h) * a.max_ctx;
-  // warp w handles keys j0 + 32*step + 4*w + sub: 4 keys per warp step,
-  // 32 keys per block step
-  for (int jb = j0 + warp * 4; jb < j1; jb += 32) {
-    const int j = jb + sub;
-    float s = 0.f;
-    if (j < j1) {
-      const uint4 kv = __ldg(reinterpret_cast<const uint4 *>(Kb + (int64_t)j * a.d));
-      const uint32_t w[4] = {kv.x, kv.y, kv.z, kv.w};
+  const int step = nwarps * 4;
+  constexpr int U = 4;
+  for (int jb = j0 + warp * 4; jb < j1; jb += step * U) {
+    uint4 kv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = jb + u * step + sub;
+      kv[u] = j < j1 ? __ldg(reinterpret_cast<const uint4 *>(Kb + (int64_t)j * a.d))
+                     : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = jb + u * step + sub;
+      const uint32_t w[4] = {kv[u].x, kv[u].y, kv[u].z, kv[u].w};
+      float s = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         s = fmaf(q[2 * i], __uint_as_float(w[i] << 16), s);
         s = fmaf(q[2 * i + 1], __uint_as_float(w[i] & 0xffff0000u), s);
       }
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      if (part == 0 && j < j1) emit(j, f2bf(s * 0.125f));
     }
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    if (part == 0 && j < j1) srow[j] = f2bf(s * 0.125f);
   }
 }
 
-// Kernel 2: softmax from the full score row + this split's share of P.V.
-__global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) {
-  __shared__ float s_red[8];
-  __shared__ float s_part[8][kHD];
-  __shared__ float s_p[1024];
-  __shared__ int s_last;
-  const int bh = blockIdx.x, split = blockIdx.y;
-  const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
-  const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
-  const int j0 = split * a.keys_per_split;
-  const int j1 = min(n, j0 + a.keys_per_split);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint16_t *srow = a.scores + ((int64_t)b * a.n_head + h) * a.max_ctx;
-
-  // max over the whole row
+// Softmax statistics of a full score row (n entries, bf16) with the
+// reference's 256-slot tree (256 threads): returns (max, 1/sum).
+template <typename Load>
+__device__ __forceinline__ void row_stats(int n, int tid, Load ld, float *s_red, float *s_tree,
+                                          float &mx_out, float &inv_out) {
+  const int warp = tid >> 5, lane = tid & 31;
   float mx = -INFINITY;
-  for (int j = tid; j < n; j += 256) mx = fmaxf(mx, bf2f(srow[j]));
+  for (int j = tid; j < n; j += 256) mx = fmaxf(mx, bf2f(ld(j)));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) s_red[warp] = mx;
@@ -388,38 +384,48 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
   mx = s_red[0];
 #pragma unroll
   for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_red[w]);
-  __syncthreads();
-  // reference tree sum: thread t adds j = t, t+256, ... ; then s = 128 .. 1
   float local_sum = 0.0f;
-  for (int j = tid; j < n; j += 256) local_sum += expf(bf2f(srow[j]) - mx);
-  __shared__ float s_tree[256];
+  for (int j = tid; j < n; j += 256) local_sum += expf(bf2f(ld(j)) - mx);
   s_tree[tid] = local_sum;
   __syncthreads();
   for (int s = 128; s > 0; s >>= 1) {
     if (tid < s) s_tree[tid] += s_tree[tid + s];
     __syncthreads();
   }
-  const float inv_sum = 1.0f / s_tree[0];
-  // P for this split's keys
-  for (int j = j0 + tid; j < j1; j += 256) {
-    float e = expf(bf2f(srow[j]) - mx);
-    s_p[j - j0] = bf2f(f2bf(bf2f(f2bf(e)) * inv_sum));
-  }
-  __syncthreads();
-  // P.V: 8 lanes per 128-byte V row (8 dims each), 4 rows per warp step
+  mx_out = mx;
+  inv_out = 1.0f / s_tree[0];
+}
+
+// Partial O = sum_{j in [j0, j1)} P_j V_j over 256 threads: 8 lanes per
+// 128-byte V row (8 dims each), 4 rows per warp step, 4 steps in flight.
+// Returns this thread's share for dim `tid` (< 64) after the block reduction.
+__device__ __forceinline__ float pv_range(const DecodeArgs &a, int b, int h, int j0, int j1,
+                                          const float *p, float (*s_part)[kHD], int tid) {
+  const int warp = tid >> 5, lane = tid & 31;
   const int sub = lane >> 3, part = lane & 7;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   const uint16_t *Vb = a.Vc + (int64_t)b * a.seq_stride + h * kHD + part * 8;
-  for (int j = j0 + warp * 4 + sub; j < j1; j += 32) {
-    const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(Vb + (int64_t)j * a.d));
-    const float p = s_p[j - j0];
-    const uint32_t w[4] = {vv.x, vv.y, vv.z, vv.w};
+  constexpr int U = 4;
+  for (int jb = j0 + warp * 4 + sub; jb < j1; jb += 32 * U) {
+    uint4 vv[U];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      acc[2 * i] = fmaf(p, __uint_as_float(w[i] << 16), acc[2 * i]);
-      acc[2 * i + 1] = fmaf(p, __uint_as_float(w[i] & 0xffff0000u), acc[2 * i + 1]);
+    for (int u = 0; u < U; ++u) {
+      const int j = jb + 32 * u;
+      vv[u] = j < j1 ? __ldg(reinterpret_cast<const uint4 *>(Vb + (int64_t)j * a.d))
+                     : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = jb + 32 * u;
+      const float pj = j < j1 ? p[j - j0] : 0.f;
+      const uint32_t w[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] = fmaf(pj, __uint_as_float(w[i] << 16), acc[2 * i]);
+        acc[2 * i + 1] = fmaf(pj, __uint_as_float(w[i] & 0xffff0000u), acc[2 * i + 1]);
+      }
     }
   }
 #pragma unroll
@@ -437,6 +443,44 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
 #pragma unroll
     for (int w = 0; w < 8; ++w) o += s_part[w][tid];
   }
+  return o;
+}
+
+// Split path, kernel 1: this split's scores into the workspace row.
+__global__ void __launch_bounds__(256) attention_decode_scores_kernel(DecodeArgs a) {
+  const int bh = blockIdx.x, split = blockIdx.y;
+  const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
+  const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
+  const int j0 = split * a.keys_per_split;
+  const int j1 = min(n, j0 + a.keys_per_split);
+  if (j0 >= j1) return;
+  uint16_t *srow = a.scores + ((int64_t)b * a.n_head + h) * a.max_ctx;
+  score_keys(a, b, h, j0, j1, threadIdx.x >> 5, 8, threadIdx.x & 31,
+             [&](int j, uint16_t s) { srow[j] = s; });
+}
+
+// Split path, kernel 2: softmax statistics from the full score row (each
+// split recomputes them), P for this split's keys, its share of P.V; the
+// last split of (b, h) to finish adds the partials in split order.
+__global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) {
+  __shared__ float s_red[8];
+  __shared__ float s_tree[256];
+  __shared__ float s_part[8][kHD];
+  __shared__ float s_p[1024];
+  __shared__ int s_last;
+  const int bh = blockIdx.x, split = blockIdx.y;
+  const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
+  const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
+  const int j0 = split * a.keys_per_split;
+  const int j1 = min(n, j0 + a.keys_per_split);
+  const int tid = threadIdx.x;
+  const uint16_t *srow = a.scores + ((int64_t)b * a.n_head + h) * a.max_ctx;
+  float mx, inv_sum;
+  row_stats(n, tid, [&](int j) { return srow[j]; }, s_red, s_tree, mx, inv_sum);
+  for (int j = j0 + tid; j < j1; j += 256)
+    s_p[j - j0] = bf2f(f2bf(bf2f(f2bf(expf(bf2f(srow[j]) - mx))) * inv_sum));
+  __syncthreads();
+  const float o = pv_range(a, b, h, j0, j1, s_p, s_part, tid);
   if (a.splits == 1) {
     if (tid < kHD) a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(o);
     return;
@@ -459,6 +503,30 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
     a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(tot);
   }
   if (tid == 0) a.tickets[b * a.n_head + h] = 0;  // ready for the next call
+}
+
+// Whole-row path (enough (b, h) pairs to fill the GPU): one CTA per (b, h)
+// keeps the scores in shared memory, so K and V are each read once and the
+// call is one launch.
+__global__ void __launch_bounds__(256) attention_decode_fused_kernel(DecodeArgs a) {
+  __shared__ float s_red[8];
+  __shared__ float s_tree[256];
+  __shared__ float s_part[8][kHD];
+  __shared__ float s_p[1024];
+  __shared__ uint16_t s_s[1024];
+  const int bh = blockIdx.x;
+  const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
+  const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
+  const int tid = threadIdx.x;
+  score_keys(a, b, h, 0, n, tid >> 5, 8, tid & 31, [&](int j, uint16_t s) { s_s[j] = s; });
+  __syncthreads();
+  float mx, inv_sum;
+  row_stats(n, tid, [&](int j) { return s_s[j]; }, s_red, s_tree, mx, inv_sum);
+  for (int j = tid; j < n; j += 256)
+    s_p[j] = bf2f(f2bf(bf2f(f2bf(expf(bf2f(s_s[j]) - mx))) * inv_sum));
+  __syncthreads();
+  const float o = pv_range(a, b, h, 0, n, s_p, s_part, tid);
+  if (tid < kHD) a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(o);
 }
 
 static int decode_splits(int n_seq, int n_head, int max_ctx, int sm_count) {
@@ -503,6 +571,10 @@ int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
   size_t scores = ((size_t)n_seq * n_head * max_ctx * 2 + 255) & ~(size_t)255;
   a.partials = (float *)(w + scores);
   a.tickets = (int *)(w + scores + (size_t)n_seq * n_head * a.splits * kHD * 4);
+  if (a.splits == 1) {
+    attention_decode_fused_kernel<<<n_seq * n_head, 256, 0, s>>>(a);
+    return check_launch("attention_decode_fused");
+  }
   dim3 grid(n_seq * n_head, a.splits);
   if (a.splits > 1 &&
       cudaMemsetAsync(a.tickets, 0, (size_t)n_seq * n_head * sizeof(int), s) != cudaSuccess)

@@ -94,6 +94,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   }
 }
 
+// Barrier among `n` threads (a multiple of 32) of the block, id 1..15.
+__device__ __forceinline__ void named_barrier_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), no multicast anywhere in this library.
 // ---------------------------------------------------------------------------

@@ -33,6 +33,13 @@ struct GemmArgs : LinearArgs {
   int stages;
   int num_n_tiles, num_m_tiles;
   int kblocks;  // ceil(K bytes / 128)
+  // split-K: each (tile, split) unit reduces k-blocks [ks*kb_per, ..); the
+  // partial int32 sums meet in `ws` ([M][N], zero between calls) through
+  // integer atomics (exact in any order), and the last unit of a tile, found
+  // by a ticket counter, applies the epilogue and re-zeroes its tile.
+  int ksplit, kb_per;
+  int32_t *ws;
+  int *tickets;
   int *err;
 };
 
@@ -50,6 +57,8 @@ struct __align__(8) SmemCtl {
   uint32_t tmem_base;
   int abort_flag;
   int consumed;  // k-iterations consumed by the MMA thread (for abort drain)
+  int last_flag; // split-K: this CTA holds the last partial of the tile
+  int vote[2][4]; // epilogue warps' wait verdicts, double-buffered by unit
 };
 
 __device__ __forceinline__ void store_out(const GemmArgs &a, int epi, int m, int n, int32_t acc,
@@ -113,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int total_tiles = a.num_n_tiles * a.num_m_tiles;
+  const int total_units = a.num_n_tiles * a.num_m_tiles * a.ksplit;
   uint32_t tmem_cols = 32;
   while (tmem_cols < (uint32_t)(2 * BN)) tmem_cols <<= 1;
 
@@ -150,10 +159,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int kbox = kBoxBytes / (KIND == 0 ? 1 : 2);
     int stage = 0;
     uint32_t phase = 0;
-    for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+    for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x) {
+      const int t = u / a.ksplit, ks = u - (u / a.ksplit) * a.ksplit;
       const int n0 = (t % a.num_n_tiles) * kBM;
       const int m0 = (t / a.num_n_tiles) * BN;
-      for (int kb = 0; kb < a.kblocks; ++kb) {
+      const int kb0 = ks * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort_flag, a.err, 0x1101)) break;
         uint8_t *sa = smem + (size_t)stage * stage_bytes;
         mbar_arrive_expect_tx(&ctl->full[stage], stage_bytes);
@@ -176,14 +187,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     int consumed = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      const int ks = u - (u / a.ksplit) * a.ksplit;
+      const int kb0 = ks * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
       if (!mbar_wait(&ctl->tmem_empty[acc], acc_phase ^ 1, abort_flag, a.err, 0x1102)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-      for (int kb = 0; kb < a.kblocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&ctl->full[stage], phase, abort_flag, a.err, 0x1103)) {
           ok = false;
           break;
@@ -195,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < 4; ++k) {  // 4 x 32-byte K steps inside the 128-byte atom
           const uint64_t da = make_sw128_desc(sa + 32 * k);
           const uint64_t db = make_sw128_desc(sb + 32 * k);
-          const uint32_t accum = (kb | k) != 0;
+          const uint32_t accum = (kb != kb0) || (k != 0);
           if (KIND == 0)
             tc_mma_i8(d_tmem, da, db, idesc, accum);
           else
@@ -226,13 +239,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+    int iter = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+      const int t = u / a.ksplit;
       // Warp-uniform wait: lane 0 polls with the bound, the verdict is
       // broadcast, so the warp-collective tcgen05.ld below never runs with
       // part of the warp gone.
+      // All four epilogue warps then agree through a vote before any of them
+      // proceeds, so the named barriers below always see all 128 threads.
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&ctl->tmem_full[acc], acc_phase, abort_flag, a.err, 0x1105);
       ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (lane == 0) ctl->vote[iter & 1][quarter] = ok;
+      named_barrier_sync(1, 128);
+      ok = ctl->vote[iter & 1][0] & ctl->vote[iter & 1][1] & ctl->vote[iter & 1][2] &
+           ctl->vote[iter & 1][3];
+      ++iter;
       if (!ok) break;
       mbar_wait(&ctl->tmem_full[acc], acc_phase, nullptr, a.err, 0x1107);  // completed: returns at once
       tc_fence_after();
@@ -250,24 +272,69 @@ __global__ void __launch_bounds__(kThreads, 1)
           qcol = n - qseg * a.dseg;
         }
       }
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        const uint32_t taddr =
-            tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN + c);
-        tmem_ld_32x32b_x32(taddr, r);
-        tmem_ld_wait();
-        const int mbase = m0 + c;
-        float sx_lane = 0.f;
-        if (EPI != EPI_S32 && EPI != EPI_F32_BF16 && mbase + lane < a.M) sx_lane = a.sX[mbase + lane];
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      if (a.ksplit == 1) {
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + (uint32_t)c, r);
+          tmem_ld_wait();
+          const int mbase = m0 + c;
+          float sx_lane = 0.f;
+          if (EPI != EPI_S32 && EPI != EPI_F32_BF16 && mbase + lane < a.M)
+            sx_lane = a.sX[mbase + lane];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float sx = __shfl_sync(0xffffffffu, sx_lane, i);
-          const int m = mbase + i;
-          if (n_ok && m < a.M) store_out(a, EPI, m, n, (int32_t)r[i], sw, sx, bias, qseg, qcol);
+          for (int i = 0; i < 32; ++i) {
+            const float sx = __shfl_sync(0xffffffffu, sx_lane, i);
+            const int m = mbase + i;
+            if (n_ok && m < a.M) store_out(a, EPI, m, n, (int32_t)r[i], sw, sx, bias, qseg, qcol);
+          }
         }
+        tc_fence_before();
+        mbar_arrive(&ctl->tmem_empty[acc]);
+      } else {
+        // add this split's partial sums into the workspace tile
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + (uint32_t)c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int m = m0 + c + i;
+            if (n_ok && m < a.M) atomicAdd(a.ws + (int64_t)m * a.N + n, (int)r[i]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&ctl->tmem_empty[acc]);  // TMEM is free for the next unit
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (warp == kEpiWarp0 && lane == 0) {
+          const int ticket = atomicAdd(a.tickets + t, 1);
+          ctl->last_flag = (ticket == a.ksplit - 1);
+        }
+        named_barrier_sync(1, 128);
+        if (ctl->last_flag) {
+          __threadfence();
+          for (int c = 0; c < BN; c += 32) {
+            const int mbase = m0 + c;
+            float sx_lane = 0.f;
+            if (EPI != EPI_S32 && EPI != EPI_F32_BF16 && mbase + lane < a.M)
+              sx_lane = a.sX[mbase + lane];
+#pragma unroll 4
+            for (int i = 0; i < 32; ++i) {
+              const float sx = __shfl_sync(0xffffffffu, sx_lane, i);
+              const int m = mbase + i;
+              if (n_ok && m < a.M) {
+                int32_t *w = a.ws + (int64_t)m * a.N + n;
+                const int32_t tot = __ldcg(w);
+                *w = 0;
+                store_out(a, EPI, m, n, tot, sw, sx, bias, qseg, qcol);
+              }
+            }
+          }
+          if (warp == kEpiWarp0 && lane == 0) a.tickets[t] = 0;
+        }
+        named_barrier_sync(1, 128);  // last_flag is reused by the next unit
       }
-      tc_fence_before();
-      mbar_arrive(&ctl->tmem_empty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -337,6 +404,27 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   a.num_m_tiles = (M + a.BN - 1) / a.BN;
   a.kblocks = (K * esz + kBoxBytes - 1) / kBoxBytes;
   a.err = ctx->err;
+  a.ksplit = 1;
+  a.kb_per = a.kblocks;
+  a.ws = nullptr;
+  a.tickets = nullptr;
+  const int tiles0 = a.num_n_tiles * a.num_m_tiles;
+  if (KIND == 0 && la.workspace && 2 * tiles0 <= ctx->sm_count && a.kblocks > 1 &&
+      la.workspace_bytes >= linear_workspace_bytes(M, N)) {
+    // Too few output tiles to occupy the GPU (decode): split K so that about
+    // one unit lands on every SM.
+    int ks = ctx->sm_count / tiles0;
+    if (ks > a.kblocks) ks = a.kblocks;
+    a.kb_per = (a.kblocks + ks - 1) / ks;
+    a.ksplit = (a.kblocks + a.kb_per - 1) / a.kb_per;
+    if (a.ksplit > 1) {
+      uint8_t *w = (uint8_t *)la.workspace;
+      a.ws = (int32_t *)w;
+      a.tickets = (int *)(w + (((size_t)M * N * 4 + 255) & ~(size_t)255));
+    } else {
+      a.kb_per = a.kblocks;
+    }
+  }
   static bool attr_set[64] = {};  // per template instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -347,10 +435,15 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
       return W8A8_ERR_CUDA;
     attr_set[dev] = true;
   }
-  int tiles = a.num_n_tiles * a.num_m_tiles;
-  int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+  int units = a.num_n_tiles * a.num_m_tiles * a.ksplit;
+  int grid = units < ctx->sm_count ? units : ctx->sm_count;
   gemm_tc_kernel<KIND, EPI><<<grid, kThreads, smem, stream>>>(tmW, tmX, a);
   return check_launch("gemm_tc");
+}
+
+size_t linear_workspace_bytes(int M, int N) {
+  const size_t tiles = (size_t)((N + kBM - 1) / kBM) * (size_t)((M + 31) / 32);
+  return (((size_t)M * N * 4 + 255) & ~(size_t)255) + tiles * 4;
 }
 
 int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,

@@ -37,7 +37,13 @@ struct LinearArgs {
   int T;
   const int32_t *pos0;
   int dseg;
+  // split-K workspace (nullable): int32 [M][N] partial sums + tile tickets,
+  // zero-filled before first use; the kernels leave it zeroed.
+  void *workspace;
+  size_t workspace_bytes;
 };
+
+size_t linear_workspace_bytes(int M, int N);
 
 // gemm_tc.cu
 int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,

@@ -22,7 +22,19 @@ constexpr int kRowWarps = 8;  // rows (warps) per block
 __device__ __forceinline__ void quantize_row_smem(const uint16_t *row, int K, int8_t *xq_row,
                                                   float *sx_out, int lane) {
   float amax = 0.0f;
-  for (int j = lane; j < K; j += 32) amax = fmaxf(amax, fabsf(bf2f(row[j])));
+  if ((K & 7) == 0) {
+    for (int j = lane * 8; j < K; j += 256) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(row + j);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        amax = fmaxf(amax, fabsf(__uint_as_float(w[e] << 16)));
+        amax = fmaxf(amax, fabsf(__uint_as_float(w[e] & 0xffff0000u)));
+      }
+    }
+  } else {
+    for (int j = lane; j < K; j += 32) amax = fmaxf(amax, fabsf(bf2f(row[j])));
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   // scale = amax/127 (1.0 for an all-zero row); q = rn(x * (1/scale)), ±127.
@@ -120,11 +132,41 @@ __device__ __forceinline__ void layernorm_row_smem(uint16_t *row, int d, const u
   const float variance = tree1024(v) / (float)d;
   const float inv_std_dev = rsqrtf(variance + eps);
   __syncwarp();
-  // phase 3: normalise, affine, round to bf16 (layernorm.cu:73-77)
-  for (int j = lane; j < d; j += 32) {
-    float val = bf2f(row[j]);
-    float normalized = (val - mean) * inv_std_dev;
-    row[j] = f2bf(normalized * bf2f(gamma[j]) + bf2f(beta[j]));
+  // phase 3: normalise, affine, round to bf16 (layernorm.cu:73-77). 16-byte
+  // vectors of γ/β, all loads of a lane issued before the arithmetic.
+  if ((d & 7) == 0 && aligned16(gamma) && aligned16(beta)) {
+    constexpr int kMaxVec = 8;  // 8 x 256 elements per lane pass
+    for (int base = lane * 8; base < d; base += 256 * kMaxVec) {
+      uint4 gv[kMaxVec], bv[kMaxVec];
+#pragma unroll
+      for (int u = 0; u < kMaxVec; ++u) {
+        const int j = base + 256 * u;
+        if (j < d) {
+          gv[u] = __ldg(reinterpret_cast<const uint4 *>(gamma + j));
+          bv[u] = __ldg(reinterpret_cast<const uint4 *>(beta + j));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kMaxVec; ++u) {
+        const int j = base + 256 * u;
+        if (j < d) {
+          const uint16_t *g = reinterpret_cast<const uint16_t *>(&gv[u]);
+          const uint16_t *bb = reinterpret_cast<const uint16_t *>(&bv[u]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float val = bf2f(row[j + e]);
+            float normalized = (val - mean) * inv_std_dev;
+            row[j + e] = f2bf(normalized * bf2f(g[e]) + bf2f(bb[e]));
+          }
+        }
+      }
+    }
+  } else {
+    for (int j = lane; j < d; j += 32) {
+      float val = bf2f(row[j]);
+      float normalized = (val - mean) * inv_std_dev;
+      row[j] = f2bf(normalized * bf2f(gamma[j]) + bf2f(beta[j]));
+    }
   }
   __syncwarp();
 }

@@ -101,7 +101,7 @@ void dot_2d_int8_fused_cuda(const act_t *x, int M, int K, const qweight_t *w_int
         "dot_2d_int8_fused_cuda (quant)", M, K);
   check(w8a8_linear(x_int8_scratch, scale_x_scratch, M, K, w_int8, scale_w,
                     (const gpt2_bf16_t *)bias, N, epilogue, (const gpt2_bf16_t *)residual, N,
-                    (gpt2_bf16_t *)y, N, NULL),
+                    (gpt2_bf16_t *)y, N, NULL, 0, NULL),
         "dot_2d_int8_fused_cuda", M, N);
 }
 

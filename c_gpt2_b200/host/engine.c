@@ -51,6 +51,8 @@ struct gpt2_engine {
   int32_t *len, *nctx, *gen, *next, *tokens_in, *out_default;
   void *attn_ws;
   size_t attn_ws_bytes;
+  void *lin_ws; /* split-K workspace of the decode-sized GEMMs (zeroed) */
+  size_t lin_ws_bytes;
   /* current batch */
   int B;
   int32_t *out;
@@ -193,6 +195,7 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   }
   /* activations */
   e->attn_ws_bytes = w8a8_attention_decode_workspace_size((int)Bm, cfg->n_head, (int)C);
+  e->lin_ws_bytes = w8a8_linear_workspace_size((int)Bm, 4 * (int)d);
   size_t off = 0, sizes[14];
   sizes[0] = Mt * d * 2;        /* H */
   sizes[1] = Mt * d * 2;        /* R1 */
@@ -207,7 +210,7 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   sizes[10] = Mt * 4;           /* tokens_in */
   sizes[11] = Bm * 4 * (size_t)C; /* default output buffer */
   sizes[12] = e->attn_ws_bytes;
-  sizes[13] = 0;
+  sizes[13] = e->lin_ws_bytes;
   size_t offs[14];
   for (int i = 0; i < 14; ++i) {
     offs[i] = off;
@@ -234,6 +237,7 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   e->tokens_in = (int32_t *)(a + offs[10]);
   e->out_default = (int32_t *)(a + offs[11]);
   e->attn_ws = a + offs[12];
+  e->lin_ws = a + offs[13];
   if (cudaMemset(e->ablob, 0, off) != cudaSuccess) {
     gpt2_engine_destroy(e);
     return W8A8_ERR_CUDA;
@@ -394,7 +398,7 @@ static int block_forward(gpt2_engine *e, int l, int B, int T, const int32_t *pos
   if (!first)
     W8_TRY(e, w8a8_layernorm_quant(e->H, d, M, d, w->ln1_g, w->ln1_b, eps, NULL, 0, e->Xq, e->sX, s));
   W8_TRY(e, w8a8_linear_qkv(e->Xq, e->sX, M, d, w->Wqkv, w->sWqkv, w->bqkv, e->Q, d, Kl, Vl,
-                            seq_stride, T, pos0, s));
+                            seq_stride, T, pos0, e->lin_ws, e->lin_ws_bytes, s));
   if (pos0 == NULL)
     W8_TRY(e, w8a8_attention_prefill(e->Q, d, Kl, Vl, seq_stride, B, T, Hh, 64, e->ATT, d, s));
   else
@@ -402,13 +406,13 @@ static int block_forward(gpt2_engine *e, int l, int B, int T, const int32_t *pos
                                     e->ATT, d, e->attn_ws, e->attn_ws_bytes, s));
   W8_TRY(e, w8a8_quant_rows(e->ATT, d, M, d, e->Xq, e->sX, s));
   W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, d, w->Wproj, w->sWproj, w->bproj, d, W8A8_EPI_BIAS_RESID,
-                        e->H, d, e->R1, d, s));
+                        e->H, d, e->R1, d, e->lin_ws, e->lin_ws_bytes, s));
   W8_TRY(e, w8a8_layernorm_quant(e->R1, d, M, d, w->ln2_g, w->ln2_b, eps, NULL, 0, e->Xq, e->sX, s));
   W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, d, w->W1, w->sW1, w->b1, f, W8A8_EPI_BIAS_GELU, NULL, 0,
-                        e->X1, f, s));
+                        e->X1, f, e->lin_ws, e->lin_ws_bytes, s));
   W8_TRY(e, w8a8_quant_rows(e->X1, f, M, f, e->Xq, e->sX, s));
   W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, f, w->W2, w->sW2, w->b2, d, W8A8_EPI_BIAS_RESID, e->R1, d,
-                        e->H, d, s));
+                        e->H, d, e->lin_ws, e->lin_ws_bytes, s));
   return W8A8_OK;
 }
 

@@ -94,23 +94,33 @@ def gemm_s32(Xq: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
     return Y
 
 
-def linear(Xq, sX, W, sW, bias, epilogue=_lib.EPI_BIAS, R=None, out=None):
+def linear_workspace(M: int, N: int, device) -> torch.Tensor:
+    """Zero-filled split-K workspace for w8a8_linear (reusable across calls)."""
+    return torch.zeros((core().w8a8_linear_workspace_size(M, N),), dtype=torch.uint8,
+                       device=device)
+
+
+def linear(Xq, sX, W, sW, bias, epilogue=_lib.EPI_BIAS, R=None, out=None, workspace=None):
     """Fused W8A8 linear: dequant (+bias) (+residual | +GELU) -> bf16 [M,N]."""
     _need(Xq, torch.int8, "Xq")
     M, K = Xq.shape
     N = W.shape[0]
     Y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=Xq.device)
     ldr = R.stride(0) if R is not None else 0
+    ws_bytes = workspace.numel() if workspace is not None else 0
     check(core().w8a8_linear(_ptr(Xq), _ptr(sX), M, K, _ptr(W), _ptr(sW), _ptr(bias), N, epilogue,
-                             _ptr(R), ldr, _ptr(Y), Y.stride(0), _stream()), "w8a8_linear")
+                             _ptr(R), ldr, _ptr(Y), Y.stride(0), _ptr(workspace), ws_bytes,
+                             _stream()), "w8a8_linear")
     return Y
 
 
-def linear_qkv(Xq, sX, Wqkv, sWqkv, bqkv, Q, Kc, Vc, seq_stride, T, pos0=None):
+def linear_qkv(Xq, sX, Wqkv, sWqkv, bqkv, Q, Kc, Vc, seq_stride, T, pos0=None, workspace=None):
     M, d = Xq.shape
+    ws_bytes = workspace.numel() if workspace is not None else 0
     check(core().w8a8_linear_qkv(_ptr(Xq), _ptr(sX), M, d, _ptr(Wqkv), _ptr(sWqkv), _ptr(bqkv),
                                  _ptr(Q), Q.stride(0), _ptr(Kc), _ptr(Vc), seq_stride, T,
-                                 _ptr(pos0), _stream()), "w8a8_linear_qkv")
+                                 _ptr(pos0), _ptr(workspace), ws_bytes, _stream()),
+          "w8a8_linear_qkv")
 
 
 def attention_prefill(Q, Kc, Vc, seq_stride, n_seq, T, n_head, out=None):

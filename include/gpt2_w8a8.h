@@ -92,7 +92,15 @@ int w8a8_gemm_s32(const int8_t *Xq, int M, int K, const int8_t *W, int N, int32_
  * alias Y (in-place residual add). bias may be NULL only for EPI_DEQUANT. */
 int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W,
                 const float *sW, const gpt2_bf16_t *bias, int N, int epilogue,
-                const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy, void *stream);
+                const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy,
+                void *workspace, size_t workspace_bytes, void *stream);
+
+/* Workspace that lets w8a8_linear / w8a8_linear_qkv split the reduction over
+ * K when M is small (decode) and the output tiles alone cannot occupy every
+ * SM. Optional (NULL disables splitting). It must be zero-filled once before
+ * its first use; every call leaves it zero again. Calls sharing a workspace
+ * must not overlap on the GPU. */
+size_t w8a8_linear_workspace_size(int M, int N);
 
 /* ---- packed QKV projection straight into Q and the KV cache ----
  * W_qkv [3d, d] stays packed (the reference splits it at load,
@@ -104,7 +112,8 @@ int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W
 int w8a8_linear_qkv(const int8_t *Xq, const float *sX, int M, int d, const int8_t *Wqkv,
                     const float *sWqkv, const gpt2_bf16_t *bqkv, gpt2_bf16_t *Q, int64_t ldq,
                     gpt2_bf16_t *Kc, gpt2_bf16_t *Vc, int64_t seq_stride, int T,
-                    const int32_t *pos0, void *stream);
+                    const int32_t *pos0, void *workspace, size_t workspace_bytes,
+                    void *stream);
 
 /* ---- causal attention over the KV cache, prefill (gpt2.c:1205-1217) ----
  * n_seq sequences of T tokens each, cached from position 0. Query row

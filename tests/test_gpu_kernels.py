@@ -76,6 +76,57 @@ def test_linear_epilogues_bit_exact(cuda, M, N, K, epi):
     np.testing.assert_array_equal(from_dev_bf16(out), want)
 
 
+@pytest.mark.parametrize("M,N,K", [(16, 768, 768), (64, 1280, 5120), (64, 3840, 1280),
+                                   (33, 5120, 1280), (100, 200, 3072)])
+@pytest.mark.parametrize("epi", [_lib.EPI_BIAS, _lib.EPI_BIAS_RESID])
+def test_linear_split_k_bit_exact(cuda, M, N, K, epi):
+    """Decode-sized GEMMs split K over the SMs and meet in an int32 workspace
+    through integer atomics: exact in any order. Two calls in a row check that
+    the workspace is left zeroed."""
+    rng = np.random.default_rng(M * N + K)
+    x = oracle.bf16_bits(outlier_activations(M, K, seed=M + epi))
+    xq, sx = oracle.quant_rows(x)
+    W = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    b = _rand_bf16(rng, (N,), 0.02)
+    R = _rand_bf16(rng, (M, N))
+    Rr = R if epi == _lib.EPI_BIAS_RESID else None
+    want = oracle.linear(xq, sx, W, sw, b, epi, Rr)
+    ws = ops.linear_workspace(M, N, cuda)
+    args = (to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw), to_dev_bf16(b), epi)
+    for _ in range(2):
+        out = ops.linear(*args, R=to_dev_bf16(R) if Rr is not None else None, workspace=ws)
+        np.testing.assert_array_equal(from_dev_bf16(out), want)
+    assert not ws.any(), "workspace not returned to zero"
+
+
+def test_linear_qkv_scatter_split_k(cuda):
+    """Packed QKV GEMM writing Q rows and K/V cache rows at per-sequence
+    positions (decode: one token per sequence), with split-K."""
+    rng = np.random.default_rng(11)
+    B, d, C = 20, 768, 64
+    x = oracle.bf16_bits(outlier_activations(B, d, seed=4))
+    xq, sx = oracle.quant_rows(x)
+    W = rng.integers(-127, 128, (3 * d, d), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, 3 * d).astype(np.float32)
+    b = _rand_bf16(rng, (3 * d,), 0.02)
+    want = oracle.linear(xq, sx, W, sw, b, oracle.EPI_BIAS)
+    pos = rng.integers(0, C, B).astype(np.int32)
+    Q = torch.zeros((B, d), dtype=torch.bfloat16, device=cuda)
+    Kc = torch.zeros((B, C, d), dtype=torch.bfloat16, device=cuda)
+    Vc = torch.zeros((B, C, d), dtype=torch.bfloat16, device=cuda)
+    ws = ops.linear_workspace(B, 3 * d, cuda)
+    ops.linear_qkv(to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw), to_dev_bf16(b), Q, Kc, Vc,
+                   C * d, 1, to_dev(pos), workspace=ws)
+    q, k, v = from_dev_bf16(Q), from_dev_bf16(Kc), from_dev_bf16(Vc)
+    np.testing.assert_array_equal(q, want[:, :d])
+    for i in range(B):
+        np.testing.assert_array_equal(k[i, pos[i]], want[i, d:2 * d])
+        np.testing.assert_array_equal(v[i, pos[i]], want[i, 2 * d:])
+        other = np.delete(np.arange(C), pos[i])
+        assert not k[i, other].any() and not v[i, other].any()
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 3072, 768), (64, 5120, 1280), (512, 3072, 768)])
 def test_linear_gelu_within_one_ulp(cuda, M, N, K):
     """GELU uses CUDA's tanhf on the GPU and the C library's on the CPU:
