@@ -161,7 +161,7 @@ def test_host_validation_without_gpu():
     lib = _lib.core()
     assert lib.w8a8_quant_rows(None, 8, 4, 8, None, None, None) == _lib.W8A8_ERR_INVALID
     assert lib.w8a8_linear(None, None, 4, 16, None, None, None, 8, 1, None, 0, None, 8,
-                           None) == _lib.W8A8_ERR_INVALID
+                           None, 0, None) == _lib.W8A8_ERR_INVALID
     assert lib.w8a8_quant_rows(None, 8, 0, 8, None, None, None) == _lib.W8A8_OK  # empty
     assert _lib.status_string(_lib.W8A8_ERR_DEVICE).startswith("a kernel")
     cfg = _lib.EngineConfig(768, 12, 10, 50257, 1024, 4, 4096)  # head_dim != 64
