@@ -1,24 +1,32 @@
 // Persistent warp-specialised tcgen05 GEMM for sm_100a.
 //
-// D[n, m] = sum_k W[n, k] * X[m, k] — the weight tile is the MMA's A operand
-// (128 rows of output channels) and the token tile its B operand (BN tokens),
-// so a decode batch of 16..256 tokens fills one MMA N dimension and prefill
-// tiles the token dimension. Both operands are K-major exactly as the
-// reference stores them (W [OUT, IN], activations [tokens, IN]).
+// Y[m, n] = epilogue(sum_k X[m, k] * W[n, k]) with both operands K-major,
+// exactly as the reference stores them (W [OUT, IN], activations
+// [tokens, IN]). Two orientations of the same pipeline:
 //
-//   warp 0      TMA producer: 128 x 128 B weight box + BN x 128 B token box
-//               per stage (SWIZZLE_128B, no multicast).
-//   warp 1      TMEM allocator + single-thread MMA issuer
-//               (kind::i8 -> s32, or kind::f16 with bf16 -> f32 for the LM head).
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator, fused dequant / bias /
-//               residual / GELU / QKV scatter, bf16 stores.
-// The accumulator is double-buffered in TMEM so the epilogue of tile i
-// overlaps the main loop of tile i+1.
+//   token-major (prefill, M > 128): A = 128 token rows, B = BN weight rows.
+//     TMEM lane = token, columns = output channels, so each epilogue thread
+//     owns a run of consecutive outputs of one row: 16-byte loads of the
+//     residual and 16-byte stores of the result.
+//   channel-major (decode, M <= 128): A = 128 weight rows, B = the BN tokens
+//     of the batch (16..128). When the output tiles alone cannot occupy the
+//     GPU the reduction is split over K; partial int32 sums meet in a
+//     workspace through integer atomics (exact in any order) and the last
+//     split of a tile, found by a ticket counter, runs the epilogue.
+//
+// Roles: warp 0 TMA producer (128-byte swizzled boxes, no multicast),
+// warp 1 TMEM allocator + single-thread MMA issuer (kind::i8 -> s32, or
+// kind::f16 with bf16 operands -> f32 for the LM head), warps 2..17 the
+// epilogue (4 warps per TMEM lane quarter, splitting the 32-column chunks).
+// The accumulator is double-buffered in TMEM so the epilogue of one tile
+// overlaps the main loop of the next. Every wait is bounded: a stalled
+// pipeline records an error code and the kernel returns.
 //
 // Replaces the reference's cublasGemmEx INT8 call (gpt2.c:404-415), its
 // dequant kernel (cuda/activation_quant.cu:117-131) and the add_bias /
 // add_2d / gelu kernels that follow each GEMM (gpt2.c:1145-1325), and the
 // bf16 LM-head GEMM (gpt2.c:2160).
+#include <stddef.h>
 #include <stdio.h>
 
 #include "common.cuh"
@@ -28,27 +36,26 @@
 
 namespace w8a8 {
 
+constexpr int kBM = 128;        // rows of the A tile (MMA M)
+constexpr int kBoxBytes = 128;  // K bytes per stage (one 128-byte swizzle atom)
+constexpr int kEpiWarps = 16;
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;
+constexpr int kEpiWarp0 = 2;
+constexpr int kEpiBarrier = 1;  // named barrier id of the epilogue warps
+
 struct GemmArgs : LinearArgs {
-  int BN;       // token tile (multiple of 32, <= 256)
+  int BN;                // rows of the B tile (multiple of 32, <= 256)
   int stages;
-  int num_n_tiles, num_m_tiles;
-  int kblocks;  // ceil(K bytes / 128)
-  // split-K: each (tile, split) unit reduces k-blocks [ks*kb_per, ..); the
-  // partial int32 sums meet in `ws` ([M][N], zero between calls) through
-  // integer atomics (exact in any order), and the last unit of a tile, found
-  // by a ticket counter, applies the epilogue and re-zeroes its tile.
-  int ksplit, kb_per;
-  int32_t *ws;
-  int *tickets;
+  int a_tiles, b_tiles;  // 128-row A tiles x BN-row B tiles
+  int kblocks;           // ceil(K bytes / 128)
+  int ksplit, kb_per;    // split-K (channel-major only)
+  int32_t *ws;           // [M][N] int32 partial sums, zero between calls
+  int *tickets;          // one per tile
   int *err;
 };
 
-constexpr int kBM = 128;            // weight rows per tile (MMA M)
-constexpr int kBoxBytes = 128;      // K bytes per stage (one 128 B swizzle atom)
-constexpr int kThreads = 192;       // 6 warps
-constexpr int kEpiWarp0 = 2;
-
-struct __align__(8) SmemCtl {
+struct __align__(16) SmemCtl {
   uint64_t full[16];
   uint64_t empty[16];
   uint64_t tmem_full[2];
@@ -56,60 +63,141 @@ struct __align__(8) SmemCtl {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
-  int consumed;  // k-iterations consumed by the MMA thread (for abort drain)
-  int last_flag; // split-K: this CTA holds the last partial of the tile
-  int vote[2][4]; // epilogue warps' wait verdicts, double-buffered by unit
+  int consumed;    // k-iterations consumed by the MMA thread (for abort drain)
+  int last_flag;   // split-K: this CTA holds the last partial of the tile
+  int vote[2][kEpiWarps];
+  // token-major: per-channel scales and biases of the B tile, read as 16- and
+  // 8-byte vectors, hence the explicit alignment
+  alignas(16) float tile_sw[256];
+  alignas(16) uint16_t tile_bias[256];
 };
+static_assert(offsetof(SmemCtl, tile_sw) % 16 == 0, "tile_sw must be 16-byte aligned");
+static_assert(offsetof(SmemCtl, tile_bias) % 16 == 0, "tile_bias must be 16-byte aligned");
 
-__device__ __forceinline__ void store_out(const GemmArgs &a, int epi, int m, int n, int32_t acc,
-                                          float sw, float sx, float bias, int qseg, int qcol) {
-  (void)qseg;
-  (void)qcol;
-  switch (epi) {
-    case EPI_S32:
+// ---------------------------------------------------------------------------
+// channel-major epilogue: one output channel n per thread, r[i] = token mbase+i
+// ---------------------------------------------------------------------------
+template <int EPI>
+__device__ __forceinline__ void finish_chunk_cm(const GemmArgs &a, int n, bool n_ok, float sw,
+                                                float bias, int qseg, int qcol, int mbase,
+                                                const uint32_t (&r)[32], int lane) {
+  const int m_lane = mbase + lane;
+  const bool m_lane_ok = m_lane < a.M;
+  float sx_lane = 0.f;
+  if (EPI != EPI_S32 && EPI != EPI_F32_BF16 && m_lane_ok) sx_lane = a.sX[m_lane];
+  int64_t kv_lane = 0;  // QKV: element offset of token m_lane's cache row
+  if (EPI == EPI_QKV && m_lane_ok) {
+    const int b = m_lane / a.T, t = m_lane - (m_lane / a.T) * a.T;
+    const int p = (a.pos0 ? a.pos0[b] : 0) + t;
+    kv_lane = (int64_t)b * a.seq_stride + (int64_t)p * a.dseg;
+  }
+  uint16_t rv[32];
+  if (EPI == EPI_RESID) {
+    // every residual value of the chunk in flight before the first store
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      rv[i] = (n_ok && mbase + i < a.M) ? a.R[(int64_t)(mbase + i) * a.ldr + n] : (uint16_t)0;
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float sx = __shfl_sync(0xffffffffu, sx_lane, i);
+    const int64_t kv = EPI == EPI_QKV ? __shfl_sync(0xffffffffu, kv_lane, i) : 0;
+    const int m = mbase + i;
+    if (!n_ok || m >= a.M) continue;
+    const int32_t acc = (int32_t)r[i];
+    uint16_t *Yb = reinterpret_cast<uint16_t *>(a.Y);
+    if (EPI == EPI_S32) {
       reinterpret_cast<int32_t *>(a.Y)[(int64_t)m * a.ldy + n] = acc;
-      break;
-    case EPI_DEQUANT:
-      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(dequant_bf(acc, sw, sx));
-      break;
-    case EPI_BIAS:
-      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] =
-          f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bias));
-      break;
-    case EPI_RESID: {
-      float y = add_bf(dequant_bf(acc, sw, sx), bias);
-      float r = bf2f(a.R[(int64_t)m * a.ldr + n]);
-      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(__fadd_rn(r, y));
-      break;
-    }
-    case EPI_GELU: {
-      float y = add_bf(dequant_bf(acc, sw, sx), bias);
-      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(gelu_tanh(y));
-      break;
-    }
-    case EPI_QKV: {
-      uint16_t v = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bias));
-      if (qseg == 0) {
-        reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + qcol] = v;
-      } else {
-        int b = m / a.T;
-        int t = m - b * a.T;
-        int p = (a.pos0 ? a.pos0[b] : 0) + t;
-        uint16_t *base = qseg == 1 ? a.Kc : a.Vc;
-        base[(int64_t)b * a.seq_stride + (int64_t)p * a.dseg + qcol] = v;
-      }
-      break;
-    }
-    default: {  // EPI_F32_BF16
-      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(__int_as_float(acc));
-      break;
+    } else if (EPI == EPI_DEQUANT) {
+      Yb[(int64_t)m * a.ldy + n] = f2bf(dequant_bf(acc, sw, sx));
+    } else if (EPI == EPI_BIAS) {
+      Yb[(int64_t)m * a.ldy + n] = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bias));
+    } else if (EPI == EPI_RESID) {
+      const float y = add_bf(dequant_bf(acc, sw, sx), bias);
+      Yb[(int64_t)m * a.ldy + n] = f2bf(__fadd_rn(bf2f(rv[i]), y));
+    } else if (EPI == EPI_GELU) {
+      const float y = add_bf(dequant_bf(acc, sw, sx), bias);
+      Yb[(int64_t)m * a.ldy + n] = f2bf(gelu_tanh(y));
+    } else if (EPI == EPI_QKV) {
+      const uint16_t v = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bias));
+      if (qseg == 0)
+        Yb[(int64_t)m * a.ldy + qcol] = v;
+      else
+        (qseg == 1 ? a.Kc : a.Vc)[kv + qcol] = v;
+    } else {  // EPI_F32_BF16
+      Yb[(int64_t)m * a.ldy + n] = f2bf(__int_as_float(acc));
     }
   }
 }
 
-template <int KIND, int EPI>
+// ---------------------------------------------------------------------------
+// token-major epilogue: one token row m per thread, r[j] = channel nbase+j.
+// Requires N % 32 == 0 and 16-byte aligned rows (checked on the host).
+// ---------------------------------------------------------------------------
+template <int EPI>
+__device__ __forceinline__ void finish_chunk_tm(const GemmArgs &a, const SmemCtl *ctl, int m,
+                                                float sx, int64_t kv_row, int nbase, int jbase,
+                                                const uint32_t (&r)[32]) {
+  if (m >= a.M || nbase >= a.N) return;
+  if (EPI == EPI_S32) {
+    int4 *dst = reinterpret_cast<int4 *>(reinterpret_cast<int32_t *>(a.Y) + (int64_t)m * a.ldy +
+                                         nbase);
+#pragma unroll
+    for (int v = 0; v < 8; ++v)
+      dst[v] = make_int4((int)r[4 * v], (int)r[4 * v + 1], (int)r[4 * v + 2], (int)r[4 * v + 3]);
+    return;
+  }
+  uint4 rv[4];
+  if (EPI == EPI_RESID) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(a.R + (int64_t)m * a.ldr + nbase);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) rv[v] = src[v];
+  }
+  uint32_t packed[16];
+#pragma unroll
+  for (int v = 0; v < 8; ++v) {
+    const float4 sw4 = *reinterpret_cast<const float4 *>(&ctl->tile_sw[jbase + 4 * v]);
+    const uint2 b4 = *reinterpret_cast<const uint2 *>(&ctl->tile_bias[jbase + 4 * v]);
+    const float swv[4] = {sw4.x, sw4.y, sw4.z, sw4.w};
+    const float bv[4] = {__uint_as_float(b4.x << 16), __uint_as_float(b4.x & 0xffff0000u),
+                         __uint_as_float(b4.y << 16), __uint_as_float(b4.y & 0xffff0000u)};
+    uint16_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = 4 * v + e;
+      const float t = dequant_bf((int32_t)r[j], swv[e], sx);
+      if (EPI == EPI_DEQUANT) {
+        o[e] = f2bf(t);
+      } else if (EPI == EPI_BIAS || EPI == EPI_QKV) {
+        o[e] = f2bf(__fadd_rn(t, bv[e]));
+      } else if (EPI == EPI_RESID) {
+        const uint32_t rw = (&rv[0].x)[j >> 1];
+        const float rf = __uint_as_float((j & 1) ? (rw & 0xffff0000u) : (rw << 16));
+        o[e] = f2bf(__fadd_rn(rf, add_bf(t, bv[e])));
+      } else {  // EPI_GELU
+        o[e] = f2bf(gelu_tanh(add_bf(t, bv[e])));
+      }
+    }
+    packed[2 * v] = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+    packed[2 * v + 1] = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+  }
+  uint16_t *dst;
+  if (EPI == EPI_QKV) {
+    const int seg = nbase / a.dseg, col = nbase - (nbase / a.dseg) * a.dseg;
+    dst = seg == 0 ? reinterpret_cast<uint16_t *>(a.Y) + (int64_t)m * a.ldy + col
+                   : (seg == 1 ? a.Kc : a.Vc) + kv_row + col;
+  } else {
+    dst = reinterpret_cast<uint16_t *>(a.Y) + (int64_t)m * a.ldy + nbase;
+  }
+  uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+  for (int v = 0; v < 4; ++v)
+    d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+}
+
+template <int KIND, int EPI, bool CM>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -122,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int total_units = a.num_n_tiles * a.num_m_tiles * a.ksplit;
+  const int total_units = a.a_tiles * a.b_tiles * a.ksplit;
   uint32_t tmem_cols = 32;
   while (tmem_cols < (uint32_t)(2 * BN)) tmem_cols <<= 1;
 
@@ -133,15 +221,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ctl->tmem_full[i], 1);
-      mbar_init(&ctl->tmem_empty[i], 128);
+      mbar_init(&ctl->tmem_empty[i], kEpiThreads);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort_flag = 0;
     ctl->consumed = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
-    prefetch_tmap(&tmW);
-    prefetch_tmap(&tmX);
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
   }
   if (warp == 1) {
     tmem_alloc(&ctl->tmem_base, tmem_cols);
@@ -161,15 +249,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x) {
       const int t = u / a.ksplit, ks = u - (u / a.ksplit) * a.ksplit;
-      const int n0 = (t % a.num_n_tiles) * kBM;
-      const int m0 = (t / a.num_n_tiles) * BN;
+      const int a0 = (t / a.b_tiles) * kBM;
+      const int b0 = (t % a.b_tiles) * BN;
       const int kb0 = ks * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort_flag, a.err, 0x1101)) break;
         uint8_t *sa = smem + (size_t)stage * stage_bytes;
         mbar_arrive_expect_tx(&ctl->full[stage], stage_bytes);
-        tma_load_2d(sa, &tmW, &ctl->full[stage], kb * kbox, n0);
-        tma_load_2d(sa + a_bytes, &tmX, &ctl->full[stage], kb * kbox, m0);
+        tma_load_2d(sa, &tmA, &ctl->full[stage], kb * kbox, a0);
+        tma_load_2d(sa + a_bytes, &tmB, &ctl->full[stage], kb * kbox, b0);
         ++issued;
         if (++stage == stages) {
           stage = 0;
@@ -179,8 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer ----------------
-    const uint32_t idesc =
-        KIND == 0 ? make_idesc(2, 1, kBM, BN) : make_idesc(1, 1, kBM, BN);
+    const uint32_t idesc = KIND == 0 ? make_idesc(2, 1, kBM, BN) : make_idesc(1, 1, kBM, BN);
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
@@ -236,104 +323,122 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kEpiWarp0) {
     // ---------------- epilogue ----------------
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32)
+    const int e = warp - kEpiWarp0;     // 0..15
+    const int quarter = warp & 3;       // TMEM lanes [32*quarter, 32*quarter+32)
+    const int group = e >> 2;           // chunks c == group (mod 4)
+    const int nchunks = BN >> 5;
     int acc = 0;
     uint32_t acc_phase = 0;
     int iter = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
       const int t = u / a.ksplit;
-      // Warp-uniform wait: lane 0 polls with the bound, the verdict is
-      // broadcast, so the warp-collective tcgen05.ld below never runs with
-      // part of the warp gone.
-      // All four epilogue warps then agree through a vote before any of them
-      // proceeds, so the named barriers below always see all 128 threads.
+      // Warp-uniform bounded wait, then a vote of all epilogue warps, so the
+      // named barriers below always see every epilogue thread.
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&ctl->tmem_full[acc], acc_phase, abort_flag, a.err, 0x1105);
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (lane == 0) ctl->vote[iter & 1][quarter] = ok;
-      named_barrier_sync(1, 128);
-      ok = ctl->vote[iter & 1][0] & ctl->vote[iter & 1][1] & ctl->vote[iter & 1][2] &
-           ctl->vote[iter & 1][3];
+      if (lane == 0) ctl->vote[iter & 1][e] = ok;
+      named_barrier_sync(kEpiBarrier, kEpiThreads);
+#pragma unroll
+      for (int w = 0; w < kEpiWarps; ++w) ok &= ctl->vote[iter & 1][w];
       ++iter;
       if (!ok) break;
       mbar_wait(&ctl->tmem_full[acc], acc_phase, nullptr, a.err, 0x1107);  // completed: returns at once
       tc_fence_after();
-      const int n0 = (t % a.num_n_tiles) * kBM;
-      const int m0 = (t / a.num_n_tiles) * BN;
-      const int n = n0 + quarter * 32 + lane;
-      const bool n_ok = n < a.N;
-      float sw = 0.f, bias = 0.f;
-      int qseg = 0, qcol = n;
-      if (n_ok) {
-        if (EPI != EPI_S32 && EPI != EPI_F32_BF16) sw = a.sW[n];
-        if (EPI >= EPI_BIAS && EPI <= EPI_QKV) bias = bf2f(a.bias[n]);
-        if (EPI == EPI_QKV) {
-          qseg = n / a.dseg;
-          qcol = n - qseg * a.dseg;
-        }
-      }
+      const int a0 = (t / a.b_tiles) * kBM;
+      const int b0 = (t % a.b_tiles) * BN;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-      if (a.ksplit == 1) {
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + (uint32_t)c, r);
-          tmem_ld_wait();
-          const int mbase = m0 + c;
-          float sx_lane = 0.f;
-          if (EPI != EPI_S32 && EPI != EPI_F32_BF16 && mbase + lane < a.M)
-            sx_lane = a.sX[mbase + lane];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float sx = __shfl_sync(0xffffffffu, sx_lane, i);
-            const int m = mbase + i;
-            if (n_ok && m < a.M) store_out(a, EPI, m, n, (int32_t)r[i], sw, sx, bias, qseg, qcol);
+      if (!CM) {
+        // token-major: stage the B tile's channel scales and biases
+        const int i = e * 32 + lane;
+        if (EPI != EPI_S32 && EPI != EPI_F32_BF16 && i < BN) {
+          const int n = b0 + i;
+          ctl->tile_sw[i] = n < a.N ? a.sW[n] : 0.f;
+          ctl->tile_bias[i] = (EPI >= EPI_BIAS && EPI <= EPI_QKV && n < a.N) ? a.bias[n] : 0;
+        }
+        named_barrier_sync(kEpiBarrier, kEpiThreads);
+        const int m = a0 + quarter * 32 + lane;
+        float sx = 0.f;
+        int64_t kv_row = 0;
+        if (m < a.M) {
+          if (EPI != EPI_S32 && EPI != EPI_F32_BF16) sx = a.sX[m];
+          if (EPI == EPI_QKV) {
+            const int b = m / a.T, tt = m - (m / a.T) * a.T;
+            kv_row = (int64_t)b * a.seq_stride + (int64_t)((a.pos0 ? a.pos0[b] : 0) + tt) * a.dseg;
           }
+        }
+        for (int c = group; c < nchunks; c += 4) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * c), r);
+          tmem_ld_wait();
+          finish_chunk_tm<EPI>(a, ctl, m, sx, kv_row, b0 + 32 * c, 32 * c, r);
         }
         tc_fence_before();
         mbar_arrive(&ctl->tmem_empty[acc]);
       } else {
-        // add this split's partial sums into the workspace tile
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_row + (uint32_t)c, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int m = m0 + c + i;
-            if (n_ok && m < a.M) atomicAdd(a.ws + (int64_t)m * a.N + n, (int)r[i]);
+        const int n = a0 + quarter * 32 + lane;
+        const bool n_ok = n < a.N;
+        float sw = 0.f, bias = 0.f;
+        int qseg = 0, qcol = n;
+        if (n_ok) {
+          if (EPI != EPI_S32 && EPI != EPI_F32_BF16) sw = a.sW[n];
+          if (EPI >= EPI_BIAS && EPI <= EPI_QKV) bias = bf2f(a.bias[n]);
+          if (EPI == EPI_QKV) {
+            qseg = n / a.dseg;
+            qcol = n - qseg * a.dseg;
           }
         }
-        tc_fence_before();
-        mbar_arrive(&ctl->tmem_empty[acc]);  // TMEM is free for the next unit
-        __threadfence();
-        named_barrier_sync(1, 128);
-        if (warp == kEpiWarp0 && lane == 0) {
-          const int ticket = atomicAdd(a.tickets + t, 1);
-          ctl->last_flag = (ticket == a.ksplit - 1);
-        }
-        named_barrier_sync(1, 128);
-        if (ctl->last_flag) {
-          __threadfence();
-          for (int c = 0; c < BN; c += 32) {
-            const int mbase = m0 + c;
-            float sx_lane = 0.f;
-            if (EPI != EPI_S32 && EPI != EPI_F32_BF16 && mbase + lane < a.M)
-              sx_lane = a.sX[mbase + lane];
-#pragma unroll 4
+        if (a.ksplit == 1) {
+          for (int c = group; c < nchunks; c += 4) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * c), r);
+            tmem_ld_wait();
+            finish_chunk_cm<EPI>(a, n, n_ok, sw, bias, qseg, qcol, b0 + 32 * c, r, lane);
+          }
+          tc_fence_before();
+          mbar_arrive(&ctl->tmem_empty[acc]);
+        } else {
+          // add this split's partial sums into the workspace tile
+          for (int c = group; c < nchunks; c += 4) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * c), r);
+            tmem_ld_wait();
+#pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const float sx = __shfl_sync(0xffffffffu, sx_lane, i);
-              const int m = mbase + i;
-              if (n_ok && m < a.M) {
-                int32_t *w = a.ws + (int64_t)m * a.N + n;
-                const int32_t tot = __ldcg(w);
-                *w = 0;
-                store_out(a, EPI, m, n, tot, sw, sx, bias, qseg, qcol);
-              }
+              const int m = b0 + 32 * c + i;
+              if (n_ok && m < a.M) atomicAdd(a.ws + (int64_t)m * a.N + n, (int)r[i]);
             }
           }
-          if (warp == kEpiWarp0 && lane == 0) a.tickets[t] = 0;
+          tc_fence_before();
+          mbar_arrive(&ctl->tmem_empty[acc]);  // TMEM is free for the next unit
+          __threadfence();
+          named_barrier_sync(kEpiBarrier, kEpiThreads);
+          if (e == 0 && lane == 0) {
+            const int ticket = atomicAdd(a.tickets + t, 1);
+            ctl->last_flag = (ticket == a.ksplit - 1);
+          }
+          named_barrier_sync(kEpiBarrier, kEpiThreads);
+          if (ctl->last_flag) {
+            __threadfence();
+            for (int c = group; c < nchunks; c += 4) {
+              // all partial sums of the chunk in flight at once, then re-zero
+              uint32_t r[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int m = b0 + 32 * c + i;
+                r[i] = (n_ok && m < a.M) ? (uint32_t)__ldcg(a.ws + (int64_t)m * a.N + n) : 0u;
+              }
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int m = b0 + 32 * c + i;
+                if (n_ok && m < a.M) a.ws[(int64_t)m * a.N + n] = 0;
+              }
+              finish_chunk_cm<EPI>(a, n, n_ok, sw, bias, qseg, qcol, b0 + 32 * c, r, lane);
+            }
+            if (e == 0 && lane == 0) a.tickets[t] = 0;
+          }
+          named_barrier_sync(kEpiBarrier, kEpiThreads);  // last_flag is reused by the next unit
         }
-        named_barrier_sync(1, 128);  // last_flag is reused by the next unit
       }
       if (++acc == 2) {
         acc = 0;
@@ -366,16 +471,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // host-side launcher
 // ---------------------------------------------------------------------------
-static int pick_bn(int M) {
-  if (M <= 32) return 32;
-  if (M <= 64) return 64;
-  if (M <= 96) return 96;
-  if (M <= 128) return 128;
-  if (M <= 192) return 192;
-  return 256;
-}
+static int round_up32(int x) { return (x + 31) & ~31; }
 
-template <int KIND, int EPI>
+template <int KIND, int EPI, bool CM>
 static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const LinearArgs &la,
                      cudaStream_t stream) {
   int st;
@@ -387,29 +485,42 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   const int esz = KIND == 0 ? 1 : 2;
   const CUtensorMapDataType dt =
       KIND == 0 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  a.BN = pick_bn(M);
-  CUtensorMap tmW, tmX;
-  st = make_tmap_2d(&tmW, W, dt, (uint64_t)N, (uint64_t)K, (uint64_t)K * esz, kBoxBytes / esz, kBM);
-  if (st) return st;
-  st = make_tmap_2d(&tmX, X, dt, (uint64_t)M, (uint64_t)K, (uint64_t)ldx_elems * esz,
-                    kBoxBytes / esz, (uint32_t)a.BN);
-  if (st) return st;
+  CUtensorMap tmA, tmB;
+  if (CM) {  // A = weights, B = tokens
+    a.BN = M >= 256 ? 256 : round_up32(M < 32 ? 32 : M);
+    st = make_tmap_2d(&tmA, W, dt, (uint64_t)N, (uint64_t)K, (uint64_t)K * esz, kBoxBytes / esz,
+                      kBM);
+    if (st) return st;
+    st = make_tmap_2d(&tmB, X, dt, (uint64_t)M, (uint64_t)K, (uint64_t)ldx_elems * esz,
+                      kBoxBytes / esz, (uint32_t)a.BN);
+    if (st) return st;
+    a.a_tiles = (N + kBM - 1) / kBM;
+    a.b_tiles = (M + a.BN - 1) / a.BN;
+  } else {   // A = tokens, B = weights
+    a.BN = N >= 256 ? 256 : round_up32(N);
+    st = make_tmap_2d(&tmA, X, dt, (uint64_t)M, (uint64_t)K, (uint64_t)ldx_elems * esz,
+                      kBoxBytes / esz, kBM);
+    if (st) return st;
+    st = make_tmap_2d(&tmB, W, dt, (uint64_t)N, (uint64_t)K, (uint64_t)K * esz, kBoxBytes / esz,
+                      (uint32_t)a.BN);
+    if (st) return st;
+    a.a_tiles = (M + kBM - 1) / kBM;
+    a.b_tiles = (N + a.BN - 1) / a.BN;
+  }
   const int stage_bytes = (kBM + a.BN) * kBoxBytes;
   const int budget = 227 * 1024 - 1024 - (int)sizeof(SmemCtl) - 64;
   a.stages = budget / stage_bytes;
   if (a.stages > 8) a.stages = 8;
   if (a.stages < 2) return W8A8_ERR_UNSUPPORTED;
   const size_t smem = 1024 + (size_t)a.stages * stage_bytes + sizeof(SmemCtl);
-  a.num_n_tiles = (N + kBM - 1) / kBM;
-  a.num_m_tiles = (M + a.BN - 1) / a.BN;
   a.kblocks = (K * esz + kBoxBytes - 1) / kBoxBytes;
   a.err = ctx->err;
   a.ksplit = 1;
   a.kb_per = a.kblocks;
   a.ws = nullptr;
   a.tickets = nullptr;
-  const int tiles0 = a.num_n_tiles * a.num_m_tiles;
-  if (KIND == 0 && la.workspace && 2 * tiles0 <= ctx->sm_count && a.kblocks > 1 &&
+  const int tiles0 = a.a_tiles * a.b_tiles;
+  if (CM && KIND == 0 && la.workspace && 2 * tiles0 <= ctx->sm_count && a.kblocks > 1 &&
       la.workspace_bytes >= linear_workspace_bytes(M, N)) {
     // Too few output tiles to occupy the GPU (decode): split K so that about
     // one unit lands on every SM.
@@ -430,14 +541,14 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return W8A8_ERR_CUDA;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<KIND, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             227 * 1024) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_tc_kernel<KIND, EPI, CM>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
       return W8A8_ERR_CUDA;
     attr_set[dev] = true;
   }
-  int units = a.num_n_tiles * a.num_m_tiles * a.ksplit;
-  int grid = units < ctx->sm_count ? units : ctx->sm_count;
-  gemm_tc_kernel<KIND, EPI><<<grid, kThreads, smem, stream>>>(tmW, tmX, a);
+  const int units = tiles0 * a.ksplit;
+  const int grid = units < ctx->sm_count ? units : ctx->sm_count;
+  gemm_tc_kernel<KIND, EPI, CM><<<grid, kThreads, smem, stream>>>(tmA, tmB, a);
   return check_launch("gemm_tc");
 }
 
@@ -446,15 +557,34 @@ size_t linear_workspace_bytes(int M, int N) {
   return (((size_t)M * N * 4 + 255) & ~(size_t)255) + tiles * 4;
 }
 
+// Token-major needs whole 32-column chunks and 16-byte aligned output rows.
+static bool token_major_ok(const LinearArgs &a) {
+  if (a.M <= kBM || (a.N & 31)) return false;
+  const int esz = a.epi == EPI_S32 ? 4 : 2;
+  if (!aligned16(a.Y) || (a.ldy * esz) % 16) return false;
+  if (a.epi == EPI_RESID && (!aligned16(a.R) || (a.ldr % 8))) return false;
+  if (a.epi == EPI_QKV &&
+      (!aligned16(a.Kc) || !aligned16(a.Vc) || (a.dseg & 31) || (a.seq_stride % 8)))
+    return false;
+  return true;
+}
+
+template <int EPI>
+static int launch_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,
+                     cudaStream_t s) {
+  return token_major_ok(a) ? launch_tc<0, EPI, false>(W, X, ldx, a, s)
+                           : launch_tc<0, EPI, true>(W, X, ldx, a, s);
+}
+
 int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,
                cudaStream_t stream) {
   switch (a.epi) {
-    case EPI_S32: return launch_tc<0, EPI_S32>(W, X, ldx, a, stream);
-    case EPI_DEQUANT: return launch_tc<0, EPI_DEQUANT>(W, X, ldx, a, stream);
-    case EPI_BIAS: return launch_tc<0, EPI_BIAS>(W, X, ldx, a, stream);
-    case EPI_RESID: return launch_tc<0, EPI_RESID>(W, X, ldx, a, stream);
-    case EPI_GELU: return launch_tc<0, EPI_GELU>(W, X, ldx, a, stream);
-    case EPI_QKV: return launch_tc<0, EPI_QKV>(W, X, ldx, a, stream);
+    case EPI_S32: return launch_i8<EPI_S32>(W, X, ldx, a, stream);
+    case EPI_DEQUANT: return launch_i8<EPI_DEQUANT>(W, X, ldx, a, stream);
+    case EPI_BIAS: return launch_i8<EPI_BIAS>(W, X, ldx, a, stream);
+    case EPI_RESID: return launch_i8<EPI_RESID>(W, X, ldx, a, stream);
+    case EPI_GELU: return launch_i8<EPI_GELU>(W, X, ldx, a, stream);
+    case EPI_QKV: return launch_i8<EPI_QKV>(W, X, ldx, a, stream);
     default: return W8A8_ERR_INVALID;
   }
 }
@@ -462,7 +592,7 @@ int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &
 int gemm_tc_bf16(const uint16_t *W, const uint16_t *X, int64_t ldx, const LinearArgs &a,
                  cudaStream_t stream) {
   if (a.epi != EPI_F32_BF16) return W8A8_ERR_INVALID;
-  return launch_tc<1, EPI_F32_BF16>(W, X, ldx, a, stream);
+  return launch_tc<1, EPI_F32_BF16, true>(W, X, ldx, a, stream);
 }
 
 }  // namespace w8a8

@@ -224,10 +224,234 @@ __global__ void __launch_bounds__(kRowWarps * 32)
   if (Xq) quantize_row_smem(srow, d, Xq + (int64_t)row * d, sX + row, lane);
 }
 
+// ---------------------------------------------------------------------------
+// Block-per-row kernels (128 threads, d % 8 == 0, d <= 8192): the hot path.
+// Thread t owns the 16-byte vectors v = t + 128k, i.e. elements
+// 8t + e + 1024k, so its eight running sums are exactly the reference's
+// slots 8t..8t+7 (thread s of the reference's 1024-thread block adds
+// elements s, s+1024, ... in order). The 1024 slots are then folded in
+// shared memory level by level (s = 512 .. 1) as the reference does. Few
+// instructions per thread and one memory round trip per row.
+// ---------------------------------------------------------------------------
+constexpr int kRowThreads = 128;
+constexpr int kMaxVec = 8;  // 8 x 1024 = 8192 elements per row
+
+struct RowShared {
+  float slots[1024];
+  float red[kRowThreads / 32];
+};
+
+__device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ float fold_slots(RowShared &sh, int t) {
+  __syncthreads();
+  for (int h = 512; h > 0; h >>= 1) {
+    for (int i = t; i < h; i += kRowThreads) sh.slots[i] += sh.slots[i + h];
+    __syncthreads();
+  }
+  const float v = sh.slots[0];
+  __syncthreads();
+  return v;
+}
+
+__device__ __forceinline__ float block_max(RowShared &sh, float v, int t) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((t & 31) == 0) sh.red[t >> 5] = v;
+  __syncthreads();
+  float m = sh.red[0];
+#pragma unroll
+  for (int w = 1; w < kRowThreads / 32; ++w) m = fmaxf(m, sh.red[w]);
+  __syncthreads();
+  return m;
+}
+
+// Quantize the row values a thread holds (bf16 bit patterns in y[k]) with the
+// row's scale (activation_quant.cu:75-91) and store them.
+__device__ __forceinline__ void quant_store(RowShared &sh, const uint4 (&y)[kMaxVec], int nv,
+                                            int t, int8_t *xq_row, float *sx_out) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    if (t + kRowThreads * k < nv) {
+      float f[8];
+      unpack8(y[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+    }
+  }
+  amax = block_max(sh, amax, t);
+  const float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+  const float inv = __fdiv_rn(1.0f, scale);
+  if (t == 0) *sx_out = scale;
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    const int v = t + kRowThreads * k;
+    if (v < nv) {
+      float f[8];
+      unpack8(y[k], f);
+      uint32_t w[2] = {0u, 0u};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int q = __float2int_rn(__fmul_rn(f[e], inv));
+        q = q > 127 ? 127 : (q < -127 ? -127 : q);
+        w[e >> 2] |= ((uint32_t)(q & 0xff)) << (8 * (e & 3));
+      }
+      *reinterpret_cast<uint2 *>(xq_row + 8 * v) = make_uint2(w[0], w[1]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kRowThreads)
+    quant_rows_block_kernel(const uint16_t *__restrict__ X, int64_t ldx, int K,
+                            int8_t *__restrict__ Xq, float *__restrict__ sX) {
+  __shared__ RowShared sh;
+  const int row = blockIdx.x, t = threadIdx.x, nv = K >> 3;
+  const uint4 *src = reinterpret_cast<const uint4 *>(X + (int64_t)row * ldx);
+  uint4 x[kMaxVec];
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    const int v = t + kRowThreads * k;
+    x[k] = v < nv ? __ldg(src + v) : make_uint4(0, 0, 0, 0);
+  }
+  quant_store(sh, x, nv, t, Xq + (int64_t)row * K, sX + row);
+}
+
+// MODE 0: rows of X. MODE 1: embedding gather wte[token] + wpe[position]
+// (embeddings.cu:18-23), written to H as the residual stream.
+template <int MODE>
+__global__ void __launch_bounds__(kRowThreads)
+    layernorm_block_kernel(const uint16_t *__restrict__ X, int64_t ldx,
+                           const uint16_t *__restrict__ wte, const uint16_t *__restrict__ wpe,
+                           const int32_t *__restrict__ tokens, int T,
+                           const int32_t *__restrict__ pos0, uint16_t *__restrict__ H, int d,
+                           const uint16_t *__restrict__ gamma, const uint16_t *__restrict__ beta,
+                           float eps, uint16_t *__restrict__ Y, int64_t ldy,
+                           int8_t *__restrict__ Xq, float *__restrict__ sX) {
+  __shared__ RowShared sh;
+  const int row = blockIdx.x, t = threadIdx.x, nv = d >> 3;
+  uint4 x[kMaxVec], g[kMaxVec], bt[kMaxVec];
+  if (MODE == 0) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(X + (int64_t)row * ldx);
+#pragma unroll
+    for (int k = 0; k < kMaxVec; ++k) {
+      const int v = t + kRowThreads * k;
+      x[k] = v < nv ? __ldg(src + v) : make_uint4(0, 0, 0, 0);
+    }
+  } else {
+    const int b = row / T, tt = row - (row / T) * T;
+    const int p = (pos0 ? pos0[b] : 0) + tt;
+    const uint4 *e = reinterpret_cast<const uint4 *>(wte + (int64_t)tokens[row] * d);
+    const uint4 *q = reinterpret_cast<const uint4 *>(wpe + (int64_t)p * d);
+#pragma unroll
+    for (int k = 0; k < kMaxVec; ++k) {
+      const int v = t + kRowThreads * k;
+      if (v < nv) {
+        float fe[8], fq[8];
+        unpack8(__ldg(e + v), fe);
+        unpack8(__ldg(q + v), fq);
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          w[i] = (uint32_t)f2bf(__fadd_rn(fe[2 * i], fq[2 * i])) |
+                 ((uint32_t)f2bf(__fadd_rn(fe[2 * i + 1], fq[2 * i + 1])) << 16);
+        x[k] = make_uint4(w[0], w[1], w[2], w[3]);
+        if (H) reinterpret_cast<uint4 *>(H + (int64_t)row * d)[v] = x[k];
+      } else {
+        x[k] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    const int v = t + kRowThreads * k;
+    if (v < nv) {
+      g[k] = __ldg(reinterpret_cast<const uint4 *>(gamma) + v);
+      bt[k] = __ldg(reinterpret_cast<const uint4 *>(beta) + v);
+    }
+  }
+  // mean: slot 8t+e accumulates elements 8t+e+1024k in order (layernorm.cu:25-41)
+  float s[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    if (t + kRowThreads * k < nv) {
+      float f[8];
+      unpack8(x[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s[e] += f[e];
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) sh.slots[8 * t + e] = s[e];
+  const float mean = fold_slots(sh, t) / (float)d;
+  // variance (layernorm.cu:45-66): diff*diff contracted into the running sum
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    if (t + kRowThreads * k < nv) {
+      float f[8];
+      unpack8(x[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float diff = f[e] - mean;
+        s[e] += diff * diff;
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) sh.slots[8 * t + e] = s[e];
+  const float variance = fold_slots(sh, t) / (float)d;
+  const float inv_std_dev = rsqrtf(variance + eps);
+  // normalise + affine, bf16 (layernorm.cu:73-77)
+  uint4 y[kMaxVec];
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    const int v = t + kRowThreads * k;
+    if (v < nv) {
+      float f[8], gf[8], bf[8];
+      unpack8(x[k], f);
+      unpack8(g[k], gf);
+      unpack8(bt[k], bf);
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float n0 = (f[2 * i] - mean) * inv_std_dev;
+        float n1 = (f[2 * i + 1] - mean) * inv_std_dev;
+        w[i] = (uint32_t)f2bf(n0 * gf[2 * i] + bf[2 * i]) |
+               ((uint32_t)f2bf(n1 * gf[2 * i + 1] + bf[2 * i + 1]) << 16);
+      }
+      y[k] = make_uint4(w[0], w[1], w[2], w[3]);
+      if (Y) reinterpret_cast<uint4 *>(Y + (int64_t)row * ldy)[v] = y[k];
+    } else {
+      y[k] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (Xq) quant_store(sh, y, nv, t, Xq + (int64_t)row * d, sX + row);
+}
+
+static bool block_path_ok(int d, const void *a, int64_t lda, const void *b, int64_t ldb) {
+  return (d & 7) == 0 && d <= 1024 * kMaxVec && aligned16(a) && (lda & 7) == 0 &&
+         (b == nullptr || (aligned16(b) && (ldb & 7) == 0));
+}
+
 static int row_grid(int M) { return (M + kRowWarps - 1) / kRowWarps; }
 
 int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, float *sX,
                       cudaStream_t s) {
+  if (block_path_ok(K, X, ldx, Xq, K) && M <= 0x7fffffff) {
+    quant_rows_block_kernel<<<M, kRowThreads, 0, s>>>(X, ldx, K, Xq, sX);
+    return check_launch("quant_rows_block");
+  }
   size_t smem = (size_t)kRowWarps * K * sizeof(uint16_t);
   if (smem > 200 * 1024) return W8A8_ERR_UNSUPPORTED;
   static bool attr[64] = {};
@@ -244,6 +468,13 @@ int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, 
 int launch_layernorm_quant(const uint16_t *X, int64_t ldx, int M, int d, const uint16_t *gamma,
                            const uint16_t *beta, float eps, uint16_t *Y, int64_t ldy, int8_t *Xq,
                            float *sX, cudaStream_t s) {
+  if (block_path_ok(d, X, ldx, Y, Y ? ldy : 0) && aligned16(gamma) && aligned16(beta) &&
+      (Xq == nullptr || aligned16(Xq))) {
+    layernorm_block_kernel<0><<<M, kRowThreads, 0, s>>>(X, ldx, nullptr, nullptr, nullptr, 1,
+                                                        nullptr, nullptr, d, gamma, beta, eps, Y,
+                                                        ldy, Xq, sX);
+    return check_launch("layernorm_block");
+  }
   size_t smem = (size_t)kRowWarps * d * sizeof(uint16_t);
   if (smem > 200 * 1024) return W8A8_ERR_UNSUPPORTED;
   static bool attr[64] = {};
@@ -263,6 +494,13 @@ int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const
                                  int M, int T, const int32_t *pos0, int d, uint16_t *H,
                                  const uint16_t *gamma, const uint16_t *beta, float eps,
                                  uint16_t *Y, int8_t *Xq, float *sX, cudaStream_t s) {
+  if (block_path_ok(d, wte, d, wpe, d) && aligned16(gamma) && aligned16(beta) &&
+      (H == nullptr || aligned16(H)) && (Y == nullptr || aligned16(Y)) &&
+      (Xq == nullptr || aligned16(Xq))) {
+    layernorm_block_kernel<1><<<M, kRowThreads, 0, s>>>(nullptr, 0, wte, wpe, tokens, T, pos0, H,
+                                                        d, gamma, beta, eps, Y, d, Xq, sX);
+    return check_launch("embed_layernorm_block");
+  }
   size_t smem = (size_t)kRowWarps * d * sizeof(uint16_t);
   if (smem > 200 * 1024) return W8A8_ERR_UNSUPPORTED;
   static bool attr[64] = {};
