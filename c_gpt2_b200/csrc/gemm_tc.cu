@@ -76,56 +76,112 @@ static_assert(offsetof(SmemCtl, tile_bias) % 16 == 0, "tile_bias must be 16-byte
 
 // ---------------------------------------------------------------------------
 // channel-major epilogue: one output channel n per thread, r[i] = token mbase+i
+// (W = 16 consecutive tokens of the TMEM accumulator)
 // ---------------------------------------------------------------------------
+template <int EPI>
+__device__ __forceinline__ void store_one_cm(const GemmArgs &a, int m, int n, int32_t acc,
+                                             float sw, float sx, float bias, uint16_t rv,
+                                             int qseg, int qcol, int64_t kv) {
+  uint16_t *Yb = reinterpret_cast<uint16_t *>(a.Y);
+  if (EPI == EPI_S32) {
+    reinterpret_cast<int32_t *>(a.Y)[(int64_t)m * a.ldy + n] = acc;
+  } else if (EPI == EPI_DEQUANT) {
+    Yb[(int64_t)m * a.ldy + n] = f2bf(dequant_bf(acc, sw, sx));
+  } else if (EPI == EPI_BIAS) {
+    Yb[(int64_t)m * a.ldy + n] = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bias));
+  } else if (EPI == EPI_RESID) {
+    const float y = add_bf(dequant_bf(acc, sw, sx), bias);
+    Yb[(int64_t)m * a.ldy + n] = f2bf(__fadd_rn(bf2f(rv), y));
+  } else if (EPI == EPI_GELU) {
+    const float y = add_bf(dequant_bf(acc, sw, sx), bias);
+    Yb[(int64_t)m * a.ldy + n] = f2bf(gelu_tanh(y));
+  } else if (EPI == EPI_QKV) {
+    const uint16_t v = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bias));
+    if (qseg == 0)
+      Yb[(int64_t)m * a.ldy + qcol] = v;
+    else
+      (qseg == 1 ? a.Kc : a.Vc)[kv + qcol] = v;
+  } else {  // EPI_F32_BF16
+    Yb[(int64_t)m * a.ldy + n] = f2bf(__int_as_float(acc));
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ int64_t qkv_row_offset(const GemmArgs &a, int m) {
+  const int b = m / a.T, t = m - (m / a.T) * a.T;
+  const int p = (a.pos0 ? a.pos0[b] : 0) + t;
+  return (int64_t)b * a.seq_stride + (int64_t)p * a.dseg;
+}
+
 template <int EPI>
 __device__ __forceinline__ void finish_chunk_cm(const GemmArgs &a, int n, bool n_ok, float sw,
                                                 float bias, int qseg, int qcol, int mbase,
-                                                const uint32_t (&r)[32], int lane) {
-  const int m_lane = mbase + lane;
+                                                const uint32_t (&r)[16], int lane) {
+  // per-token values fetched lane-parallel (lanes 0..15) and broadcast
+  const int m_lane = mbase + (lane & 15);
   const bool m_lane_ok = m_lane < a.M;
   float sx_lane = 0.f;
   if (EPI != EPI_S32 && EPI != EPI_F32_BF16 && m_lane_ok) sx_lane = a.sX[m_lane];
-  int64_t kv_lane = 0;  // QKV: element offset of token m_lane's cache row
-  if (EPI == EPI_QKV && m_lane_ok) {
-    const int b = m_lane / a.T, t = m_lane - (m_lane / a.T) * a.T;
-    const int p = (a.pos0 ? a.pos0[b] : 0) + t;
-    kv_lane = (int64_t)b * a.seq_stride + (int64_t)p * a.dseg;
-  }
-  uint16_t rv[32];
+  int64_t kv_lane = 0;
+  if (EPI == EPI_QKV && m_lane_ok) kv_lane = qkv_row_offset<EPI>(a, m_lane);
+  uint16_t rv[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) rv[i] = 0;
   if (EPI == EPI_RESID) {
     // every residual value of the chunk in flight before the first store
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      rv[i] = (n_ok && mbase + i < a.M) ? a.R[(int64_t)(mbase + i) * a.ldr + n] : (uint16_t)0;
+    for (int i = 0; i < 16; ++i)
+      if (n_ok && mbase + i < a.M) rv[i] = a.R[(int64_t)(mbase + i) * a.ldr + n];
   }
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
+  for (int i = 0; i < 16; ++i) {
     const float sx = __shfl_sync(0xffffffffu, sx_lane, i);
     const int64_t kv = EPI == EPI_QKV ? __shfl_sync(0xffffffffu, kv_lane, i) : 0;
     const int m = mbase + i;
-    if (!n_ok || m >= a.M) continue;
-    const int32_t acc = (int32_t)r[i];
-    uint16_t *Yb = reinterpret_cast<uint16_t *>(a.Y);
-    if (EPI == EPI_S32) {
-      reinterpret_cast<int32_t *>(a.Y)[(int64_t)m * a.ldy + n] = acc;
-    } else if (EPI == EPI_DEQUANT) {
-      Yb[(int64_t)m * a.ldy + n] = f2bf(dequant_bf(acc, sw, sx));
-    } else if (EPI == EPI_BIAS) {
-      Yb[(int64_t)m * a.ldy + n] = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bias));
-    } else if (EPI == EPI_RESID) {
-      const float y = add_bf(dequant_bf(acc, sw, sx), bias);
-      Yb[(int64_t)m * a.ldy + n] = f2bf(__fadd_rn(bf2f(rv[i]), y));
-    } else if (EPI == EPI_GELU) {
-      const float y = add_bf(dequant_bf(acc, sw, sx), bias);
-      Yb[(int64_t)m * a.ldy + n] = f2bf(gelu_tanh(y));
-    } else if (EPI == EPI_QKV) {
-      const uint16_t v = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bias));
-      if (qseg == 0)
-        Yb[(int64_t)m * a.ldy + qcol] = v;
-      else
-        (qseg == 1 ? a.Kc : a.Vc)[kv + qcol] = v;
-    } else {  // EPI_F32_BF16
-      Yb[(int64_t)m * a.ldy + n] = f2bf(__int_as_float(acc));
+    if (n_ok && m < a.M)
+      store_one_cm<EPI>(a, m, n, (int32_t)r[i], sw, sx, bias, rv[i], qseg, qcol, kv);
+  }
+}
+
+// Split-K: the last unit of a tile reads the summed int32 tile back from the
+// workspace, re-zeroes it, and applies the epilogue. The tile is spread over
+// all epilogue threads (thread -> channel tid % 128, tokens (tid / 128) + 4j)
+// with every load of a batch in flight together.
+template <int EPI>
+__device__ __forceinline__ void final_from_ws(const GemmArgs &a, int n0, int m0, int etid) {
+  const int n = n0 + (etid & 127);
+  if (n >= a.N) return;
+  float sw = 0.f, bias = 0.f;
+  int qseg = 0, qcol = n;
+  if (EPI != EPI_S32 && EPI != EPI_F32_BF16) sw = a.sW[n];
+  if (EPI >= EPI_BIAS && EPI <= EPI_QKV) bias = bf2f(a.bias[n]);
+  if (EPI == EPI_QKV) {
+    qseg = n / a.dseg;
+    qcol = n - qseg * a.dseg;
+  }
+  const int mq = etid >> 7;  // 0..3
+  const int per = a.BN >> 2;
+  for (int j0 = 0; j0 < per; j0 += 16) {
+    int32_t v[16];
+    float sxv[16];
+    uint16_t rv[16];
+    int64_t kvv[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int m = m0 + mq + 4 * (j0 + j);
+      const bool ok = (j0 + j < per) && m < a.M;
+      v[j] = ok ? __ldcg(a.ws + (int64_t)m * a.N + n) : 0;
+      sxv[j] = (ok && EPI != EPI_S32 && EPI != EPI_F32_BF16) ? a.sX[m] : 0.f;
+      rv[j] = (ok && EPI == EPI_RESID) ? a.R[(int64_t)m * a.ldr + n] : (uint16_t)0;
+      kvv[j] = (ok && EPI == EPI_QKV) ? qkv_row_offset<EPI>(a, m) : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int m = m0 + mq + 4 * (j0 + j);
+      if ((j0 + j < per) && m < a.M) {
+        a.ws[(int64_t)m * a.N + n] = 0;
+        store_one_cm<EPI>(a, m, n, v[j], sw, sxv[j], bias, rv[j], qseg, qcol, kvv[j]);
+      }
     }
   }
 }
@@ -389,23 +445,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (a.ksplit == 1) {
-          for (int c = group; c < nchunks; c += 4) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * c), r);
+          for (int c = group; c < 2 * nchunks; c += 4) {  // 16-token chunks
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(t_row + (uint32_t)(16 * c), r);
             tmem_ld_wait();
-            finish_chunk_cm<EPI>(a, n, n_ok, sw, bias, qseg, qcol, b0 + 32 * c, r, lane);
+            finish_chunk_cm<EPI>(a, n, n_ok, sw, bias, qseg, qcol, b0 + 16 * c, r, lane);
           }
           tc_fence_before();
           mbar_arrive(&ctl->tmem_empty[acc]);
         } else {
           // add this split's partial sums into the workspace tile
-          for (int c = group; c < nchunks; c += 4) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * c), r);
+          for (int c = group; c < 2 * nchunks; c += 4) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(t_row + (uint32_t)(16 * c), r);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int m = b0 + 32 * c + i;
+            for (int i = 0; i < 16; ++i) {
+              const int m = b0 + 16 * c + i;
               if (n_ok && m < a.M) atomicAdd(a.ws + (int64_t)m * a.N + n, (int)r[i]);
             }
           }
@@ -420,21 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           named_barrier_sync(kEpiBarrier, kEpiThreads);
           if (ctl->last_flag) {
             __threadfence();
-            for (int c = group; c < nchunks; c += 4) {
-              // all partial sums of the chunk in flight at once, then re-zero
-              uint32_t r[32];
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int m = b0 + 32 * c + i;
-                r[i] = (n_ok && m < a.M) ? (uint32_t)__ldcg(a.ws + (int64_t)m * a.N + n) : 0u;
-              }
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const int m = b0 + 32 * c + i;
-                if (n_ok && m < a.M) a.ws[(int64_t)m * a.N + n] = 0;
-              }
-              finish_chunk_cm<EPI>(a, n, n_ok, sw, bias, qseg, qcol, b0 + 32 * c, r, lane);
-            }
+            final_from_ws<EPI>(a, a0, b0, e * 32 + lane);
             if (e == 0 && lane == 0) a.tickets[t] = 0;
           }
           named_barrier_sync(kEpiBarrier, kEpiThreads);  // last_flag is reused by the next unit
