@@ -127,6 +127,8 @@ struct PrefillArgs {
 
 __global__ void __launch_bounds__(128)
     attention_prefill_kernel(PrefillArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) uint16_t sm[];
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int q0 = qt * kQT;
@@ -299,7 +301,7 @@ int launch_attention_prefill(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
     attr[dev & 63] = true;
   }
   dim3 grid((T + kQT - 1) / kQT, n_head, n_seq);
-  attention_prefill_kernel<<<grid, 128, smem, s>>>(a);
+  launch_pdl(attention_prefill_kernel, dim3(grid), dim3(128), smem, s, a);
   return check_launch("attention_prefill");
 }
 
@@ -448,6 +450,8 @@ __device__ __forceinline__ float pv_range(const DecodeArgs &a, int b, int h, int
 
 // Split path, kernel 1: this split's scores into the workspace row.
 __global__ void __launch_bounds__(256) attention_decode_scores_kernel(DecodeArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
   const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
@@ -463,6 +467,8 @@ __global__ void __launch_bounds__(256) attention_decode_scores_kernel(DecodeArgs
 // split recomputes them), P for this split's keys, its share of P.V; the
 // last split of (b, h) to finish adds the partials in split order.
 __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ float s_red[8];
   __shared__ float s_tree[256];
   __shared__ float s_part[8][kHD];
@@ -509,6 +515,8 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
 // keeps the scores in shared memory, so K and V are each read once and the
 // call is one launch.
 __global__ void __launch_bounds__(256) attention_decode_fused_kernel(DecodeArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ float s_red[8];
   __shared__ float s_tree[256];
   __shared__ float s_part[8][kHD];
@@ -572,17 +580,17 @@ int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
   a.partials = (float *)(w + scores);
   a.tickets = (int *)(w + scores + (size_t)n_seq * n_head * a.splits * kHD * 4);
   if (a.splits == 1) {
-    attention_decode_fused_kernel<<<n_seq * n_head, 256, 0, s>>>(a);
+    launch_pdl(attention_decode_fused_kernel, dim3(n_seq * n_head), dim3(256), 0, s, a);
     return check_launch("attention_decode_fused");
   }
   dim3 grid(n_seq * n_head, a.splits);
   if (a.splits > 1 &&
       cudaMemsetAsync(a.tickets, 0, (size_t)n_seq * n_head * sizeof(int), s) != cudaSuccess)
     return W8A8_ERR_CUDA;
-  attention_decode_scores_kernel<<<grid, 256, 0, s>>>(a);
+  launch_pdl(attention_decode_scores_kernel, dim3(grid), dim3(256), 0, s, a);
   int st = check_launch("attention_decode_scores");
   if (st) return st;
-  attention_decode_pv_kernel<<<grid, 256, 0, s>>>(a);
+  launch_pdl(attention_decode_pv_kernel, dim3(grid), dim3(256), 0, s, a);
   return check_launch("attention_decode_pv");
 }
 

@@ -94,6 +94,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   }
 }
 
+// Programmatic dependent launch. Every kernel of this library is launched
+// with programmatic stream serialization, so it may start while the previous
+// kernel in the stream is still running: pdl_wait() blocks until that kernel
+// has completed and its writes are visible, and must precede any read of
+// data it produced; pdl_launch_dependents() lets the next kernel start
+// launching (it still waits in its own pdl_wait()). Without the launch
+// attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Barrier among `n` threads (a multiple of 32) of the block, id 1..15.
 __device__ __forceinline__ void named_barrier_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");

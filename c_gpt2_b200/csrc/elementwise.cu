@@ -23,6 +23,8 @@ static int grid_for(int64_t total) {
 // embeddings.cu:18-23: emb[row][col] = bf16(wte[tok[row]][col] + wpe[row][col])
 __global__ void ref_embeddings_kernel(const uint16_t *wte, const uint16_t *wpe, const int *tok,
                                       uint16_t *emb, int d, int start_row, int n_rows) {
+  pdl_wait();
+  pdl_launch_dependents();
   W8A8_GRID_LOOP(i, (int64_t)n_rows * d) {
     int row = start_row + (int)(i / d), col = (int)(i % d);
     emb[(int64_t)row * d + col] =
@@ -32,6 +34,8 @@ __global__ void ref_embeddings_kernel(const uint16_t *wte, const uint16_t *wpe, 
 
 // add_bias.cu:14 (in place)
 __global__ void ref_add_bias_kernel(uint16_t *a, const uint16_t *b, int rows, int cols) {
+  pdl_wait();
+  pdl_launch_dependents();
   W8A8_GRID_LOOP(i, (int64_t)rows * cols) {
     a[i] = f2bf(__fadd_rn(bf2f(a[i]), bf2f(b[i % cols])));
   }
@@ -40,17 +44,23 @@ __global__ void ref_add_bias_kernel(uint16_t *a, const uint16_t *b, int rows, in
 // add_2d.cu:14
 __global__ void ref_add_2d_kernel(const uint16_t *a, const uint16_t *b, uint16_t *out, int rows,
                                   int cols) {
+  pdl_wait();
+  pdl_launch_dependents();
   W8A8_GRID_LOOP(i, (int64_t)rows * cols) { out[i] = f2bf(__fadd_rn(bf2f(a[i]), bf2f(b[i]))); }
 }
 
 // gelu.cu:12-16 (in place)
 __global__ void ref_gelu_kernel(uint16_t *x, int rows, int cols) {
+  pdl_wait();
+  pdl_launch_dependents();
   W8A8_GRID_LOOP(i, (int64_t)rows * cols) { x[i] = f2bf(gelu_tanh(bf2f(x[i]))); }
 }
 
 // activation_quant.cu:124-130
 __global__ void ref_dequant_kernel(const int32_t *Y, const float *sW, const float *sX,
                                    uint16_t *out, int M, int N) {
+  pdl_wait();
+  pdl_launch_dependents();
   W8A8_GRID_LOOP(i, (int64_t)M * N) {
     int row = (int)(i / N), col = (int)(i % N);
     out[i] = f2bf(dequant_bf(Y[i], sW[col], sX[row]));
@@ -59,6 +69,8 @@ __global__ void ref_dequant_kernel(const int32_t *Y, const float *sW, const floa
 
 // casual_masking.cu:7-14: for rows i < tokens, columns i < j < tokens := -inf
 __global__ void ref_causal_mask_kernel(uint16_t *x, int stride, int tokens) {
+  pdl_wait();
+  pdl_launch_dependents();
   W8A8_GRID_LOOP(k, (int64_t)tokens * tokens) {
     int i = (int)(k / tokens), j = (int)(k % tokens);
     if (j > i) x[(int64_t)i * stride + j] = 0xFF80u;  // bf16 -inf
@@ -68,6 +80,8 @@ __global__ void ref_causal_mask_kernel(uint16_t *x, int stride, int tokens) {
 // concat_heads.cu:14-23: dest[tok][h*hd + c] = src[h][tok][c]
 __global__ void ref_concat_heads_kernel(const uint16_t *src, uint16_t *dest, int token_index,
                                         int H, int hd, int ctx) {
+  pdl_wait();
+  pdl_launch_dependents();
   W8A8_GRID_LOOP(i, (int64_t)H * hd) {
     int h = (int)(i / hd), c = (int)(i % hd);
     dest[(int64_t)token_index * (H * hd) + h * hd + c] =
@@ -81,6 +95,8 @@ __global__ void ref_concat_heads_kernel(const uint16_t *src, uint16_t *dest, int
 __global__ void __launch_bounds__(256)
     ref_softmax_kernel(const uint16_t *in, uint16_t *out, int rows, int cols, int stride,
                        float temperature, int causal_mask) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ float s_data[256];
   const int tid = threadIdx.x, row_idx = blockIdx.x;
   if (row_idx >= rows) return;
@@ -141,7 +157,7 @@ extern "C" int w8a8_ref_embeddings(const gpt2_bf16_t *wte, const gpt2_bf16_t *wp
   W8A8_CHECK_PTR(tokens);
   W8A8_CHECK_PTR(emb);
   if (d <= 0 || start_row < 0) return W8A8_ERR_INVALID;
-  ref_embeddings_kernel<<<grid_for((int64_t)n_rows * d), 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ref_embeddings_kernel, dim3(grid_for((int64_t)n_rows * d)), dim3(256), 0, (cudaStream_t)stream, 
       wte, wpe, tokens, emb, d, start_row, n_rows);
   return check_launch("ref_embeddings");
 }
@@ -151,7 +167,7 @@ extern "C" int w8a8_ref_add_bias(gpt2_bf16_t *a, int rows, int cols, const gpt2_
   if (rows <= 0 || cols <= 0) return W8A8_OK;
   W8A8_CHECK_PTR(a);
   W8A8_CHECK_PTR(b);
-  ref_add_bias_kernel<<<grid_for((int64_t)rows * cols), 256, 0, (cudaStream_t)stream>>>(a, b, rows,
+  launch_pdl(ref_add_bias_kernel, dim3(grid_for((int64_t)rows * cols)), dim3(256), 0, (cudaStream_t)stream, a, b, rows,
                                                                                        cols);
   return check_launch("ref_add_bias");
 }
@@ -162,7 +178,7 @@ extern "C" int w8a8_ref_add_2d(const gpt2_bf16_t *a, int rows, int cols, const g
   W8A8_CHECK_PTR(a);
   W8A8_CHECK_PTR(b);
   W8A8_CHECK_PTR(out);
-  ref_add_2d_kernel<<<grid_for((int64_t)rows * cols), 256, 0, (cudaStream_t)stream>>>(a, b, out,
+  launch_pdl(ref_add_2d_kernel, dim3(grid_for((int64_t)rows * cols)), dim3(256), 0, (cudaStream_t)stream, a, b, out,
                                                                                      rows, cols);
   return check_launch("ref_add_2d");
 }
@@ -170,7 +186,7 @@ extern "C" int w8a8_ref_add_2d(const gpt2_bf16_t *a, int rows, int cols, const g
 extern "C" int w8a8_ref_gelu(gpt2_bf16_t *x, int cols, int rows, void *stream) {
   if (rows <= 0 || cols <= 0) return W8A8_OK;
   W8A8_CHECK_PTR(x);
-  ref_gelu_kernel<<<grid_for((int64_t)rows * cols), 256, 0, (cudaStream_t)stream>>>(x, rows, cols);
+  launch_pdl(ref_gelu_kernel, dim3(grid_for((int64_t)rows * cols)), dim3(256), 0, (cudaStream_t)stream, x, rows, cols);
   return check_launch("ref_gelu");
 }
 
@@ -181,7 +197,7 @@ extern "C" int w8a8_ref_dequant(const int32_t *Y, const float *sW, const float *
   W8A8_CHECK_PTR(sW);
   W8A8_CHECK_PTR(sX);
   W8A8_CHECK_PTR(out);
-  ref_dequant_kernel<<<grid_for((int64_t)M * N), 256, 0, (cudaStream_t)stream>>>(Y, sW, sX, out, M,
+  launch_pdl(ref_dequant_kernel, dim3(grid_for((int64_t)M * N)), dim3(256), 0, (cudaStream_t)stream, Y, sW, sX, out, M,
                                                                                 N);
   return check_launch("ref_dequant");
 }
@@ -190,7 +206,7 @@ extern "C" int w8a8_ref_causal_mask(gpt2_bf16_t *x, int stride, int tokens, void
   if (tokens <= 0) return W8A8_OK;
   W8A8_CHECK_PTR(x);
   if (stride < tokens) return W8A8_ERR_INVALID;
-  ref_causal_mask_kernel<<<grid_for((int64_t)tokens * tokens), 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ref_causal_mask_kernel, dim3(grid_for((int64_t)tokens * tokens)), dim3(256), 0, (cudaStream_t)stream, 
       x, stride, tokens);
   return check_launch("ref_causal_mask");
 }
@@ -201,7 +217,7 @@ extern "C" int w8a8_ref_concat_heads(const gpt2_bf16_t *src, gpt2_bf16_t *dest, 
   W8A8_CHECK_PTR(dest);
   if (n_head <= 0 || head_dim <= 0 || token_index < 0 || token_index >= ctx)
     return W8A8_ERR_INVALID;
-  ref_concat_heads_kernel<<<grid_for((int64_t)n_head * head_dim), 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ref_concat_heads_kernel, dim3(grid_for((int64_t)n_head * head_dim)), dim3(256), 0, (cudaStream_t)stream, 
       src, dest, token_index, n_head, head_dim, ctx);
   return check_launch("ref_concat_heads");
 }
@@ -213,7 +229,7 @@ extern "C" int w8a8_ref_softmax(const gpt2_bf16_t *a, int rows, int cols, int st
   W8A8_CHECK_PTR(a);
   W8A8_CHECK_PTR(out);
   if (stride < cols) return W8A8_ERR_INVALID;
-  ref_softmax_kernel<<<rows, 256, 0, (cudaStream_t)stream>>>(a, out, rows, cols, stride,
+  launch_pdl(ref_softmax_kernel, dim3(rows), dim3(256), 0, (cudaStream_t)stream, a, out, rows, cols, stride,
                                                              temperature, causal_mask);
   return check_launch("ref_softmax");
 }

@@ -296,13 +296,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int *abort_flag = &ctl->abort_flag;
-  int issued = 0;
 
+  pdl_launch_dependents();
+  int issued = 0;
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
+    // The weight operand does not depend on the previous kernel: the boxes of
+    // the first unit's first stages are issued before waiting for it
+    // (programmatic dependent launch), so they stream while it finishes.
     const int kbox = kBoxBytes / (KIND == 0 ? 1 : 2);
+    const CUtensorMap *tmW = CM ? &tmA : &tmB;
+    const CUtensorMap *tmX = CM ? &tmB : &tmA;
+    const uint32_t w_off = CM ? 0u : a_bytes, x_off = CM ? a_bytes : 0u;
+    int pre = 0, pre_kb0 = 0, pre_x = 0, pre_w = 0;
+    if ((int)blockIdx.x < total_units) {
+      const int u = blockIdx.x;
+      const int t = u / a.ksplit, ks = u - (u / a.ksplit) * a.ksplit;
+      const int a0 = (t / a.b_tiles) * kBM, b0 = (t % a.b_tiles) * BN;
+      pre_kb0 = ks * a.kb_per;
+      const int kb1 = min(a.kblocks, pre_kb0 + a.kb_per);
+      pre_w = CM ? a0 : b0;
+      pre_x = CM ? b0 : a0;
+      for (int kb = pre_kb0; kb < kb1 && pre < stages; ++kb, ++pre) {
+        uint8_t *sa = smem + (size_t)pre * stage_bytes;
+        mbar_arrive_expect_tx(&ctl->full[pre], stage_bytes);
+        tma_load_2d(sa + w_off, tmW, &ctl->full[pre], kb * kbox, pre_w);
+      }
+    }
+    pdl_wait();
     int stage = 0;
     uint32_t phase = 0;
+    int it = 0;
     for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x) {
       const int t = u / a.ksplit, ks = u - (u / a.ksplit) * a.ksplit;
       const int a0 = (t / a.b_tiles) * kBM;
@@ -311,9 +335,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort_flag, a.err, 0x1101)) break;
         uint8_t *sa = smem + (size_t)stage * stage_bytes;
-        mbar_arrive_expect_tx(&ctl->full[stage], stage_bytes);
-        tma_load_2d(sa, &tmA, &ctl->full[stage], kb * kbox, a0);
-        tma_load_2d(sa + a_bytes, &tmB, &ctl->full[stage], kb * kbox, b0);
+        if (it >= pre) {
+          mbar_arrive_expect_tx(&ctl->full[stage], stage_bytes);
+          tma_load_2d(sa + w_off, tmW, &ctl->full[stage], kb * kbox, CM ? a0 : b0);
+        }
+        tma_load_2d(sa + x_off, tmX, &ctl->full[stage], kb * kbox, CM ? b0 : a0);
+        ++it;
         ++issued;
         if (++stage == stages) {
           stage = 0;
@@ -321,8 +348,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // On abort, complete any prefetched stage whose activation box was never
+    // issued, so every issued copy has a barrier to drain on below.
+    for (; it < pre; ++it, ++issued)
+      tma_load_2d(smem + (size_t)it * stage_bytes + x_off, tmX, &ctl->full[it],
+                  (pre_kb0 + it) * kbox, pre_x);
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer ----------------
+    pdl_wait();
     const uint32_t idesc = KIND == 0 ? make_idesc(2, 1, kBM, BN) : make_idesc(1, 1, kBM, BN);
     int stage = 0;
     uint32_t phase = 0;
@@ -379,6 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kEpiWarp0) {
     // ---------------- epilogue ----------------
+    pdl_wait();
     const int e = warp - kEpiWarp0;     // 0..15
     const int quarter = warp & 3;       // TMEM lanes [32*quarter, 32*quarter+32)
     const int group = e >> 2;           // chunks c == group (mod 4)
@@ -590,7 +624,7 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   }
   const int units = tiles0 * a.ksplit;
   const int grid = units < ctx->sm_count ? units : ctx->sm_count;
-  gemm_tc_kernel<KIND, EPI, CM><<<grid, kThreads, smem, stream>>>(tmA, tmB, a);
+  launch_pdl(gemm_tc_kernel<KIND, EPI, CM>, dim3(grid), dim3(kThreads), smem, stream, tmA, tmB, a);
   return check_launch("gemm_tc");
 }
 

@@ -65,6 +65,8 @@ template <int MT>
 __global__ void __launch_bounds__(kGemvWarps * 32)
     gemv_i8_vec_kernel(const int8_t *__restrict__ X, int64_t ldx, const int8_t *__restrict__ W,
                        GemvArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ int4 xs4[];  // [MT][K] int8
   int8_t *xs = reinterpret_cast<int8_t *>(xs4);
   const int K = a.K;
@@ -126,6 +128,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
 // Scalar fallback for any K / alignment (correctness path, not a hot path).
 __global__ void gemv_i8_scalar_kernel(const int8_t *__restrict__ X, int64_t ldx,
                                       const int8_t *__restrict__ W, GemvArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x * kGemvWarps + warp;
   const int m = blockIdx.y;
@@ -152,7 +156,7 @@ static int launch_vec(const int8_t *X, int64_t ldx, const int8_t *W, const GemvA
     attr[dev & 63] = true;
   }
   dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps);
-  gemv_i8_vec_kernel<MT><<<grid, kGemvWarps * 32, smem, s>>>(X, ldx, W, a);
+  launch_pdl(gemv_i8_vec_kernel<MT>, dim3(grid), dim3(kGemvWarps * 32), smem, s, X, ldx, W, a);
   return check_launch("gemv_i8_vec");
 }
 
@@ -168,7 +172,7 @@ int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs
   }
   if (a.M > 65535) return W8A8_ERR_UNSUPPORTED;
   dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps, a.M);
-  gemv_i8_scalar_kernel<<<grid, kGemvWarps * 32, 0, s>>>(X, ldx, W, a);
+  launch_pdl(gemv_i8_scalar_kernel, dim3(grid), dim3(kGemvWarps * 32), 0, s, X, ldx, W, a);
   return check_launch("gemv_i8_scalar");
 }
 

@@ -74,6 +74,8 @@ __device__ __forceinline__ void load_row(uint16_t *dst, const uint16_t *src, int
 __global__ void __launch_bounds__(kRowWarps * 32)
     quant_rows_kernel(const uint16_t *__restrict__ X, int64_t ldx, int M, int K,
                       int8_t *__restrict__ Xq, float *__restrict__ sX) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ uint16_t srow_all[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kRowWarps + warp;
@@ -185,6 +187,8 @@ __global__ void __launch_bounds__(kRowWarps * 32)
                            const uint16_t *__restrict__ gamma, const uint16_t *__restrict__ beta,
                            float eps, uint16_t *__restrict__ Y, int64_t ldy,
                            int8_t *__restrict__ Xq, float *__restrict__ sX) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ uint16_t srow_all[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kRowWarps + warp;
@@ -207,6 +211,8 @@ __global__ void __launch_bounds__(kRowWarps * 32)
                                  const uint16_t *__restrict__ beta, float eps,
                                  uint16_t *__restrict__ Y, int8_t *__restrict__ Xq,
                                  float *__restrict__ sX) {
+  pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ uint16_t srow_all[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * kRowWarps + warp;
@@ -312,6 +318,8 @@ __device__ __forceinline__ void quant_store(RowShared &sh, const uint4 (&y)[kMax
 __global__ void __launch_bounds__(kRowThreads)
     quant_rows_block_kernel(const uint16_t *__restrict__ X, int64_t ldx, int K,
                             int8_t *__restrict__ Xq, float *__restrict__ sX) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ RowShared sh;
   const int row = blockIdx.x, t = threadIdx.x, nv = K >> 3;
   const uint4 *src = reinterpret_cast<const uint4 *>(X + (int64_t)row * ldx);
@@ -335,6 +343,8 @@ __global__ void __launch_bounds__(kRowThreads)
                            const uint16_t *__restrict__ gamma, const uint16_t *__restrict__ beta,
                            float eps, uint16_t *__restrict__ Y, int64_t ldy,
                            int8_t *__restrict__ Xq, float *__restrict__ sX) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ RowShared sh;
   const int row = blockIdx.x, t = threadIdx.x, nv = d >> 3;
   uint4 x[kMaxVec], g[kMaxVec], bt[kMaxVec];
@@ -449,7 +459,7 @@ static int row_grid(int M) { return (M + kRowWarps - 1) / kRowWarps; }
 int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, float *sX,
                       cudaStream_t s) {
   if (block_path_ok(K, X, ldx, Xq, K) && M <= 0x7fffffff) {
-    quant_rows_block_kernel<<<M, kRowThreads, 0, s>>>(X, ldx, K, Xq, sX);
+    launch_pdl(quant_rows_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, Xq, sX);
     return check_launch("quant_rows_block");
   }
   size_t smem = (size_t)kRowWarps * K * sizeof(uint16_t);
@@ -461,7 +471,7 @@ int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, 
     cudaFuncSetAttribute(quant_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr[dev & 63] = true;
   }
-  quant_rows_kernel<<<row_grid(M), kRowWarps * 32, smem, s>>>(X, ldx, M, K, Xq, sX);
+  launch_pdl(quant_rows_kernel, dim3(row_grid(M)), dim3(kRowWarps * 32), smem, s, X, ldx, M, K, Xq, sX);
   return check_launch("quant_rows");
 }
 
@@ -470,7 +480,7 @@ int launch_layernorm_quant(const uint16_t *X, int64_t ldx, int M, int d, const u
                            float *sX, cudaStream_t s) {
   if (block_path_ok(d, X, ldx, Y, Y ? ldy : 0) && aligned16(gamma) && aligned16(beta) &&
       (Xq == nullptr || aligned16(Xq))) {
-    layernorm_block_kernel<0><<<M, kRowThreads, 0, s>>>(X, ldx, nullptr, nullptr, nullptr, 1,
+    launch_pdl(layernorm_block_kernel<0>, dim3(M), dim3(kRowThreads), 0, s, X, ldx, nullptr, nullptr, nullptr, 1,
                                                         nullptr, nullptr, d, gamma, beta, eps, Y,
                                                         ldy, Xq, sX);
     return check_launch("layernorm_block");
@@ -485,7 +495,7 @@ int launch_layernorm_quant(const uint16_t *X, int64_t ldx, int M, int d, const u
                          200 * 1024);
     attr[dev & 63] = true;
   }
-  layernorm_quant_kernel<<<row_grid(M), kRowWarps * 32, smem, s>>>(X, ldx, M, d, gamma, beta,
+  launch_pdl(layernorm_quant_kernel, dim3(row_grid(M)), dim3(kRowWarps * 32), smem, s, X, ldx, M, d, gamma, beta,
                                                                      eps, Y, ldy, Xq, sX);
   return check_launch("layernorm_quant");
 }
@@ -497,7 +507,7 @@ int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const
   if (block_path_ok(d, wte, d, wpe, d) && aligned16(gamma) && aligned16(beta) &&
       (H == nullptr || aligned16(H)) && (Y == nullptr || aligned16(Y)) &&
       (Xq == nullptr || aligned16(Xq))) {
-    layernorm_block_kernel<1><<<M, kRowThreads, 0, s>>>(nullptr, 0, wte, wpe, tokens, T, pos0, H,
+    launch_pdl(layernorm_block_kernel<1>, dim3(M), dim3(kRowThreads), 0, s, nullptr, 0, wte, wpe, tokens, T, pos0, H,
                                                         d, gamma, beta, eps, Y, d, Xq, sX);
     return check_launch("embed_layernorm_block");
   }
@@ -511,7 +521,7 @@ int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const
                          200 * 1024);
     attr[dev & 63] = true;
   }
-  embed_layernorm_quant_kernel<<<row_grid(M), kRowWarps * 32, smem, s>>>(
+  launch_pdl(embed_layernorm_quant_kernel, dim3(row_grid(M)), dim3(kRowWarps * 32), smem, s, 
       wte, wpe, tokens, M, T, pos0, d, H, gamma, beta, eps, Y, Xq, sX);
   return check_launch("embed_layernorm_quant");
 }

@@ -1,5 +1,6 @@
 // Per-device state, status strings and the device error word.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "runtime.cuh"
@@ -11,6 +12,15 @@ namespace w8a8 {
 __device__ int g_device_error;
 
 static DeviceCtx g_ctx[64];
+
+bool pdl_enabled() {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char *v = getenv("W8A8_PDL");
+    enabled = (v && v[0] == '0') ? 0 : 1;
+  }
+  return enabled == 1;
+}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,

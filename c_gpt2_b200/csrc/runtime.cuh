@@ -26,6 +26,28 @@ DeviceCtx *device_ctx(int *status);
 int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, uint64_t rows,
                  uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows);
 
+// Whether kernels are launched with programmatic stream serialization
+// (W8A8_PDL=0 in the environment turns it off).
+bool pdl_enabled();
+
+// Launch `kernel` with programmatic dependent launch allowed: it may begin
+// while the preceding kernel of the stream finishes (see pdl_wait()).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 inline int check_launch(const char *what) {
   cudaError_t e = cudaGetLastError();
   (void)what;

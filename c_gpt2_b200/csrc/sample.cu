@@ -15,6 +15,8 @@ __global__ void __launch_bounds__(256)
     greedy_sample_kernel(const uint16_t *__restrict__ logits, int64_t ldl, int V,
                          int32_t *__restrict__ out, int32_t *__restrict__ append_to,
                          int64_t append_stride, int32_t *__restrict__ append_pos) {
+  pdl_wait();
+  pdl_launch_dependents();
   __shared__ float s_red[256];
   __shared__ int s_idx[256];
   const int row = blockIdx.x, tid = threadIdx.x;
@@ -77,6 +79,8 @@ __global__ void __launch_bounds__(256)
 }
 
 __global__ void advance_kernel(int32_t *dst, const int32_t *src, int n, int delta) {
+  pdl_wait();
+  pdl_launch_dependents();
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) dst[i] = src[i] + delta;
 }
@@ -84,13 +88,13 @@ __global__ void advance_kernel(int32_t *dst, const int32_t *src, int n, int delt
 int launch_greedy_sample(const uint16_t *logits, int64_t ldl, int M, int V, int32_t *out,
                          int32_t *append_to, int64_t append_stride, int32_t *append_pos,
                          cudaStream_t s) {
-  greedy_sample_kernel<<<M, 256, 0, s>>>(logits, ldl, V, out, append_to, append_stride,
+  launch_pdl(greedy_sample_kernel, dim3(M), dim3(256), 0, s, logits, ldl, V, out, append_to, append_stride,
                                          append_pos);
   return check_launch("greedy_sample");
 }
 
 int launch_advance(int32_t *dst, const int32_t *src, int n, int delta, cudaStream_t s) {
-  advance_kernel<<<(n + 255) / 256, 256, 0, s>>>(dst, src, n, delta);
+  launch_pdl(advance_kernel, dim3((n + 255) / 256), dim3(256), 0, s, dst, src, n, delta);
   return check_launch("advance");
 }
 
