@@ -95,6 +95,24 @@ int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W
                 const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy,
                 void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- w8a8_linear without a caller-provided workspace ----
+ * No counterpart in the reference. For callers that cannot allocate device
+ * memory (a host that sizes all device memory once at start-up, a plugin whose
+ * host owns the allocator, a path that must not pay cudaMalloc's implicit
+ * synchronisation): the split-K scratch comes from a fixed array compiled into
+ * this library (W8A8_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the
+ * library until exit). Shapes whose scratch would exceed it, i.e.
+ * M*N*4 bytes plus one 4-byte counter per 128 x 32 output tile, return
+ * W8A8_ERR_UNSUPPORTED. Nothing is allocated. The first call on a device
+ * looks up the array's device address and must come before any stream capture.
+ * All calls share the array: calls whose GPU work overlaps race and must be
+ * serialised by the caller. Same arguments and results as w8a8_linear. */
+#define W8A8_NOALLOC_SCRATCH_BYTES (4u << 20)
+int w8a8_linear_noalloc(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W,
+                        const float *sW, const gpt2_bf16_t *bias, int N, int epilogue,
+                        const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy,
+                        void *stream);
+
 /* Workspace that lets w8a8_linear / w8a8_linear_qkv split the reduction over
  * K when M is small (decode) and the output tiles alone cannot occupy every
  * SM. Optional (NULL disables splitting). It must be zero-filled once before
