@@ -1,0 +1,161 @@
+"""Single-kernel cases for profiling: one kernel of the decode/prefill path on
+seeded synthetic inputs, launched a few times and nothing else, so that a
+profiler capture (`ncu -k <kernel> -c 1..3`) sees exactly that kernel at the
+size of the large model (d_model 1280, 20 heads, context 1024).
+
+    python -m c_gpt2_b200.profcase attention-decode [--batch 64] [--n-ctx 768]
+    python -m c_gpt2_b200.profcase attention-prefill [--seqs 64] [--tokens 512]
+    python -m c_gpt2_b200.profcase linear --m 32768 --n 5120 --k 1280 --epi gelu
+    python -m c_gpt2_b200.profcase linear --m 64 --n 5120 --k 1280 --epi gelu
+
+Every case holds well under 1 GB on the device and exceeds the 126 MB L2 only
+where the workload itself does (the attention KV cache, the prefill
+activations). Prints one line with the CUDA-event time per launch, measured
+after the profiled launches.
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import _lib, ops
+
+EPI = {"dequant": _lib.EPI_DEQUANT, "bias": _lib.EPI_BIAS, "resid": _lib.EPI_BIAS_RESID,
+       "gelu": _lib.EPI_BIAS_GELU}
+
+
+_FLUSH = None
+
+
+def _time(fn, reps: int) -> float:
+    """Mean microseconds per launch. With --flush every launch is timed alone
+    after a 256 MB write that evicts the 126 MB L2, so weights are read from
+    HBM as in a full model step; otherwise launches run back to back."""
+    if _FLUSH is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return 1000.0 * e0.elapsed_time(e1) / reps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(reps)]
+    for e0, e1 in ev:
+        _FLUSH.fill_(1)
+        e0.record()
+        fn()
+        e1.record()
+    torch.cuda.synchronize()
+    return 1000.0 * sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps
+
+
+def attention_decode(a) -> None:
+    B, H, C, n = a.batch, a.heads, a.ctx, a.n_ctx
+    d = 64 * H
+    g = torch.Generator(device="cuda").manual_seed(0)
+    K = torch.randn((B, C, d), device="cuda", generator=g).to(torch.bfloat16)
+    V = torch.randn((B, C, d), device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn((B, d), device="cuda", generator=g).to(torch.bfloat16)
+    o = torch.empty((B, d), dtype=torch.bfloat16, device="cuda")
+    nctx = torch.full((B,), n, dtype=torch.int32, device="cuda")
+    ws = torch.empty((_lib.core().w8a8_attention_decode_workspace_size(B, H, C),),
+                     dtype=torch.uint8, device="cuda")
+
+    def run():
+        ops.attention_decode(q, K, V, C * d, nctx, C, H, out=o, workspace=ws)
+
+    for _ in range(a.launches):
+        run()
+    torch.cuda.synchronize()
+    us = _time(run, a.timed)
+    kv = 2 * B * n * d * 2
+    print(f"attention_decode B={B} H={H} n_ctx={n}: {us:.2f} us/launch, "
+          f"KV {kv / 1e6:.1f} MB, {kv / us / 1e3:.0f} GB/s")
+
+
+def attention_prefill(a) -> None:
+    B, H, T = a.seqs, a.heads, a.tokens
+    d = 64 * H
+    g = torch.Generator(device="cuda").manual_seed(0)
+    K = torch.randn((B, T, d), device="cuda", generator=g).to(torch.bfloat16)
+    V = torch.randn((B, T, d), device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn((B * T, d), device="cuda", generator=g).to(torch.bfloat16)
+    o = torch.empty((B * T, d), dtype=torch.bfloat16, device="cuda")
+
+    def run():
+        ops.attention_prefill(q, K, V, T * d, B, T, H, out=o)
+
+    for _ in range(a.launches):
+        run()
+    torch.cuda.synchronize()
+    us = _time(run, a.timed)
+    flops = B * H * 2.0 * 2 * 64 * T * (T + 1) / 2  # causal QK^T and PV
+    print(f"attention_prefill seqs={B} T={T} H={H}: {us:.2f} us/launch, "
+          f"{flops / us / 1e6:.1f} TFLOP/s (causal)")
+
+
+def linear(a) -> None:
+    M, N, K = a.m, a.n, a.k
+    g = torch.Generator(device="cuda").manual_seed(0)
+    xq = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+    W = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g)
+    sx = torch.rand((M,), device="cuda", generator=g) * 0.01 + 1e-3
+    sw = torch.rand((N,), device="cuda", generator=g) * 0.01 + 1e-3
+    b = (torch.randn((N,), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    R = torch.randn((M, N), device="cuda", generator=g).to(torch.bfloat16) \
+        if a.epi == "resid" else None
+    y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    # Only decode-sized GEMMs (M <= 128) split K and use the workspace.
+    ws = ops.linear_workspace(M, N, "cuda") if M <= 128 else None
+    epi = EPI[a.epi]
+
+    def run():
+        ops.linear(xq, sx, W, sw, b, epi, R=R, out=y, workspace=ws)
+
+    for _ in range(a.launches):
+        run()
+    torch.cuda.synchronize()
+    us = _time(run, a.timed)
+    ops_ = 2.0 * M * N * K
+    byts = M * K + N * K + 2 * M * N + (2 * M * N if R is not None else 0)
+    print(f"linear M={M} N={N} K={K} epi={a.epi}: {us:.2f} us/launch, "
+          f"{ops_ / us / 1e6:.0f} TOP/s, {byts / us / 1e3:.0f} GB/s algorithmic")
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    sub = ap.add_subparsers(dest="case", required=True)
+    p = sub.add_parser("attention-decode")
+    p.add_argument("--batch", type=int, default=64)
+    p.add_argument("--heads", type=int, default=20)
+    p.add_argument("--ctx", type=int, default=1024)
+    p.add_argument("--n-ctx", type=int, default=768)
+    p = sub.add_parser("attention-prefill")
+    p.add_argument("--seqs", type=int, default=64)
+    p.add_argument("--tokens", type=int, default=512)
+    p.add_argument("--heads", type=int, default=20)
+    p = sub.add_parser("linear")
+    p.add_argument("--m", type=int, required=True)
+    p.add_argument("--n", type=int, required=True)
+    p.add_argument("--k", type=int, required=True)
+    p.add_argument("--epi", choices=sorted(EPI), default="bias")
+    for p in sub.choices.values():
+        p.add_argument("--launches", type=int, default=3, help="launches before timing")
+        p.add_argument("--timed", type=int, default=20, help="launches timed after them")
+        p.add_argument("--flush", action="store_true", help="evict L2 before each timed launch")
+    a = ap.parse_args(argv)
+    ops.init(0)
+    if a.flush:
+        global _FLUSH
+        _FLUSH = torch.empty((256 << 20,), dtype=torch.uint8, device="cuda")
+    {"attention-decode": attention_decode, "attention-prefill": attention_prefill,
+     "linear": linear}[a.case](a)
+    st = ops.device_error()
+    if st:
+        raise SystemExit(f"device error word {st}")
+
+
+if __name__ == "__main__":
+    main()
