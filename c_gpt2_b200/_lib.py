@@ -41,6 +41,12 @@ SIGNATURES = {
     "w8a8_linear_noalloc": (_i, [_p, _p, _i, _i, _p, _p, _p, _i, _i, _p, _i64, _p, _i64, _p]),
     "w8a8_linear_qkv": (_i, [_p, _p, _i, _i, _p, _p, _p, _p, _i64, _p, _p, _i64, _i, _p, _p,
                              _sz, _p]),
+    "w8a8_linear_qkv_heads": (_i, [_p, _p, _i, _i, _i, _p, _p, _p, _p, _i64, _p, _p, _i64, _i,
+                                   _p, _p, _sz, _p]),
+    "w8a8_row_amax": (_i, [_p, _i64, _i, _i, _p, _p]),
+    "w8a8_quant_rows_amax": (_i, [_p, _i64, _i, _i, _p, _i, _i64, _p, _i64, _p, _p]),
+    "w8a8_reduce_residual_layernorm_quant": (_i, [_p, _i64, _i, _i64, _i, _i, _p, _p, _p, _p, _i64,
+                                                  _p, _i64, _p, _p, _f, _p, _i64, _p, _p]),
     "w8a8_attention_prefill": (_i, [_p, _i64, _p, _p, _i64, _i, _i, _i, _i, _p, _i64, _p]),
     "w8a8_attention_decode_workspace_size": (_sz, [_i, _i, _i]),
     "w8a8_attention_decode": (_i, [_p, _i64, _p, _p, _i64, _i, _p, _i, _i, _i, _p, _i64, _p, _sz, _p]),

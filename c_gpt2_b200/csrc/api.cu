@@ -131,27 +131,103 @@ extern "C" size_t w8a8_linear_workspace_size(int M, int N) {
   return linear_workspace_bytes(M, N);
 }
 
-extern "C" int w8a8_linear_qkv(const int8_t *Xq, const float *sX, int M, int d,
-                               const int8_t *Wqkv, const float *sWqkv, const gpt2_bf16_t *bqkv,
-                               gpt2_bf16_t *Q, int64_t ldq, gpt2_bf16_t *Kc, gpt2_bf16_t *Vc,
-                               int64_t seq_stride, int T, const int32_t *pos0,
-                               void *workspace, size_t workspace_bytes, void *stream) {
+static int linear_qkv_impl(const int8_t *Xq, const float *sX, int M, int K, int dq,
+                           const int8_t *Wqkv, const float *sWqkv, const gpt2_bf16_t *bqkv,
+                           gpt2_bf16_t *Q, int64_t ldq, gpt2_bf16_t *Kc, gpt2_bf16_t *Vc,
+                           int64_t seq_stride, int T, const int32_t *pos0, void *workspace,
+                           size_t workspace_bytes, void *stream) {
   if (M == 0) return W8A8_OK;
-  if (!Xq || !sX || !Wqkv || !sWqkv || !bqkv || !Q || !Kc || !Vc || M < 0 || d <= 0 || T <= 0 ||
-      M % T != 0 || ldq < d)
+  if (!Xq || !sX || !Wqkv || !sWqkv || !bqkv || !Q || !Kc || !Vc || M < 0 || K <= 0 ||
+      dq <= 0 || T <= 0 || M % T != 0 || ldq < dq)
     return W8A8_ERR_INVALID;
   int st = ready();
   if (st) return st;
-  LinearArgs a = make_args(EPI_QKV, M, 3 * d, d, sX, sWqkv, bqkv, nullptr, 0, Q, ldq);
+  LinearArgs a = make_args(EPI_QKV, M, 3 * dq, K, sX, sWqkv, bqkv, nullptr, 0, Q, ldq);
   a.Kc = Kc;
   a.Vc = Vc;
   a.seq_stride = seq_stride;
   a.T = T;
   a.pos0 = pos0;
-  a.dseg = d;
+  a.dseg = dq;
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
-  return dispatch_linear(Xq, d, Wqkv, a, (cudaStream_t)stream);
+  return dispatch_linear(Xq, K, Wqkv, a, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_linear_qkv(const int8_t *Xq, const float *sX, int M, int d,
+                               const int8_t *Wqkv, const float *sWqkv, const gpt2_bf16_t *bqkv,
+                               gpt2_bf16_t *Q, int64_t ldq, gpt2_bf16_t *Kc, gpt2_bf16_t *Vc,
+                               int64_t seq_stride, int T, const int32_t *pos0,
+                               void *workspace, size_t workspace_bytes, void *stream) {
+  return linear_qkv_impl(Xq, sX, M, d, d, Wqkv, sWqkv, bqkv, Q, ldq, Kc, Vc, seq_stride, T, pos0,
+                         workspace, workspace_bytes, stream);
+}
+
+extern "C" int w8a8_linear_qkv_heads(const int8_t *Xq, const float *sX, int M, int K,
+                                     int d_heads, const int8_t *Wqkv, const float *sWqkv,
+                                     const gpt2_bf16_t *bqkv, gpt2_bf16_t *Q, int64_t ldq,
+                                     gpt2_bf16_t *Kc, gpt2_bf16_t *Vc, int64_t seq_stride, int T,
+                                     const int32_t *pos0, void *workspace,
+                                     size_t workspace_bytes, void *stream) {
+  if (d_heads % 32) return W8A8_ERR_INVALID;
+  return linear_qkv_impl(Xq, sX, M, K, d_heads, Wqkv, sWqkv, bqkv, Q, ldq, Kc, Vc, seq_stride, T,
+                         pos0, workspace, workspace_bytes, stream);
+}
+
+extern "C" int w8a8_row_amax(const gpt2_bf16_t *X, int64_t ldx, int M, int K, float *amax,
+                             void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!X || !amax || M < 0 || K <= 0 || ldx < K) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  return launch_row_amax(X, ldx, M, K, amax, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_quant_rows_amax(const gpt2_bf16_t *X, int64_t ldx, int M, int K,
+                                    const float *amax, int n_amax, int64_t amax_stride,
+                                    int8_t *Xq, int64_t ldq, float *sX, void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!X || !amax || !Xq || !sX || M < 0 || K <= 0 || ldx < K || ldq < K || n_amax <= 0 ||
+      (n_amax > 1 && amax_stride < M))
+    return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  return launch_quant_rows_amax(X, ldx, M, K, amax, n_amax, amax_stride, Xq, ldq, sX,
+                                (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_reduce_residual_layernorm_quant(
+    const int32_t *acc, int64_t lda, int n_slots, int64_t slot_stride, int M, int d,
+    const float *sX, const float *sW, const gpt2_bf16_t *bias, const gpt2_bf16_t *R, int64_t ldr,
+    gpt2_bf16_t *H, int64_t ldh, const gpt2_bf16_t *gamma, const gpt2_bf16_t *beta, float eps,
+    int8_t *Xq, int64_t ldq, float *sXq, void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!acc || !sX || !sW || !bias || !R || !H || M < 0 || d <= 0 || lda < d || ldr < d ||
+      ldh < d || n_slots <= 0 || (n_slots > 1 && slot_stride < (int64_t)M * lda))
+    return W8A8_ERR_INVALID;
+  if (gamma && (!beta || !Xq || !sXq || ldq < d)) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  ReduceArgs a = {};
+  a.acc = acc;
+  a.lda = lda;
+  a.slot_stride = slot_stride;
+  a.n_slots = n_slots;
+  a.sX = sX;
+  a.sW = sW;
+  a.bias = bias;
+  a.R = R;
+  a.ldr = ldr;
+  a.H = H;
+  a.ldh = ldh;
+  a.gamma = gamma;
+  a.beta = beta;
+  a.eps = eps;
+  a.Xq = Xq;
+  a.ldq = ldq;
+  a.sXq = sXq;
+  a.d = d;
+  return launch_reduce_layernorm_quant(a, M, (cudaStream_t)stream);
 }
 
 extern "C" int w8a8_attention_prefill(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,

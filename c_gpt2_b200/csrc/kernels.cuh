@@ -45,6 +45,28 @@ struct LinearArgs {
 
 size_t linear_workspace_bytes(int M, int N);
 
+// Residual-stream epilogue of a GEMM whose reduction over K was split across
+// GPUs: H = R + (sum of n_slots int32 partials, dequantized, + bias), then
+// optionally (gamma != NULL) LayerNorm + per-token quantization into Xq/sXq.
+struct ReduceArgs {
+  const int32_t *acc;   // partial sums, slot j row m at acc + j*slot_stride + m*lda
+  int64_t lda, slot_stride;
+  int n_slots;
+  const float *sX;      // per-token scale of the GEMM input [M]
+  const float *sW;      // per-channel weight scale [d]
+  const uint16_t *bias; // [d]
+  const uint16_t *R;    // residual input, row stride ldr
+  int64_t ldr;
+  uint16_t *H;          // residual output, row stride ldh (may equal R)
+  int64_t ldh;
+  const uint16_t *gamma, *beta;
+  float eps;
+  int8_t *Xq;           // quantized LayerNorm output, row stride ldq
+  int64_t ldq;
+  float *sXq;
+  int d;
+};
+
 // gemm_tc.cu
 int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,
                cudaStream_t stream);
@@ -63,6 +85,11 @@ int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const
                                  int M, int T, const int32_t *pos0, int d, uint16_t *H,
                                  const uint16_t *gamma, const uint16_t *beta, float eps,
                                  uint16_t *Y, int8_t *Xq, float *sX, cudaStream_t s);
+int launch_row_amax(const uint16_t *X, int64_t ldx, int M, int K, float *amax, cudaStream_t s);
+int launch_quant_rows_amax(const uint16_t *X, int64_t ldx, int M, int K, const float *amax,
+                           int n_amax, int64_t amax_stride, int8_t *Xq, int64_t ldq, float *sX,
+                           cudaStream_t s);
+int launch_reduce_layernorm_quant(const ReduceArgs &a, int M, cudaStream_t s);
 // attention.cu
 int launch_attention_prefill(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
                              const uint16_t *Vc, int64_t seq_stride, int n_seq, int T, int n_head,

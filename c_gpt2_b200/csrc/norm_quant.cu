@@ -10,6 +10,8 @@
 //                 the reference's 1024-thread block uses, then rsqrtf)
 //   embedding     cuda/embeddings.cu:18-23
 #include "common.cuh"
+#include "epilogue.cuh"
+#include "kernels.cuh"
 #include "runtime.cuh"
 
 namespace w8a8 {
@@ -279,10 +281,10 @@ __device__ __forceinline__ float block_max(RowShared &sh, float v, int t) {
   return m;
 }
 
-// Quantize the row values a thread holds (bf16 bit patterns in y[k]) with the
-// row's scale (activation_quant.cu:75-91) and store them.
-__device__ __forceinline__ void quant_store(RowShared &sh, const uint4 (&y)[kMaxVec], int nv,
-                                            int t, int8_t *xq_row, float *sx_out) {
+// Largest |value| of the row values a thread holds (bf16 bit patterns in
+// y[k]), reduced over the block.
+__device__ __forceinline__ float block_row_amax(RowShared &sh, const uint4 (&y)[kMaxVec], int nv,
+                                                int t) {
   float amax = 0.0f;
 #pragma unroll
   for (int k = 0; k < kMaxVec; ++k) {
@@ -293,7 +295,13 @@ __device__ __forceinline__ void quant_store(RowShared &sh, const uint4 (&y)[kMax
       for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
     }
   }
-  amax = block_max(sh, amax, t);
+  return block_max(sh, amax, t);
+}
+
+// Quantize the row values a thread holds with the scale of the row's absolute
+// maximum amax (activation_quant.cu:75-91) and store them.
+__device__ __forceinline__ void quant_store_amax(const uint4 (&y)[kMaxVec], int nv, int t,
+                                                 float amax, int8_t *xq_row, float *sx_out) {
   const float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
   const float inv = __fdiv_rn(1.0f, scale);
   if (t == 0) *sx_out = scale;
@@ -315,6 +323,21 @@ __device__ __forceinline__ void quant_store(RowShared &sh, const uint4 (&y)[kMax
   }
 }
 
+__device__ __forceinline__ void quant_store(RowShared &sh, const uint4 (&y)[kMaxVec], int nv,
+                                            int t, int8_t *xq_row, float *sx_out) {
+  quant_store_amax(y, nv, t, block_row_amax(sh, y, nv, t), xq_row, sx_out);
+}
+
+__device__ __forceinline__ void load_row_vec(const uint16_t *row, int nv, int t,
+                                             uint4 (&x)[kMaxVec]) {
+  const uint4 *src = reinterpret_cast<const uint4 *>(row);
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    const int v = t + kRowThreads * k;
+    x[k] = v < nv ? __ldg(src + v) : make_uint4(0, 0, 0, 0);
+  }
+}
+
 __global__ void __launch_bounds__(kRowThreads)
     quant_rows_block_kernel(const uint16_t *__restrict__ X, int64_t ldx, int K,
                             int8_t *__restrict__ Xq, float *__restrict__ sX) {
@@ -322,14 +345,112 @@ __global__ void __launch_bounds__(kRowThreads)
   pdl_launch_dependents();
   __shared__ RowShared sh;
   const int row = blockIdx.x, t = threadIdx.x, nv = K >> 3;
-  const uint4 *src = reinterpret_cast<const uint4 *>(X + (int64_t)row * ldx);
   uint4 x[kMaxVec];
+  load_row_vec(X + (int64_t)row * ldx, nv, t, x);
+  quant_store(sh, x, nv, t, Xq + (int64_t)row * K, sX + row);
+}
+
+// Row absolute maxima of a column block of the rows, for rows whose columns
+// are spread over several GPUs (tensor-parallel attention heads, d_ff slices):
+// the per-token scale of the whole row comes from the maximum of the parts.
+__global__ void __launch_bounds__(kRowThreads)
+    row_amax_block_kernel(const uint16_t *__restrict__ X, int64_t ldx, int K,
+                          float *__restrict__ amax) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ RowShared sh;
+  const int row = blockIdx.x, t = threadIdx.x, nv = K >> 3;
+  uint4 x[kMaxVec];
+  load_row_vec(X + (int64_t)row * ldx, nv, t, x);
+  const float m = block_row_amax(sh, x, nv, t);
+  if (t == 0) amax[row] = m;
+}
+
+// Per-token quantization of a column block with the scale of the whole row,
+// whose absolute maximum is given (the maximum over n_amax partial maxima
+// amax[j * amax_stride + row]). Identical to quant_rows on the whole row.
+__global__ void __launch_bounds__(kRowThreads)
+    quant_rows_amax_block_kernel(const uint16_t *__restrict__ X, int64_t ldx, int K,
+                                 const float *__restrict__ amax, int n_amax,
+                                 int64_t amax_stride, int8_t *__restrict__ Xq, int64_t ldq,
+                                 float *__restrict__ sX) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int row = blockIdx.x, t = threadIdx.x, nv = K >> 3;
+  uint4 x[kMaxVec];
+  load_row_vec(X + (int64_t)row * ldx, nv, t, x);
+  float m = 0.0f;
+  for (int j = 0; j < n_amax; ++j) m = fmaxf(m, __ldcg(amax + j * amax_stride + row));
+  quant_store_amax(x, nv, t, m, Xq + (int64_t)row * ldq, sX + row);
+}
+
+// LayerNorm of one row held as bf16 vectors x[k] (thread t owns vectors
+// t + 128k), then the optional bf16 output and the per-token quantization.
+__device__ __forceinline__ void ln_quant_tail(RowShared &sh, const uint4 (&x)[kMaxVec],
+                                              const uint4 (&g)[kMaxVec],
+                                              const uint4 (&bt)[kMaxVec], int nv, int t, int d,
+                                              float eps, uint16_t *y_row, int8_t *xq_row,
+                                              float *sx_out) {
+  // mean: slot 8t+e accumulates elements 8t+e+1024k in order (layernorm.cu:25-41)
+  float s[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    if (t + kRowThreads * k < nv) {
+      float f[8];
+      unpack8(x[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s[e] += f[e];
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) sh.slots[8 * t + e] = s[e];
+  const float mean = fold_slots(sh, t) / (float)d;
+  // variance (layernorm.cu:45-66): diff*diff contracted into the running sum
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kMaxVec; ++k) {
+    if (t + kRowThreads * k < nv) {
+      float f[8];
+      unpack8(x[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float diff = f[e] - mean;
+        s[e] += diff * diff;
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) sh.slots[8 * t + e] = s[e];
+  const float variance = fold_slots(sh, t) / (float)d;
+  const float inv_std_dev = rsqrtf(variance + eps);
+  // normalise + affine, bf16 (layernorm.cu:73-77)
+  uint4 y[kMaxVec];
 #pragma unroll
   for (int k = 0; k < kMaxVec; ++k) {
     const int v = t + kRowThreads * k;
-    x[k] = v < nv ? __ldg(src + v) : make_uint4(0, 0, 0, 0);
+    if (v < nv) {
+      float f[8], gf[8], bf[8];
+      unpack8(x[k], f);
+      unpack8(g[k], gf);
+      unpack8(bt[k], bf);
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float n0 = (f[2 * i] - mean) * inv_std_dev;
+        float n1 = (f[2 * i + 1] - mean) * inv_std_dev;
+        w[i] = (uint32_t)f2bf(n0 * gf[2 * i] + bf[2 * i]) |
+               ((uint32_t)f2bf(n1 * gf[2 * i + 1] + bf[2 * i + 1]) << 16);
+      }
+      y[k] = make_uint4(w[0], w[1], w[2], w[3]);
+      if (y_row) reinterpret_cast<uint4 *>(y_row)[v] = y[k];
+    } else {
+      y[k] = make_uint4(0, 0, 0, 0);
+    }
   }
-  quant_store(sh, x, nv, t, Xq + (int64_t)row * K, sX + row);
+  if (xq_row) quant_store(sh, y, nv, t, xq_row, sx_out);
 }
 
 // MODE 0: rows of X. MODE 1: embedding gather wte[token] + wpe[position]
@@ -387,66 +508,66 @@ __global__ void __launch_bounds__(kRowThreads)
       bt[k] = __ldg(reinterpret_cast<const uint4 *>(beta) + v);
     }
   }
-  // mean: slot 8t+e accumulates elements 8t+e+1024k in order (layernorm.cu:25-41)
-  float s[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+  ln_quant_tail(sh, x, g, bt, nv, t, d, eps, Y ? Y + (int64_t)row * ldy : nullptr,
+                Xq ? Xq + (int64_t)row * d : nullptr, sX + row);
+}
+
+// Residual stream after a GEMM whose reduction was split over GPUs
+// (tensor-parallel attn_proj / W2): acc = the sum of n_slots int32 partial rows,
+// H = bf16(R + bf16(bf16(acc*sW*sX) + b)) with the rounding points of the
+// single-GPU epilogue (activation_quant.cu:129-130, add_bias.cu:14,
+// add_2d.cu:14), then optionally LayerNorm and per-token quantization of H.
+// Integer sums are exact in any order, so the result equals the single-GPU
+// layer bit for bit.
+__global__ void __launch_bounds__(kRowThreads) reduce_layernorm_quant_kernel(ReduceArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ RowShared sh;
+  const int row = blockIdx.x, t = threadIdx.x, nv = a.d >> 3;
+  const float sx = a.sX[row];
+  uint4 x[kMaxVec], g[kMaxVec], bt[kMaxVec];
 #pragma unroll
   for (int k = 0; k < kMaxVec; ++k) {
-    if (t + kRowThreads * k < nv) {
-      float f[8];
-      unpack8(x[k], f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) s[e] += f[e];
-    }
-  }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) sh.slots[8 * t + e] = s[e];
-  const float mean = fold_slots(sh, t) / (float)d;
-  // variance (layernorm.cu:45-66): diff*diff contracted into the running sum
-#pragma unroll
-  for (int e = 0; e < 8; ++e) s[e] = 0.0f;
-#pragma unroll
-  for (int k = 0; k < kMaxVec; ++k) {
-    if (t + kRowThreads * k < nv) {
-      float f[8];
-      unpack8(x[k], f);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float diff = f[e] - mean;
-        s[e] += diff * diff;
+    const int v = t + kRowThreads * k;
+    x[k] = make_uint4(0, 0, 0, 0);
+    if (v < nv) {
+      int32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int j = 0; j < a.n_slots; ++j) {
+        const int4 *src = reinterpret_cast<const int4 *>(a.acc + j * a.slot_stride +
+                                                         (int64_t)row * a.lda) + 2 * v;
+        const int4 lo = __ldcg(src), hi = __ldcg(src + 1);
+        acc[0] += lo.x; acc[1] += lo.y; acc[2] += lo.z; acc[3] += lo.w;
+        acc[4] += hi.x; acc[5] += hi.y; acc[6] += hi.z; acc[7] += hi.w;
       }
+      const float4 w0 = __ldg(reinterpret_cast<const float4 *>(a.sW) + 2 * v);
+      const float4 w1 = __ldg(reinterpret_cast<const float4 *>(a.sW) + 2 * v + 1);
+      const float sw[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      float bf[8], rf[8];
+      unpack8(__ldg(reinterpret_cast<const uint4 *>(a.bias) + v), bf);
+      unpack8(__ldg(reinterpret_cast<const uint4 *>(a.R + (int64_t)row * a.ldr) + v), rf);
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float y0 = add_bf(dequant_bf(acc[2 * i], sw[2 * i], sx), bf[2 * i]);
+        const float y1 = add_bf(dequant_bf(acc[2 * i + 1], sw[2 * i + 1], sx), bf[2 * i + 1]);
+        w[i] = (uint32_t)f2bf(__fadd_rn(rf[2 * i], y0)) |
+               ((uint32_t)f2bf(__fadd_rn(rf[2 * i + 1], y1)) << 16);
+      }
+      x[k] = make_uint4(w[0], w[1], w[2], w[3]);
+      reinterpret_cast<uint4 *>(a.H + (int64_t)row * a.ldh)[v] = x[k];
     }
   }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) sh.slots[8 * t + e] = s[e];
-  const float variance = fold_slots(sh, t) / (float)d;
-  const float inv_std_dev = rsqrtf(variance + eps);
-  // normalise + affine, bf16 (layernorm.cu:73-77)
-  uint4 y[kMaxVec];
+  if (!a.gamma) return;
 #pragma unroll
   for (int k = 0; k < kMaxVec; ++k) {
     const int v = t + kRowThreads * k;
     if (v < nv) {
-      float f[8], gf[8], bf[8];
-      unpack8(x[k], f);
-      unpack8(g[k], gf);
-      unpack8(bt[k], bf);
-      uint32_t w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float n0 = (f[2 * i] - mean) * inv_std_dev;
-        float n1 = (f[2 * i + 1] - mean) * inv_std_dev;
-        w[i] = (uint32_t)f2bf(n0 * gf[2 * i] + bf[2 * i]) |
-               ((uint32_t)f2bf(n1 * gf[2 * i + 1] + bf[2 * i + 1]) << 16);
-      }
-      y[k] = make_uint4(w[0], w[1], w[2], w[3]);
-      if (Y) reinterpret_cast<uint4 *>(Y + (int64_t)row * ldy)[v] = y[k];
-    } else {
-      y[k] = make_uint4(0, 0, 0, 0);
+      g[k] = __ldg(reinterpret_cast<const uint4 *>(a.gamma) + v);
+      bt[k] = __ldg(reinterpret_cast<const uint4 *>(a.beta) + v);
     }
   }
-  if (Xq) quant_store(sh, y, nv, t, Xq + (int64_t)row * d, sX + row);
+  ln_quant_tail(sh, x, g, bt, nv, t, a.d, a.eps, nullptr, a.Xq + (int64_t)row * a.ldq,
+                a.sXq + row);
 }
 
 static bool block_path_ok(int d, const void *a, int64_t lda, const void *b, int64_t ldb) {
@@ -524,6 +645,33 @@ int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const
   launch_pdl(embed_layernorm_quant_kernel, dim3(row_grid(M)), dim3(kRowWarps * 32), smem, s, 
       wte, wpe, tokens, M, T, pos0, d, H, gamma, beta, eps, Y, Xq, sX);
   return check_launch("embed_layernorm_quant");
+}
+
+int launch_row_amax(const uint16_t *X, int64_t ldx, int M, int K, float *amax, cudaStream_t s) {
+  if (!block_path_ok(K, X, ldx, nullptr, 0)) return W8A8_ERR_UNSUPPORTED;
+  launch_pdl(row_amax_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, amax);
+  return check_launch("row_amax_block");
+}
+
+int launch_quant_rows_amax(const uint16_t *X, int64_t ldx, int M, int K, const float *amax,
+                           int n_amax, int64_t amax_stride, int8_t *Xq, int64_t ldq, float *sX,
+                           cudaStream_t s) {
+  if (!block_path_ok(K, X, ldx, Xq, ldq)) return W8A8_ERR_UNSUPPORTED;
+  launch_pdl(quant_rows_amax_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, amax,
+             n_amax, amax_stride, Xq, ldq, sX);
+  return check_launch("quant_rows_amax_block");
+}
+
+int launch_reduce_layernorm_quant(const ReduceArgs &a, int M, cudaStream_t s) {
+  const int d = a.d;
+  bool ok = (d & 7) == 0 && d <= 1024 * kMaxVec && aligned16(a.acc) && (a.lda & 3) == 0 &&
+            (a.slot_stride & 3) == 0 && aligned16(a.sW) && aligned16(a.bias) &&
+            aligned16(a.R) && (a.ldr & 7) == 0 && aligned16(a.H) && (a.ldh & 7) == 0;
+  if (a.gamma)
+    ok = ok && aligned16(a.gamma) && aligned16(a.beta) && aligned16(a.Xq) && (a.ldq & 7) == 0;
+  if (!ok) return W8A8_ERR_UNSUPPORTED;
+  launch_pdl(reduce_layernorm_quant_kernel, dim3(M), dim3(kRowThreads), 0, s, a);
+  return check_launch("reduce_layernorm_quant");
 }
 
 }  // namespace w8a8

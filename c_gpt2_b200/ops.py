@@ -123,6 +123,56 @@ def linear_qkv(Xq, sX, Wqkv, sWqkv, bqkv, Q, Kc, Vc, seq_stride, T, pos0=None, w
           "w8a8_linear_qkv")
 
 
+def linear_qkv_heads(Xq, sX, Wqkv, sWqkv, bqkv, Q, Kc, Vc, seq_stride, T, pos0=None,
+                     workspace=None):
+    """QKV projection of a subset of heads: Wqkv [3*d_heads, K]."""
+    M, K = Xq.shape
+    dh = Wqkv.shape[0] // 3
+    ws_bytes = workspace.numel() if workspace is not None else 0
+    check(core().w8a8_linear_qkv_heads(_ptr(Xq), _ptr(sX), M, K, dh, _ptr(Wqkv), _ptr(sWqkv),
+                                       _ptr(bqkv), _ptr(Q), Q.stride(0), _ptr(Kc), _ptr(Vc),
+                                       seq_stride, T, _ptr(pos0), _ptr(workspace), ws_bytes,
+                                       _stream()), "w8a8_linear_qkv_heads")
+
+
+def row_amax(X, out=None):
+    """Per-row max |x| of a bf16 [M, K] block -> f32 [M]."""
+    _need(X, torch.bfloat16, "X")
+    M, K = X.shape
+    out = out if out is not None else torch.empty((M,), dtype=torch.float32, device=X.device)
+    check(core().w8a8_row_amax(_ptr(X), X.stride(0), M, K, _ptr(out), _stream()), "w8a8_row_amax")
+    return out
+
+
+def quant_rows_amax(X, amax, Xq=None, sX=None):
+    """Per-token quantization of X [M, K] with the row maxima amax ([M] or
+    [n, M], the maximum over the n partial maxima)."""
+    _need(X, torch.bfloat16, "X")
+    M, K = X.shape
+    amax2 = amax.reshape(-1, M)
+    Xq = Xq if Xq is not None else torch.empty((M, K), dtype=torch.int8, device=X.device)
+    sX = sX if sX is not None else torch.empty((M,), dtype=torch.float32, device=X.device)
+    check(core().w8a8_quant_rows_amax(_ptr(X), X.stride(0), M, K, _ptr(amax2), amax2.shape[0],
+                                      amax2.stride(0), _ptr(Xq), Xq.stride(0), _ptr(sX), _stream()),
+          "w8a8_quant_rows_amax")
+    return Xq, sX
+
+
+def reduce_residual_layernorm_quant(acc, sX, sW, bias, R, H, gamma=None, beta=None, eps=1e-5,
+                                    Xq=None, sXq=None):
+    """H = R + dequant(sum of int32 partials acc [n, M, d] or [M, d]) + bias,
+    then optionally LayerNorm + quant of H into Xq / sXq."""
+    _need(acc, torch.int32, "acc")
+    acc3 = acc if acc.dim() == 3 else acc.unsqueeze(0)
+    n, M, d = acc3.shape
+    check(core().w8a8_reduce_residual_layernorm_quant(
+        _ptr(acc3), acc3.stride(1), n, acc3.stride(0), M, d, _ptr(sX), _ptr(sW), _ptr(bias),
+        _ptr(R), R.stride(0), _ptr(H), H.stride(0), _ptr(gamma), _ptr(beta), eps, _ptr(Xq),
+        Xq.stride(0) if Xq is not None else 0, _ptr(sXq), _stream()),
+        "w8a8_reduce_residual_layernorm_quant")
+    return H
+
+
 def attention_prefill(Q, Kc, Vc, seq_stride, n_seq, T, n_head, out=None):
     d = n_head * 64
     O = out if out is not None else torch.empty((n_seq * T, d), dtype=torch.bfloat16,

@@ -1,0 +1,338 @@
+"""Tensor-parallel W8A8 prefill of GPT-2 over G GPUs (one process per GPU),
+bit-identical to the single-GPU layer.
+
+The reference runs every layer on one GPU (transformer_block_gpu,
+gpt2.c:1124-1330). Here each layer is split the Megatron way, with the
+exchange steps chosen so that no rounding changes:
+
+* W_qkv is column-split by whole heads and attention runs on the local heads;
+  W1 is column-split into a d_ff slice. Both read the full quantized LayerNorm
+  output, which every GPU holds (all-gather of int8 rows + fp32 scales).
+* attn_proj and W2 are row-split over the same head dims / d_ff slice. Their
+  inputs are quantized per token over the WHOLE row (activation_quant.cu:
+  75-91), so each GPU contributes its row maxima and the scale comes from a
+  max-allreduce of [M] floats; quantizing the local columns with it gives
+  exactly the single-GPU int8 values.
+* The row-split GEMMs produce int32 partial sums, reduce-scattered (exact in
+  any order) so that each GPU owns whole sequences of the residual stream.
+  The owner applies dequant + bias + residual with the single-GPU rounding
+  points, then the next LayerNorm + quant, and the int8 rows are all-gathered.
+
+Per sub-block the exchange is an int32 reduce-scatter of [M, d] plus an int8
+all-gather of [M, d] (5 bytes per element against the 4 of a bf16
+all-reduce), in exchange for outputs equal to one GPU's bit for bit.
+
+`Kernels` is the device side (the library's CUDA kernels through ops);
+`Collectives` is the exchange (torch.distributed: NCCL on GPUs). Both are
+parameters so that the host logic can be exercised on CPU ranks.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .quant8 import GPT2Dims
+
+HEAD_DIM = 64
+
+
+def split_even(n: int, parts: int) -> list[tuple[int, int]]:
+    """[start, end) of `parts` contiguous pieces of n, the first n % parts one
+    larger (20 heads over 8 GPUs: 3,3,3,3,2,2,2,2)."""
+    if parts <= 0 or n < parts:
+        raise ValueError(f"cannot split {n} into {parts} non-empty parts")
+    base, extra = divmod(n, parts)
+    out, s = [], 0
+    for r in range(parts):
+        e = s + base + (1 if r < extra else 0)
+        out.append((s, e))
+        s = e
+    return out
+
+
+@dataclass(frozen=True)
+class TPPlan:
+    """Which heads, d_ff columns and sequences each rank owns."""
+    dims: GPT2Dims
+    world: int
+    heads: tuple[tuple[int, int], ...]  # per rank [h0, h1)
+    ff: tuple[tuple[int, int], ...]     # per rank [f0, f1) of d_ff, multiples of 64
+
+    @staticmethod
+    def make(dims: GPT2Dims, world: int) -> "TPPlan":
+        heads = tuple(split_even(dims.n_head, world))
+        units = split_even(dims.d_ff // HEAD_DIM, world)
+        ff = tuple((a * HEAD_DIM, b * HEAD_DIM) for a, b in units)
+        return TPPlan(dims, world, heads, ff)
+
+    def d_heads(self, rank: int) -> int:
+        h0, h1 = self.heads[rank]
+        return (h1 - h0) * HEAD_DIM
+
+    def qkv_rows(self, rank: int) -> np.ndarray:
+        """Rows of the packed W_qkv [3d, d] (Q, K, V blocks) of rank's heads."""
+        d = self.dims.d_model
+        h0, h1 = self.heads[rank]
+        cols = np.arange(h0 * HEAD_DIM, h1 * HEAD_DIM)
+        return np.concatenate([cols, d + cols, 2 * d + cols])
+
+    def seqs(self, n_seq: int, rank: int) -> tuple[int, int]:
+        """Sequences [s0, s1) whose residual stream rank owns."""
+        if n_seq % self.world:
+            raise ValueError(f"{n_seq} sequences do not split evenly over {self.world} GPUs")
+        per = n_seq // self.world
+        return rank * per, (rank + 1) * per
+
+
+@dataclass
+class TPShard:
+    """One rank's weights: replicated embeddings and norms, its slices of the
+    four GEMM weights (int8 + fp32 scales) and biases (bf16)."""
+    wte: torch.Tensor
+    wpe: torch.Tensor
+    lnf_gamma: torch.Tensor
+    lnf_beta: torch.Tensor
+    layers: list[dict[str, torch.Tensor]]
+
+
+def _bf16(a: np.ndarray, device) -> torch.Tensor:
+    # fp32 -> bf16 with round-to-nearest-even, as the weight loader does
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(device).to(
+        torch.bfloat16)
+
+
+def _dev(a: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def shard_weights(w: dict[str, np.ndarray], plan: TPPlan, rank: int, device) -> TPShard:
+    """Slice a parsed quant8 image (quant8.read_quant8) for `rank`."""
+    d = plan.dims.d_model
+    h0, h1 = plan.heads[rank]
+    c0, c1 = h0 * HEAD_DIM, h1 * HEAD_DIM
+    f0, f1 = plan.ff[rank]
+    rows = plan.qkv_rows(rank)
+    layers = []
+    for l in range(plan.dims.n_layer):
+        p = f"h{l}."
+        layers.append({
+            "ln1_gamma": _bf16(w[p + "ln1_gamma"], device),
+            "ln1_beta": _bf16(w[p + "ln1_beta"], device),
+            "W_qkv": _dev(w[p + "W_qkv"][rows], device),
+            "W_qkv.scale": _dev(w[p + "W_qkv.scale"][rows], device),
+            "b_qkv": _bf16(w[p + "b_qkv"][rows], device),
+            "attn_proj": _dev(w[p + "attn_proj"][:, c0:c1], device),
+            "attn_proj.scale": _dev(w[p + "attn_proj.scale"], device),
+            "attn_proj_bias": _bf16(w[p + "attn_proj_bias"], device),
+            "ln2_gamma": _bf16(w[p + "ln2_gamma"], device),
+            "ln2_beta": _bf16(w[p + "ln2_beta"], device),
+            "W1": _dev(w[p + "W1"][f0:f1], device),
+            "W1.scale": _dev(w[p + "W1.scale"][f0:f1], device),
+            "b1": _bf16(w[p + "b1"][f0:f1], device),
+            "W2": _dev(w[p + "W2"][:, f0:f1], device),
+            "W2.scale": _dev(w[p + "W2.scale"], device),
+            "b2": _bf16(w[p + "b2"], device),
+        })
+    assert d == w["wte"].shape[1]
+    return TPShard(_bf16(w["wte"], device), _bf16(w["wpe"], device),
+                   _bf16(w["lnf_gamma"], device), _bf16(w["lnf_beta"], device), layers)
+
+
+class Collectives:
+    """The three exchange steps, over a torch.distributed process group (none
+    needed when the group has one rank)."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+
+    def all_gather_rows(self, full: torch.Tensor, rank: int, world: int) -> None:
+        """full [world*m, ...]: rank's chunk is filled in, every chunk comes back."""
+        if self.world == 1:
+            return
+        m = full.shape[0] // world
+        dist.all_gather_into_tensor(full, full[rank * m:(rank + 1) * m].clone(), group=self.group)
+
+    def reduce_scatter_sum(self, out: torch.Tensor, full: torch.Tensor) -> None:
+        if self.world == 1:
+            out.copy_(full)
+            return
+        dist.reduce_scatter_tensor(out, full, op=dist.ReduceOp.SUM, group=self.group)
+
+    def all_reduce_max(self, x: torch.Tensor) -> None:
+        if self.world > 1:
+            dist.all_reduce(x, op=dist.ReduceOp.MAX, group=self.group)
+
+
+class Kernels:
+    """Device side of one tensor-parallel layer: the library's CUDA kernels."""
+
+    embed_layernorm_quant = staticmethod(ops.embed_layernorm_quant)
+    linear_qkv_heads = staticmethod(ops.linear_qkv_heads)
+    attention_prefill = staticmethod(ops.attention_prefill)
+    row_amax = staticmethod(ops.row_amax)
+    quant_rows_amax = staticmethod(ops.quant_rows_amax)
+    gemm_s32 = staticmethod(ops.gemm_s32)
+    linear = staticmethod(ops.linear)
+    reduce_residual_layernorm_quant = staticmethod(ops.reduce_residual_layernorm_quant)
+    layernorm_quant = staticmethod(ops.layernorm_quant)
+    lm_head = staticmethod(ops.lm_head)
+    sample_greedy = staticmethod(ops.sample_greedy)
+
+
+class TPPrefill:
+    """Prefill of n_seq prompts of T tokens on `world` ranks; returns the
+    greedy next token of every sequence (on every rank) and the last-position
+    logits of the sequences this rank owns."""
+
+    def __init__(self, plan: TPPlan, shard: TPShard, rank: int, kernels=None,
+                 collectives: Collectives | None = None, eps: float = 1e-5):
+        self.plan, self.w, self.rank = plan, shard, rank
+        self.k = kernels or Kernels()
+        self.c = collectives or Collectives()
+        self.eps = eps
+
+    def run(self, tokens: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        plan, w, k, c, r, G = self.plan, self.w, self.k, self.c, self.rank, self.plan.world
+        n_seq, T = tokens.shape
+        d = plan.dims.d_model
+        dh = plan.d_heads(r)
+        hl = dh // HEAD_DIM
+        M = n_seq * T
+        s0, s1 = plan.seqs(n_seq, r)
+        m0, m1 = s0 * T, s1 * T
+        dev = w.wte.device
+        L0 = w.layers[0]
+        # residual stream of the owned sequences; int8 LayerNorm output of all rows
+        Xq = torch.empty((M, d), dtype=torch.int8, device=dev)
+        sX = torch.empty((M,), dtype=torch.float32, device=dev)
+        own_tok = tokens[s0:s1].contiguous().reshape(-1)
+        H, _, xq, sx = k.embed_layernorm_quant(w.wte, w.wpe, own_tok, T, None, L0["ln1_gamma"],
+                                               L0["ln1_beta"], self.eps)
+        Xq[m0:m1].copy_(xq)
+        sX[m0:m1].copy_(sx)
+        self._gather(Xq, sX)
+        Kc = torch.empty((n_seq, T, dh), dtype=torch.bfloat16, device=dev)
+        Vc = torch.empty_like(Kc)
+        Q = torch.empty((M, dh), dtype=torch.bfloat16, device=dev)
+        P_own = torch.empty((m1 - m0, d), dtype=torch.int32, device=dev)
+        n_layer = len(w.layers)
+        for l, L in enumerate(w.layers):
+            # attention on the local heads
+            k.linear_qkv_heads(Xq, sX, L["W_qkv"], L["W_qkv.scale"], L["b_qkv"], Q, Kc, Vc,
+                               T * dh, T)
+            O = k.attention_prefill(Q, Kc, Vc, T * dh, n_seq, T, hl)
+            # attn_proj, row-split: whole-row scale, int32 partials, reduce-scatter
+            amax = k.row_amax(O)
+            c.all_reduce_max(amax)
+            Oq, sO = k.quant_rows_amax(O, amax)
+            P = k.gemm_s32(Oq, L["attn_proj"])
+            c.reduce_scatter_sum(P_own, P)
+            del P
+            k.reduce_residual_layernorm_quant(P_own, sO[m0:m1], L["attn_proj.scale"],
+                                              L["attn_proj_bias"], H, H, L["ln2_gamma"],
+                                              L["ln2_beta"], self.eps, Xq[m0:m1], sX[m0:m1])
+            self._gather(Xq, sX)
+            # MLP: W1 column-split with GELU, W2 row-split
+            Gk = k.linear(Xq, sX, L["W1"], L["W1.scale"], L["b1"], epilogue=3)
+            amax = k.row_amax(Gk)
+            c.all_reduce_max(amax)
+            Gq, sG = k.quant_rows_amax(Gk, amax)
+            del Gk
+            P = k.gemm_s32(Gq, L["W2"])
+            c.reduce_scatter_sum(P_own, P)
+            del P
+            if l + 1 < n_layer:
+                N = w.layers[l + 1]
+                k.reduce_residual_layernorm_quant(P_own, sG[m0:m1], L["W2.scale"], L["b2"], H, H,
+                                                  N["ln1_gamma"], N["ln1_beta"], self.eps,
+                                                  Xq[m0:m1], sX[m0:m1])
+                self._gather(Xq, sX)
+            else:
+                k.reduce_residual_layernorm_quant(P_own, sG[m0:m1], L["W2.scale"], L["b2"], H, H)
+        # final LayerNorm of each owned sequence's last position, LM head, greedy
+        last = H.view(s1 - s0, T, d)[:, T - 1, :]
+        Xf, _, _ = k.layernorm_quant(last, w.lnf_gamma, w.lnf_beta, self.eps, want_q=False)
+        logits = k.lm_head(Xf, w.wte)
+        nxt = torch.empty((n_seq,), dtype=torch.int32, device=dev)
+        nxt[s0:s1].copy_(k.sample_greedy(logits))
+        c.all_gather_rows(nxt, r, G)
+        return nxt, logits
+
+    def _gather(self, Xq: torch.Tensor, sX: torch.Tensor) -> None:
+        self.c.all_gather_rows(Xq, self.rank, self.plan.world)
+        self.c.all_gather_rows(sX, self.rank, self.plan.world)
+
+
+def main(argv=None) -> None:
+    """Time the tensor-parallel prefill of GPT-2 large, 32 x 1024 tokens:
+    python -m torch.distributed.run --nproc-per-node G --master-addr 127.0.0.1 \\
+        -m c_gpt2_b200.tp [--n-seq 32] [--tokens 1024] [--steps 3] [--warmup 3]
+    Prints one JSON line on rank 0 (device time, max over ranks)."""
+    import argparse
+    import json
+    from datetime import timedelta
+
+    from .dp import dist_env, max_over_ranks
+    from .quant8 import DIMS, read_quant8
+    from .synthetic import prompts, quant8_image_gpu
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--n-seq", type=int, default=32)
+    ap.add_argument("--tokens", type=int, default=1024)
+    ap.add_argument("--layers", type=int, default=None, help="fewer layers (smoke runs only)")
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args(argv)
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=timedelta(seconds=300))
+    ops.init(local)
+    dims = DIMS["large"]
+    if a.layers:
+        dims = GPT2Dims(dims.d_model, a.layers, dims.n_head, dims.vocab, dims.ctx)
+    img = quant8_image_gpu(dims, seed=0, device=dev)
+    plan = TPPlan.make(dims, world)
+    shard = shard_weights(read_quant8(img, dims), plan, rank, dev)
+    del img
+    P = torch.from_numpy(prompts(a.n_seq, a.tokens, dims.vocab, seed=0)).to(dev)
+    tp = TPPrefill(plan, shard, rank)
+    for _ in range(a.warmup):
+        tp.run(P)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        nxt, _ = tp.run(P)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps, dev)
+    if world > 1:
+        dist.barrier()
+    M = a.n_seq * a.tokens
+    gemm_ops = 2.0 * M * 12 * dims.d_model ** 2 * dims.n_layer
+    if rank == 0:
+        print(json.dumps({
+            "workload": f"gpt2-large W8A8 prefill {a.n_seq} x {a.tokens} tokens, "
+                        f"{dims.n_layer} layers, tensor-parallel tp{world}",
+            "n_gpus": world, "ms_per_prefill": round(ms, 3),
+            "tok_per_s": round(M / (ms / 1e3), 1),
+            "gemm_tops_effective": round(gemm_ops / (ms / 1e3) / 1e12, 1),
+            "exchange": "int32 reduce-scatter + int8 all-gather + fp32 max-allreduce (NCCL)",
+            "steps": a.steps, "warmup": a.warmup,
+            "first_tokens": nxt[:4].tolist()}))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -175,6 +175,50 @@ int w8a8_sample_greedy(const gpt2_bf16_t *logits, int64_t ldl, int M, int V,
 /* dst[i] = src[i] + delta for i < n (device arrays; dst may equal src). */
 int w8a8_advance_positions(int32_t *dst, const int32_t *src, int n, int delta, void *stream);
 
+/* ---- tensor-parallel building blocks ----
+ * No counterpart in the reference, which runs each layer on one GPU
+ * (transformer_block_gpu, gpt2.c:1124-1330). These split that layer over G
+ * GPUs so that every output equals the single-GPU layer bit for bit:
+ * QKV and W1 column-split (whole heads / a d_ff slice per GPU), attn_proj and
+ * W2 row-split with int32 partial sums reduced exactly, and the per-token
+ * scale of a row whose columns are spread over GPUs taken from the maximum
+ * of the per-GPU row maxima. */
+
+/* amax[m] = max_k |X[m, k]| over the K columns given (K % 8 == 0). */
+int w8a8_row_amax(const gpt2_bf16_t *X, int64_t ldx, int M, int K, float *amax, void *stream);
+
+/* per_token_quant of a column block with the scale of the whole row: the
+ * row's absolute maximum is the largest of n_amax partial maxima
+ * amax[j * amax_stride + m]. Identical to w8a8_quant_rows on the whole row
+ * restricted to these columns. */
+int w8a8_quant_rows_amax(const gpt2_bf16_t *X, int64_t ldx, int M, int K, const float *amax,
+                         int n_amax, int64_t amax_stride, int8_t *Xq, int64_t ldq, float *sX,
+                         void *stream);
+
+/* Residual stream after a row-split GEMM: acc is the sum of n_slots int32
+ * partial rows (slot j, row m at acc + j*slot_stride + m*lda), and
+ *   H[m, n] = bf16(R[m, n] + bf16(bf16(acc*sW[n]*sX[m]) + bias[n]))
+ * as w8a8_linear's W8A8_EPI_BIAS_RESID (activation_quant.cu:129-130,
+ * add_bias.cu:14, add_2d.cu:14). With gamma != NULL, then LayerNorm of H
+ * (layernorm.cu:7-100) quantized per token into Xq (row stride ldq) / sXq.
+ * H may equal R. d % 8 == 0, 16-byte aligned rows. */
+int w8a8_reduce_residual_layernorm_quant(const int32_t *acc, int64_t lda, int n_slots,
+                                         int64_t slot_stride, int M, int d, const float *sX,
+                                         const float *sW, const gpt2_bf16_t *bias,
+                                         const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *H,
+                                         int64_t ldh, const gpt2_bf16_t *gamma,
+                                         const gpt2_bf16_t *beta, float eps, int8_t *Xq,
+                                         int64_t ldq, float *sXq, void *stream);
+
+/* w8a8_linear_qkv for a subset of the heads: Wqkv [3*d_heads, K] holds the
+ * Q, K and V rows of those heads (d_heads = 64 * heads, a multiple of 32),
+ * and Q, Kc and Vc have rows of d_heads. */
+int w8a8_linear_qkv_heads(const int8_t *Xq, const float *sX, int M, int K, int d_heads,
+                          const int8_t *Wqkv, const float *sWqkv, const gpt2_bf16_t *bqkv,
+                          gpt2_bf16_t *Q, int64_t ldq, gpt2_bf16_t *Kc, gpt2_bf16_t *Vc,
+                          int64_t seq_stride, int T, const int32_t *pos0, void *workspace,
+                          size_t workspace_bytes, void *stream);
+
 /* ---- reference-shaped element-wise operations ----
  * Runtime-dimension forms of the reference's cuda/ kernels with their
  * exact per-element results; include/cuda_kernels.h maps its drop-in symbols

@@ -1,0 +1,135 @@
+"""Tensor-parallel prefill on the GPU: its building-block kernels against the
+single-GPU kernels they split, and the whole prefill against the single-GPU
+engine, bit for bit (one rank on one GPU; two NCCL ranks when two GPUs are
+present)."""
+import os
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from c_gpt2_b200 import _lib, ops
+from c_gpt2_b200.engine import Engine
+from c_gpt2_b200.quant8 import GPT2Dims, read_quant8
+from c_gpt2_b200.synthetic import outlier_activations, prompts, quant8_image_gpu
+from c_gpt2_b200.tp import Collectives, TPPlan, TPPrefill, shard_weights
+from oracle import oracle
+from tests.gpu_util import from_dev_bf16, to_dev, to_dev_bf16
+
+pytestmark = pytest.mark.gpu
+# GPT-2 large layer shapes, two layers
+LARGE2 = GPT2Dims(d_model=1280, n_layer=2, n_head=20)
+
+
+def _bf16_rows(M, K, seed):
+    return to_dev_bf16(oracle.bf16_bits(outlier_activations(M, K, seed=seed)))
+
+
+def test_quant_with_split_row_maxima_equals_quant_rows(cuda):
+    M, K = 300, 5120
+    X = _bf16_rows(M, K, 1)
+    want_q, want_s = ops.per_token_quant(X)
+    parts = [(0, 1280), (1280, 3200), (3200, 5120)]
+    amax = torch.stack([ops.row_amax(X[:, a:b]) for a, b in parts])
+    np.testing.assert_array_equal(amax.amax(0).cpu().numpy(),
+                                  X.float().abs().amax(1).cpu().numpy())
+    for a, b in parts:
+        q, s = ops.quant_rows_amax(X[:, a:b], amax)
+        assert torch.equal(q, want_q[:, a:b])
+        assert torch.equal(s, want_s)
+
+
+@pytest.mark.parametrize("slots", [1, 2, 4])
+def test_reduce_residual_layernorm_quant_equals_linear_then_layernorm(cuda, slots):
+    M, K, d = 256, 2560, 1280
+    rng = np.random.default_rng(slots)
+    xq, sx = oracle.quant_rows(oracle.bf16_bits(outlier_activations(M, K, seed=3)))
+    W = rng.integers(-127, 128, (d, K), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, d).astype(np.float32)
+    b = to_dev_bf16(oracle.bf16_bits(rng.standard_normal(d).astype(np.float32) * 0.02))
+    R = to_dev_bf16(oracle.bf16_bits(rng.standard_normal((M, d)).astype(np.float32)))
+    g = to_dev_bf16(oracle.bf16_bits(1 + 0.1 * rng.standard_normal(d).astype(np.float32)))
+    be = to_dev_bf16(oracle.bf16_bits(0.1 * rng.standard_normal(d).astype(np.float32)))
+    Xq, sX, Wd, sW = to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw)
+    want_h = ops.linear(Xq, sX, Wd, sW, b, _lib.EPI_BIAS_RESID, R=R)
+    _, want_q, want_s = ops.layernorm_quant(want_h, g, be, want_y=False)
+    # partial sums over K slices, as the row-split GEMM on `slots` GPUs makes them
+    cuts = np.linspace(0, K // 64, slots + 1).astype(int) * 64
+    acc = torch.stack([ops.gemm_s32(Xq[:, a:c].contiguous(), Wd[:, a:c].contiguous())
+                       for a, c in zip(cuts, cuts[1:])])
+    H = R.clone()
+    q = torch.empty((M, d), dtype=torch.int8, device=cuda)
+    s = torch.empty((M,), dtype=torch.float32, device=cuda)
+    ops.reduce_residual_layernorm_quant(acc, sX, sW, b, H, H, g, be, 1e-5, q, s)
+    np.testing.assert_array_equal(from_dev_bf16(H), from_dev_bf16(want_h))
+    assert torch.equal(q, want_q) and torch.equal(s, want_s)
+
+
+@pytest.fixture(scope="module")
+def large2_image():
+    return quant8_image_gpu(LARGE2, seed=5)
+
+
+def _engine_prefill(img, dims, P):
+    n_seq, T = P.shape
+    eng = Engine(dims, max_batch=n_seq, max_tokens=n_seq * T)
+    eng.load_quant8(img)
+    p_d = torch.from_numpy(P).cuda()
+    out = torch.empty((n_seq,), dtype=torch.int32, device="cuda")
+    eng.prefill(p_d, out, 1)
+    torch.cuda.synchronize()
+    logits = eng.logits(n_seq)
+    eng.close()
+    return out.cpu().numpy(), logits
+
+
+def test_tp_one_rank_matches_engine(cuda, large2_image):
+    P = prompts(4, 128, seed=9)
+    want_next, want_logits = _engine_prefill(large2_image, LARGE2, P)
+    plan = TPPlan.make(LARGE2, 1)
+    shard = shard_weights(read_quant8(large2_image, LARGE2), plan, 0, cuda)
+    nxt, logits = TPPrefill(plan, shard, 0).run(torch.from_numpy(P).cuda())
+    np.testing.assert_array_equal(nxt.cpu().numpy(), want_next)
+    got = (from_dev_bf16(logits).astype(np.uint32) << 16).view(np.float32)
+    np.testing.assert_array_equal(got, want_logits)
+
+
+def _tp_rank(rank, world, port, img_path, p_path, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    try:
+        ops.init(rank)
+        img = np.load(img_path)
+        P = np.load(p_path)
+        plan = TPPlan.make(LARGE2, world)
+        shard = shard_weights(read_quant8(img, LARGE2), plan, rank, f"cuda:{rank}")
+        nxt, logits = TPPrefill(plan, shard, rank, collectives=Collectives()).run(
+            torch.from_numpy(P).cuda())
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"next{rank}.npy"), nxt.cpu().numpy())
+        np.save(os.path.join(out_dir, f"logits{rank}.npy"), from_dev_bf16(logits))
+        assert ops.device_error() == 0
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp_two_ranks_match_engine(cuda, large2_image, tmp_path):
+    P = prompts(4, 128, seed=9)
+    want_next, want_logits = _engine_prefill(large2_image, LARGE2, P)
+    np.save(tmp_path / "img.npy", large2_image)
+    np.save(tmp_path / "p.npy", P)
+    port = 29600 + os.getpid() % 1000
+    mp.start_processes(_tp_rank, args=(2, port, str(tmp_path / "img.npy"),
+                                       str(tmp_path / "p.npy"), str(tmp_path)),
+                       nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        np.testing.assert_array_equal(np.load(tmp_path / f"next{r}.npy"), want_next)
+    bits = np.concatenate([np.load(tmp_path / f"logits{r}.npy") for r in range(2)])
+    np.testing.assert_array_equal((bits.astype(np.uint32) << 16).view(np.float32), want_logits)
