@@ -28,6 +28,7 @@
 // bf16 LM-head GEMM (gpt2.c:2160).
 #include <stddef.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "epilogue.cuh"
@@ -633,6 +634,17 @@ size_t linear_workspace_bytes(int M, int N) {
   return (((size_t)M * N * 4 + 255) & ~(size_t)255) + tiles * 4;
 }
 
+// W8A8_CLUSTER_GEMM=0 in the environment keeps decode GEMMs on the
+// global-workspace split-K path (for comparison).
+static bool getenv_cluster_on() {
+  static int on = -1;
+  if (on < 0) {
+    const char *v = getenv("W8A8_CLUSTER_GEMM");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 // Token-major needs whole 32-column chunks and 16-byte aligned output rows.
 static bool token_major_ok(const LinearArgs &a) {
   if (a.M <= kBM || (a.N & 31)) return false;
@@ -648,8 +660,16 @@ static bool token_major_ok(const LinearArgs &a) {
 template <int EPI>
 static int launch_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,
                      cudaStream_t s) {
-  return token_major_ok(a) ? launch_tc<0, EPI, false>(W, X, ldx, a, s)
-                           : launch_tc<0, EPI, true>(W, X, ldx, a, s);
+  if (token_major_ok(a)) return launch_tc<0, EPI, false>(W, X, ldx, a, s);
+  // Decode: too few 128-channel tiles to occupy the GPU; split K over a
+  // cluster and reduce in distributed shared memory.
+  int st;
+  DeviceCtx *ctx = device_ctx(&st);
+  if (!ctx) return st;
+  const int tiles = (a.N + kBM - 1) / kBM;
+  if (2 * tiles <= ctx->sm_count && cluster_gemm_ok(a, X, ldx) && getenv_cluster_on())
+    return gemm_cluster_i8(W, X, ldx, a, s);
+  return launch_tc<0, EPI, true>(W, X, ldx, a, s);
 }
 
 int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,

@@ -1,9 +1,9 @@
 // HBM-streaming INT8 GEMV for decode (1..15 tokens) and the CUDA-core
 // fallback for shapes the TMA path cannot take (K % 16 != 0, unaligned rows).
 //
-// One warp owns one output channel n: it streams W[n, :] with 16-byte loads
-// (8 independent loads in flight per lane), multiplies against the token
-// rows held in shared memory with dp4a, and reduces across lanes. A block
+// One warp owns one output channel n: it holds W[n, :] in registers (16-byte
+// loads, all in flight at once), multiplies against the token rows with dp4a,
+// and reduces across lanes. A block
 // holds 4 warps; the grid covers N/4 blocks, so even the 768-row projections
 // of GPT-2 small spread over more blocks than the B200 has SMs. Exact integer
 // accumulation: results are identical to the tensor-core path, and the same
@@ -60,58 +60,50 @@ __device__ __forceinline__ void gemv_store(const GemvArgs &a, int m, int n, int3
   }
 }
 
-// Vector path: K % 16 == 0 and 16-byte aligned rows.
-template <int MT>
+// Vector path: K % 16 == 0 and 16-byte aligned rows. Lane l of the warp
+// owning channel n holds the 16-byte weight vectors l + 32u (u < NVL) of
+// W[n, :] in registers. The weights do not depend on the previous kernel, so
+// they are requested before waiting for it (programmatic dependent launch):
+// the weight stream overlaps the previous kernel's tail, and only the small
+// activation rows (L2-resident, shared by the block's warps through L1) are
+// read after the wait.
+template <int MT, int NVL>
 __global__ void __launch_bounds__(kGemvWarps * 32)
     gemv_i8_vec_kernel(const int8_t *__restrict__ X, int64_t ldx, const int8_t *__restrict__ W,
                        GemvArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();
-  extern __shared__ int4 xs4[];  // [MT][K] int8
-  int8_t *xs = reinterpret_cast<int8_t *>(xs4);
-  const int K = a.K;
-  const int kv = K >> 4;  // 16-byte vectors per row
-  for (int i = threadIdx.x; i < MT * kv; i += blockDim.x) {
-    int m = i / kv, v = i - (i / kv) * kv;
-    int4 val = make_int4(0, 0, 0, 0);
-    if (m < a.M) val = __ldg(reinterpret_cast<const int4 *>(X + (int64_t)m * ldx) + v);
-    xs4[i] = val;
-  }
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x * kGemvWarps + warp;
+  const int kv = a.K >> 4;  // 16-byte vectors per row
+  int4 w[NVL];
+  if (n < a.N) {
+    const int4 *wrow = reinterpret_cast<const int4 *>(W + (int64_t)n * a.K);
+#pragma unroll
+    for (int u = 0; u < NVL; ++u) {
+      const int v = lane + 32 * u;
+      w[u] = v < kv ? __ldg(wrow + v) : make_int4(0, 0, 0, 0);
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
   if (n >= a.N) return;
-  const int4 *wrow = reinterpret_cast<const int4 *>(W + (int64_t)n * K);
   int acc[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = 0;
-  constexpr int U = 8;
-  int v = lane;
-  for (; v + 32 * (U - 1) < kv; v += 32 * U) {
-    int4 w[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) w[u] = __ldg(wrow + v + 32 * u);
+  for (int m = 0; m < MT; ++m) {
+    if (m < a.M) {
+      const int4 *xrow = reinterpret_cast<const int4 *>(X + (int64_t)m * ldx);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-#pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        int4 x = xs4[m * kv + v + 32 * u];
-        acc[m] = __dp4a(w[u].x, x.x, acc[m]);
-        acc[m] = __dp4a(w[u].y, x.y, acc[m]);
-        acc[m] = __dp4a(w[u].z, x.z, acc[m]);
-        acc[m] = __dp4a(w[u].w, x.w, acc[m]);
+      for (int u = 0; u < NVL; ++u) {
+        const int v = lane + 32 * u;
+        if (v < kv) {
+          const int4 x = __ldg(xrow + v);
+          acc[m] = __dp4a(w[u].x, x.x, acc[m]);
+          acc[m] = __dp4a(w[u].y, x.y, acc[m]);
+          acc[m] = __dp4a(w[u].z, x.z, acc[m]);
+          acc[m] = __dp4a(w[u].w, x.w, acc[m]);
+        }
       }
-    }
-  }
-  for (; v < kv; v += 32) {
-    int4 w = __ldg(wrow + v);
-#pragma unroll
-    for (int m = 0; m < MT; ++m) {
-      int4 x = xs4[m * kv + v];
-      acc[m] = __dp4a(w.x, x.x, acc[m]);
-      acc[m] = __dp4a(w.y, x.y, acc[m]);
-      acc[m] = __dp4a(w.z, x.z, acc[m]);
-      acc[m] = __dp4a(w.w, x.w, acc[m]);
     }
   }
 #pragma unroll
@@ -142,33 +134,34 @@ __global__ void gemv_i8_scalar_kernel(const int8_t *__restrict__ X, int64_t ldx,
   if (lane == 0) gemv_store(a, m, n, acc);
 }
 
-template <int MT>
+template <int MT, int NVL>
 static int launch_vec(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs &a,
                       cudaStream_t s) {
-  size_t smem = (size_t)MT * a.K;
-  if (smem > 160 * 1024) return W8A8_ERR_UNSUPPORTED;
-  static bool attr[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
-    cudaFuncSetAttribute(gemv_i8_vec_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         160 * 1024);
-    attr[dev & 63] = true;
-  }
   dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps);
-  launch_pdl(gemv_i8_vec_kernel<MT>, dim3(grid), dim3(kGemvWarps * 32), smem, s, X, ldx, W, a);
+  launch_pdl(gemv_i8_vec_kernel<MT, NVL>, dim3(grid), dim3(kGemvWarps * 32), 0, s, X, ldx, W, a);
   return check_launch("gemv_i8_vec");
+}
+
+template <int MT>
+static int launch_vec_k(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs &a,
+                        cudaStream_t s) {
+  const int nvl = ((a.K >> 4) + 31) / 32;  // weight vectors per lane
+  if (nvl <= 2) return launch_vec<MT, 2>(X, ldx, W, a, s);
+  if (nvl <= 4) return launch_vec<MT, 4>(X, ldx, W, a, s);
+  if (nvl <= 8) return launch_vec<MT, 8>(X, ldx, W, a, s);
+  if (nvl <= 16) return launch_vec<MT, 16>(X, ldx, W, a, s);
+  return W8A8_ERR_UNSUPPORTED;
 }
 
 int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs &a,
                    cudaStream_t s) {
   const bool vec = (a.K % 16 == 0) && (ldx % 16 == 0) && aligned16(X) && aligned16(W);
-  if (vec && a.M <= 16) {
-    if (a.M <= 1) return launch_vec<1>(X, ldx, W, a, s);
-    if (a.M <= 2) return launch_vec<2>(X, ldx, W, a, s);
-    if (a.M <= 4) return launch_vec<4>(X, ldx, W, a, s);
-    if (a.M <= 8) return launch_vec<8>(X, ldx, W, a, s);
-    return launch_vec<16>(X, ldx, W, a, s);
+  if (vec && a.M <= 16 && a.K <= 16 * 32 * 16) {
+    if (a.M <= 1) return launch_vec_k<1>(X, ldx, W, a, s);
+    if (a.M <= 2) return launch_vec_k<2>(X, ldx, W, a, s);
+    if (a.M <= 4) return launch_vec_k<4>(X, ldx, W, a, s);
+    if (a.M <= 8) return launch_vec_k<8>(X, ldx, W, a, s);
+    return launch_vec_k<16>(X, ldx, W, a, s);
   }
   if (a.M > 65535) return W8A8_ERR_UNSUPPORTED;
   dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps, a.M);

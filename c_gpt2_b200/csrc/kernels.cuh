@@ -72,6 +72,10 @@ int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &
                cudaStream_t stream);
 int gemm_tc_bf16(const uint16_t *W, const uint16_t *X, int64_t ldx, const LinearArgs &a,
                  cudaStream_t stream);
+// gemm_cluster.cu: decode-sized GEMMs (M <= 128) with split-K in a cluster
+bool cluster_gemm_ok(const LinearArgs &a, const void *X, int64_t ldx);
+int gemm_cluster_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,
+                    cudaStream_t stream);
 // gemv_i8.cu
 int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const LinearArgs &a,
                    cudaStream_t s);

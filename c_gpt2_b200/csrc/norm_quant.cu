@@ -570,6 +570,303 @@ __global__ void __launch_bounds__(kRowThreads) reduce_layernorm_quant_kernel(Red
                 a.sXq + row);
 }
 
+// ---------------------------------------------------------------------------
+// Warp-per-row kernels with the row held in registers: no shared memory and
+// no block barriers, so thousands of rows stream at HBM speed (prefill) and a
+// few rows finish in a short dependency chain (decode).
+//
+// Lane l owns the 16-byte vectors v = l + 32k, i.e. elements 8l + e + 256k.
+// The reference's LayerNorm block has 1024 threads; slot s (thread s) sums
+// elements s, s + 1024, ... in order, then the slots are folded pairwise
+// (h = 512 .. 1: slot i += slot i + h). Element 8l + e + 256k lands in slot
+// 8l + e + 256(k mod 4), so lane l owns slots 8l + e + 256m (m < 4): folds
+// h = 512 and 256 are register adds, h = 128 .. 8 shuffle-down steps between
+// lanes (slot 8l + e + h sits in lane l + h/8), h = 4, 2, 1 register adds in
+// lane 0. Every addition is the reference's, in the reference's order.
+// ---------------------------------------------------------------------------
+constexpr int kWarpRows = 4;       // rows (warps) per block
+constexpr int kWarpVec = 8;        // LayerNorm rows up to 8 * 256 = 2048 elements
+constexpr int kWarpQuantVec = 24;  // quantized rows up to 6144 elements
+// Kernels are instantiated for NV = 4, 8 (LayerNorm) and 8, 16, 24 (quant)
+// vectors per lane; a row of n elements uses the smallest NV >= n / 256.
+
+__device__ __forceinline__ float warp_fold1024(float (&s)[4][8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    s[0][e] += s[2][e];  // h = 512
+    s[1][e] += s[3][e];
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s[0][e] += s[1][e];  // h = 256
+#pragma unroll
+  for (int h = 16; h >= 1; h >>= 1) {  // h = 128 .. 8 (lane distance h)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[0][e] += __shfl_down_sync(0xffffffffu, s[0][e], h);
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) s[0][e] += s[0][e + 4];  // h = 4
+#pragma unroll
+  for (int e = 0; e < 2; ++e) s[0][e] += s[0][e + 2];  // h = 2
+  const float total = s[0][0] + s[0][1];                // h = 1
+  return __shfl_sync(0xffffffffu, total, 0);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Quantize the row values a lane holds (vectors l + 32k, k < NV) with the
+// scale of the row's absolute maximum amax (activation_quant.cu:75-91).
+template <int NV>
+__device__ __forceinline__ void warp_quant_store(const uint4 (&y)[NV], int nv, int lane,
+                                                 float amax, int8_t *xq_row, float *sx_out) {
+  const float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+  const float inv = __fdiv_rn(1.0f, scale);
+  if (lane == 0) *sx_out = scale;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int v = lane + 32 * k;
+    if (v < nv) {
+      float f[8];
+      unpack8(y[k], f);
+      uint32_t w[2] = {0u, 0u};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int q = __float2int_rn(__fmul_rn(f[e], inv));
+        q = q > 127 ? 127 : (q < -127 ? -127 : q);
+        w[e >> 2] |= ((uint32_t)(q & 0xff)) << (8 * (e & 3));
+      }
+      *reinterpret_cast<uint2 *>(xq_row + 8 * v) = make_uint2(w[0], w[1]);
+    }
+  }
+}
+
+template <int NV>
+__device__ __forceinline__ float warp_row_amax(const uint4 (&y)[NV], int nv, int lane) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    if (lane + 32 * k < nv) {
+      float f[8];
+      unpack8(y[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(f[e]));
+    }
+  }
+  return warp_max(amax);
+}
+
+template <int NV>
+__device__ __forceinline__ void warp_load_row(const uint16_t *row, int nv, int lane,
+                                              uint4 (&x)[NV]) {
+  const uint4 *src = reinterpret_cast<const uint4 *>(row);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int v = lane + 32 * k;
+    x[k] = v < nv ? __ldg(src + v) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// modes of quant_warp_kernel
+enum { QW_ROW = 0, QW_AMAX_ONLY = 1, QW_GIVEN_AMAX = 2 };
+
+template <int MODE, int NV>
+__global__ void __launch_bounds__(kWarpRows * 32)
+    quant_warp_kernel(const uint16_t *__restrict__ X, int64_t ldx, int M, int K,
+                      const float *__restrict__ amax_in, int n_amax, int64_t amax_stride,
+                      int8_t *__restrict__ Xq, int64_t ldq, float *__restrict__ sX,
+                      float *__restrict__ amax_out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kWarpRows + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const int nv = K >> 3;
+  uint4 x[NV];
+  warp_load_row(X + (int64_t)row * ldx, nv, lane, x);
+  float amax;
+  if (MODE == QW_GIVEN_AMAX) {
+    amax = 0.0f;
+    for (int j = 0; j < n_amax; ++j) amax = fmaxf(amax, __ldcg(amax_in + j * amax_stride + row));
+  } else {
+    amax = warp_row_amax(x, nv, lane);
+  }
+  if (MODE == QW_AMAX_ONLY) {
+    if (lane == 0) amax_out[row] = amax;
+    return;
+  }
+  warp_quant_store(x, nv, lane, amax, Xq + (int64_t)row * ldq, sX + row);
+}
+
+// Arguments of the warp-per-row LayerNorm (+ quant) kernels.
+struct LnWarpArgs {
+  int M, d;
+  const uint16_t *X;  // LN_ROWS: input rows
+  int64_t ldx;
+  const uint16_t *wte, *wpe;  // LN_EMBED: token + position embedding gather
+  const int32_t *tokens;
+  int T;
+  const int32_t *pos0;
+  ReduceArgs red;  // LN_REDUCE: residual from split-K int32 partial sums
+  uint16_t *H;     // residual stream out (LN_EMBED, LN_REDUCE), row stride ldh
+  int64_t ldh;
+  const uint16_t *gamma, *beta;  // NULL: no LayerNorm (LN_REDUCE only)
+  float eps;
+  uint16_t *Y;  // LayerNorm output (optional)
+  int64_t ldy;
+  int8_t *Xq;  // quantized LayerNorm output (optional)
+  int64_t ldq;
+  float *sX;
+};
+
+enum { LN_ROWS = 0, LN_EMBED = 1, LN_REDUCE = 2 };
+
+template <int MODE, int NV>
+__global__ void __launch_bounds__(kWarpRows * 32) layernorm_warp_kernel(LnWarpArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kWarpRows + (threadIdx.x >> 5);
+  if (row >= a.M) return;
+  const int d = a.d, nv = d >> 3;
+  uint4 x[NV];
+  if (MODE == LN_ROWS) {
+    warp_load_row(a.X + (int64_t)row * a.ldx, nv, lane, x);
+  } else if (MODE == LN_EMBED) {
+    // embeddings.cu:18-23: bf16(wte[token] + wpe[position])
+    const int b = row / a.T, tt = row - (row / a.T) * a.T;
+    const int p = (a.pos0 ? a.pos0[b] : 0) + tt;
+    const uint4 *e = reinterpret_cast<const uint4 *>(a.wte + (int64_t)a.tokens[row] * d);
+    const uint4 *q = reinterpret_cast<const uint4 *>(a.wpe + (int64_t)p * d);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int v = lane + 32 * k;
+      x[k] = make_uint4(0, 0, 0, 0);
+      if (v < nv) {
+        float fe[8], fq[8];
+        unpack8(__ldg(e + v), fe);
+        unpack8(__ldg(q + v), fq);
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          w[i] = (uint32_t)f2bf(__fadd_rn(fe[2 * i], fq[2 * i])) |
+                 ((uint32_t)f2bf(__fadd_rn(fe[2 * i + 1], fq[2 * i + 1])) << 16);
+        x[k] = make_uint4(w[0], w[1], w[2], w[3]);
+        if (a.H) reinterpret_cast<uint4 *>(a.H + (int64_t)row * a.ldh)[v] = x[k];
+      }
+    }
+  } else {
+    // H = bf16(R + bf16(bf16(acc*sW*sX) + b)), acc = sum of the int32 partials
+    const ReduceArgs &r = a.red;
+    const float sx = r.sX[row];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int v = lane + 32 * k;
+      x[k] = make_uint4(0, 0, 0, 0);
+      if (v < nv) {
+        int32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < r.n_slots; ++j) {
+          const int4 *src = reinterpret_cast<const int4 *>(r.acc + j * r.slot_stride +
+                                                           (int64_t)row * r.lda) + 2 * v;
+          const int4 lo = __ldcg(src), hi = __ldcg(src + 1);
+          acc[0] += lo.x; acc[1] += lo.y; acc[2] += lo.z; acc[3] += lo.w;
+          acc[4] += hi.x; acc[5] += hi.y; acc[6] += hi.z; acc[7] += hi.w;
+        }
+        const float4 w0 = __ldg(reinterpret_cast<const float4 *>(r.sW) + 2 * v);
+        const float4 w1 = __ldg(reinterpret_cast<const float4 *>(r.sW) + 2 * v + 1);
+        const float sw[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float bf[8], rf[8];
+        unpack8(__ldg(reinterpret_cast<const uint4 *>(r.bias) + v), bf);
+        unpack8(__ldg(reinterpret_cast<const uint4 *>(r.R + (int64_t)row * r.ldr) + v), rf);
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float y0 = add_bf(dequant_bf(acc[2 * i], sw[2 * i], sx), bf[2 * i]);
+          const float y1 = add_bf(dequant_bf(acc[2 * i + 1], sw[2 * i + 1], sx), bf[2 * i + 1]);
+          w[i] = (uint32_t)f2bf(__fadd_rn(rf[2 * i], y0)) |
+                 ((uint32_t)f2bf(__fadd_rn(rf[2 * i + 1], y1)) << 16);
+        }
+        x[k] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4 *>(a.H + (int64_t)row * a.ldh)[v] = x[k];
+      }
+    }
+    if (!a.gamma) return;
+  }
+  // mean (layernorm.cu:25-41)
+  float s[4][8];
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[m][e] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    if (lane + 32 * k < nv) {
+      float f[8];
+      unpack8(x[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s[k & 3][e] += f[e];
+    }
+  }
+  const float mean = warp_fold1024(s) / (float)d;
+  // variance (layernorm.cu:45-66): diff*diff contracted into the running sum
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[m][e] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    if (lane + 32 * k < nv) {
+      float f[8];
+      unpack8(x[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float diff = f[e] - mean;
+        s[k & 3][e] += diff * diff;
+      }
+    }
+  }
+  const float variance = warp_fold1024(s) / (float)d;
+  const float inv_std_dev = rsqrtf(variance + a.eps);
+  // normalise + affine, bf16 (layernorm.cu:73-77)
+  uint4 y[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int v = lane + 32 * k;
+    y[k] = make_uint4(0, 0, 0, 0);
+    if (v < nv) {
+      float f[8], gf[8], bf[8];
+      unpack8(x[k], f);
+      unpack8(__ldg(reinterpret_cast<const uint4 *>(a.gamma) + v), gf);
+      unpack8(__ldg(reinterpret_cast<const uint4 *>(a.beta) + v), bf);
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float n0 = (f[2 * i] - mean) * inv_std_dev;
+        float n1 = (f[2 * i + 1] - mean) * inv_std_dev;
+        w[i] = (uint32_t)f2bf(n0 * gf[2 * i] + bf[2 * i]) |
+               ((uint32_t)f2bf(n1 * gf[2 * i + 1] + bf[2 * i + 1]) << 16);
+      }
+      y[k] = make_uint4(w[0], w[1], w[2], w[3]);
+      if (a.Y) reinterpret_cast<uint4 *>(a.Y + (int64_t)row * a.ldy)[v] = y[k];
+    }
+  }
+  if (a.Xq)
+    warp_quant_store(y, nv, lane, warp_row_amax(y, nv, lane), a.Xq + (int64_t)row * a.ldq,
+                     a.sX + row);
+}
+
+static int warp_grid(int M) { return (M + kWarpRows - 1) / kWarpRows; }
+
+// Below this many rows the block-per-row kernels finish sooner: a decode step
+// has too few rows for one warp per row to spread over the SMs.
+constexpr int kWarpMinRows = 1024;
+
+static bool warp_rows_ok(int n, int max_vec, const void *p, int64_t ld) {
+  return (n & 7) == 0 && n <= 256 * max_vec && aligned16(p) && (ld & 7) == 0;
+}
+
 static bool block_path_ok(int d, const void *a, int64_t lda, const void *b, int64_t ldb) {
   return (d & 7) == 0 && d <= 1024 * kMaxVec && aligned16(a) && (lda & 7) == 0 &&
          (b == nullptr || (aligned16(b) && (ldb & 7) == 0));
@@ -577,8 +874,45 @@ static bool block_path_ok(int d, const void *a, int64_t lda, const void *b, int6
 
 static int row_grid(int M) { return (M + kRowWarps - 1) / kRowWarps; }
 
+template <int MODE>
+static int launch_quant_warp(const uint16_t *X, int64_t ldx, int M, int K, const float *amax_in,
+                             int n_amax, int64_t amax_stride, int8_t *Xq, int64_t ldq, float *sX,
+                             float *amax_out, cudaStream_t s) {
+  const int need = ((K >> 3) + 31) / 32;
+  const dim3 g(warp_grid(M)), b(kWarpRows * 32);
+  if (need <= 8)
+    launch_pdl(quant_warp_kernel<MODE, 8>, g, b, 0, s, X, ldx, M, K, amax_in, n_amax, amax_stride,
+               Xq, ldq, sX, amax_out);
+  else if (need <= 16)
+    launch_pdl(quant_warp_kernel<MODE, 16>, g, b, 0, s, X, ldx, M, K, amax_in, n_amax,
+               amax_stride, Xq, ldq, sX, amax_out);
+  else
+    launch_pdl(quant_warp_kernel<MODE, 24>, g, b, 0, s, X, ldx, M, K, amax_in, n_amax,
+               amax_stride, Xq, ldq, sX, amax_out);
+  return check_launch("quant_warp");
+}
+
+template <int MODE>
+static int launch_ln_warp(const LnWarpArgs &a, cudaStream_t s) {
+  const dim3 g(warp_grid(a.M)), b(kWarpRows * 32);
+  if (a.d <= 256 * 4)
+    launch_pdl(layernorm_warp_kernel<MODE, 4>, g, b, 0, s, a);
+  else
+    launch_pdl(layernorm_warp_kernel<MODE, 8>, g, b, 0, s, a);
+  return check_launch("layernorm_warp");
+}
+
+static bool ln_warp_ok(const LnWarpArgs &a) {
+  return (a.d & 7) == 0 && a.d <= 256 * kWarpVec && aligned16(a.gamma) && aligned16(a.beta) &&
+         (a.Y == nullptr || (aligned16(a.Y) && (a.ldy & 7) == 0)) &&
+         (a.Xq == nullptr || (aligned16(a.Xq) && (a.ldq & 7) == 0)) &&
+         (a.H == nullptr || (aligned16(a.H) && (a.ldh & 7) == 0));
+}
+
 int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, float *sX,
                       cudaStream_t s) {
+  if (M >= kWarpMinRows && warp_rows_ok(K, kWarpQuantVec, X, ldx) && aligned16(Xq))
+    return launch_quant_warp<QW_ROW>(X, ldx, M, K, nullptr, 0, 0, Xq, K, sX, nullptr, s);
   if (block_path_ok(K, X, ldx, Xq, K) && M <= 0x7fffffff) {
     launch_pdl(quant_rows_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, Xq, sX);
     return check_launch("quant_rows_block");
@@ -599,6 +933,23 @@ int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, 
 int launch_layernorm_quant(const uint16_t *X, int64_t ldx, int M, int d, const uint16_t *gamma,
                            const uint16_t *beta, float eps, uint16_t *Y, int64_t ldy, int8_t *Xq,
                            float *sX, cudaStream_t s) {
+  {
+    LnWarpArgs a = {};
+    a.M = M;
+    a.d = d;
+    a.X = X;
+    a.ldx = ldx;
+    a.gamma = gamma;
+    a.beta = beta;
+    a.eps = eps;
+    a.Y = Y;
+    a.ldy = ldy;
+    a.Xq = Xq;
+    a.ldq = d;
+    a.sX = sX;
+    if (M >= kWarpMinRows && ln_warp_ok(a) && aligned16(X) && (ldx & 7) == 0)
+      return launch_ln_warp<LN_ROWS>(a, s);
+  }
   if (block_path_ok(d, X, ldx, Y, Y ? ldy : 0) && aligned16(gamma) && aligned16(beta) &&
       (Xq == nullptr || aligned16(Xq))) {
     launch_pdl(layernorm_block_kernel<0>, dim3(M), dim3(kRowThreads), 0, s, X, ldx, nullptr, nullptr, nullptr, 1,
@@ -625,6 +976,28 @@ int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const
                                  int M, int T, const int32_t *pos0, int d, uint16_t *H,
                                  const uint16_t *gamma, const uint16_t *beta, float eps,
                                  uint16_t *Y, int8_t *Xq, float *sX, cudaStream_t s) {
+  {
+    LnWarpArgs a = {};
+    a.M = M;
+    a.d = d;
+    a.wte = wte;
+    a.wpe = wpe;
+    a.tokens = tokens;
+    a.T = T;
+    a.pos0 = pos0;
+    a.H = H;
+    a.ldh = d;
+    a.gamma = gamma;
+    a.beta = beta;
+    a.eps = eps;
+    a.Y = Y;
+    a.ldy = d;
+    a.Xq = Xq;
+    a.ldq = d;
+    a.sX = sX;
+    if (M >= kWarpMinRows && ln_warp_ok(a) && aligned16(wte) && aligned16(wpe))
+      return launch_ln_warp<LN_EMBED>(a, s);
+  }
   if (block_path_ok(d, wte, d, wpe, d) && aligned16(gamma) && aligned16(beta) &&
       (H == nullptr || aligned16(H)) && (Y == nullptr || aligned16(Y)) &&
       (Xq == nullptr || aligned16(Xq))) {
@@ -648,6 +1021,9 @@ int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const
 }
 
 int launch_row_amax(const uint16_t *X, int64_t ldx, int M, int K, float *amax, cudaStream_t s) {
+  if (M >= kWarpMinRows && warp_rows_ok(K, kWarpQuantVec, X, ldx))
+    return launch_quant_warp<QW_AMAX_ONLY>(X, ldx, M, K, nullptr, 0, 0, nullptr, 0, nullptr, amax,
+                                           s);
   if (!block_path_ok(K, X, ldx, nullptr, 0)) return W8A8_ERR_UNSUPPORTED;
   launch_pdl(row_amax_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, amax);
   return check_launch("row_amax_block");
@@ -656,6 +1032,10 @@ int launch_row_amax(const uint16_t *X, int64_t ldx, int M, int K, float *amax, c
 int launch_quant_rows_amax(const uint16_t *X, int64_t ldx, int M, int K, const float *amax,
                            int n_amax, int64_t amax_stride, int8_t *Xq, int64_t ldq, float *sX,
                            cudaStream_t s) {
+  if (M >= kWarpMinRows && warp_rows_ok(K, kWarpQuantVec, X, ldx) && aligned16(Xq) &&
+      (ldq & 7) == 0)
+    return launch_quant_warp<QW_GIVEN_AMAX>(X, ldx, M, K, amax, n_amax, amax_stride, Xq, ldq, sX,
+                                            nullptr, s);
   if (!block_path_ok(K, X, ldx, Xq, ldq)) return W8A8_ERR_UNSUPPORTED;
   launch_pdl(quant_rows_amax_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, amax,
              n_amax, amax_stride, Xq, ldq, sX);
@@ -670,6 +1050,21 @@ int launch_reduce_layernorm_quant(const ReduceArgs &a, int M, cudaStream_t s) {
   if (a.gamma)
     ok = ok && aligned16(a.gamma) && aligned16(a.beta) && aligned16(a.Xq) && (a.ldq & 7) == 0;
   if (!ok) return W8A8_ERR_UNSUPPORTED;
+  if (M >= kWarpMinRows && d <= 256 * kWarpVec) {
+    LnWarpArgs w = {};
+    w.M = M;
+    w.d = d;
+    w.red = a;
+    w.H = a.H;
+    w.ldh = a.ldh;
+    w.gamma = a.gamma;
+    w.beta = a.beta;
+    w.eps = a.eps;
+    w.Xq = a.Xq;
+    w.ldq = a.ldq;
+    w.sX = a.sXq;
+    return launch_ln_warp<LN_REDUCE>(w, s);
+  }
   launch_pdl(reduce_layernorm_quant_kernel, dim3(M), dim3(kRowThreads), 0, s, a);
   return check_launch("reduce_layernorm_quant");
 }

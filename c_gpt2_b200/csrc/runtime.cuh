@@ -30,11 +30,19 @@ int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, 
 // (W8A8_PDL=0 in the environment turns it off).
 bool pdl_enabled();
 
+// With W8A8_CARVEOUT=1 in the environment, give `func` the largest
+// shared-memory carveout, once per kernel and device, so that an SM never
+// changes its L1/shared split between two kernels (the tensor-core GEMM needs
+// ~200 KB of shared memory per CTA). Off by default: measured slower, since
+// the kernels that stream the KV cache lose their L1.
+void prefer_max_carveout(const void *func);
+
 // Launch `kernel` with programmatic dependent launch allowed: it may begin
 // while the preceding kernel of the stream finishes (see pdl_wait()).
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                              cudaStream_t stream, Args &&...args) {
+  prefer_max_carveout(reinterpret_cast<const void *>(kernel));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;

@@ -5,6 +5,7 @@ size of the large model (d_model 1280, 20 heads, context 1024).
 
     python -m c_gpt2_b200.profcase attention-decode [--batch 64] [--n-ctx 768]
     python -m c_gpt2_b200.profcase attention-prefill [--seqs 64] [--tokens 512]
+    python -m c_gpt2_b200.profcase layernorm-quant [--m 32768] [--d 1280]
     python -m c_gpt2_b200.profcase linear --m 32768 --n 5120 --k 1280 --epi gelu
     python -m c_gpt2_b200.profcase linear --m 64 --n 5120 --k 1280 --epi gelu
 
@@ -28,27 +29,39 @@ EPI = {"dequant": _lib.EPI_DEQUANT, "bias": _lib.EPI_BIAS, "resid": _lib.EPI_BIA
 _FLUSH = None
 
 
-def _time(fn, reps: int) -> float:
-    """Mean microseconds per launch. With --flush every launch is timed alone
-    after a 256 MB write that evicts the 126 MB L2, so weights are read from
-    HBM as in a full model step; otherwise launches run back to back."""
-    if _FLUSH is None:
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+def _graph(fn, reps: int, flush: bool):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
         for _ in range(reps):
-            fn()
-        e1.record()
-        torch.cuda.synchronize()
-        return 1000.0 * e0.elapsed_time(e1) / reps
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(reps)]
-    for e0, e1 in ev:
-        _FLUSH.fill_(1)
-        e0.record()
-        fn()
-        e1.record()
+            if flush:
+                torch.amax(_FLUSH)
+            if fn is not None:
+                fn()
+    return g
+
+
+def _replay_ms(g) -> float:
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g.replay()
     torch.cuda.synchronize()
-    return 1000.0 * sum(e0.elapsed_time(e1) for e0, e1 in ev) / reps
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def _time(fn, reps: int) -> float:
+    """Mean microseconds per launch on the device: the launches are captured
+    in a CUDA graph and replayed, so no host launch overhead falls between
+    them. With --flush every launch follows a 256 MB read that evicts the
+    126 MB L2 (a read leaves no dirty lines to be written back during the
+    launch), and the time of a graph of the reads alone is subtracted."""
+    flush = _FLUSH is not None
+    t = _replay_ms(_graph(fn, reps, flush))
+    if flush:
+        t -= _replay_ms(_graph(None, reps, True))
+    return 1000.0 * t / reps
 
 
 def attention_decode(a) -> None:
@@ -96,6 +109,24 @@ def attention_prefill(a) -> None:
           f"{flops / us / 1e6:.1f} TFLOP/s (causal)")
 
 
+def layernorm_quant(a) -> None:
+    M, d = a.m, a.d
+    g = torch.Generator(device="cuda").manual_seed(0)
+    X = torch.randn((M, d), device="cuda", generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn((d,), device="cuda", generator=g)).to(torch.bfloat16)
+    beta = (0.1 * torch.randn((d,), device="cuda", generator=g)).to(torch.bfloat16)
+
+    def run():
+        ops.layernorm_quant(X, gamma, beta, want_y=False)
+
+    for _ in range(a.launches):
+        run()
+    torch.cuda.synchronize()
+    us = _time(run, a.timed)
+    byts = M * d * 2 + M * d + M * 4
+    print(f"layernorm_quant M={M} d={d}: {us:.2f} us/launch, {byts / us / 1e3:.0f} GB/s")
+
+
 def linear(a) -> None:
     M, N, K = a.m, a.n, a.k
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -136,6 +167,9 @@ def main(argv=None) -> None:
     p.add_argument("--seqs", type=int, default=64)
     p.add_argument("--tokens", type=int, default=512)
     p.add_argument("--heads", type=int, default=20)
+    p = sub.add_parser("layernorm-quant")
+    p.add_argument("--m", type=int, default=32768)
+    p.add_argument("--d", type=int, default=1280)
     p = sub.add_parser("linear")
     p.add_argument("--m", type=int, required=True)
     p.add_argument("--n", type=int, required=True)
@@ -149,9 +183,9 @@ def main(argv=None) -> None:
     ops.init(0)
     if a.flush:
         global _FLUSH
-        _FLUSH = torch.empty((256 << 20,), dtype=torch.uint8, device="cuda")
+        _FLUSH = torch.ones((64 << 20,), dtype=torch.float32, device="cuda")
     {"attention-decode": attention_decode, "attention-prefill": attention_prefill,
-     "linear": linear}[a.case](a)
+     "layernorm-quant": layernorm_quant, "linear": linear}[a.case](a)
     st = ops.device_error()
     if st:
         raise SystemExit(f"device error word {st}")

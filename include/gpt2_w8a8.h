@@ -12,6 +12,13 @@
  * reference's quant8.bin holds them (tools/offline_quant/src/quantizer.py:3-4),
  * so X[M,K] · W[N,K]^T needs no transpose.
  *
+ * Kernels are launched with programmatic dependent launch: a GEMM or GEMV
+ * starts reading its weight matrix W before the preceding
+ * kernel of the stream has finished, and reads everything else only after.
+ * W must therefore not be written by the kernel launched just before the call
+ * on the same stream (a copy, an event wait or W8A8_PDL=0 in the environment
+ * orders it fully).
+ *
  * Every entry point returns W8A8_OK (0) or a negative status; nothing aborts.
  * The reference-shaped drop-in functions (include/cuda_kernels.h) wrap these
  * and keep the reference's abort-on-error convention.

@@ -264,3 +264,55 @@ def test_rejects_bad_arguments(cuda):
     q = torch.zeros((4, 64), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(_lib.W8A8Error):  # max_ctx beyond the 1024-row cache
         ops.attention_decode(q, q, q, 0, None, 2048, 1)
+
+
+# Row counts >= 1024 take the warp-per-row kernels (row in registers), fewer
+# rows the block-per-row kernels: both must produce identical bits.
+WARP_M = 1536
+
+
+def _chunks(M, step=512):
+    return [(i, min(M, i + step)) for i in range(0, M, step)]
+
+
+@pytest.mark.parametrize("d", [768, 1024, 1280, 2000])
+def test_layernorm_warp_rows_equal_block_rows(cuda, d):
+    rng = np.random.default_rng(d)
+    X = to_dev_bf16(_rand_bf16(rng, (WARP_M, d), 2.0))
+    g = to_dev_bf16(oracle.bf16_bits(rng.uniform(0.5, 1.5, d).astype(np.float32)))
+    b = to_dev_bf16(_rand_bf16(rng, (d,), 0.1))
+    Y, Xq, sX = ops.layernorm_quant(X, g, b)
+    for i, j in _chunks(WARP_M):
+        y, q, s = ops.layernorm_quant(X[i:j], g, b)
+        assert torch.equal(Y[i:j], y) and torch.equal(Xq[i:j], q) and torch.equal(sX[i:j], s)
+
+
+@pytest.mark.parametrize("K", [768, 1280, 5120])
+def test_quant_warp_rows_equal_block_rows(cuda, K):
+    X = to_dev_bf16(oracle.bf16_bits(outlier_activations(WARP_M, K, seed=K)))
+    Xq, sX = ops.per_token_quant(X)
+    amax = ops.row_amax(X)
+    Xq2, sX2 = ops.quant_rows_amax(X, amax)
+    assert torch.equal(Xq, Xq2) and torch.equal(sX, sX2)
+    for i, j in _chunks(WARP_M):
+        q, s = ops.per_token_quant(X[i:j])
+        assert torch.equal(Xq[i:j], q) and torch.equal(sX[i:j], s)
+        assert torch.equal(amax[i:j], ops.row_amax(X[i:j]))
+
+
+def test_embed_layernorm_warp_rows_equal_block_rows(cuda):
+    rng = np.random.default_rng(9)
+    V, C, d, B, T = 500, 1024, 1280, 3, 512
+    wte = to_dev_bf16(_rand_bf16(rng, (V, d), 0.02))
+    wpe = to_dev_bf16(_rand_bf16(rng, (C, d), 0.02))
+    g = to_dev_bf16(oracle.bf16_bits(rng.uniform(0.5, 1.5, d).astype(np.float32)))
+    b = to_dev_bf16(_rand_bf16(rng, (d,), 0.1))
+    toks = to_dev(rng.integers(0, V, B * T).astype(np.int32))
+    pos0 = to_dev(np.array([0, 100, 512], np.int32))
+    H, Y, Xq, sX = ops.embed_layernorm_quant(wte, wpe, toks, T, pos0, g, b)
+    for s in range(B):
+        h, y, q, sx = ops.embed_layernorm_quant(wte, wpe, toks[s * T:(s + 1) * T], T,
+                                                pos0[s:s + 1], g, b)
+        r = slice(s * T, (s + 1) * T)
+        assert torch.equal(H[r], h) and torch.equal(Y[r], y)
+        assert torch.equal(Xq[r], q) and torch.equal(sX[r], sx)

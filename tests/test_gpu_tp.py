@@ -133,3 +133,30 @@ def test_tp_two_ranks_match_engine(cuda, large2_image, tmp_path):
         np.testing.assert_array_equal(np.load(tmp_path / f"next{r}.npy"), want_next)
     bits = np.concatenate([np.load(tmp_path / f"logits{r}.npy") for r in range(2)])
     np.testing.assert_array_equal((bits.astype(np.uint32) << 16).view(np.float32), want_logits)
+
+
+def test_reduce_warp_rows_equal_block_rows(cuda):
+    """Row counts >= 1024 take the warp-per-row kernel, fewer rows the
+    block-per-row kernel: identical bits."""
+    M, d, slots = 1536, 1280, 2
+    g = torch.Generator(device="cuda").manual_seed(1)
+    acc = torch.randint(-2 ** 24, 2 ** 24, (slots, M, d), dtype=torch.int32, device=cuda,
+                        generator=g)
+    sX = torch.rand((M,), device=cuda, generator=g) * 1e-2 + 1e-4
+    sW = torch.rand((d,), device=cuda, generator=g) * 1e-2 + 1e-4
+    b = (torch.randn((d,), device=cuda, generator=g) * 0.02).to(torch.bfloat16)
+    R = torch.randn((M, d), device=cuda, generator=g).to(torch.bfloat16)
+    gam = (1 + 0.1 * torch.randn((d,), device=cuda, generator=g)).to(torch.bfloat16)
+    bet = (0.1 * torch.randn((d,), device=cuda, generator=g)).to(torch.bfloat16)
+    H = torch.empty_like(R)
+    q = torch.empty((M, d), dtype=torch.int8, device=cuda)
+    s = torch.empty((M,), dtype=torch.float32, device=cuda)
+    ops.reduce_residual_layernorm_quant(acc, sX, sW, b, R, H, gam, bet, 1e-5, q, s)
+    for i in range(0, M, 512):
+        j = i + 512
+        h = torch.empty_like(R[i:j])
+        q2 = torch.empty_like(q[i:j])
+        s2 = torch.empty_like(s[i:j])
+        ops.reduce_residual_layernorm_quant(acc[:, i:j], sX[i:j], sW, b, R[i:j], h, gam, bet,
+                                            1e-5, q2, s2)
+        assert torch.equal(H[i:j], h) and torch.equal(q[i:j], q2) and torch.equal(s[i:j], s2)
