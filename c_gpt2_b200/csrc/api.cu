@@ -253,22 +253,52 @@ extern "C" size_t w8a8_attention_decode_workspace_size(int n_seq, int n_head, in
   return decode_workspace_bytes(n_seq, n_head, max_ctx, splits);
 }
 
-extern "C" int w8a8_attention_decode(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,
-                                     const gpt2_bf16_t *Vc, int64_t seq_stride, int n_seq,
-                                     const int32_t *n_ctx, int max_ctx, int n_head, int head_dim,
-                                     gpt2_bf16_t *O, int64_t ldo, void *workspace,
-                                     size_t workspace_bytes, void *stream) {
+extern "C" int w8a8_attention_decode_launches(int n_seq, int n_head, int max_ctx) {
+  int st;
+  DeviceCtx *c = device_ctx(&st);
+  if (!c || n_seq <= 0 || n_head <= 0 || max_ctx <= 0) return 0;
+  return decode_launches(n_seq, n_head, max_ctx, c->sm_count);
+}
+
+static int attention_decode_impl(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,
+                                 const gpt2_bf16_t *Vc, int64_t seq_stride, int n_seq,
+                                 const int32_t *n_ctx, int max_ctx, int n_head, int head_dim,
+                                 gpt2_bf16_t *O, int64_t ldo, int8_t *Xq, float *sXq,
+                                 void *workspace, size_t workspace_bytes, void *stream) {
   if (n_seq == 0) return W8A8_OK;
   if (!Q || !Kc || !Vc || !O || !workspace || n_seq < 0 || n_head <= 0 || max_ctx <= 0)
     return W8A8_ERR_INVALID;
   if (head_dim != 64 || max_ctx > 1024) return W8A8_ERR_UNSUPPORTED;
   if (ldq % 8 || seq_stride % 8 || !aligned16(Q) || !aligned16(Kc) || !aligned16(Vc))
     return W8A8_ERR_INVALID;
+  if (Xq && (!sXq || ldo % 8 || !aligned16(O) || ((uintptr_t)Xq & 7))) return W8A8_ERR_INVALID;
   int st;
   DeviceCtx *c = device_ctx(&st);
   if (!c) return st;
   return launch_attention_decode(Q, ldq, Kc, Vc, seq_stride, n_seq, n_ctx, max_ctx, n_head, O, ldo,
-                                 workspace, workspace_bytes, c->sm_count, (cudaStream_t)stream);
+                                 Xq, sXq, workspace, workspace_bytes, c->sm_count,
+                                 (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_attention_decode(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,
+                                     const gpt2_bf16_t *Vc, int64_t seq_stride, int n_seq,
+                                     const int32_t *n_ctx, int max_ctx, int n_head, int head_dim,
+                                     gpt2_bf16_t *O, int64_t ldo, void *workspace,
+                                     size_t workspace_bytes, void *stream) {
+  return attention_decode_impl(Q, ldq, Kc, Vc, seq_stride, n_seq, n_ctx, max_ctx, n_head,
+                               head_dim, O, ldo, nullptr, nullptr, workspace, workspace_bytes,
+                               stream);
+}
+
+extern "C" int w8a8_attention_decode_quant(const gpt2_bf16_t *Q, int64_t ldq,
+                                           const gpt2_bf16_t *Kc, const gpt2_bf16_t *Vc,
+                                           int64_t seq_stride, int n_seq, const int32_t *n_ctx,
+                                           int max_ctx, int n_head, int head_dim, gpt2_bf16_t *O,
+                                           int64_t ldo, int8_t *Xq, float *sX, void *workspace,
+                                           size_t workspace_bytes, void *stream) {
+  if (!Xq || !sX) return W8A8_ERR_INVALID;
+  return attention_decode_impl(Q, ldq, Kc, Vc, seq_stride, n_seq, n_ctx, max_ctx, n_head,
+                               head_dim, O, ldo, Xq, sX, workspace, workspace_bytes, stream);
 }
 
 extern "C" int w8a8_lm_head(const gpt2_bf16_t *Xf, int64_t ldx, int M, int d,

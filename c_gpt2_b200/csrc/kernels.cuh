@@ -99,11 +99,12 @@ int launch_attention_prefill(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
                              const uint16_t *Vc, int64_t seq_stride, int n_seq, int T, int n_head,
                              uint16_t *O, int64_t ldo, cudaStream_t s);
 size_t decode_workspace_bytes(int n_seq, int n_head, int max_ctx, int splits);
+int decode_launches(int n_seq, int n_head, int max_ctx, int sm_count);
 int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
                             const uint16_t *Vc, int64_t seq_stride, int n_seq,
                             const int32_t *n_ctx, int max_ctx, int n_head, uint16_t *O,
-                            int64_t ldo, void *ws, size_t ws_bytes, int sm_count,
-                            cudaStream_t s);
+                            int64_t ldo, int8_t *Xq, float *sXq, void *ws, size_t ws_bytes,
+                            int sm_count, cudaStream_t s);
 // sample.cu
 int launch_greedy_sample(const uint16_t *logits, int64_t ldl, int M, int V, int32_t *out,
                          int32_t *append_to, int64_t append_stride, int32_t *append_pos,

@@ -401,10 +401,11 @@ static int block_forward(gpt2_engine *e, int l, int B, int T, const int32_t *pos
                             seq_stride, T, pos0, e->lin_ws, e->lin_ws_bytes, s));
   if (pos0 == NULL)
     W8_TRY(e, w8a8_attention_prefill(e->Q, d, Kl, Vl, seq_stride, B, T, Hh, 64, e->ATT, d, s));
-  else
-    W8_TRY(e, w8a8_attention_decode(e->Q, d, Kl, Vl, seq_stride, B, e->nctx, c->ctx, Hh, 64,
-                                    e->ATT, d, e->attn_ws, e->attn_ws_bytes, s));
-  W8_TRY(e, w8a8_quant_rows(e->ATT, d, M, d, e->Xq, e->sX, s));
+  else  /* decode: the attention kernel also quantizes its output rows */
+    W8_TRY(e, w8a8_attention_decode_quant(e->Q, d, Kl, Vl, seq_stride, B, e->nctx, c->ctx, Hh, 64,
+                                          e->ATT, d, e->Xq, e->sX, e->attn_ws, e->attn_ws_bytes,
+                                          s));
+  if (pos0 == NULL) W8_TRY(e, w8a8_quant_rows(e->ATT, d, M, d, e->Xq, e->sX, s));
   W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, d, w->Wproj, w->sWproj, w->bproj, d, W8A8_EPI_BIAS_RESID,
                         e->H, d, e->R1, d, e->lin_ws, e->lin_ws_bytes, s));
   W8_TRY(e, w8a8_layernorm_quant(e->R1, d, M, d, w->ln2_g, w->ln2_b, eps, NULL, 0, e->Xq, e->sX, s));
@@ -441,11 +442,13 @@ static int model_forward(gpt2_engine *e, const int32_t *tokens_d, int B, int T,
 }
 
 int gpt2_engine_launches_per_decode_step(const gpt2_engine *e) {
-  /* embed+LN1, 9 per block minus the fused first LN1, nctx, final LN, LM
-   * head, sample, len advance (+ the attention's second kernel and ticket
-   * reset per block) */
+  /* embed+LN1; per block LN1 (not in the first), QKV, attention (one or two
+   * kernels, output quantization fused), attn_proj, LN2, W1, quant, W2; then
+   * nctx, final LN, LM head, sample, len advance */
   if (!e) return 0;
-  return 1 + e->cfg.n_layer * 10 - 1 + 1 + 3 + 1;
+  const int attn = w8a8_attention_decode_launches(e->B > 0 ? e->B : e->cfg.max_batch,
+                                                  e->cfg.n_head, e->cfg.ctx);
+  return 1 + e->cfg.n_layer * (7 + attn) - 1 + 1 + 3 + 1;
 }
 
 int gpt2_engine_launches_per_prefill(const gpt2_engine *e) {

@@ -197,6 +197,23 @@ def attention_decode(Q, Kc, Vc, seq_stride, n_ctx, max_ctx, n_head, out=None, wo
     return O
 
 
+def attention_decode_quant(Q, Kc, Vc, seq_stride, n_ctx, max_ctx, n_head, workspace, out=None):
+    """attention_decode + per-token quantization of each sequence's output
+    row in the same launch. `workspace` must start zero-filled (it is left so).
+    Returns (O, Xq, sX)."""
+    n_seq = Q.shape[0]
+    d = n_head * 64
+    O = out if out is not None else torch.empty((n_seq, d), dtype=torch.bfloat16, device=Q.device)
+    Xq = torch.empty((n_seq, d), dtype=torch.int8, device=Q.device)
+    sX = torch.empty((n_seq,), dtype=torch.float32, device=Q.device)
+    check(core().w8a8_attention_decode_quant(_ptr(Q), Q.stride(0), _ptr(Kc), _ptr(Vc), seq_stride,
+                                             n_seq, _ptr(n_ctx), max_ctx, n_head, 64, _ptr(O),
+                                             O.stride(0), _ptr(Xq), _ptr(sX), _ptr(workspace),
+                                             workspace.numel(), _stream()),
+          "w8a8_attention_decode_quant")
+    return O, Xq, sX
+
+
 def lm_head(Xf, wte):
     M, d = Xf.shape
     V = wte.shape[0]

@@ -8,6 +8,7 @@ size of the large model (d_model 1280, 20 heads, context 1024).
     python -m c_gpt2_b200.profcase layernorm-quant [--m 32768] [--d 1280]
     python -m c_gpt2_b200.profcase linear --m 32768 --n 5120 --k 1280 --epi gelu
     python -m c_gpt2_b200.profcase linear --m 64 --n 5120 --k 1280 --epi gelu
+    python -m c_gpt2_b200.profcase decode [--model medium] [--batch 1] [--prompt 512] [--gen 256]
 
 Every case holds well under 1 GB on the device and exceeds the 126 MB L2 only
 where the workload itself does (the attention KV cache, the prefill
@@ -155,6 +156,39 @@ def linear(a) -> None:
           f"{ops_ / us / 1e6:.0f} TOP/s, {byts / us / 1e3:.0f} GB/s algorithmic")
 
 
+def decode(a) -> None:
+    """Whole greedy decode steps of the engine (CUDA-graph replays): per-step
+    time and the bytes a step must read (int8 weights + bf16 LM head + the KV
+    cache at the mean context), i.e. the HBM roofline of batched decode."""
+    from .engine import Engine
+    from .quant8 import DIMS
+    from .synthetic import prompts, quant8_image_gpu
+    dims = DIMS[a.model]
+    B, T, G = a.batch, a.prompt, a.gen
+    eng = Engine(dims, max_batch=B, max_tokens=B * T)
+    eng.load_quant8(quant8_image_gpu(dims, 0, "cuda"))
+    P = torch.from_numpy(prompts(B, T, dims.vocab, 0)).cuda()
+    out = torch.empty((B, G), dtype=torch.int32, device="cuda")
+    s = torch.cuda.ExternalStream(eng.stream_handle)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for _ in range(2):  # the first pass builds the decode graph
+        e[0].record(s)
+        eng.prefill(P, out, G)
+        e[1].record(s)
+        eng.decode_steps(G - 1)
+        e[2].record(s)
+        torch.cuda.synchronize()
+    pre_ms, dec_ms = e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2])
+    d, L = dims.d_model, dims.n_layer
+    w_bytes = L * 12 * d * d + dims.vocab * d * 2
+    kv_bytes = L * B * 2 * (T + G / 2) * d * 2
+    us = 1000.0 * dec_ms / (G - 1)
+    gbs = (w_bytes + kv_bytes) / us / 1e3
+    print(f"decode {a.model} batch {B}, prompt {T}, {G} tokens: prefill {pre_ms:.2f} ms, "
+          f"{us:.1f} us/step ({B / us * 1e6:.0f} tok/s); bytes/step {(w_bytes + kv_bytes) / 1e6:.0f}"
+          f" MB -> {gbs:.0f} GB/s")
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     sub = ap.add_subparsers(dest="case", required=True)
@@ -170,6 +204,11 @@ def main(argv=None) -> None:
     p = sub.add_parser("layernorm-quant")
     p.add_argument("--m", type=int, default=32768)
     p.add_argument("--d", type=int, default=1280)
+    p = sub.add_parser("decode")
+    p.add_argument("--model", choices=["small", "medium", "large"], default="medium")
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--gen", type=int, default=256)
     p = sub.add_parser("linear")
     p.add_argument("--m", type=int, required=True)
     p.add_argument("--n", type=int, required=True)
@@ -185,7 +224,7 @@ def main(argv=None) -> None:
         global _FLUSH
         _FLUSH = torch.ones((64 << 20,), dtype=torch.float32, device="cuda")
     {"attention-decode": attention_decode, "attention-prefill": attention_prefill,
-     "layernorm-quant": layernorm_quant, "linear": linear}[a.case](a)
+     "layernorm-quant": layernorm_quant, "linear": linear, "decode": decode}[a.case](a)
     st = ops.device_error()
     if st:
         raise SystemExit(f"device error word {st}")

@@ -163,6 +163,23 @@ int w8a8_attention_decode(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *
                           gpt2_bf16_t *O, int64_t ldo, void *workspace,
                           size_t workspace_bytes, void *stream);
 
+/* Kernels one w8a8_attention_decode(_quant) call launches for this shape:
+ * 1 (one CTA per sequence and head) or 2 (keys split over CTAs). */
+int w8a8_attention_decode_launches(int n_seq, int n_head, int max_ctx);
+
+/* w8a8_attention_decode fused with the per-token quantization that feeds the
+ * attention projection (gpt2.c:1235, per_token_quant_cuda on the concatenated
+ * heads): besides O, writes Xq [n_seq][n_head*64] int8 and sX [n_seq] exactly
+ * as w8a8_quant_rows(O) would. The CTA that finishes the last head of a
+ * sequence quantizes that sequence's row, so no second launch is needed. The
+ * workspace must be zero-filled before its first use; every call leaves it
+ * so. */
+int w8a8_attention_decode_quant(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,
+                                const gpt2_bf16_t *Vc, int64_t seq_stride, int n_seq,
+                                const int32_t *n_ctx, int max_ctx, int n_head, int hd,
+                                gpt2_bf16_t *O, int64_t ldo, int8_t *Xq, float *sX,
+                                void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- LM head (gpt2.c:2160): logits[M,V] = bf16(Xf[M,d] · wte[V,d]^T), fp32
  * accumulation. wte is used as stored ([vocab, d], K-major); the reference's
  * host transpose wte_T (gpt2.c:1915-1918) is not needed. */

@@ -229,6 +229,27 @@ def test_attention_decode(cuda, n_seq, H, lens):
         _attn_tolerance(got[s:s + 1], want)
 
 
+@pytest.mark.parametrize("n_seq,H", [(64, 20), (2, 20), (5, 12)])
+def test_attention_decode_quant_fused(cuda, n_seq, H):
+    """The fused output quantization equals quant_rows of the same output, on
+    two calls in a row (the per-sequence tickets must come back to zero), for
+    both the one-kernel (many sequences) and the split-key path."""
+    rng = np.random.default_rng(n_seq + H)
+    C, d = 1024, 64 * H
+    K = to_dev_bf16(_rand_bf16(rng, (n_seq, C, d)))
+    V = to_dev_bf16(_rand_bf16(rng, (n_seq, C, d)))
+    q = to_dev_bf16(_rand_bf16(rng, (n_seq, d)))
+    n_ctx = to_dev(rng.integers(1, C + 1, n_seq).astype(np.int32))
+    ws = torch.zeros((_lib.core().w8a8_attention_decode_workspace_size(n_seq, H, C),),
+                     dtype=torch.uint8, device=cuda)
+    want = ops.attention_decode(q, K, V, C * d, n_ctx, C, H, workspace=ws)
+    want_q, want_s = ops.per_token_quant(want)
+    for _ in range(2):
+        O, Xq, sX = ops.attention_decode_quant(q, K, V, C * d, n_ctx, C, H, ws)
+        assert torch.equal(O, want)
+        assert torch.equal(Xq, want_q) and torch.equal(sX, want_s)
+
+
 @pytest.mark.parametrize("M", [1, 3, 16, 64])
 def test_lm_head_and_greedy(cuda, M):
     rng = np.random.default_rng(M)
