@@ -320,6 +320,11 @@ struct DecodeArgs {
   uint16_t *scores;   // [n_seq][n_head][max_ctx]
   float *partials;    // [n_seq][n_head][splits][64]
   int *tickets;       // [n_seq][n_head]
+  // optional fused per-token quantization of each sequence's whole output
+  // row (all heads): the last (b, h) of sequence b to finish quantizes O[b]
+  int8_t *Xq;         // [n_seq][d], NULL: no quantization
+  float *sXq;         // [n_seq]
+  int *seq_tickets;   // [n_seq], zero between calls
 };
 
 // q row of (b, h) in registers: lane part p holds dims 8p .. 8p+7.
@@ -372,25 +377,34 @@ __device__ __forceinline__ void score_keys(const DecodeArgs &a, int b, int h, in
 }
 
 // Softmax statistics of a full score row (n entries, bf16) with the
-// reference's 256-slot tree (256 threads): returns (max, 1/sum).
-template <typename Load>
+// reference's 256-slot tree: slot t adds e_j for j = t, t + 256, ... in
+// order, then the slots fold pairwise (s = 128 .. 1). With NT = 128 threads,
+// thread t owns slots t and t + 128 (the first fold is its own addition).
+// Returns (max, 1/sum).
+template <int NT, typename Load>
 __device__ __forceinline__ void row_stats(int n, int tid, Load ld, float *s_red, float *s_tree,
                                           float &mx_out, float &inv_out) {
+  static_assert(NT == 128 || NT == 256, "row_stats: 128 or 256 threads");
   const int warp = tid >> 5, lane = tid & 31;
   float mx = -INFINITY;
-  for (int j = tid; j < n; j += 256) mx = fmaxf(mx, bf2f(ld(j)));
+  for (int j = tid; j < n; j += NT) mx = fmaxf(mx, bf2f(ld(j)));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) s_red[warp] = mx;
   __syncthreads();
   mx = s_red[0];
 #pragma unroll
-  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_red[w]);
+  for (int w = 1; w < NT / 32; ++w) mx = fmaxf(mx, s_red[w]);
   float local_sum = 0.0f;
   for (int j = tid; j < n; j += 256) local_sum += expf(bf2f(ld(j)) - mx);
+  if (NT == 128) {
+    float hi_sum = 0.0f;
+    for (int j = tid + 128; j < n; j += 256) hi_sum += expf(bf2f(ld(j)) - mx);
+    local_sum += hi_sum;  // fold s = 128: slot t += slot t + 128
+  }
   s_tree[tid] = local_sum;
   __syncthreads();
-  for (int s = 128; s > 0; s >>= 1) {
+  for (int s = (NT == 128 ? 64 : 128); s > 0; s >>= 1) {
     if (tid < s) s_tree[tid] += s_tree[tid + s];
     __syncthreads();
   }
@@ -398,9 +412,10 @@ __device__ __forceinline__ void row_stats(int n, int tid, Load ld, float *s_red,
   inv_out = 1.0f / s_tree[0];
 }
 
-// Partial O = sum_{j in [j0, j1)} P_j V_j over 256 threads: 8 lanes per
+// Partial O = sum_{j in [j0, j1)} P_j V_j over NT threads: 8 lanes per
 // 128-byte V row (8 dims each), 4 rows per warp step, 4 steps in flight.
 // Returns this thread's share for dim `tid` (< 64) after the block reduction.
+template <int NT>
 __device__ __forceinline__ float pv_range(const DecodeArgs &a, int b, int h, int j0, int j1,
                                           const float *p, float (*s_part)[kHD], int tid) {
   const int warp = tid >> 5, lane = tid & 31;
@@ -410,17 +425,18 @@ __device__ __forceinline__ float pv_range(const DecodeArgs &a, int b, int h, int
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   const uint16_t *Vb = a.Vc + (int64_t)b * a.seq_stride + h * kHD + part * 8;
   constexpr int U = 4;
-  for (int jb = j0 + warp * 4 + sub; jb < j1; jb += 32 * U) {
+  constexpr int kRows = NT / 8;  // V rows per step over the block
+  for (int jb = j0 + warp * 4 + sub; jb < j1; jb += kRows * U) {
     uint4 vv[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = jb + 32 * u;
+      const int j = jb + kRows * u;
       vv[u] = j < j1 ? __ldg(reinterpret_cast<const uint4 *>(Vb + (int64_t)j * a.d))
                      : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = jb + 32 * u;
+      const int j = jb + kRows * u;
       const float pj = j < j1 ? p[j - j0] : 0.f;
       const uint32_t w[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
 #pragma unroll
@@ -443,9 +459,63 @@ __device__ __forceinline__ float pv_range(const DecodeArgs &a, int b, int h, int
   float o = 0.f;
   if (tid < kHD) {
 #pragma unroll
-    for (int w = 0; w < 8; ++w) o += s_part[w][tid];
+    for (int w = 0; w < NT / 32; ++w) o += s_part[w][tid];
   }
   return o;
+}
+
+// Per-token quantization (activation_quant.cu:75-91) of sequence b's whole
+// output row O[b, 0:d) once its last head is written: the CTA that finishes
+// the last (b, h) of the sequence (ticket counter, no waiting) reads the row
+// back from L2 and writes Xq[b], sXq[b]. Identical to w8a8_quant_rows.
+template <int NT>
+__device__ __forceinline__ void quant_row_when_complete(const DecodeArgs &a, int b, int tid,
+                                                        float *s_red, int *s_flag) {
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) *s_flag = (atomicAdd(&a.seq_tickets[b], 1) == a.n_head - 1);
+  __syncthreads();
+  if (!*s_flag) return;
+  __threadfence();
+  const uint16_t *row = a.O + (int64_t)b * a.ldo;
+  const int nv = a.d >> 3;
+  float m = 0.0f;
+  for (int v = tid; v < nv; v += NT) {
+    const uint4 x = __ldcg(reinterpret_cast<const uint4 *>(row) + v);
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      m = fmaxf(m, fabsf(__uint_as_float(w[i] << 16)));
+      m = fmaxf(m, fabsf(__uint_as_float(w[i] & 0xffff0000u)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((tid & 31) == 0) s_red[tid >> 5] = m;
+  __syncthreads();
+  m = s_red[0];
+#pragma unroll
+  for (int w = 1; w < NT / 32; ++w) m = fmaxf(m, s_red[w]);
+  const float scale = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+  const float inv = __fdiv_rn(1.0f, scale);
+  if (tid == 0) {
+    a.sXq[b] = scale;
+    a.seq_tickets[b] = 0;  // ready for the next call
+  }
+  for (int v = tid; v < nv; v += NT) {
+    const uint4 x = __ldcg(reinterpret_cast<const uint4 *>(row) + v);
+    const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+    uint32_t q8[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float f = (e & 1) ? __uint_as_float(w[e >> 1] & 0xffff0000u)
+                              : __uint_as_float(w[e >> 1] << 16);
+      int q = __float2int_rn(__fmul_rn(f, inv));
+      q = q > 127 ? 127 : (q < -127 ? -127 : q);
+      q8[e >> 2] |= ((uint32_t)(q & 0xff)) << (8 * (e & 3));
+    }
+    *reinterpret_cast<uint2 *>(a.Xq + (int64_t)b * a.d + 8 * v) = make_uint2(q8[0], q8[1]);
+  }
 }
 
 // Split path, kernel 1: this split's scores into the workspace row.
@@ -482,13 +552,14 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
   const int tid = threadIdx.x;
   const uint16_t *srow = a.scores + ((int64_t)b * a.n_head + h) * a.max_ctx;
   float mx, inv_sum;
-  row_stats(n, tid, [&](int j) { return srow[j]; }, s_red, s_tree, mx, inv_sum);
+  row_stats<256>(n, tid, [&](int j) { return srow[j]; }, s_red, s_tree, mx, inv_sum);
   for (int j = j0 + tid; j < j1; j += 256)
     s_p[j - j0] = bf2f(f2bf(bf2f(f2bf(expf(bf2f(srow[j]) - mx))) * inv_sum));
   __syncthreads();
-  const float o = pv_range(a, b, h, j0, j1, s_p, s_part, tid);
+  const float o = pv_range<256>(a, b, h, j0, j1, s_p, s_part, tid);
   if (a.splits == 1) {
     if (tid < kHD) a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(o);
+    if (a.Xq) quant_row_when_complete<256>(a, b, tid, s_red, &s_last);
     return;
   }
   float *part_out = a.partials + (((int64_t)b * a.n_head + h) * a.splits + split) * kHD;
@@ -509,32 +580,40 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
     a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(tot);
   }
   if (tid == 0) a.tickets[b * a.n_head + h] = 0;  // ready for the next call
+  if (a.Xq) quant_row_when_complete<256>(a, b, tid, s_red, &s_last);
 }
 
-// Whole-row path (enough (b, h) pairs to fill the GPU): one CTA per (b, h)
-// keeps the scores in shared memory, so K and V are each read once and the
-// call is one launch.
-__global__ void __launch_bounds__(256) attention_decode_fused_kernel(DecodeArgs a) {
+// Whole-row path (enough (b, h) pairs to fill the GPU): one CTA of 128
+// threads per (b, h) keeps the scores in shared memory, so K and V are each
+// read once and the call is one launch. Small CTAs (48 registers, ~8 KB of
+// shared memory) let ten of them share an SM, so a 64-sequence batch of
+// GPT-2 large (1280 pairs) runs as a single wave.
+constexpr int kFusedThreads = 128;
+
+__global__ void __launch_bounds__(kFusedThreads) attention_decode_fused_kernel(DecodeArgs a) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float s_red[8];
-  __shared__ float s_tree[256];
-  __shared__ float s_part[8][kHD];
+  constexpr int NT = kFusedThreads;
+  __shared__ float s_red[NT / 32];
+  __shared__ float s_tree[NT];
+  __shared__ float s_part[NT / 32][kHD];
   __shared__ float s_p[1024];
   __shared__ uint16_t s_s[1024];
+  __shared__ int s_flag;
   const int bh = blockIdx.x;
   const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
   const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
   const int tid = threadIdx.x;
-  score_keys(a, b, h, 0, n, tid >> 5, 8, tid & 31, [&](int j, uint16_t s) { s_s[j] = s; });
+  score_keys(a, b, h, 0, n, tid >> 5, NT / 32, tid & 31, [&](int j, uint16_t s) { s_s[j] = s; });
   __syncthreads();
   float mx, inv_sum;
-  row_stats(n, tid, [&](int j) { return s_s[j]; }, s_red, s_tree, mx, inv_sum);
-  for (int j = tid; j < n; j += 256)
+  row_stats<NT>(n, tid, [&](int j) { return s_s[j]; }, s_red, s_tree, mx, inv_sum);
+  for (int j = tid; j < n; j += NT)
     s_p[j] = bf2f(f2bf(bf2f(f2bf(expf(bf2f(s_s[j]) - mx))) * inv_sum));
   __syncthreads();
-  const float o = pv_range(a, b, h, 0, n, s_p, s_part, tid);
+  const float o = pv_range<NT>(a, b, h, 0, n, s_p, s_part, tid);
   if (tid < kHD) a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(o);
+  if (a.Xq) quant_row_when_complete<NT>(a, b, tid, s_red, &s_flag);
 }
 
 static int decode_splits(int n_seq, int n_head, int max_ctx, int sm_count) {
@@ -544,19 +623,30 @@ static int decode_splits(int n_seq, int n_head, int max_ctx, int sm_count) {
   return splits;
 }
 
+// Per-sequence tickets of the fused output quantization live in the last
+// kSeqTicketBytes of the caller's workspace: a fixed place for a given
+// buffer whatever the shape of the call, so that they stay zero between calls
+// that use the buffer for different batch sizes.
+constexpr int kMaxSeqTickets = 4096;
+constexpr size_t kSeqTicketBytes = kMaxSeqTickets * sizeof(int);
+
+int decode_launches(int n_seq, int n_head, int max_ctx, int sm_count) {
+  return decode_splits(n_seq, n_head, max_ctx, sm_count) == 1 ? 1 : 2;
+}
+
 size_t decode_workspace_bytes(int n_seq, int n_head, int max_ctx, int splits) {
   size_t scores = (size_t)n_seq * n_head * max_ctx * 2;
   scores = (scores + 255) & ~(size_t)255;
   size_t parts = (size_t)n_seq * n_head * splits * kHD * 4;
   size_t tick = (size_t)n_seq * n_head * 4;
-  return scores + parts + tick + 256;
+  return scores + parts + tick + 512 + kSeqTicketBytes;  // 512: base alignment slack
 }
 
 int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
                             const uint16_t *Vc, int64_t seq_stride, int n_seq,
                             const int32_t *n_ctx, int max_ctx, int n_head, uint16_t *O,
-                            int64_t ldo, void *ws, size_t ws_bytes, int sm_count,
-                            cudaStream_t s) {
+                            int64_t ldo, int8_t *Xq, float *sXq, void *ws, size_t ws_bytes,
+                            int sm_count, cudaStream_t s) {
   DecodeArgs a;
   a.Q = Q;
   a.ldq = ldq;
@@ -579,8 +669,13 @@ int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
   size_t scores = ((size_t)n_seq * n_head * max_ctx * 2 + 255) & ~(size_t)255;
   a.partials = (float *)(w + scores);
   a.tickets = (int *)(w + scores + (size_t)n_seq * n_head * a.splits * kHD * 4);
+  if (Xq && n_seq > kMaxSeqTickets) return W8A8_ERR_UNSUPPORTED;
+  a.seq_tickets = reinterpret_cast<int *>(
+      (((uintptr_t)ws + ws_bytes - kSeqTicketBytes) & ~(uintptr_t)15));
+  a.Xq = Xq;
+  a.sXq = sXq;
   if (a.splits == 1) {
-    launch_pdl(attention_decode_fused_kernel, dim3(n_seq * n_head), dim3(256), 0, s, a);
+    launch_pdl(attention_decode_fused_kernel, dim3(n_seq * n_head), dim3(kFusedThreads), 0, s, a);
     return check_launch("attention_decode_fused");
   }
   dim3 grid(n_seq * n_head, a.splits);
