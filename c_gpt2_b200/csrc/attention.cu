@@ -125,7 +125,12 @@ struct PrefillArgs {
   int s_stride;  // bf16 elements per score row in smem
 };
 
-__global__ void __launch_bounds__(128)
+// 8 warps per CTA: warp w owns query rows 16*(w%4) .. +15 and, in Q.K^T, keys
+// [32*(w/4), +32) of each 64-key tile, in P.V head dims [32*(w/4), +32).
+// Every output element is still accumulated by one thread in the same order.
+constexpr int kPrefillThreads = 256;
+
+__global__ void __launch_bounds__(kPrefillThreads)
     attention_prefill_kernel(PrefillArgs a) {
   pdl_wait();
   pdl_launch_dependents();
@@ -142,16 +147,17 @@ __global__ void __launch_bounds__(128)
   uint16_t *sS = sKV + 2 * kKT * kTileStride;   // [64][s_stride]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
+  const int mt = warp & 3, half = warp >> 2;
 
   const uint16_t *Kb = a.Kc + (int64_t)b * a.seq_stride + h * kHD;
   const uint16_t *Vb = a.Vc + (int64_t)b * a.seq_stride + h * kHD;
   const uint16_t *Qb = a.Q + ((int64_t)b * a.T) * a.ldq + h * kHD;
 
-  // tile loader: 64 rows x 128 bytes = 512 x 16 B chunks, 4 per thread
+  // tile loader: 64 rows x 128 bytes = 512 x 16 B chunks, 2 per thread
   auto load_tile = [&](uint16_t *dst, const uint16_t *src, int64_t ld, int row0, int nrows) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      int c = tid + 128 * i;
+    for (int i = 0; i < 512 / kPrefillThreads; ++i) {
+      int c = tid + kPrefillThreads * i;
       int r = c >> 3, cc = (c & 7) * 8;
       bool ok = row0 + r < nrows;
       const uint16_t *g = src + (int64_t)(ok ? row0 + r : 0) * ld + cc;
@@ -163,7 +169,7 @@ __global__ void __launch_bounds__(128)
   load_tile(sKV, Kb, a.d, 0, nk);
   cp_async_commit();
 
-  // Q fragments (rows 16*warp .. +15), 4 k-steps of 16
+  // Q fragments (rows 16*mt .. +15), 4 k-steps of 16
   uint32_t qa[4][4];
   const int g = lane >> 2, tq = lane & 3;
 
@@ -178,34 +184,35 @@ __global__ void __launch_bounds__(128)
     if (kt == 0) {
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks) {
-        const uint16_t *p = sQ + (warp * 16 + (lane & 15)) * kTileStride + ks * 16 + (lane >> 4) * 8;
+        const uint16_t *p = sQ + (mt * 16 + (lane & 15)) * kTileStride + ks * 16 + (lane >> 4) * 8;
         ldsm_x4(smem_u32(p), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
       }
     }
     const uint16_t *sK = sKV + (kt & 1) * kKT * kTileStride;
-    float c[8][4];
+    float c[4][4];
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb)
+    for (int nb = 0; nb < 4; ++nb)
 #pragma unroll
       for (int i = 0; i < 4; ++i) c[nb][i] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
-      for (int nb2 = 0; nb2 < 4; ++nb2) {  // pairs of 8-key blocks
+      for (int j = 0; j < 2; ++j) {  // pairs of 8-key blocks of this warp's 32 keys
+        const int nb2 = half * 2 + j;
         const int q = lane >> 3;
         const uint16_t *p =
             sK + (nb2 * 16 + (q >> 1) * 8 + (lane & 7)) * kTileStride + ks * 16 + (q & 1) * 8;
         uint32_t b0, b1, b2, b3;
         ldsm_x4(smem_u32(p), b0, b1, b2, b3);
-        mma_bf16_16816(c[2 * nb2], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
-        mma_bf16_16816(c[2 * nb2 + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+        mma_bf16_16816(c[2 * j], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+        mma_bf16_16816(c[2 * j + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
       }
     }
     // scale, round, store (columns beyond a row's causal limit are never read)
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      const int col = kt * kKT + nb * 8 + 2 * tq;
-      const int r0 = warp * 16 + g;
+    for (int nb = 0; nb < 4; ++nb) {
+      const int col = kt * kKT + half * 32 + nb * 8 + 2 * tq;
+      const int r0 = mt * 16 + g;
       uint32_t lo = (uint32_t)f2bf(c[nb][0] * 0.125f) | ((uint32_t)f2bf(c[nb][1] * 0.125f) << 16);
       uint32_t hi = (uint32_t)f2bf(c[nb][2] * 0.125f) | ((uint32_t)f2bf(c[nb][3] * 0.125f) << 16);
       *reinterpret_cast<uint32_t *>(sS + r0 * a.s_stride + col) = lo;
@@ -218,17 +225,17 @@ __global__ void __launch_bounds__(128)
   load_tile(sKV, Vb, a.d, 0, nk);
   cp_async_commit();
 
-  // ---- phase B: causal softmax per row (warp w: rows w, w+4, ...) ----
-  for (int r = warp; r < kQT; r += 4) {
+  // ---- phase B: causal softmax per row (warp w: rows w, w+8, ...) ----
+  for (int r = warp; r < kQT; r += kPrefillThreads / 32) {
     const int qpos = q0 + r;
     const int n = qpos < a.T ? qpos + 1 : 0;
     softmax_row_inplace(sS + r * a.s_stride, n, nk_pad, lane);
   }
 
-  // ---- phase C: O = P V ----
-  float o[8][4];
+  // ---- phase C: O = P V (this warp: 16 rows x 32 head dims) ----
+  float o[4][4];
 #pragma unroll
-  for (int nb = 0; nb < 8; ++nb)
+  for (int nb = 0; nb < 4; ++nb)
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[nb][i] = 0.f;
   for (int kt = 0; kt < n_ktiles; ++kt) {
@@ -243,25 +250,26 @@ __global__ void __launch_bounds__(128)
     for (int ks = 0; ks < 4; ++ks) {  // 16 keys per step
       uint32_t pa0, pa1, pa2, pa3;
       const uint16_t *pp =
-          sS + (warp * 16 + (lane & 15)) * a.s_stride + kt * kKT + ks * 16 + (lane >> 4) * 8;
+          sS + (mt * 16 + (lane & 15)) * a.s_stride + kt * kKT + ks * 16 + (lane >> 4) * 8;
       ldsm_x4(smem_u32(pp), pa0, pa1, pa2, pa3);
 #pragma unroll
-      for (int nb2 = 0; nb2 < 4; ++nb2) {  // pairs of 8-dim blocks
+      for (int j = 0; j < 2; ++j) {  // pairs of 8-dim blocks of this warp's 32 dims
+        const int nb2 = half * 2 + j;
         const int q = lane >> 3;
         const uint16_t *p =
             sV + (ks * 16 + (q & 1) * 8 + (lane & 7)) * kTileStride + nb2 * 16 + (q >> 1) * 8;
         uint32_t b0, b1, b2, b3;
         ldsm_x4_t(smem_u32(p), b0, b1, b2, b3);
-        mma_bf16_16816(o[2 * nb2], pa0, pa1, pa2, pa3, b0, b1);
-        mma_bf16_16816(o[2 * nb2 + 1], pa0, pa1, pa2, pa3, b2, b3);
+        mma_bf16_16816(o[2 * j], pa0, pa1, pa2, pa3, b0, b1);
+        mma_bf16_16816(o[2 * j + 1], pa0, pa1, pa2, pa3, b2, b3);
       }
     }
   }
   // ---- store O ----
-  const int r0 = warp * 16 + g;
+  const int r0 = mt * 16 + g;
 #pragma unroll
-  for (int nb = 0; nb < 8; ++nb) {
-    const int col = h * kHD + nb * 8 + 2 * tq;
+  for (int nb = 0; nb < 4; ++nb) {
+    const int col = h * kHD + half * 32 + nb * 8 + 2 * tq;
     if (q0 + r0 < a.T) {
       uint32_t v = (uint32_t)f2bf(o[nb][0]) | ((uint32_t)f2bf(o[nb][1]) << 16);
       *reinterpret_cast<uint32_t *>(a.O + ((int64_t)b * a.T + q0 + r0) * a.ldo + col) = v;
@@ -301,7 +309,7 @@ int launch_attention_prefill(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
     attr[dev & 63] = true;
   }
   dim3 grid((T + kQT - 1) / kQT, n_head, n_seq);
-  launch_pdl(attention_prefill_kernel, dim3(grid), dim3(128), smem, s, a);
+  launch_pdl(attention_prefill_kernel, dim3(grid), dim3(kPrefillThreads), smem, s, a);
   return check_launch("attention_prefill");
 }
 

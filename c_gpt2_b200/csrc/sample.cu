@@ -68,7 +68,9 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
   }
   if (tid == 0) {
-    const int tok = s_idx[0];
+    // A row with no ordered maximum (all NaN) keeps index 0, as a host argmax
+    // that starts from the first entry does; never an id outside the vocabulary.
+    const int tok = s_idx[0] < V ? s_idx[0] : 0;
     out[row] = tok;
     if (append_to) {
       const int p = append_pos[row];

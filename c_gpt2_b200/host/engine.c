@@ -553,6 +553,10 @@ int gpt2_engine_generate(gpt2_engine *e, const int32_t *prompts, int B, int T, i
     return fail(e, W8A8_ERR_INVALID, "batch %d x %d exceeds engine limits", B, T);
   if ((size_t)B * n_gen > (size_t)e->cfg.max_batch * e->cfg.ctx)
     return fail(e, W8A8_ERR_INVALID, "output buffer too small");
+  for (size_t i = 0; i < (size_t)B * T; ++i)
+    if (prompts[i] < 0 || prompts[i] >= e->cfg.vocab)
+      return fail(e, W8A8_ERR_INVALID, "prompt token %d at %zu outside the vocabulary",
+                  prompts[i], i);
   CUDA_TRY(e, cudaMemcpyAsync(e->tokens_in, prompts, (size_t)B * T * 4, cudaMemcpyHostToDevice,
                               e->stream));
   int st = gpt2_engine_generate_device(e, e->tokens_in, B, T, n_gen, e->out_default, NULL);

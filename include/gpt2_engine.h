@@ -56,14 +56,17 @@ size_t gpt2_engine_quant8_bytes(const gpt2_engine_config *cfg);
  * from prefill, the other n_gen-1 from decode steps (the reference counts
  * tokens the same way, gpt2.c:2094-2247). KV caches start empty.
  * Host-buffer form: prompts [B*T] and out_tokens [B*n_gen] are host memory;
- * the call copies prompts in and tokens out (synchronous). */
+ * the call checks every id against the vocabulary, copies prompts in and
+ * tokens out (synchronous). */
 int gpt2_engine_generate(gpt2_engine *e, const int32_t *prompts, int B, int T, int n_gen,
                          int32_t *out_tokens);
-/* Device-buffer form, asynchronous on `stream` (NULL = engine stream). */
+/* Device-buffer form, asynchronous on `stream` (NULL = engine stream). The
+ * ids in prompts_d are not checked: each must lie in [0, vocab). */
 int gpt2_engine_generate_device(gpt2_engine *e, const int32_t *prompts_d, int B, int T, int n_gen,
                                 int32_t *out_tokens_d, void *stream);
 
 /* Step-level interface (device buffers, engine stream):
+ * prompt ids must lie in [0, vocab) (not checked);
  * prefill resets the batch, fills the KV caches and writes the first token
  * of each sequence to out_tokens_d[b*out_stride]; decode_steps runs `steps`
  * further greedy steps, appending tokens after those already produced. */

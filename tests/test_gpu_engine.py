@@ -123,3 +123,17 @@ def test_gpt2_small_config1_stream(cuda):
     same = assert_same_stream_up_to_ties(out, img, dims, z["prompt"], 64)
     assert same >= 16
     eng.close()
+
+
+def test_engine_rejects_out_of_vocabulary_prompt(cuda, tiny_image):
+    from c_gpt2_b200._lib import W8A8Error
+    eng = Engine(TINY, max_batch=2, max_tokens=2 * 16)
+    eng.load_quant8(tiny_image)
+    P = prompts(2, 16, TINY.vocab, seed=1)
+    P[1, 3] = TINY.vocab
+    with pytest.raises(W8A8Error):
+        eng.generate(P, 4)
+    P[1, 3] = -1
+    with pytest.raises(W8A8Error):
+        eng.generate(P, 4)
+    eng.close()
