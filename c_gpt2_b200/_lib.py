@@ -47,6 +47,18 @@ SIGNATURES = {
     "w8a8_quant_rows_amax": (_i, [_p, _i64, _i, _i, _p, _i, _i64, _p, _i64, _p, _p]),
     "w8a8_reduce_residual_layernorm_quant": (_i, [_p, _i64, _i, _i64, _i, _i, _p, _p, _p, _p, _i64,
                                                   _p, _i64, _p, _p, _f, _p, _i64, _p, _p]),
+    "w8a8_row_amax_to": (_i, [_p, _i64, _i, _i, _p, _i, _p]),
+    "w8a8_reduce_residual_layernorm_quant_bcast": (_i, [_p, _i64, _i, _i64, _i, _i, _p, _p, _p, _p,
+                                                        _i64, _p, _i64, _p, _p, _f, _p, _i64, _p,
+                                                        _p, _p, _i, _i64, _p]),
+    "w8a8_gemm_s32_scatter": (_i, [_p, _i, _i, _p, _i, _p, _i, _i, _p]),
+    "w8a8_peer_alloc": (_i, [_sz, _p, _p]),
+    "w8a8_peer_open": (_i, [_p, _p]),
+    "w8a8_peer_close": (_i, [_p]),
+    "w8a8_peer_free": (_i, [_p]),
+    "w8a8_peer_copy": (_i, [_p, _p, _sz, _p]),
+    "w8a8_peer_signal": (_i, [_p, _i, C.c_uint32, _p]),
+    "w8a8_peer_wait": (_i, [_p, _i, C.c_uint32, _p]),
     "w8a8_attention_prefill": (_i, [_p, _i64, _p, _p, _i64, _i, _i, _i, _i, _p, _i64, _p]),
     "w8a8_attention_decode_workspace_size": (_sz, [_i, _i, _i]),
     "w8a8_attention_decode": (_i, [_p, _i64, _p, _p, _i64, _i, _p, _i, _i, _i, _p, _i64, _p, _sz, _p]),

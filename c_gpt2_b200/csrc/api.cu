@@ -180,7 +180,19 @@ extern "C" int w8a8_row_amax(const gpt2_bf16_t *X, int64_t ldx, int M, int K, fl
   if (!X || !amax || M < 0 || K <= 0 || ldx < K) return W8A8_ERR_INVALID;
   int st = ready();
   if (st) return st;
-  return launch_row_amax(X, ldx, M, K, amax, (cudaStream_t)stream);
+  return launch_row_amax(X, ldx, M, K, &amax, 1, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_row_amax_to(const gpt2_bf16_t *X, int64_t ldx, int M, int K,
+                                float *const *amax, int n_out, void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!X || !amax || M < 0 || K <= 0 || ldx < K || n_out < 1 || n_out > 8)
+    return W8A8_ERR_INVALID;
+  for (int j = 0; j < n_out; ++j)
+    if (!amax[j]) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  return launch_row_amax(X, ldx, M, K, amax, n_out, (cudaStream_t)stream);
 }
 
 extern "C" int w8a8_quant_rows_amax(const gpt2_bf16_t *X, int64_t ldx, int M, int K,
@@ -196,16 +208,19 @@ extern "C" int w8a8_quant_rows_amax(const gpt2_bf16_t *X, int64_t ldx, int M, in
                                 (cudaStream_t)stream);
 }
 
-extern "C" int w8a8_reduce_residual_layernorm_quant(
+extern "C" int w8a8_reduce_residual_layernorm_quant_bcast(
     const int32_t *acc, int64_t lda, int n_slots, int64_t slot_stride, int M, int d,
     const float *sX, const float *sW, const gpt2_bf16_t *bias, const gpt2_bf16_t *R, int64_t ldr,
     gpt2_bf16_t *H, int64_t ldh, const gpt2_bf16_t *gamma, const gpt2_bf16_t *beta, float eps,
-    int8_t *Xq, int64_t ldq, float *sXq, void *stream) {
+    int8_t *Xq, int64_t ldq, float *sXq, int8_t *const *xq_bcast, float *const *sx_bcast,
+    int n_bcast, int64_t bcast_row0, void *stream) {
   if (M == 0) return W8A8_OK;
   if (!acc || !sX || !sW || !bias || !R || !H || M < 0 || d <= 0 || lda < d || ldr < d ||
       ldh < d || n_slots <= 0 || (n_slots > 1 && slot_stride < (int64_t)M * lda))
     return W8A8_ERR_INVALID;
   if (gamma && (!beta || !Xq || !sXq || ldq < d)) return W8A8_ERR_INVALID;
+  if (n_bcast < 0 || n_bcast > 8 || (n_bcast > 0 && (!xq_bcast || !sx_bcast || bcast_row0 < 0)))
+    return W8A8_ERR_INVALID;
   int st = ready();
   if (st) return st;
   ReduceArgs a = {};
@@ -227,7 +242,40 @@ extern "C" int w8a8_reduce_residual_layernorm_quant(
   a.ldq = ldq;
   a.sXq = sXq;
   a.d = d;
+  for (int j = 0; j < n_bcast; ++j) {
+    a.xq_bcast[j] = xq_bcast[j];
+    a.sx_bcast[j] = sx_bcast[j];
+  }
+  a.n_bcast = n_bcast;
+  a.bcast_row0 = bcast_row0;
   return launch_reduce_layernorm_quant(a, M, (cudaStream_t)stream);
+}
+
+extern "C" int w8a8_reduce_residual_layernorm_quant(
+    const int32_t *acc, int64_t lda, int n_slots, int64_t slot_stride, int M, int d,
+    const float *sX, const float *sW, const gpt2_bf16_t *bias, const gpt2_bf16_t *R, int64_t ldr,
+    gpt2_bf16_t *H, int64_t ldh, const gpt2_bf16_t *gamma, const gpt2_bf16_t *beta, float eps,
+    int8_t *Xq, int64_t ldq, float *sXq, void *stream) {
+  return w8a8_reduce_residual_layernorm_quant_bcast(acc, lda, n_slots, slot_stride, M, d, sX, sW,
+                                                    bias, R, ldr, H, ldh, gamma, beta, eps, Xq,
+                                                    ldq, sXq, nullptr, nullptr, 0, 0, stream);
+}
+
+extern "C" int w8a8_gemm_s32_scatter(const int8_t *Xq, int M, int K, const int8_t *W, int N,
+                                     int32_t *const *dst, int n_dst, int rows_per_dst,
+                                     void *stream) {
+  if (M == 0 || N == 0) return W8A8_OK;
+  if (!Xq || !W || !dst || M < 0 || N < 0 || K <= 0 || n_dst < 1 || n_dst > 8 ||
+      rows_per_dst <= 0 || (int64_t)rows_per_dst * n_dst < M)
+    return W8A8_ERR_INVALID;
+  for (int j = 0; j < n_dst; ++j)
+    if (!dst[j] || !aligned16(dst[j])) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  LinearArgs a = make_args(EPI_S32, M, N, K, nullptr, nullptr, nullptr, nullptr, 0, dst[0], N);
+  for (int j = 0; j < n_dst; ++j) a.dst[j] = dst[j];
+  a.rows_per_dst = rows_per_dst;
+  return dispatch_linear(Xq, K, W, a, (cudaStream_t)stream);
 }
 
 extern "C" int w8a8_attention_prefill(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,

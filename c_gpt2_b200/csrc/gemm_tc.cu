@@ -85,7 +85,7 @@ __device__ __forceinline__ void store_one_cm(const GemmArgs &a, int m, int n, in
                                              int qseg, int qcol, int64_t kv) {
   uint16_t *Yb = reinterpret_cast<uint16_t *>(a.Y);
   if (EPI == EPI_S32) {
-    reinterpret_cast<int32_t *>(a.Y)[(int64_t)m * a.ldy + n] = acc;
+    s32_row(a, m)[n] = acc;
   } else if (EPI == EPI_DEQUANT) {
     Yb[(int64_t)m * a.ldy + n] = f2bf(dequant_bf(acc, sw, sx));
   } else if (EPI == EPI_BIAS) {
@@ -197,8 +197,7 @@ __device__ __forceinline__ void finish_chunk_tm(const GemmArgs &a, const SmemCtl
                                                 const uint32_t (&r)[32]) {
   if (m >= a.M || nbase >= a.N) return;
   if (EPI == EPI_S32) {
-    int4 *dst = reinterpret_cast<int4 *>(reinterpret_cast<int32_t *>(a.Y) + (int64_t)m * a.ldy +
-                                         nbase);
+    int4 *dst = reinterpret_cast<int4 *>(s32_row(a, m) + nbase);
 #pragma unroll
     for (int v = 0; v < 8; ++v)
       dst[v] = make_int4((int)r[4 * v], (int)r[4 * v + 1], (int)r[4 * v + 2], (int)r[4 * v + 3]);
@@ -298,7 +297,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int *abort_flag = &ctl->abort_flag;
 
-  pdl_launch_dependents();
+  // No early griddepcontrol.launch_dependents: the next kernel launches when
+  // this grid exits. Measured on a graphed decode step of GPT-2 large (64
+  // sequences), letting the next kernel's CTAs become resident during the GEMM
+  // made the step 15% slower, even when triggered after the MMAs.
   int issued = 0;
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------

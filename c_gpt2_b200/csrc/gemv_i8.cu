@@ -24,7 +24,7 @@ __device__ __forceinline__ void gemv_store(const GemvArgs &a, int m, int n, int3
   float sx = (a.epi != 0) ? a.sX[m] : 0.f;
   switch (a.epi) {
     case 0:
-      reinterpret_cast<int32_t *>(a.Y)[(int64_t)m * a.ldy + n] = acc;
+      s32_row(a, m)[n] = acc;
       break;
     case 1:
       reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(dequant_bf(acc, sw, sx));

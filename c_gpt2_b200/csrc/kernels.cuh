@@ -41,7 +41,21 @@ struct LinearArgs {
   // zero-filled before first use; the kernels leave it zeroed.
   void *workspace;
   size_t workspace_bytes;
+  // EPI_S32 scatter (rows_per_dst > 0): output row m goes to
+  // dst[m / rows_per_dst] + (m % rows_per_dst) * ldy, e.g. into the partial-
+  // sum slot that this GPU owns in the buffer of the GPU owning row m.
+  int32_t *dst[8];
+  int rows_per_dst;
 };
+
+// Row address of the int32 output of row m (plain or scattered).
+__host__ __device__ inline int32_t *s32_row(const LinearArgs &a, int m) {
+  if (a.rows_per_dst > 0) {
+    const int o = m / a.rows_per_dst;
+    return a.dst[o] + (int64_t)(m - o * a.rows_per_dst) * a.ldy;
+  }
+  return reinterpret_cast<int32_t *>(a.Y) + (int64_t)m * a.ldy;
+}
 
 size_t linear_workspace_bytes(int M, int N);
 
@@ -65,6 +79,12 @@ struct ReduceArgs {
   int64_t ldq;
   float *sXq;
   int d;
+  // optional extra copies of the quantized rows (n_bcast <= 8): row m also
+  // goes to xq_bcast[j] + (bcast_row0 + m) * ldq and sx_bcast[j][bcast_row0 + m]
+  int8_t *xq_bcast[8];
+  float *sx_bcast[8];
+  int n_bcast;
+  int64_t bcast_row0;
 };
 
 // gemm_tc.cu
@@ -89,7 +109,8 @@ int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const
                                  int M, int T, const int32_t *pos0, int d, uint16_t *H,
                                  const uint16_t *gamma, const uint16_t *beta, float eps,
                                  uint16_t *Y, int8_t *Xq, float *sX, cudaStream_t s);
-int launch_row_amax(const uint16_t *X, int64_t ldx, int M, int K, float *amax, cudaStream_t s);
+int launch_row_amax(const uint16_t *X, int64_t ldx, int M, int K, float *const *amax, int n_out,
+                    cudaStream_t s);
 int launch_quant_rows_amax(const uint16_t *X, int64_t ldx, int M, int K, const float *amax,
                            int n_amax, int64_t amax_stride, int8_t *Xq, int64_t ldq, float *sX,
                            cudaStream_t s);

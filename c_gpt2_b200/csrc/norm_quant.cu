@@ -618,29 +618,48 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Quantize the row values a lane holds (vectors l + 32k, k < NV) with the
-// scale of the row's absolute maximum amax (activation_quant.cu:75-91).
+// scale of the row's absolute maximum amax (activation_quant.cu:75-91): q[k]
+// holds the 8 int8 values of vector k, the return value is the scale.
 template <int NV>
-__device__ __forceinline__ void warp_quant_store(const uint4 (&y)[NV], int nv, int lane,
-                                                 float amax, int8_t *xq_row, float *sx_out) {
+__device__ __forceinline__ float warp_quant_pack(const uint4 (&y)[NV], int nv, int lane,
+                                                 float amax, uint2 (&q)[NV]) {
   const float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
   const float inv = __fdiv_rn(1.0f, scale);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    uint32_t w[2] = {0u, 0u};
+    if (lane + 32 * k < nv) {
+      float f[8];
+      unpack8(y[k], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int qv = __float2int_rn(__fmul_rn(f[e], inv));
+        qv = qv > 127 ? 127 : (qv < -127 ? -127 : qv);
+        w[e >> 2] |= ((uint32_t)(qv & 0xff)) << (8 * (e & 3));
+      }
+    }
+    q[k] = make_uint2(w[0], w[1]);
+  }
+  return scale;
+}
+
+template <int NV>
+__device__ __forceinline__ void warp_quant_put(const uint2 (&q)[NV], float scale, int nv, int lane,
+                                               int8_t *xq_row, float *sx_out) {
   if (lane == 0) *sx_out = scale;
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int v = lane + 32 * k;
-    if (v < nv) {
-      float f[8];
-      unpack8(y[k], f);
-      uint32_t w[2] = {0u, 0u};
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        int q = __float2int_rn(__fmul_rn(f[e], inv));
-        q = q > 127 ? 127 : (q < -127 ? -127 : q);
-        w[e >> 2] |= ((uint32_t)(q & 0xff)) << (8 * (e & 3));
-      }
-      *reinterpret_cast<uint2 *>(xq_row + 8 * v) = make_uint2(w[0], w[1]);
-    }
+    if (v < nv) *reinterpret_cast<uint2 *>(xq_row + 8 * v) = q[k];
   }
+}
+
+template <int NV>
+__device__ __forceinline__ void warp_quant_store(const uint4 (&y)[NV], int nv, int lane,
+                                                 float amax, int8_t *xq_row, float *sx_out) {
+  uint2 q[NV];
+  const float scale = warp_quant_pack(y, nv, lane, amax, q);
+  warp_quant_put(q, scale, nv, lane, xq_row, sx_out);
 }
 
 template <int NV>
@@ -672,12 +691,19 @@ __device__ __forceinline__ void warp_load_row(const uint16_t *row, int nv, int l
 // modes of quant_warp_kernel
 enum { QW_ROW = 0, QW_AMAX_ONLY = 1, QW_GIVEN_AMAX = 2 };
 
+// Row-maximum outputs of QW_AMAX_ONLY: the same [M] values into n arrays
+// (this GPU's and its peers' exchange slots).
+struct AmaxOut {
+  float *p[8];
+  int n;
+};
+
 template <int MODE, int NV>
 __global__ void __launch_bounds__(kWarpRows * 32)
     quant_warp_kernel(const uint16_t *__restrict__ X, int64_t ldx, int M, int K,
                       const float *__restrict__ amax_in, int n_amax, int64_t amax_stride,
                       int8_t *__restrict__ Xq, int64_t ldq, float *__restrict__ sX,
-                      float *__restrict__ amax_out) {
+                      AmaxOut amax_out) {
   pdl_wait();
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
@@ -694,7 +720,7 @@ __global__ void __launch_bounds__(kWarpRows * 32)
     amax = warp_row_amax(x, nv, lane);
   }
   if (MODE == QW_AMAX_ONLY) {
-    if (lane == 0) amax_out[row] = amax;
+    if (lane < amax_out.n) amax_out.p[lane][row] = amax;
     return;
   }
   warp_quant_store(x, nv, lane, amax, Xq + (int64_t)row * ldq, sX + row);
@@ -852,9 +878,16 @@ __global__ void __launch_bounds__(kWarpRows * 32) layernorm_warp_kernel(LnWarpAr
       if (a.Y) reinterpret_cast<uint4 *>(a.Y + (int64_t)row * a.ldy)[v] = y[k];
     }
   }
-  if (a.Xq)
-    warp_quant_store(y, nv, lane, warp_row_amax(y, nv, lane), a.Xq + (int64_t)row * a.ldq,
-                     a.sX + row);
+  if (a.Xq) {
+    uint2 q[NV];
+    const float scale = warp_quant_pack(y, nv, lane, warp_row_amax(y, nv, lane), q);
+    warp_quant_put(q, scale, nv, lane, a.Xq + (int64_t)row * a.ldq, a.sX + row);
+    if (MODE == LN_REDUCE) {  // copies into the peers' all-gather buffers
+      const int64_t r = a.red.bcast_row0 + row;
+      for (int j = 0; j < a.red.n_bcast; ++j)
+        warp_quant_put(q, scale, nv, lane, a.red.xq_bcast[j] + r * a.ldq, a.red.sx_bcast[j] + r);
+    }
+  }
 }
 
 static int warp_grid(int M) { return (M + kWarpRows - 1) / kWarpRows; }
@@ -877,7 +910,7 @@ static int row_grid(int M) { return (M + kRowWarps - 1) / kRowWarps; }
 template <int MODE>
 static int launch_quant_warp(const uint16_t *X, int64_t ldx, int M, int K, const float *amax_in,
                              int n_amax, int64_t amax_stride, int8_t *Xq, int64_t ldq, float *sX,
-                             float *amax_out, cudaStream_t s) {
+                             AmaxOut amax_out, cudaStream_t s) {
   const int need = ((K >> 3) + 31) / 32;
   const dim3 g(warp_grid(M)), b(kWarpRows * 32);
   if (need <= 8)
@@ -912,7 +945,7 @@ static bool ln_warp_ok(const LnWarpArgs &a) {
 int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, float *sX,
                       cudaStream_t s) {
   if (M >= kWarpMinRows && warp_rows_ok(K, kWarpQuantVec, X, ldx) && aligned16(Xq))
-    return launch_quant_warp<QW_ROW>(X, ldx, M, K, nullptr, 0, 0, Xq, K, sX, nullptr, s);
+    return launch_quant_warp<QW_ROW>(X, ldx, M, K, nullptr, 0, 0, Xq, K, sX, AmaxOut{}, s);
   if (block_path_ok(K, X, ldx, Xq, K) && M <= 0x7fffffff) {
     launch_pdl(quant_rows_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, Xq, sX);
     return check_launch("quant_rows_block");
@@ -1020,12 +1053,18 @@ int launch_embed_layernorm_quant(const uint16_t *wte, const uint16_t *wpe, const
   return check_launch("embed_layernorm_quant");
 }
 
-int launch_row_amax(const uint16_t *X, int64_t ldx, int M, int K, float *amax, cudaStream_t s) {
-  if (M >= kWarpMinRows && warp_rows_ok(K, kWarpQuantVec, X, ldx))
-    return launch_quant_warp<QW_AMAX_ONLY>(X, ldx, M, K, nullptr, 0, 0, nullptr, 0, nullptr, amax,
-                                           s);
-  if (!block_path_ok(K, X, ldx, nullptr, 0)) return W8A8_ERR_UNSUPPORTED;
-  launch_pdl(row_amax_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, amax);
+int launch_row_amax(const uint16_t *X, int64_t ldx, int M, int K, float *const *amax, int n_out,
+                    cudaStream_t s) {
+  if (n_out < 1 || n_out > 8) return W8A8_ERR_INVALID;
+  // several outputs (peer exchange slots) always take the warp kernel
+  if ((M >= kWarpMinRows || n_out > 1) && warp_rows_ok(K, kWarpQuantVec, X, ldx)) {
+    AmaxOut o = {};
+    for (int j = 0; j < n_out; ++j) o.p[j] = amax[j];
+    o.n = n_out;
+    return launch_quant_warp<QW_AMAX_ONLY>(X, ldx, M, K, nullptr, 0, 0, nullptr, 0, nullptr, o, s);
+  }
+  if (n_out > 1 || !block_path_ok(K, X, ldx, nullptr, 0)) return W8A8_ERR_UNSUPPORTED;
+  launch_pdl(row_amax_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, amax[0]);
   return check_launch("row_amax_block");
 }
 
@@ -1035,7 +1074,7 @@ int launch_quant_rows_amax(const uint16_t *X, int64_t ldx, int M, int K, const f
   if (M >= kWarpMinRows && warp_rows_ok(K, kWarpQuantVec, X, ldx) && aligned16(Xq) &&
       (ldq & 7) == 0)
     return launch_quant_warp<QW_GIVEN_AMAX>(X, ldx, M, K, amax, n_amax, amax_stride, Xq, ldq, sX,
-                                            nullptr, s);
+                                            AmaxOut{}, s);
   if (!block_path_ok(K, X, ldx, Xq, ldq)) return W8A8_ERR_UNSUPPORTED;
   launch_pdl(quant_rows_amax_block_kernel, dim3(M), dim3(kRowThreads), 0, s, X, ldx, K, amax,
              n_amax, amax_stride, Xq, ldq, sX);
@@ -1049,8 +1088,11 @@ int launch_reduce_layernorm_quant(const ReduceArgs &a, int M, cudaStream_t s) {
             aligned16(a.R) && (a.ldr & 7) == 0 && aligned16(a.H) && (a.ldh & 7) == 0;
   if (a.gamma)
     ok = ok && aligned16(a.gamma) && aligned16(a.beta) && aligned16(a.Xq) && (a.ldq & 7) == 0;
+  if (a.n_bcast < 0 || a.n_bcast > 8 || (a.n_bcast > 0 && !a.gamma)) return W8A8_ERR_INVALID;
+  for (int j = 0; j < a.n_bcast; ++j)
+    if (!aligned16(a.xq_bcast[j]) || !a.sx_bcast[j]) return W8A8_ERR_INVALID;
   if (!ok) return W8A8_ERR_UNSUPPORTED;
-  if (M >= kWarpMinRows && d <= 256 * kWarpVec) {
+  if ((M >= kWarpMinRows || a.n_bcast > 0) && d <= 256 * kWarpVec) {
     LnWarpArgs w = {};
     w.M = M;
     w.d = d;
@@ -1065,6 +1107,7 @@ int launch_reduce_layernorm_quant(const ReduceArgs &a, int M, cudaStream_t s) {
     w.sX = a.sXq;
     return launch_ln_warp<LN_REDUCE>(w, s);
   }
+  if (a.n_bcast > 0) return W8A8_ERR_UNSUPPORTED;
   launch_pdl(reduce_layernorm_quant_kernel, dim3(M), dim3(kRowThreads), 0, s, a);
   return check_launch("reduce_layernorm_quant");
 }

@@ -173,6 +173,39 @@ def reduce_residual_layernorm_quant(acc, sX, sW, bias, R, H, gamma=None, beta=No
     return H
 
 
+def row_amax_to(X, out_ptrs):
+    """Row maxima of X [M, K] into several [M] f32 arrays given by address."""
+    from .peer import ptr_array
+    M, K = X.shape
+    check(core().w8a8_row_amax_to(_ptr(X), X.stride(0), M, K, ptr_array(out_ptrs), len(out_ptrs),
+                                  _stream()), "w8a8_row_amax_to")
+
+
+def gemm_s32_scatter(Xq, W, dst_ptrs, rows_per_dst):
+    """Xq [M, K] . W[N, K]^T as int32, row m stored at dst[m // rows_per_dst]."""
+    from .peer import ptr_array
+    _need(Xq, torch.int8, "Xq")
+    M, K = Xq.shape
+    N = W.shape[0]
+    check(core().w8a8_gemm_s32_scatter(_ptr(Xq), M, K, _ptr(W), N, ptr_array(dst_ptrs),
+                                       len(dst_ptrs), rows_per_dst, _stream()),
+          "w8a8_gemm_s32_scatter")
+
+
+def reduce_residual_layernorm_quant_bcast(acc, sX, sW, bias, R, H, gamma, beta, eps, Xq, sXq,
+                                          xq_bcast, sx_bcast, bcast_row0):
+    """reduce_residual_layernorm_quant whose quantized rows are also stored
+    into other GPUs' buffers (addresses) at row bcast_row0 + m."""
+    from .peer import ptr_array
+    acc3 = acc if acc.dim() == 3 else acc.unsqueeze(0)
+    n, M, d = acc3.shape
+    check(core().w8a8_reduce_residual_layernorm_quant_bcast(
+        _ptr(acc3), acc3.stride(1), n, acc3.stride(0), M, d, _ptr(sX), _ptr(sW), _ptr(bias),
+        _ptr(R), R.stride(0), _ptr(H), H.stride(0), _ptr(gamma), _ptr(beta), eps, _ptr(Xq),
+        Xq.stride(0), _ptr(sXq), ptr_array(xq_bcast), ptr_array(sx_bcast), len(xq_bcast),
+        bcast_row0, _stream()), "w8a8_reduce_residual_layernorm_quant_bcast")
+
+
 def attention_prefill(Q, Kc, Vc, seq_stride, n_seq, T, n_head, out=None):
     d = n_head * 64
     O = out if out is not None else torch.empty((n_seq * T, d), dtype=torch.bfloat16,

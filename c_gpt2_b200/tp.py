@@ -184,20 +184,205 @@ class Kernels:
     sample_greedy = staticmethod(ops.sample_greedy)
 
 
+class CollectiveExchange:
+    """The exchange steps through collectives (NCCL on GPUs, gloo on CPU):
+    fp32 max all-reduce of row maxima, int32 reduce-scatter of partial sums,
+    all-gather of the owners' quantized rows."""
+
+    def __init__(self, kernels, collectives: Collectives, rank: int, world: int, M: int, d: int,
+                 device):
+        self.k, self.c, self.rank, self.world = kernels, collectives, rank, world
+        self.Mo = M // world
+        self.Xq = torch.empty((M, d), dtype=torch.int8, device=device)
+        self.sX = torch.empty((M,), dtype=torch.float32, device=device)
+        self.P_own = torch.empty((self.Mo, d), dtype=torch.int32, device=device)
+
+    def own_rows(self):
+        m0 = self.rank * self.Mo
+        return self.Xq[m0:m0 + self.Mo], self.sX[m0:m0 + self.Mo]
+
+    def publish_rows(self) -> None:
+        self.c.all_gather_rows(self.Xq, self.rank, self.world)
+        self.c.all_gather_rows(self.sX, self.rank, self.world)
+
+    def row_maxima(self, X: torch.Tensor, kind: int) -> torch.Tensor:
+        amax = self.k.row_amax(X)
+        self.c.all_reduce_max(amax)
+        return amax
+
+    def partial_sums(self, Xq: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
+        P = self.k.gemm_s32(Xq, W)
+        self.c.reduce_scatter_sum(self.P_own, P)
+        return self.P_own
+
+    def reduce(self, acc, sx, sW, b, H, gamma=None, beta=None, eps=1e-5) -> None:
+        if gamma is None:
+            self.k.reduce_residual_layernorm_quant(acc, sx, sW, b, H, H)
+            return
+        xq, sxq = self.own_rows()
+        self.k.reduce_residual_layernorm_quant(acc, sx, sW, b, H, H, gamma, beta, eps, xq, sxq)
+        self.publish_rows()
+
+    def gather_tokens(self, nxt: torch.Tensor) -> None:
+        self.c.all_gather_rows(nxt, self.rank, self.world)
+
+
+class PeerExchange:
+    """The same exchange steps done by the library's kernels over NVLink peer
+    memory, with no collective on the data path:
+
+    * row maxima: `w8a8_row_amax_to` stores this GPU's [M] maxima into slot
+      `rank` of every GPU's [G][M] array; the quantization takes the max over
+      the G slots;
+    * partial sums: `w8a8_gemm_s32_scatter` stores the int32 rows each GPU owns
+      straight into slot `rank` of that GPU's [G][M/G][d] receive area (16-byte
+      peer stores from the GEMM epilogue); the owner's reduce kernel adds the
+      G slots in rank order;
+    * quantized rows: the owner's reduce + LayerNorm + quant kernel also stores
+      its int8 rows and scales into every other GPU's [M][d] buffer.
+
+    Each step ends with a flag per (kind, source) on every destination GPU
+    (`w8a8_peer_signal`, system-scope release) and a bounded wait for the G
+    flags of this GPU (`w8a8_peer_wait`). Flag values are per-kind epoch
+    counters, so no flag is ever reset. Every buffer is reused only after a
+    later exchange step has proven that all GPUs finished reading it."""
+
+    KINDS = 5  # 0 partial sums, 1 quantized rows, 2 attention maxima, 3 GELU maxima, 4 tokens
+
+    def __init__(self, rank: int, world: int, M: int, d: int, group=None):
+        from . import peer
+        self.peer = peer
+        self.rank, self.world, self.M, self.d = rank, world, M, d
+        self.Mo = Mo = M // world
+        G = world
+        off = 0
+
+        def region(nbytes):
+            nonlocal off
+            o = off
+            off += (nbytes + 255) & ~255
+            return o
+
+        self.o_acc = region(G * Mo * d * 4)
+        self.o_xq = region(M * d)
+        self.o_sx = region(M * 4)
+        self.o_amax = [region(G * M * 4), region(G * M * 4)]
+        self.o_tok = region(M * 4)
+        self.o_flags = region(self.KINDS * G * 4)
+        self.buf = peer.PeerBuffer(off, group)
+        base = self.buf.local
+        self.acc = peer.view(base + self.o_acc, (G, Mo, d), torch.int32)
+        self.Xq = peer.view(base + self.o_xq, (M, d), torch.int8)
+        self.sX = peer.view(base + self.o_sx, (M,), torch.float32)
+        self.amax = [peer.view(base + o, (G, M), torch.float32) for o in self.o_amax]
+        self.epoch = [0] * self.KINDS
+
+    def close(self) -> None:
+        self.buf.close()
+
+    def _flag(self, r: int, kind: int, src: int) -> int:
+        return self.buf.base[r] + self.o_flags + (kind * self.world + src) * 4
+
+    def _step(self, kind: int) -> None:
+        """Publish this GPU's part of step `kind`, then wait for everyone's."""
+        self.epoch[kind] += 1
+        e = self.epoch[kind]
+        self.peer.signal([self._flag(r, kind, self.rank) for r in range(self.world)], e)
+        self.peer.wait(self._flag(self.rank, kind, 0), self.world, e)
+
+    def own_rows(self):
+        m0 = self.rank * self.Mo
+        return self.Xq[m0:m0 + self.Mo], self.sX[m0:m0 + self.Mo]
+
+    def publish_rows(self) -> None:
+        """Copy this GPU's rows of Xq/sX into every other GPU's buffers."""
+        m0, Mo, d = self.rank * self.Mo, self.Mo, self.d
+        for r in range(self.world):
+            if r != self.rank:
+                b = self.buf.base[r]
+                self.peer.copy(b + self.o_xq + m0 * d, self.buf.local + self.o_xq + m0 * d, Mo * d)
+                self.peer.copy(b + self.o_sx + m0 * 4, self.buf.local + self.o_sx + m0 * 4, Mo * 4)
+        self._step(1)
+
+    def row_maxima(self, X: torch.Tensor, kind: int) -> torch.Tensor:
+        o = self.o_amax[kind]
+        ops.row_amax_to(X, [self.buf.base[r] + o + self.rank * self.M * 4
+                            for r in range(self.world)])
+        self._step(2 + kind)
+        return self.amax[kind]
+
+    def partial_sums(self, Xq: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
+        slot = self.rank * self.Mo * self.d * 4
+        ops.gemm_s32_scatter(Xq, W, [self.buf.base[r] + self.o_acc + slot
+                                     for r in range(self.world)], self.Mo)
+        self._step(0)
+        return self.acc
+
+    def reduce(self, acc, sx, sW, b, H, gamma=None, beta=None, eps=1e-5) -> None:
+        if gamma is None:
+            ops.reduce_residual_layernorm_quant(acc, sx, sW, b, H, H)
+            return
+        xq, sxq = self.own_rows()
+        others = [r for r in range(self.world) if r != self.rank]
+        ops.reduce_residual_layernorm_quant_bcast(
+            acc, sx, sW, b, H, H, gamma, beta, eps, xq, sxq,
+            [self.buf.base[r] + self.o_xq for r in others],
+            [self.buf.base[r] + self.o_sx for r in others], self.rank * self.Mo)
+        self._step(1)
+
+    def gather_tokens(self, nxt: torch.Tensor) -> None:
+        n = nxt.numel() // self.world
+        s0 = self.rank * n
+        tok = self.buf.local + self.o_tok
+        self.peer.copy(tok + s0 * 4, nxt[s0:s0 + n].data_ptr(), n * 4)
+        for r in range(self.world):
+            if r != self.rank:
+                self.peer.copy(self.buf.base[r] + self.o_tok + s0 * 4, nxt[s0:s0 + n].data_ptr(),
+                               n * 4)
+        self._step(4)
+        nxt.copy_(self.peer.view(tok, (nxt.numel(),), torch.int32))
+
+
 class TPPrefill:
     """Prefill of n_seq prompts of T tokens on `world` ranks; returns the
     greedy next token of every sequence (on every rank) and the last-position
-    logits of the sequences this rank owns."""
+    logits of the sequences this rank owns.
+
+    exchange: "collective" (NCCL / gloo collectives) or "peer" (the library's
+    own kernels over NVLink peer memory; GPUs only)."""
 
     def __init__(self, plan: TPPlan, shard: TPShard, rank: int, kernels=None,
-                 collectives: Collectives | None = None, eps: float = 1e-5):
+                 collectives: Collectives | None = None, eps: float = 1e-5,
+                 exchange: str = "collective", group=None):
         self.plan, self.w, self.rank = plan, shard, rank
         self.k = kernels or Kernels()
-        self.c = collectives or Collectives()
+        self.c = collectives or Collectives(group)
         self.eps = eps
+        self.mode = exchange
+        self.group = group
+        self._ex = None
+
+    def _exchange(self, M: int, d: int, device):
+        ex = self._ex
+        if ex is not None and ex.M_key == (M, d):
+            return ex
+        if ex is not None and hasattr(ex, "close"):
+            ex.close()
+        if self.mode == "peer":
+            ex = PeerExchange(self.rank, self.plan.world, M, d, self.group)
+        else:
+            ex = CollectiveExchange(self.k, self.c, self.rank, self.plan.world, M, d, device)
+        ex.M_key = (M, d)
+        self._ex = ex
+        return ex
+
+    def close(self) -> None:
+        if self._ex is not None and hasattr(self._ex, "close"):
+            self._ex.close()
+        self._ex = None
 
     def run(self, tokens: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        plan, w, k, c, r, G = self.plan, self.w, self.k, self.c, self.rank, self.plan.world
+        plan, w, k, r = self.plan, self.w, self.k, self.rank
         n_seq, T = tokens.shape
         d = plan.dims.d_model
         dh = plan.d_heads(r)
@@ -207,65 +392,48 @@ class TPPrefill:
         m0, m1 = s0 * T, s1 * T
         dev = w.wte.device
         L0 = w.layers[0]
+        ex = self._exchange(M, d, dev)
+        Xq, sX = ex.Xq, ex.sX
         # residual stream of the owned sequences; int8 LayerNorm output of all rows
-        Xq = torch.empty((M, d), dtype=torch.int8, device=dev)
-        sX = torch.empty((M,), dtype=torch.float32, device=dev)
         own_tok = tokens[s0:s1].contiguous().reshape(-1)
         H, _, xq, sx = k.embed_layernorm_quant(w.wte, w.wpe, own_tok, T, None, L0["ln1_gamma"],
                                                L0["ln1_beta"], self.eps)
         Xq[m0:m1].copy_(xq)
         sX[m0:m1].copy_(sx)
-        self._gather(Xq, sX)
+        ex.publish_rows()
         Kc = torch.empty((n_seq, T, dh), dtype=torch.bfloat16, device=dev)
         Vc = torch.empty_like(Kc)
         Q = torch.empty((M, dh), dtype=torch.bfloat16, device=dev)
-        P_own = torch.empty((m1 - m0, d), dtype=torch.int32, device=dev)
         n_layer = len(w.layers)
         for l, L in enumerate(w.layers):
             # attention on the local heads
             k.linear_qkv_heads(Xq, sX, L["W_qkv"], L["W_qkv.scale"], L["b_qkv"], Q, Kc, Vc,
                                T * dh, T)
             O = k.attention_prefill(Q, Kc, Vc, T * dh, n_seq, T, hl)
-            # attn_proj, row-split: whole-row scale, int32 partials, reduce-scatter
-            amax = k.row_amax(O)
-            c.all_reduce_max(amax)
-            Oq, sO = k.quant_rows_amax(O, amax)
-            P = k.gemm_s32(Oq, L["attn_proj"])
-            c.reduce_scatter_sum(P_own, P)
-            del P
-            k.reduce_residual_layernorm_quant(P_own, sO[m0:m1], L["attn_proj.scale"],
-                                              L["attn_proj_bias"], H, H, L["ln2_gamma"],
-                                              L["ln2_beta"], self.eps, Xq[m0:m1], sX[m0:m1])
-            self._gather(Xq, sX)
+            # attn_proj, row-split: whole-row scale, int32 partials to the row owners
+            Oq, sO = k.quant_rows_amax(O, ex.row_maxima(O, 0))
+            acc = ex.partial_sums(Oq, L["attn_proj"])
+            ex.reduce(acc, sO[m0:m1], L["attn_proj.scale"], L["attn_proj_bias"], H,
+                      L["ln2_gamma"], L["ln2_beta"], self.eps)
             # MLP: W1 column-split with GELU, W2 row-split
             Gk = k.linear(Xq, sX, L["W1"], L["W1.scale"], L["b1"], epilogue=3)
-            amax = k.row_amax(Gk)
-            c.all_reduce_max(amax)
-            Gq, sG = k.quant_rows_amax(Gk, amax)
+            Gq, sG = k.quant_rows_amax(Gk, ex.row_maxima(Gk, 1))
             del Gk
-            P = k.gemm_s32(Gq, L["W2"])
-            c.reduce_scatter_sum(P_own, P)
-            del P
+            acc = ex.partial_sums(Gq, L["W2"])
             if l + 1 < n_layer:
                 N = w.layers[l + 1]
-                k.reduce_residual_layernorm_quant(P_own, sG[m0:m1], L["W2.scale"], L["b2"], H, H,
-                                                  N["ln1_gamma"], N["ln1_beta"], self.eps,
-                                                  Xq[m0:m1], sX[m0:m1])
-                self._gather(Xq, sX)
+                ex.reduce(acc, sG[m0:m1], L["W2.scale"], L["b2"], H, N["ln1_gamma"],
+                          N["ln1_beta"], self.eps)
             else:
-                k.reduce_residual_layernorm_quant(P_own, sG[m0:m1], L["W2.scale"], L["b2"], H, H)
+                ex.reduce(acc, sG[m0:m1], L["W2.scale"], L["b2"], H)
         # final LayerNorm of each owned sequence's last position, LM head, greedy
         last = H.view(s1 - s0, T, d)[:, T - 1, :]
         Xf, _, _ = k.layernorm_quant(last, w.lnf_gamma, w.lnf_beta, self.eps, want_q=False)
         logits = k.lm_head(Xf, w.wte)
         nxt = torch.empty((n_seq,), dtype=torch.int32, device=dev)
         nxt[s0:s1].copy_(k.sample_greedy(logits))
-        c.all_gather_rows(nxt, r, G)
+        ex.gather_tokens(nxt)
         return nxt, logits
-
-    def _gather(self, Xq: torch.Tensor, sX: torch.Tensor) -> None:
-        self.c.all_gather_rows(Xq, self.rank, self.plan.world)
-        self.c.all_gather_rows(sX, self.rank, self.plan.world)
 
 
 def main(argv=None) -> None:
@@ -287,6 +455,7 @@ def main(argv=None) -> None:
     ap.add_argument("--layers", type=int, default=None, help="fewer layers (smoke runs only)")
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--exchange", choices=["collective", "peer"], default="collective")
     a = ap.parse_args(argv)
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -303,7 +472,7 @@ def main(argv=None) -> None:
     shard = shard_weights(read_quant8(img, dims), plan, rank, dev)
     del img
     P = torch.from_numpy(prompts(a.n_seq, a.tokens, dims.vocab, seed=0)).to(dev)
-    tp = TPPrefill(plan, shard, rank)
+    tp = TPPrefill(plan, shard, rank, exchange=a.exchange if world > 1 else "collective")
     for _ in range(a.warmup):
         tp.run(P)
     torch.cuda.synchronize()
@@ -327,9 +496,14 @@ def main(argv=None) -> None:
             "n_gpus": world, "ms_per_prefill": round(ms, 3),
             "tok_per_s": round(M / (ms / 1e3), 1),
             "gemm_tops_effective": round(gemm_ops / (ms / 1e3) / 1e12, 1),
-            "exchange": "int32 reduce-scatter + int8 all-gather + fp32 max-allreduce (NCCL)",
+            "exchange": ("int32 partial sums stored into the owners' memory by the GEMM "
+                         "epilogue, int8 rows broadcast by the LayerNorm kernel, fp32 row "
+                         "maxima, over NVLink peer memory" if a.exchange == "peer" and world > 1
+                         else "int32 reduce-scatter + int8 all-gather + fp32 max-allreduce "
+                              "(NCCL)"),
             "steps": a.steps, "warmup": a.warmup,
             "first_tokens": nxt[:4].tolist()}))
+    tp.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -210,6 +210,10 @@ int w8a8_advance_positions(int32_t *dst, const int32_t *src, int n, int delta, v
 
 /* amax[m] = max_k |X[m, k]| over the K columns given (K % 8 == 0). */
 int w8a8_row_amax(const gpt2_bf16_t *X, int64_t ldx, int M, int K, float *amax, void *stream);
+/* The same maxima written into n_out <= 8 arrays (host array of device
+ * pointers, e.g. this GPU's and its peers' exchange slots). */
+int w8a8_row_amax_to(const gpt2_bf16_t *X, int64_t ldx, int M, int K, float *const *amax,
+                     int n_out, void *stream);
 
 /* per_token_quant of a column block with the scale of the whole row: the
  * row's absolute maximum is the largest of n_amax partial maxima
@@ -233,6 +237,41 @@ int w8a8_reduce_residual_layernorm_quant(const int32_t *acc, int64_t lda, int n_
                                          int64_t ldh, const gpt2_bf16_t *gamma,
                                          const gpt2_bf16_t *beta, float eps, int8_t *Xq,
                                          int64_t ldq, float *sXq, void *stream);
+
+/* As above, and the quantized rows (gamma != NULL) are also stored into
+ * n_bcast <= 8 more buffers: row m to xq_bcast[j] + (bcast_row0 + m) * ldq and
+ * sx_bcast[j][bcast_row0 + m] (the other GPUs' all-gather buffers). */
+int w8a8_reduce_residual_layernorm_quant_bcast(
+    const int32_t *acc, int64_t lda, int n_slots, int64_t slot_stride, int M, int d,
+    const float *sX, const float *sW, const gpt2_bf16_t *bias, const gpt2_bf16_t *R, int64_t ldr,
+    gpt2_bf16_t *H, int64_t ldh, const gpt2_bf16_t *gamma, const gpt2_bf16_t *beta, float eps,
+    int8_t *Xq, int64_t ldq, float *sXq, int8_t *const *xq_bcast, float *const *sx_bcast,
+    int n_bcast, int64_t bcast_row0, void *stream);
+
+/* w8a8_gemm_s32 whose output row m goes to dst[m / rows_per_dst] +
+ * (m % rows_per_dst) * N: the partial sums of the rows other GPUs own are
+ * stored straight into their buffers (peer memory, 16-byte stores), the
+ * int32 reduce-scatter of a row-split GEMM without a separate collective. */
+int w8a8_gemm_s32_scatter(const int8_t *Xq, int M, int K, const int8_t *W, int N,
+                          int32_t *const *dst, int n_dst, int rows_per_dst, void *stream);
+
+/* ---- peer memory between the GPUs of one node (no counterpart in the
+ * reference) ----
+ * w8a8_peer_alloc: zero-filled device buffer + its 64-byte CUDA IPC handle;
+ * w8a8_peer_open maps another process's buffer (NVLink peer access).
+ * w8a8_peer_signal: after the work before it on the stream, writes `value`
+ * into each of the n <= 8 flag words (host array of device pointers, this or
+ * other GPUs) with system-scope release; w8a8_peer_wait: the work after it on
+ * the stream waits until the n flag words flags[0..n) of this GPU are >= value
+ * (system-scope acquire; gives up after ~2 s and records a device error). */
+int w8a8_peer_alloc(size_t bytes, void **ptr, void *ipc_handle);
+int w8a8_peer_open(const void *ipc_handle, void **ptr);
+int w8a8_peer_close(void *ptr);
+int w8a8_peer_free(void *ptr);
+/* Device-to-device copy on `stream` (either side may be a mapped peer buffer). */
+int w8a8_peer_copy(void *dst, const void *src, size_t bytes, void *stream);
+int w8a8_peer_signal(uint32_t *const *flags, int n, uint32_t value, void *stream);
+int w8a8_peer_wait(const uint32_t *flags, int n, uint32_t value, void *stream);
 
 /* w8a8_linear_qkv for a subset of the heads: Wqkv [3*d_heads, K] holds the
  * Q, K and V rows of those heads (d_heads = 64 * heads, a multiple of 32),

@@ -96,7 +96,7 @@ def test_tp_one_rank_matches_engine(cuda, large2_image):
     np.testing.assert_array_equal(got, want_logits)
 
 
-def _tp_rank(rank, world, port, img_path, p_path, out_dir):
+def _tp_rank(rank, world, port, img_path, p_path, out_dir, exchange="collective"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
@@ -109,9 +109,11 @@ def _tp_rank(rank, world, port, img_path, p_path, out_dir):
         P = np.load(p_path)
         plan = TPPlan.make(LARGE2, world)
         shard = shard_weights(read_quant8(img, LARGE2), plan, rank, f"cuda:{rank}")
-        nxt, logits = TPPrefill(plan, shard, rank, collectives=Collectives()).run(
-            torch.from_numpy(P).cuda())
+        tp = TPPrefill(plan, shard, rank, collectives=Collectives(), exchange=exchange)
+        for _ in range(2):  # twice: the exchange buffers and flags are reused
+            nxt, logits = tp.run(torch.from_numpy(P).cuda())
         torch.cuda.synchronize()
+        tp.close()
         np.save(os.path.join(out_dir, f"next{rank}.npy"), nxt.cpu().numpy())
         np.save(os.path.join(out_dir, f"logits{rank}.npy"), from_dev_bf16(logits))
         assert ops.device_error() == 0
@@ -120,14 +122,17 @@ def _tp_rank(rank, world, port, img_path, p_path, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp_two_ranks_match_engine(cuda, large2_image, tmp_path):
+@pytest.mark.parametrize("exchange", ["collective", "peer"])
+def test_tp_two_ranks_match_engine(cuda, large2_image, tmp_path, exchange):
+    """Two ranks, exchange through NCCL or through the library's peer-memory
+    kernels over NVLink: the same logits and tokens as one GPU, bit for bit."""
     P = prompts(4, 128, seed=9)
     want_next, want_logits = _engine_prefill(large2_image, LARGE2, P)
     np.save(tmp_path / "img.npy", large2_image)
     np.save(tmp_path / "p.npy", P)
-    port = 29600 + os.getpid() % 1000
+    port = 29600 + os.getpid() % 500 + (500 if exchange == "peer" else 0)
     mp.start_processes(_tp_rank, args=(2, port, str(tmp_path / "img.npy"),
-                                       str(tmp_path / "p.npy"), str(tmp_path)),
+                                       str(tmp_path / "p.npy"), str(tmp_path), exchange),
                        nprocs=2, join=True, start_method="spawn")
     for r in range(2):
         np.testing.assert_array_equal(np.load(tmp_path / f"next{r}.npy"), want_next)
