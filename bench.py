@@ -214,7 +214,7 @@ def kernel_rooflines(count: int, peaks: dict, dev) -> dict:
     q = torch.randn((B, d), device=dev).to(torch.bfloat16)
     o = torch.empty((B, d), dtype=torch.bfloat16, device=dev)
     nctx = torch.full((B,), n, dtype=torch.int32, device=dev)
-    ws = torch.empty((_lib.core().w8a8_attention_decode_workspace_size(B, H, C),),
+    ws = torch.zeros((_lib.core().w8a8_attention_decode_workspace_size(B, H, C),),
                      dtype=torch.uint8, device=dev)
     ms = time_kernel(lambda: ops.attention_decode(q, K, V, C * d, nctx, C, H, out=o,
                                                   workspace=ws), 50, stream)

@@ -63,6 +63,7 @@ SIGNATURES = {
     "w8a8_attention_decode_workspace_size": (_sz, [_i, _i, _i]),
     "w8a8_attention_decode": (_i, [_p, _i64, _p, _p, _i64, _i, _p, _i, _i, _i, _p, _i64, _p, _sz, _p]),
     "w8a8_attention_decode_launches": (_i, [_i, _i, _i]),
+    "w8a8_attention_decode_workspace_reset": (_i, [_p, _sz, _p]),
     "w8a8_attention_decode_quant": (_i, [_p, _i64, _p, _p, _i64, _i, _p, _i, _i, _i, _p, _i64, _p,
                                          _p, _p, _sz, _p]),
     "w8a8_lm_head": (_i, [_p, _i64, _i, _i, _p, _i, _p, _i64, _p]),

@@ -6,10 +6,11 @@
 
 namespace w8a8 {
 
-// Smallest token count that takes the tensor-core path; below it the
-// weight-streaming GEMV wins (the MMA's N dimension cannot go below 16 and
-// the work is pure HBM streaming).
-constexpr int kTcMinM = 16;
+// Smallest token count that takes the tensor-core path. A single token takes
+// the weight-streaming GEMV; from two tokens on, the cluster split-K GEMM
+// (tokens padded to the MMA's N = 32, zero rows from TMA's out-of-bounds fill)
+// is faster than a GEMV that re-reads the token rows per output channel.
+constexpr int kTcMinM = 2;
 
 static bool tc_ok_i8(const void *X, int64_t ldx, const void *W, int K) {
   return (K % 16 == 0) && (ldx % 16 == 0) && aligned16(X) && aligned16(W);
@@ -297,8 +298,13 @@ extern "C" int w8a8_attention_prefill(const gpt2_bf16_t *Q, int64_t ldq, const g
 extern "C" size_t w8a8_attention_decode_workspace_size(int n_seq, int n_head, int max_ctx) {
   // sized for the largest split count the launcher may pick
   int splits = 1;
-  while (splits * 2 * 64 <= max_ctx) splits *= 2;
+  while (splits * 2 * 128 <= max_ctx) splits *= 2;
   return decode_workspace_bytes(n_seq, n_head, max_ctx, splits);
+}
+
+extern "C" int w8a8_attention_decode_workspace_reset(void *workspace, size_t workspace_bytes,
+                                                    void *stream) {
+  return decode_workspace_reset(workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int w8a8_attention_decode_launches(int n_seq, int n_head, int max_ctx) {

@@ -624,19 +624,34 @@ __global__ void __launch_bounds__(kFusedThreads) attention_decode_fused_kernel(D
   if (a.Xq) quant_row_when_complete<NT>(a, b, tid, s_red, &s_flag);
 }
 
+// One CTA per (sequence, head) as soon as the pairs alone cover the SMs (one
+// launch, K and V read once); below that, split the keys so that about two
+// CTAs land on every SM, with at least 128 keys per split. Measured on GPT-2
+// large decode steps: 8 sequences (160 pairs) run 15% faster unsplit than in
+// 2 splits, a single sequence 6% faster in 8 splits than in 16.
 static int decode_splits(int n_seq, int n_head, int max_ctx, int sm_count) {
   const int pairs = n_seq * n_head;
+  if (pairs >= sm_count) return 1;
   int splits = 1;
-  while (pairs * splits < 2 * sm_count && splits * 2 * 64 <= max_ctx) splits *= 2;
+  while (pairs * splits < 2 * sm_count && splits * 2 * 128 <= max_ctx) splits *= 2;
   return splits;
 }
 
-// Per-sequence tickets of the fused output quantization live in the last
-// kSeqTicketBytes of the caller's workspace: a fixed place for a given
-// buffer whatever the shape of the call, so that they stay zero between calls
-// that use the buffer for different batch sizes.
+// The ticket counters (per (sequence, head) for the split path, per sequence
+// for the fused output quantization) live in the last kTicketBytes of the
+// caller's workspace: a fixed place for a given buffer whatever the shape of
+// the call. Every call leaves them zero (the last CTA resets its counter), so
+// a workspace zero-filled once needs no clearing between calls — in a CUDA
+// graph, no memset node per layer.
+constexpr int kMaxPairTickets = 16384;
 constexpr int kMaxSeqTickets = 4096;
-constexpr size_t kSeqTicketBytes = kMaxSeqTickets * sizeof(int);
+constexpr size_t kTicketBytes = (size_t)(kMaxPairTickets + kMaxSeqTickets) * sizeof(int);
+
+int decode_workspace_reset(void *ws, size_t ws_bytes, cudaStream_t s) {
+  if (!ws || ws_bytes < kTicketBytes + 16) return W8A8_ERR_INVALID;
+  void *t = reinterpret_cast<void *>((((uintptr_t)ws + ws_bytes - kTicketBytes) & ~(uintptr_t)15));
+  return cudaMemsetAsync(t, 0, kTicketBytes, s) == cudaSuccess ? W8A8_OK : W8A8_ERR_CUDA;
+}
 
 int decode_launches(int n_seq, int n_head, int max_ctx, int sm_count) {
   return decode_splits(n_seq, n_head, max_ctx, sm_count) == 1 ? 1 : 2;
@@ -646,8 +661,7 @@ size_t decode_workspace_bytes(int n_seq, int n_head, int max_ctx, int splits) {
   size_t scores = (size_t)n_seq * n_head * max_ctx * 2;
   scores = (scores + 255) & ~(size_t)255;
   size_t parts = (size_t)n_seq * n_head * splits * kHD * 4;
-  size_t tick = (size_t)n_seq * n_head * 4;
-  return scores + parts + tick + 512 + kSeqTicketBytes;  // 512: base alignment slack
+  return scores + parts + 512 + kTicketBytes;  // 512: base alignment slack
 }
 
 int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
@@ -676,10 +690,9 @@ int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
   a.scores = (uint16_t *)w;
   size_t scores = ((size_t)n_seq * n_head * max_ctx * 2 + 255) & ~(size_t)255;
   a.partials = (float *)(w + scores);
-  a.tickets = (int *)(w + scores + (size_t)n_seq * n_head * a.splits * kHD * 4);
-  if (Xq && n_seq > kMaxSeqTickets) return W8A8_ERR_UNSUPPORTED;
-  a.seq_tickets = reinterpret_cast<int *>(
-      (((uintptr_t)ws + ws_bytes - kSeqTicketBytes) & ~(uintptr_t)15));
+  if (n_seq * n_head > kMaxPairTickets || n_seq > kMaxSeqTickets) return W8A8_ERR_UNSUPPORTED;
+  a.tickets = reinterpret_cast<int *>((((uintptr_t)ws + ws_bytes - kTicketBytes) & ~(uintptr_t)15));
+  a.seq_tickets = a.tickets + kMaxPairTickets;
   a.Xq = Xq;
   a.sXq = sXq;
   if (a.splits == 1) {
@@ -687,9 +700,6 @@ int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
     return check_launch("attention_decode_fused");
   }
   dim3 grid(n_seq * n_head, a.splits);
-  if (a.splits > 1 &&
-      cudaMemsetAsync(a.tickets, 0, (size_t)n_seq * n_head * sizeof(int), s) != cudaSuccess)
-    return W8A8_ERR_CUDA;
   launch_pdl(attention_decode_scores_kernel, dim3(grid), dim3(256), 0, s, a);
   int st = check_launch("attention_decode_scores");
   if (st) return st;

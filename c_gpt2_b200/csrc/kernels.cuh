@@ -121,6 +121,7 @@ int launch_attention_prefill(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
                              uint16_t *O, int64_t ldo, cudaStream_t s);
 size_t decode_workspace_bytes(int n_seq, int n_head, int max_ctx, int splits);
 int decode_launches(int n_seq, int n_head, int max_ctx, int sm_count);
+int decode_workspace_reset(void *ws, size_t ws_bytes, cudaStream_t s);
 int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
                             const uint16_t *Vc, int64_t seq_stride, int n_seq,
                             const int32_t *n_ctx, int max_ctx, int n_head, uint16_t *O,

@@ -119,6 +119,10 @@ void attention_decode_cuda(act_t *Q_d, act_t *k_cache_layer, act_t *v_cache_laye
                            act_t *out, void *workspace, size_t workspace_bytes) {
   if (n_tokens <= 0) return;
   const int row = n_tokens - 1;
+  /* the workspace is gpt2.c's score buffer, also used by other kernels:
+   * clear the attention's ticket counters before each call */
+  check(w8a8_attention_decode_workspace_reset(workspace, workspace_bytes, NULL),
+        "attention_decode_cuda (workspace)", n_tokens, d_model);
   check(w8a8_attention_decode((const gpt2_bf16_t *)Q_d + (size_t)row * d_model, d_model,
                               (const gpt2_bf16_t *)k_cache_layer,
                               (const gpt2_bf16_t *)v_cache_layer, 0, 1, NULL, n_tokens, nof_heads,

@@ -221,8 +221,8 @@ def attention_decode(Q, Kc, Vc, seq_stride, n_ctx, max_ctx, n_head, out=None, wo
     d = n_head * 64
     O = out if out is not None else torch.empty((n_seq, d), dtype=torch.bfloat16, device=Q.device)
     need = core().w8a8_attention_decode_workspace_size(n_seq, n_head, max_ctx)
-    if workspace is None:
-        workspace = torch.empty((need,), dtype=torch.uint8, device=Q.device)
+    if workspace is None:  # zero-filled: the ticket counters must start at zero
+        workspace = torch.zeros((need,), dtype=torch.uint8, device=Q.device)
     check(core().w8a8_attention_decode(_ptr(Q), Q.stride(0), _ptr(Kc), _ptr(Vc), seq_stride,
                                        n_seq, _ptr(n_ctx), max_ctx, n_head, 64, _ptr(O),
                                        O.stride(0), _ptr(workspace), workspace.numel(),

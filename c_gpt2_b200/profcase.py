@@ -74,7 +74,7 @@ def attention_decode(a) -> None:
     q = torch.randn((B, d), device="cuda", generator=g).to(torch.bfloat16)
     o = torch.empty((B, d), dtype=torch.bfloat16, device="cuda")
     nctx = torch.full((B,), n, dtype=torch.int32, device="cuda")
-    ws = torch.empty((_lib.core().w8a8_attention_decode_workspace_size(B, H, C),),
+    ws = torch.zeros((_lib.core().w8a8_attention_decode_workspace_size(B, H, C),),
                      dtype=torch.uint8, device="cuda")
 
     def run():

@@ -154,9 +154,13 @@ int w8a8_attention_prefill(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t 
  * Sequence b attends its first n_ctx[b] cache rows (n_ctx includes the new
  * token, device array). max_ctx bounds every n_ctx[b] (<= 1024); with
  * n_ctx == NULL every sequence attends exactly max_ctx rows. The
- * workspace holds scores and split partials; size it with
- * w8a8_attention_decode_workspace_size(). */
+ * workspace holds scores, split partials and, in its last bytes, ticket
+ * counters that must be zero before a call: zero-fill the workspace once
+ * (every call leaves the counters zero), or call
+ * w8a8_attention_decode_workspace_reset after using the memory for anything
+ * else. Size it with w8a8_attention_decode_workspace_size(). */
 size_t w8a8_attention_decode_workspace_size(int n_seq, int n_head, int max_ctx);
+int w8a8_attention_decode_workspace_reset(void *workspace, size_t workspace_bytes, void *stream);
 int w8a8_attention_decode(const gpt2_bf16_t *Q, int64_t ldq, const gpt2_bf16_t *Kc,
                           const gpt2_bf16_t *Vc, int64_t seq_stride, int n_seq,
                           const int32_t *n_ctx, int max_ctx, int n_head, int hd,
