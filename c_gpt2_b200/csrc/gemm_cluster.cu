@@ -84,45 +84,63 @@ __device__ __forceinline__ int4 ld_dsmem_v4(uint32_t addr) {
   return v;
 }
 
+// Epilogue inputs of 4 consecutive channels n..n+3 of token m (loaded before
+// the partial sums so that both latencies overlap).
+struct Epi4In {
+  float sx;
+  float sw[4];
+  float b[4];
+  float r[4];
+};
+
+template <int EPI>
+__device__ __forceinline__ Epi4In load4(const ClusterGemmArgs &a, int m, int n) {
+  Epi4In in = {};
+  if (EPI == EPI_S32) return in;
+  in.sx = a.sX[m];
+  const float4 sw = __ldg(reinterpret_cast<const float4 *>(a.sW + n));
+  in.sw[0] = sw.x;
+  in.sw[1] = sw.y;
+  in.sw[2] = sw.z;
+  in.sw[3] = sw.w;
+  if (EPI >= EPI_BIAS && EPI <= EPI_QKV) {
+    const uint2 b = __ldg(reinterpret_cast<const uint2 *>(a.bias + n));
+    in.b[0] = __uint_as_float(b.x << 16);
+    in.b[1] = __uint_as_float(b.x & 0xffff0000u);
+    in.b[2] = __uint_as_float(b.y << 16);
+    in.b[3] = __uint_as_float(b.y & 0xffff0000u);
+  }
+  if (EPI == EPI_RESID) {
+    const uint2 r = *reinterpret_cast<const uint2 *>(a.R + (int64_t)m * a.ldr + n);
+    in.r[0] = __uint_as_float(r.x << 16);
+    in.r[1] = __uint_as_float(r.x & 0xffff0000u);
+    in.r[2] = __uint_as_float(r.y << 16);
+    in.r[3] = __uint_as_float(r.y & 0xffff0000u);
+  }
+  return in;
+}
+
 // Epilogue of 4 consecutive channels n..n+3 (same QKV segment) of token m.
 template <int EPI>
-__device__ __forceinline__ void store4(const ClusterGemmArgs &a, int m, int n, const int4 &acc) {
+__device__ __forceinline__ void store4(const ClusterGemmArgs &a, int m, int n, const int4 &acc,
+                                       const Epi4In &in) {
   const int32_t v[4] = {acc.x, acc.y, acc.z, acc.w};
   if (EPI == EPI_S32) {
     *reinterpret_cast<int4 *>(s32_row(a, m) + n) = acc;
     return;
   }
-  const float sx = a.sX[m];
-  const float4 sw = __ldg(reinterpret_cast<const float4 *>(a.sW + n));
-  const float swv[4] = {sw.x, sw.y, sw.z, sw.w};
-  float bv[4] = {0.f, 0.f, 0.f, 0.f};
-  if (EPI >= EPI_BIAS && EPI <= EPI_QKV) {
-    const uint2 b = __ldg(reinterpret_cast<const uint2 *>(a.bias + n));
-    bv[0] = __uint_as_float(b.x << 16);
-    bv[1] = __uint_as_float(b.x & 0xffff0000u);
-    bv[2] = __uint_as_float(b.y << 16);
-    bv[3] = __uint_as_float(b.y & 0xffff0000u);
-  }
-  float rv[4] = {0.f, 0.f, 0.f, 0.f};
-  if (EPI == EPI_RESID) {
-    const uint2 r = *reinterpret_cast<const uint2 *>(a.R + (int64_t)m * a.ldr + n);
-    rv[0] = __uint_as_float(r.x << 16);
-    rv[1] = __uint_as_float(r.x & 0xffff0000u);
-    rv[2] = __uint_as_float(r.y << 16);
-    rv[3] = __uint_as_float(r.y & 0xffff0000u);
-  }
   uint16_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float t = dequant_bf(v[i], swv[i], sx);
+    const float t = dequant_bf(v[i], in.sw[i], in.sx);
     if (EPI == EPI_DEQUANT) {
       o[i] = f2bf(t);
     } else if (EPI == EPI_BIAS || EPI == EPI_QKV) {
-      o[i] = f2bf(__fadd_rn(t, bv[i]));
+      o[i] = f2bf(__fadd_rn(t, in.b[i]));
     } else if (EPI == EPI_RESID) {
-      o[i] = f2bf(__fadd_rn(rv[i], add_bf(t, bv[i])));
+      o[i] = f2bf(__fadd_rn(in.r[i], add_bf(t, in.b[i])));
     } else {  // EPI_GELU
-      o[i] = f2bf(gelu_tanh(add_bf(t, bv[i])));
+      o[i] = f2bf(gelu_tanh(add_bf(t, in.b[i])));
     }
   }
   const uint2 packed = make_uint2((uint32_t)o[0] | ((uint32_t)o[1] << 16),
@@ -285,16 +303,26 @@ __global__ void __launch_bounds__(kCThreads, 1)
     for (int g = g0 + (int)threadIdx.x; g < g1; g += kCThreads) {
       const int tok = g >> 5, ch = (g & 31) * 4;
       const int m = tok, n = n0 + ch;
+      const bool live = m < a.M && n < a.N;
+      Epi4In in = {};
+      if (live) in = load4<EPI>(a, m, n);
       const int32_t *src = partial + tok * kCBM + ch;
+      // all ks loads in flight before the first addition
+      int4 p[kCMaxCluster];
+#pragma unroll
+      for (int r = 0; r < kCMaxCluster; ++r)
+        if (r < a.ksplit) p[r] = ld_dsmem_v4(dsmem_addr(src, (uint32_t)r));
       int4 sum = make_int4(0, 0, 0, 0);
-      for (int r = 0; r < a.ksplit; ++r) {
-        const int4 p = ld_dsmem_v4(dsmem_addr(src, (uint32_t)r));
-        sum.x += p.x;
-        sum.y += p.y;
-        sum.z += p.z;
-        sum.w += p.w;
+#pragma unroll
+      for (int r = 0; r < kCMaxCluster; ++r) {
+        if (r < a.ksplit) {
+          sum.x += p[r].x;
+          sum.y += p[r].y;
+          sum.z += p[r].z;
+          sum.w += p[r].w;
+        }
       }
-      if (m < a.M && n < a.N) store4<EPI>(a, m, n, sum);
+      if (live) store4<EPI>(a, m, n, sum, in);
     }
   }
   cluster_sync_all();  // no CTA leaves while another still reads its partial tile
