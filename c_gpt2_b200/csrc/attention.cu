@@ -110,7 +110,7 @@ __device__ __forceinline__ void softmax_row_inplace(uint16_t *row, int n, int n_
 // ---------------------------------------------------------------------------
 // prefill
 // ---------------------------------------------------------------------------
-constexpr int kQT = 64;          // query rows per CTA
+constexpr int kQT = 32;          // query rows per CTA
 constexpr int kKT = 64;          // keys per K/V tile
 constexpr int kTileStride = 72;  // bf16 elements per smem tile row (64 + 8 pad)
 
@@ -125,9 +125,12 @@ struct PrefillArgs {
   int s_stride;  // bf16 elements per score row in smem
 };
 
-// 8 warps per CTA: warp w owns query rows 16*(w%4) .. +15 and, in Q.K^T, keys
-// [32*(w/4), +32) of each 64-key tile, in P.V head dims [32*(w/4), +32).
-// Every output element is still accumulated by one thread in the same order.
+// 8 warps per CTA: warp w owns query rows 16*(w%2) .. +15 and, in Q.K^T, keys
+// [16*(w/2), +16) of each 64-key tile, in P.V head dims [16*(w/2), +16).
+// Every output element is accumulated by one thread in key order. 32-query
+// tiles keep the bf16 score rows of a 1024-token causal block in 66 KB of
+// shared memory, so two CTAs (16 warps) share an SM at 1024 tokens and four
+// at 512.
 constexpr int kPrefillThreads = 256;
 
 __global__ void __launch_bounds__(kPrefillThreads)
@@ -142,21 +145,22 @@ __global__ void __launch_bounds__(kPrefillThreads)
   const int n_ktiles = (nk + kKT - 1) / kKT;
   const int nk_pad = n_ktiles * kKT;
 
-  uint16_t *sQ = sm;                            // [64][72]
+  uint16_t *sQ = sm;                            // [32][72]
   uint16_t *sKV = sQ + kQT * kTileStride;       // [2][64][72]
-  uint16_t *sS = sKV + 2 * kKT * kTileStride;   // [64][s_stride]
+  uint16_t *sS = sKV + 2 * kKT * kTileStride;   // [32][s_stride]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
-  const int mt = warp & 3, half = warp >> 2;
+  const int mt = warp & 1, quarter = warp >> 1;
 
   const uint16_t *Kb = a.Kc + (int64_t)b * a.seq_stride + h * kHD;
   const uint16_t *Vb = a.Vc + (int64_t)b * a.seq_stride + h * kHD;
   const uint16_t *Qb = a.Q + ((int64_t)b * a.T) * a.ldq + h * kHD;
 
-  // tile loader: 64 rows x 128 bytes = 512 x 16 B chunks, 2 per thread
-  auto load_tile = [&](uint16_t *dst, const uint16_t *src, int64_t ld, int row0, int nrows) {
-#pragma unroll
-    for (int i = 0; i < 512 / kPrefillThreads; ++i) {
+  // tile loader: rows x 128 bytes in 16 B chunks (64-row K/V tiles: 2 per
+  // thread; the 32-row Q tile: 1)
+  auto load_tile = [&](uint16_t *dst, const uint16_t *src, int64_t ld, int row0, int nrows,
+                       int rows) {
+    for (int i = 0; i < rows * 8 / kPrefillThreads; ++i) {
       int c = tid + kPrefillThreads * i;
       int r = c >> 3, cc = (c & 7) * 8;
       bool ok = row0 + r < nrows;
@@ -165,8 +169,8 @@ __global__ void __launch_bounds__(kPrefillThreads)
     }
   };
 
-  load_tile(sQ, Qb, a.ldq, q0, a.T);
-  load_tile(sKV, Kb, a.d, 0, nk);
+  load_tile(sQ, Qb, a.ldq, q0, a.T, kQT);
+  load_tile(sKV, Kb, a.d, 0, nk, kKT);
   cp_async_commit();
 
   // Q fragments (rows 16*mt .. +15), 4 k-steps of 16
@@ -178,7 +182,7 @@ __global__ void __launch_bounds__(kPrefillThreads)
     cp_async_wait_all();
     __syncthreads();
     if (kt + 1 < n_ktiles) {
-      load_tile(sKV + ((kt + 1) & 1) * kKT * kTileStride, Kb, a.d, (kt + 1) * kKT, nk);
+      load_tile(sKV + ((kt + 1) & 1) * kKT * kTileStride, Kb, a.d, (kt + 1) * kKT, nk, kKT);
       cp_async_commit();
     }
     if (kt == 0) {
@@ -189,29 +193,26 @@ __global__ void __launch_bounds__(kPrefillThreads)
       }
     }
     const uint16_t *sK = sKV + (kt & 1) * kKT * kTileStride;
-    float c[4][4];
+    float c[2][4];
 #pragma unroll
-    for (int nb = 0; nb < 4; ++nb)
+    for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
       for (int i = 0; i < 4; ++i) c[nb][i] = 0.f;
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {  // pairs of 8-key blocks of this warp's 32 keys
-        const int nb2 = half * 2 + j;
-        const int q = lane >> 3;
-        const uint16_t *p =
-            sK + (nb2 * 16 + (q >> 1) * 8 + (lane & 7)) * kTileStride + ks * 16 + (q & 1) * 8;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(smem_u32(p), b0, b1, b2, b3);
-        mma_bf16_16816(c[2 * j], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
-        mma_bf16_16816(c[2 * j + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
-      }
+    for (int ks = 0; ks < 4; ++ks) {  // the pair of 8-key blocks of this warp's 16 keys
+      const int nb2 = quarter;
+      const int q = lane >> 3;
+      const uint16_t *p =
+          sK + (nb2 * 16 + (q >> 1) * 8 + (lane & 7)) * kTileStride + ks * 16 + (q & 1) * 8;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(smem_u32(p), b0, b1, b2, b3);
+      mma_bf16_16816(c[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+      mma_bf16_16816(c[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
     }
     // scale, round, store (columns beyond a row's causal limit are never read)
 #pragma unroll
-    for (int nb = 0; nb < 4; ++nb) {
-      const int col = kt * kKT + half * 32 + nb * 8 + 2 * tq;
+    for (int nb = 0; nb < 2; ++nb) {
+      const int col = kt * kKT + quarter * 16 + nb * 8 + 2 * tq;
       const int r0 = mt * 16 + g;
       uint32_t lo = (uint32_t)f2bf(c[nb][0] * 0.125f) | ((uint32_t)f2bf(c[nb][1] * 0.125f) << 16);
       uint32_t hi = (uint32_t)f2bf(c[nb][2] * 0.125f) | ((uint32_t)f2bf(c[nb][3] * 0.125f) << 16);
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(kPrefillThreads)
   __syncthreads();
 
   // prefetch V tile 0 while the softmax runs
-  load_tile(sKV, Vb, a.d, 0, nk);
+  load_tile(sKV, Vb, a.d, 0, nk, kKT);
   cp_async_commit();
 
   // ---- phase B: causal softmax per row (warp w: rows w, w+8, ...) ----
@@ -232,17 +233,17 @@ __global__ void __launch_bounds__(kPrefillThreads)
     softmax_row_inplace(sS + r * a.s_stride, n, nk_pad, lane);
   }
 
-  // ---- phase C: O = P V (this warp: 16 rows x 32 head dims) ----
-  float o[4][4];
+  // ---- phase C: O = P V (this warp: 16 rows x 16 head dims) ----
+  float o[2][4];
 #pragma unroll
-  for (int nb = 0; nb < 4; ++nb)
+  for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[nb][i] = 0.f;
   for (int kt = 0; kt < n_ktiles; ++kt) {
     cp_async_wait_all();
     __syncthreads();
     if (kt + 1 < n_ktiles) {
-      load_tile(sKV + ((kt + 1) & 1) * kKT * kTileStride, Vb, a.d, (kt + 1) * kKT, nk);
+      load_tile(sKV + ((kt + 1) & 1) * kKT * kTileStride, Vb, a.d, (kt + 1) * kKT, nk, kKT);
       cp_async_commit();
     }
     const uint16_t *sV = sKV + (kt & 1) * kKT * kTileStride;
@@ -252,24 +253,23 @@ __global__ void __launch_bounds__(kPrefillThreads)
       const uint16_t *pp =
           sS + (mt * 16 + (lane & 15)) * a.s_stride + kt * kKT + ks * 16 + (lane >> 4) * 8;
       ldsm_x4(smem_u32(pp), pa0, pa1, pa2, pa3);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {  // pairs of 8-dim blocks of this warp's 32 dims
-        const int nb2 = half * 2 + j;
+      {  // the pair of 8-dim blocks of this warp's 16 dims
+        const int nb2 = quarter;
         const int q = lane >> 3;
         const uint16_t *p =
             sV + (ks * 16 + (q & 1) * 8 + (lane & 7)) * kTileStride + nb2 * 16 + (q >> 1) * 8;
         uint32_t b0, b1, b2, b3;
         ldsm_x4_t(smem_u32(p), b0, b1, b2, b3);
-        mma_bf16_16816(o[2 * j], pa0, pa1, pa2, pa3, b0, b1);
-        mma_bf16_16816(o[2 * j + 1], pa0, pa1, pa2, pa3, b2, b3);
+        mma_bf16_16816(o[0], pa0, pa1, pa2, pa3, b0, b1);
+        mma_bf16_16816(o[1], pa0, pa1, pa2, pa3, b2, b3);
       }
     }
   }
   // ---- store O ----
   const int r0 = mt * 16 + g;
 #pragma unroll
-  for (int nb = 0; nb < 4; ++nb) {
-    const int col = h * kHD + half * 32 + nb * 8 + 2 * tq;
+  for (int nb = 0; nb < 2; ++nb) {
+    const int col = h * kHD + quarter * 16 + nb * 8 + 2 * tq;
     if (q0 + r0 < a.T) {
       uint32_t v = (uint32_t)f2bf(o[nb][0]) | ((uint32_t)f2bf(o[nb][1]) << 16);
       *reinterpret_cast<uint32_t *>(a.O + ((int64_t)b * a.T + q0 + r0) * a.ldo + col) = v;
