@@ -258,13 +258,47 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
   }
 }
 
-__device__ __forceinline__ float fold_slots(RowShared &sh, int t) {
-  __syncthreads();
-  for (int h = 512; h > 0; h >>= 1) {
-    for (int i = t; i < h; i += kRowThreads) sh.slots[i] += sh.slots[i + h];
-    __syncthreads();
+// The reference's 1024-slot fold (h = 512 .. 1: slot i += slot i + h) over
+// the 8 slots each of the 128 threads holds (thread t: slots 8t .. 8t+7):
+// h = 512 and 256 through shared memory, h = 128 .. 8 as shuffle-downs inside
+// warp 0 (slot 8t + e + h sits in thread t + h/8), h = 4, 2, 1 in thread 0's
+// registers. The same additions in the same order, with three block
+// barriers instead of ten. `s` is consumed.
+__device__ __forceinline__ float fold_slots(RowShared &sh, float (&s)[8], int t) {
+  static_assert(kRowThreads == 128, "fold_slots: 128 threads x 8 slots");
+  if (t >= 64) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sh.slots[8 * (t - 64) + e] = s[e];
   }
-  const float v = sh.slots[0];
+  __syncthreads();
+  if (t < 64) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[e] += sh.slots[8 * t + e];  // h = 512
+  }
+  __syncthreads();
+  if (t >= 32 && t < 64) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sh.slots[8 * (t - 32) + e] = s[e];
+  }
+  __syncthreads();
+  if (t < 32) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[e] += sh.slots[8 * t + e];  // h = 256
+#pragma unroll
+    for (int h = 16; h >= 1; h >>= 1) {  // h = 128 .. 8
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s[e] += __shfl_down_sync(0xffffffffu, s[e], h);
+    }
+    if (t == 0) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[e] += s[e + 4];  // h = 4
+      s[0] += s[2];                                   // h = 2
+      s[1] += s[3];
+      sh.red[0] = s[0] + s[1];                        // h = 1
+    }
+  }
+  __syncthreads();
+  const float v = sh.red[0];
   __syncthreads();
   return v;
 }
@@ -404,9 +438,7 @@ __device__ __forceinline__ void ln_quant_tail(RowShared &sh, const uint4 (&x)[kM
       for (int e = 0; e < 8; ++e) s[e] += f[e];
     }
   }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) sh.slots[8 * t + e] = s[e];
-  const float mean = fold_slots(sh, t) / (float)d;
+  const float mean = fold_slots(sh, s, t) / (float)d;
   // variance (layernorm.cu:45-66): diff*diff contracted into the running sum
 #pragma unroll
   for (int e = 0; e < 8; ++e) s[e] = 0.0f;
@@ -422,9 +454,7 @@ __device__ __forceinline__ void ln_quant_tail(RowShared &sh, const uint4 (&x)[kM
       }
     }
   }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) sh.slots[8 * t + e] = s[e];
-  const float variance = fold_slots(sh, t) / (float)d;
+  const float variance = fold_slots(sh, s, t) / (float)d;
   const float inv_std_dev = rsqrtf(variance + eps);
   // normalise + affine, bf16 (layernorm.cu:73-77)
   uint4 y[kMaxVec];
