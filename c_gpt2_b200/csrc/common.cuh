@@ -29,6 +29,27 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
   return *reinterpret_cast<uint16_t *>(&b);
 }
 __device__ __forceinline__ float round_bf(float f) { return bf2f(f2bf(f)); }
+// Two round-to-nearest-even conversions in one instruction: lo -> bits 0..15,
+// hi -> bits 16..31 (each rounded exactly as f2bf rounds it).
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&b);
+}
+// Two bf16 additions (round to nearest even), operands and result packed as
+// bf16x2. For bf16 operands this is bit-identical to f2bf(fp32(a) + fp32(b)):
+// the fp32 sum of two bf16 values is exact unless their exponents differ by
+// more than 16, and then both forms return the larger operand.
+__device__ __forceinline__ uint32_t add_bf2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// round_bf of two values, through one paired conversion.
+__device__ __forceinline__ void round_bf2(float &lo, float &hi) {
+  const uint32_t p = pack_bf2(lo, hi);
+  lo = __uint_as_float(p << 16);
+  hi = __uint_as_float(p & 0xffff0000u);
+}
 
 // ---------------------------------------------------------------------------
 // Error reporting. Kernels never trap: a failed bounded wait or a bad shape
@@ -121,6 +142,12 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, ui
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+// Pull one box of a tensor map into L2 (nothing is written to shared memory).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void *tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap),
+               "r"(x), "r"(y)
+               : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");

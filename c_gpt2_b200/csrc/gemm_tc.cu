@@ -5,9 +5,9 @@
 // [tokens, IN]). Two orientations of the same pipeline:
 //
 //   token-major (prefill, M > 128): A = 128 token rows, B = BN weight rows.
-//     TMEM lane = token, columns = output channels, so each epilogue thread
-//     owns a run of consecutive outputs of one row: 16-byte loads of the
-//     residual and 16-byte stores of the result.
+//     TMEM lane = token, columns = output channels. Each epilogue warp turns
+//     its 32 x 16 blocks into whole-sector coalesced stores (and residual
+//     loads) through a 1 KiB shared buffer; see epilogue_tm.
 //   channel-major (decode, M <= 128): A = 128 weight rows, B = the BN tokens
 //     of the batch (16..128). When the output tiles alone cannot occupy the
 //     GPU the reduction is split over K; partial int32 sums meet in a
@@ -18,6 +18,8 @@
 // warp 1 TMEM allocator + single-thread MMA issuer (kind::i8 -> s32, or
 // kind::f16 with bf16 operands -> f32 for the LM head), warps 2..17 the
 // epilogue (4 warps per TMEM lane quarter, splitting the 32-column chunks).
+// In token-major residual GEMMs the TMA warp also pulls the next tile's
+// residual block into L2 (one tensor-map prefetch per tile).
 // The accumulator is double-buffered in TMEM so the epilogue of one tile
 // overlaps the main loop of the next. Every wait is bounded: a stalled
 // pipeline records an error code and the kernel returns.
@@ -29,6 +31,7 @@
 #include <stddef.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "epilogue.cuh"
@@ -54,6 +57,7 @@ struct GemmArgs : LinearArgs {
   int32_t *ws;           // [M][N] int32 partial sums, zero between calls
   int *tickets;          // one per tile
   int *err;
+  int vec_params;        // sW and bias 16-byte aligned (token-major epilogue)
 };
 
 struct __align__(16) SmemCtl {
@@ -67,13 +71,7 @@ struct __align__(16) SmemCtl {
   int consumed;    // k-iterations consumed by the MMA thread (for abort drain)
   int last_flag;   // split-K: this CTA holds the last partial of the tile
   int vote[2][kEpiWarps];
-  // token-major: per-channel scales and biases of the B tile, read as 16- and
-  // 8-byte vectors, hence the explicit alignment
-  alignas(16) float tile_sw[256];
-  alignas(16) uint16_t tile_bias[256];
 };
-static_assert(offsetof(SmemCtl, tile_sw) % 16 == 0, "tile_sw must be 16-byte aligned");
-static_assert(offsetof(SmemCtl, tile_bias) % 16 == 0, "tile_bias must be 16-byte aligned");
 
 // ---------------------------------------------------------------------------
 // channel-major epilogue: one output channel n per thread, r[i] = token mbase+i
@@ -188,73 +186,349 @@ __device__ __forceinline__ void final_from_ws(const GemmArgs &a, int n0, int m0,
 }
 
 // ---------------------------------------------------------------------------
-// token-major epilogue: one token row m per thread, r[j] = channel nbase+j.
-// Requires N % 32 == 0 and 16-byte aligned rows (checked on the host).
+// token-major epilogue, int32 output (tensor-parallel partial sums): one token
+// row m per thread, r[j] = channel nbase+j, written to the (possibly remote)
+// row of s32_row().
 // ---------------------------------------------------------------------------
-template <int EPI>
-__device__ __forceinline__ void finish_chunk_tm(const GemmArgs &a, const SmemCtl *ctl, int m,
-                                                float sx, int64_t kv_row, int nbase, int jbase,
-                                                const uint32_t (&r)[32]) {
+__device__ __forceinline__ void finish_chunk_tm_s32(const GemmArgs &a, int m, int nbase,
+                                                    const uint32_t (&r)[32]) {
   if (m >= a.M || nbase >= a.N) return;
-  if (EPI == EPI_S32) {
-    int4 *dst = reinterpret_cast<int4 *>(s32_row(a, m) + nbase);
+  int4 *dst = reinterpret_cast<int4 *>(s32_row(a, m) + nbase);
 #pragma unroll
-    for (int v = 0; v < 8; ++v)
-      dst[v] = make_int4((int)r[4 * v], (int)r[4 * v + 1], (int)r[4 * v + 2], (int)r[4 * v + 3]);
-    return;
-  }
-  uint4 rv[4];
-  if (EPI == EPI_RESID) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(a.R + (int64_t)m * a.ldr + nbase);
+  for (int v = 0; v < 8; ++v)
+    dst[v] = make_int4((int)r[4 * v], (int)r[4 * v + 1], (int)r[4 * v + 2], (int)r[4 * v + 3]);
+}
+
+// ---------------------------------------------------------------------------
+// token-major epilogue, bf16 outputs (DEQUANT, BIAS, RESID, GELU, QKV).
+//
+// Each epilogue warp owns TMEM lanes [32*quarter, +32) (32 token rows) and,
+// of every 128 x BN tile, the 16-column halves of chunks `group` and
+// `group + 4`: four items per tile. Per item the warp
+//   - reads its 32 x 16 accumulators (a lane per token row),
+//   - reads the residual block with two coalesced 16-byte loads per lane
+//     (two lanes per row, sixteen rows per instruction), issued one item
+//     ahead, and turns it into a lane-per-row layout through its 1 KiB
+//     shared-memory buffer,
+//   - computes 16 bf16 outputs per row into the same buffer, and
+//   - stores the 32 x 32-byte block with two coalesced 16-byte stores per
+//     lane, whole 32-byte sectors.
+// Channel scales and biases are warp-uniform vector loads; the per-token
+// scale (and the QKV cache row) of the next tile is loaded a tile ahead.
+// There is no barrier between the epilogue warps.
+// ---------------------------------------------------------------------------
+constexpr int kStageRowBytes = 32;                    // 16 bf16 of one token row
+constexpr int kWarpStageBytes = 32 * kStageRowBytes;  // 1 KiB output / residual block
+// channel scales (fp32) and biases (bf16) of the warp's 64 columns of a tile,
+// double-buffered so the next tile's are copied while this tile's are used
+constexpr int kParamBytes = 64 * 4 + 64 * 2;
+constexpr int kWarpEpiBytes = kWarpStageBytes + 2 * kParamBytes;
+constexpr int kEpiStageBytes = kEpiWarps * kWarpEpiBytes;  // 28 KiB
+
+// Byte offset of 16-byte half h of row r in a warp's buffer. The half is
+// flipped on rows 4..7 of every 8, which makes both access patterns below
+// (a lane per row; two lanes per row over sixteen rows) free of bank conflicts.
+__device__ __forceinline__ uint32_t stage_off(int r, int h) {
+  return (uint32_t)(r * kStageRowBytes + ((h ^ ((r >> 2) & 1)) << 4));
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Copy the channel scales and biases of the warp's two 32-column chunks of
+// tile t into its parameter buffer: [64] fp32 scales, then [64] bf16 biases.
+template <int EPI>
+__device__ __forceinline__ void tm_load_params(const GemmArgs &a, int t, int group, int lane,
+                                               uint32_t buf, bool vec) {
+  const int b0 = (t % a.b_tiles) * a.BN;
 #pragma unroll
-    for (int v = 0; v < 4; ++v) rv[v] = src[v];
-  }
-  uint32_t packed[16];
-#pragma unroll
-  for (int v = 0; v < 8; ++v) {
-    const float4 sw4 = *reinterpret_cast<const float4 *>(&ctl->tile_sw[jbase + 4 * v]);
-    const uint2 b4 = *reinterpret_cast<const uint2 *>(&ctl->tile_bias[jbase + 4 * v]);
-    const float swv[4] = {sw4.x, sw4.y, sw4.z, sw4.w};
-    const float bv[4] = {__uint_as_float(b4.x << 16), __uint_as_float(b4.x & 0xffff0000u),
-                         __uint_as_float(b4.y << 16), __uint_as_float(b4.y & 0xffff0000u)};
-    uint16_t o[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int j = 4 * v + e;
-      const float t = dequant_bf((int32_t)r[j], swv[e], sx);
-      if (EPI == EPI_DEQUANT) {
-        o[e] = f2bf(t);
-      } else if (EPI == EPI_BIAS || EPI == EPI_QKV) {
-        o[e] = f2bf(__fadd_rn(t, bv[e]));
-      } else if (EPI == EPI_RESID) {
-        const uint32_t rw = (&rv[0].x)[j >> 1];
-        const float rf = __uint_as_float((j & 1) ? (rw & 0xffff0000u) : (rw << 16));
-        o[e] = f2bf(__fadd_rn(rf, add_bf(t, bv[e])));
-      } else {  // EPI_GELU
-        o[e] = f2bf(gelu_tanh(add_bf(t, bv[e])));
-      }
+  for (int cs = 0; cs < 2; ++cs) {
+    const int col0 = 32 * (group + 4 * cs), n0 = b0 + col0;
+    if (col0 >= a.BN || n0 >= a.N) continue;  // N % 32 == 0: a live chunk is whole
+    if (vec) {
+      if (lane < 8)
+        cp_async16(buf + (uint32_t)((32 * cs + 4 * lane) * 4), a.sW + n0 + 4 * lane);
+      else if (lane < 12 && EPI != EPI_DEQUANT)
+        cp_async16(buf + 256u + (uint32_t)((32 * cs + 8 * (lane - 8)) * 2),
+                   a.bias + n0 + 8 * (lane - 8));
+    } else {
+      const float w = a.sW[n0 + lane];
+      const uint16_t bb = EPI != EPI_DEQUANT ? a.bias[n0 + lane] : (uint16_t)0;
+      asm volatile("st.shared.f32 [%0], %1;" ::"r"(buf + (uint32_t)((32 * cs + lane) * 4)),
+                   "f"(w) : "memory");
+      asm volatile("st.shared.u16 [%0], %1;" ::"r"(buf + 256u + (uint32_t)((32 * cs + lane) * 2)),
+                   "h"(bb) : "memory");
     }
-    packed[2 * v] = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
-    packed[2 * v + 1] = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
   }
-  uint16_t *dst;
-  if (EPI == EPI_QKV) {
-    const int seg = nbase / a.dseg, col = nbase - (nbase / a.dseg) * a.dseg;
-    dst = seg == 0 ? reinterpret_cast<uint16_t *>(a.Y) + (int64_t)m * a.ldy + col
-                   : (seg == 1 ? a.Kc : a.Vc) + kv_row + col;
-  } else {
-    dst = reinterpret_cast<uint16_t *>(a.Y) + (int64_t)m * a.ldy + nbase;
-  }
-  uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+  cp_async_commit();
+}
+
+// Column offset (within the tile) of item j of an epilogue warp of `group`.
+__device__ __forceinline__ int tm_item_col(int group, int j) {
+  return 32 * (group + 4 * (j >> 1)) + 16 * (j & 1);
+}
+
+// Geometry of one tile for one epilogue lane, computed once per tile. The
+// lane moves two 16-byte pieces per item: rows (lane >> 1) and 16 + (lane >> 1)
+// of the warp's 32, half (lane & 1) of the item's 16 columns.
+struct TmTile {
+  int a0, b0;
+  int64_t rpiece;          // element offset of piece 0 in R (without the column)
+  bool ok0, ok1;           // the pieces' rows are inside M
+  bool live0, live1;       // chunk slots group and group + 4 exist in this tile
+};
+
+__device__ __forceinline__ TmTile tm_tile(const GemmArgs &a, int t, int quarter, int group,
+                                          int lane) {
+  TmTile g;
+  const int ta = t / a.b_tiles;
+  g.a0 = ta * kBM;
+  g.b0 = (t - ta * a.b_tiles) * a.BN;
+  const int r0 = g.a0 + 32 * quarter + (lane >> 1);
+  g.ok0 = r0 < a.M;
+  g.ok1 = r0 + 16 < a.M;
+  g.rpiece = (int64_t)r0 * a.ldr + 8 * (lane & 1);
+  const int c0 = 32 * group, c1 = 32 * (group + 4);
+  g.live0 = c0 < a.BN && g.b0 + c0 < a.N;  // N % 32 == 0: a live chunk is whole
+  g.live1 = c1 < a.BN && g.b0 + c1 < a.N;
+  return g;
+}
+
+// Residual pieces of item j of tile g (zeros where there is nothing to read).
+template <int EPI>
+__device__ __forceinline__ void tm_load_resid(const GemmArgs &a, const TmTile &g, int group, int j,
+                                              uint4 (&rp)[2]) {
+  rp[0] = rp[1] = make_uint4(0, 0, 0, 0);
+  if (EPI != EPI_RESID || !((j >> 1) ? g.live1 : g.live0)) return;
+  const uint16_t *p = a.R + g.rpiece + g.b0 + tm_item_col(group, j);
+  if (g.ok0) rp[0] = __ldcs(reinterpret_cast<const uint4 *>(p));
+  if (g.ok1) rp[1] = __ldcs(reinterpret_cast<const uint4 *>(p + 16 * a.ldr));
+}
+
+// Copy the channel scales and biases of the warp's two 32-column chunks of
+// tile g into its parameter buffer: [64] fp32 scales, then [64] bf16 biases.
+template <int EPI>
+__device__ __forceinline__ void tm_load_params(const GemmArgs &a, const TmTile &g, int group,
+                                               int lane, uint32_t buf, bool vec) {
 #pragma unroll
-  for (int v = 0; v < 4; ++v)
-    d4[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+  for (int cs = 0; cs < 2; ++cs) {
+    if (!(cs ? g.live1 : g.live0)) continue;
+    const int n0 = g.b0 + 32 * (group + 4 * cs);
+    if (vec) {
+      if (lane < 8)
+        cp_async16(buf + (uint32_t)((32 * cs + 4 * lane) * 4), a.sW + n0 + 4 * lane);
+      else if (lane < 12 && EPI != EPI_DEQUANT)
+        cp_async16(buf + 256u + (uint32_t)((32 * cs + 8 * (lane - 8)) * 2),
+                   a.bias + n0 + 8 * (lane - 8));
+    } else {
+      const float w = a.sW[n0 + lane];
+      const uint16_t bb = EPI != EPI_DEQUANT ? a.bias[n0 + lane] : (uint16_t)0;
+      asm volatile("st.shared.f32 [%0], %1;" ::"r"(buf + (uint32_t)((32 * cs + lane) * 4)),
+                   "f"(w) : "memory");
+      asm volatile("st.shared.u16 [%0], %1;" ::"r"(buf + 256u + (uint32_t)((32 * cs + lane) * 2)),
+                   "h"(bb) : "memory");
+    }
+  }
+  cp_async_commit();
+}
+
+// Per-token scale (and QKV cache-row offset) of this lane's own row of tile g.
+template <int EPI>
+__device__ __forceinline__ void tm_row_info(const GemmArgs &a, const TmTile &g, int quarter,
+                                            int lane, float &sx, int64_t &kv) {
+  sx = 0.f;
+  kv = 0;
+  const int m = g.a0 + 32 * quarter + lane;
+  if (m >= a.M) return;
+  sx = a.sX[m];
+  if (EPI == EPI_QKV) kv = qkv_row_offset<EPI>(a, m);
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_tm(const GemmArgs &a, SmemCtl *ctl, uint32_t tmem_base,
+                                            uint32_t stage, int quarter, int group, int lane,
+                                            volatile int *abort_flag, bool vec_params) {
+  const int total_units = a.a_tiles * a.b_tiles;
+  const uint32_t params = stage + kWarpStageBytes;  // two buffers of kParamBytes
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  // residual pieces of the next two items (items run 0..3 within a tile,
+  // then on to the CTA's next tile)
+  uint4 rp[2], rq[2];
+  float sx_next = 0.f;
+  int64_t kv_next = 0;
+  TmTile gn = {};
+  if ((int)blockIdx.x < total_units) {
+    gn = tm_tile(a, blockIdx.x, quarter, group, lane);
+    tm_load_params<EPI>(a, gn, group, lane, params, vec_params);
+    tm_load_resid<EPI>(a, gn, group, 0, rp);
+    tm_load_resid<EPI>(a, gn, group, 1, rq);
+    tm_row_info<EPI>(a, gn, quarter, lane, sx_next, kv_next);
+  }
+  int iter = 0;
+  for (int t = blockIdx.x; t < total_units; t += gridDim.x, ++iter) {
+    const TmTile g = gn;
+    const bool has_next = t + (int)gridDim.x < total_units;
+    if (has_next) gn = tm_tile(a, t + gridDim.x, quarter, group, lane);
+    const uint32_t pbuf = params + (uint32_t)((iter & 1) * kParamBytes);
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(&ctl->tmem_full[acc], acc_phase, abort_flag, a.err, 0x1105);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) break;
+    mbar_wait(&ctl->tmem_full[acc], acc_phase, nullptr, a.err, 0x1107);  // completed: returns at once
+    tc_fence_after();
+    const float sx = sx_next;
+    const int64_t kv_own = kv_next;
+    cp_async_wait_all();  // this tile's parameters
+    __syncwarp();
+    if (has_next) {
+      tm_row_info<EPI>(a, gn, quarter, lane, sx_next, kv_next);
+      tm_load_params<EPI>(a, gn, group, lane,
+                          params + (uint32_t)(((iter + 1) & 1) * kParamBytes), vec_params);
+    }
+    // cache-row offsets of the two rows this lane stores (QKV)
+    int64_t kvp[2] = {0, 0};
+    if (EPI == EPI_QKV) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        kvp[i] = __shfl_sync(0xffffffffu, kv_own, (lane >> 1) + 16 * i) + 8 * (lane & 1);
+    }
+    const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * a.BN);
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      const int jcol = tm_item_col(group, j);
+      const int n = g.b0 + jcol;
+      const bool live = (j >> 1) ? g.live1 : g.live0;  // warp-uniform
+      uint32_t r[16];
+      float sw[16];
+      uint32_t bias2[8];
+      if (live) {
+        tmem_ld_32x32b_x16(t_row + (uint32_t)jcol, r);
+        if (EPI == EPI_RESID) {  // this item's residual pieces into the row buffer
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+            st_shared_v4(stage + stage_off((lane >> 1) + 16 * i, lane & 1), rp[i]);
+        }
+      }
+      rp[0] = rq[0];
+      rp[1] = rq[1];
+      if (j < 2)
+        tm_load_resid<EPI>(a, g, group, j + 2, rq);
+      else if (has_next)
+        tm_load_resid<EPI>(a, gn, group, j - 2, rq);
+      if (live) {
+        const uint32_t pi = (uint32_t)(32 * (j >> 1) + 16 * (j & 1));  // column in the buffer
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const uint4 x = ld_shared_v4(pbuf + (pi + 4 * v) * 4);
+          sw[4 * v] = __uint_as_float(x.x);
+          sw[4 * v + 1] = __uint_as_float(x.y);
+          sw[4 * v + 2] = __uint_as_float(x.z);
+          sw[4 * v + 3] = __uint_as_float(x.w);
+        }
+        if (EPI != EPI_DEQUANT) {
+#pragma unroll
+          for (int v = 0; v < 2; ++v) {
+            const uint4 x = ld_shared_v4(pbuf + 256u + (pi + 8 * v) * 2);
+            bias2[4 * v] = x.x;
+            bias2[4 * v + 1] = x.y;
+            bias2[4 * v + 2] = x.z;
+            bias2[4 * v + 3] = x.w;
+          }
+        }
+        tmem_ld_wait();
+      }
+      if (j == 3) {  // the tile's accumulator is read: hand it back to the MMA warp
+        tc_fence_before();
+        mbar_arrive(&ctl->tmem_empty[acc]);
+      }
+      if (!live) continue;
+      uint4 rown[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+      if (EPI == EPI_RESID) {  // the residual of this lane's own row
+        __syncwarp();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) rown[h] = ld_shared_v4(stage + stage_off(lane, h));
+      }
+      // Same operations and rounding points as dequant_bf / add_bf / f2bf,
+      // on pairs of channels: t = bf16(y) by one paired conversion, then the
+      // bias and residual additions of bf16 values as bf16x2 additions.
+      uint32_t packed[8];
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        const float y0 = __fmul_rn(__fmul_rn((float)(int32_t)r[i], sw[i]), sx);
+        const float y1 = __fmul_rn(__fmul_rn((float)(int32_t)r[i + 1], sw[i + 1]), sx);
+        const uint32_t t2 = pack_bf2(y0, y1);  // dequant_bf of both
+        if (EPI == EPI_DEQUANT) {
+          packed[i >> 1] = t2;
+        } else if (EPI == EPI_BIAS || EPI == EPI_QKV) {
+          packed[i >> 1] = add_bf2(t2, bias2[i >> 1]);
+        } else if (EPI == EPI_RESID) {
+          packed[i >> 1] = add_bf2((&rown[0].x)[i >> 1], add_bf2(t2, bias2[i >> 1]));
+        } else {  // EPI_GELU
+          const uint32_t u2 = add_bf2(t2, bias2[i >> 1]);
+          packed[i >> 1] = pack_bf2(gelu_tanh(__uint_as_float(u2 << 16)),
+                                    gelu_tanh(__uint_as_float(u2 & 0xffff0000u)));
+        }
+      }
+      st_shared_v4(stage + stage_off(lane, 0), make_uint4(packed[0], packed[1], packed[2], packed[3]));
+      st_shared_v4(stage + stage_off(lane, 1), make_uint4(packed[4], packed[5], packed[6], packed[7]));
+      __syncwarp();
+      uint16_t *dst0, *dst1;  // this lane's two 16-byte pieces of the item
+      const int64_t ypiece = (int64_t)(g.a0 + 32 * quarter + (lane >> 1)) * a.ldy + 8 * (lane & 1);
+      if (EPI == EPI_QKV) {
+        const int seg = n / a.dseg;
+        const int64_t col = n - (int64_t)seg * a.dseg;
+        if (seg == 0) {
+          uint16_t *y = reinterpret_cast<uint16_t *>(a.Y) + ypiece + col;
+          dst0 = y;
+          dst1 = y + 16 * a.ldy;
+        } else {
+          uint16_t *c = (seg == 1 ? a.Kc : a.Vc) + col;
+          dst0 = c + kvp[0];
+          dst1 = c + kvp[1];
+        }
+      } else {
+        dst0 = reinterpret_cast<uint16_t *>(a.Y) + ypiece + n;
+        dst1 = dst0 + 16 * a.ldy;
+      }
+      const uint4 v0 = ld_shared_v4(stage + stage_off(lane >> 1, lane & 1));
+      const uint4 v1 = ld_shared_v4(stage + stage_off(16 + (lane >> 1), lane & 1));
+      if (g.ok0) *reinterpret_cast<uint4 *>(dst0) = v0;
+      if (g.ok1) *reinterpret_cast<uint4 *>(dst1) = v1;
+      __syncwarp();  // the buffer is rewritten by the next item
+    }
+    if (++acc == 2) {
+      acc = 0;
+      acc_phase ^= 1;
+    }
+  }
+  cp_async_wait_all();  // no copy into shared memory outlives the loop
 }
 
 template <int KIND, int EPI, bool CM>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   GemmArgs a) {
+                   const __grid_constant__ CUtensorMap tmR, GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int BN = a.BN;
@@ -262,7 +536,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t a_bytes = kBM * kBoxBytes;
   const uint32_t b_bytes = (uint32_t)BN * kBoxBytes;
   const uint32_t stage_bytes = a_bytes + b_bytes;
-  SmemCtl *ctl = reinterpret_cast<SmemCtl *>(smem + (size_t)stages * stage_bytes);
+  // [stages][A box | B box] | token-major bf16: epilogue buffers | SmemCtl
+  constexpr bool kStaged = !CM && EPI != EPI_S32;
+  uint8_t *epi_stage = smem + (size_t)stages * stage_bytes;
+  SmemCtl *ctl = reinterpret_cast<SmemCtl *>(epi_stage + (kStaged ? kEpiStageBytes : 0));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -286,6 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async_smem();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (!CM && EPI == EPI_RESID) prefetch_tmap(&tmR);
   }
   if (warp == 1) {
     tmem_alloc(&ctl->tmem_base, tmem_cols);
@@ -335,6 +613,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int a0 = (t / a.b_tiles) * kBM;
       const int b0 = (t % a.b_tiles) * BN;
       const int kb0 = ks * a.kb_per, kb1 = min(a.kblocks, kb0 + a.kb_per);
+      if (!CM && EPI == EPI_RESID && u + (int)gridDim.x < total_units) {
+        // the residual block of this CTA's next tile: into L2 now, so the
+        // epilogue's loads of it hit L2 instead of waiting on DRAM
+        const int un = u + gridDim.x;
+        tma_prefetch_l2_2d(&tmR, (un % a.b_tiles) * BN, (un / a.b_tiles) * kBM);
+      }
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort_flag, a.err, 0x1101)) break;
         uint8_t *sa = smem + (size_t)stage * stage_bytes;
@@ -413,6 +697,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(&ctl->drain);
       mbar_wait(&ctl->drain, 0, nullptr, a.err, 0x1104);
     }
+  } else if (kStaged && warp >= kEpiWarp0) {
+    // ---------------- epilogue (token-major, bf16) ----------------
+    pdl_wait();
+    const int e = warp - kEpiWarp0;
+    epilogue_tm<EPI>(a, ctl, tmem_base, smem_u32(epi_stage) + (uint32_t)(e * kWarpEpiBytes),
+                     warp & 3, e >> 2, lane, abort_flag, a.vec_params != 0);
   } else if (warp >= kEpiWarp0) {
     // ---------------- epilogue ----------------
     pdl_wait();
@@ -442,29 +732,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b0 = (t % a.b_tiles) * BN;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
       if (!CM) {
-        // token-major: stage the B tile's channel scales and biases
-        const int i = e * 32 + lane;
-        if (EPI != EPI_S32 && EPI != EPI_F32_BF16 && i < BN) {
-          const int n = b0 + i;
-          ctl->tile_sw[i] = n < a.N ? a.sW[n] : 0.f;
-          ctl->tile_bias[i] = (EPI >= EPI_BIAS && EPI <= EPI_QKV && n < a.N) ? a.bias[n] : 0;
-        }
-        named_barrier_sync(kEpiBarrier, kEpiThreads);
+        // token-major int32 (only EPI_S32 reaches this branch)
         const int m = a0 + quarter * 32 + lane;
-        float sx = 0.f;
-        int64_t kv_row = 0;
-        if (m < a.M) {
-          if (EPI != EPI_S32 && EPI != EPI_F32_BF16) sx = a.sX[m];
-          if (EPI == EPI_QKV) {
-            const int b = m / a.T, tt = m - (m / a.T) * a.T;
-            kv_row = (int64_t)b * a.seq_stride + (int64_t)((a.pos0 ? a.pos0[b] : 0) + tt) * a.dseg;
-          }
-        }
         for (int c = group; c < nchunks; c += 4) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + (uint32_t)(32 * c), r);
           tmem_ld_wait();
-          finish_chunk_tm<EPI>(a, ctl, m, sx, kv_row, b0 + 32 * c, 32 * c, r);
+          finish_chunk_tm_s32(a, m, b0 + 32 * c, r);
         }
         tc_fence_before();
         mbar_arrive(&ctl->tmem_empty[acc]);
@@ -564,7 +838,8 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   const int esz = KIND == 0 ? 1 : 2;
   const CUtensorMapDataType dt =
       KIND == 0 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmR;
+  memset(&tmR, 0, sizeof(tmR));
   if (CM) {  // A = weights, B = tokens
     a.BN = M >= 256 ? 256 : round_up32(M < 32 ? 32 : M);
     st = make_tmap_2d(&tmA, W, dt, (uint64_t)N, (uint64_t)K, (uint64_t)K * esz, kBoxBytes / esz,
@@ -585,13 +860,21 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
     if (st) return st;
     a.a_tiles = (M + kBM - 1) / kBM;
     a.b_tiles = (N + a.BN - 1) / a.BN;
+    if (EPI == EPI_RESID) {  // L2 prefetch of the residual, one 128 x BN box per tile
+      st = make_tmap_2d(&tmR, la.R, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)M, (uint64_t)N,
+                        (uint64_t)la.ldr * 2, (uint32_t)a.BN, kBM, false);
+      if (st) return st;
+    }
   }
   const int stage_bytes = (kBM + a.BN) * kBoxBytes;
-  const int budget = 227 * 1024 - 1024 - (int)sizeof(SmemCtl) - 64;
+  const int epi_bytes = (!CM && EPI != EPI_S32) ? kEpiStageBytes : 0;
+  const int budget = 227 * 1024 - 1024 - epi_bytes - (int)sizeof(SmemCtl) - 64;
   a.stages = budget / stage_bytes;
   if (a.stages > 8) a.stages = 8;
   if (a.stages < 2) return W8A8_ERR_UNSUPPORTED;
-  const size_t smem = 1024 + (size_t)a.stages * stage_bytes + sizeof(SmemCtl);
+  const size_t smem = 1024 + (size_t)a.stages * stage_bytes + epi_bytes + sizeof(SmemCtl);
+  // 16-byte vector loads of channel scales and biases (16-channel runs)
+  a.vec_params = aligned16(la.sW) && (la.bias == nullptr || aligned16(la.bias));
   a.kblocks = (K * esz + kBoxBytes - 1) / kBoxBytes;
   a.err = ctx->err;
   a.ksplit = 1;
@@ -627,7 +910,8 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   }
   const int units = tiles0 * a.ksplit;
   const int grid = units < ctx->sm_count ? units : ctx->sm_count;
-  launch_pdl(gemm_tc_kernel<KIND, EPI, CM>, dim3(grid), dim3(kThreads), smem, stream, tmA, tmB, a);
+  launch_pdl(gemm_tc_kernel<KIND, EPI, CM>, dim3(grid), dim3(kThreads), smem, stream, tmA, tmB, tmR,
+             a);
   return check_launch("gemm_tc");
 }
 

@@ -60,7 +60,8 @@ def test_gemm_s32_extreme_values(cuda):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 2304, 768), (9, 768, 3072), (16, 2304, 768),
-                                   (128, 3072, 768), (300, 768, 3072), (1024, 2304, 768)])
+                                   (128, 3072, 768), (300, 768, 3072), (1024, 2304, 768),
+                                   (300, 320, 768), (129, 96, 256)])
 @pytest.mark.parametrize("epi", [_lib.EPI_DEQUANT, _lib.EPI_BIAS, _lib.EPI_BIAS_RESID])
 def test_linear_epilogues_bit_exact(cuda, M, N, K, epi):
     rng = np.random.default_rng(M + N + K + epi)
@@ -127,7 +128,63 @@ def test_linear_qkv_scatter_split_k(cuda):
         assert not k[i, other].any() and not v[i, other].any()
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 3072, 768), (64, 5120, 1280), (512, 3072, 768)])
+@pytest.mark.parametrize("zero_acc", [True, False])
+def test_linear_resid_bf16_edge_values(cuda, zero_acc):
+    """Bias and residual additions at the edges of bf16: subnormals, signed
+    zeros, the largest finite values and infinities (token-major tiles). With
+    zero weights every dequantized product is +0, so the sums see the edge
+    values themselves; with random weights tiny biases meet normal values."""
+    rng = np.random.default_rng(21 + zero_acc)
+    M, N, K = 256, 512, 128
+    x = oracle.bf16_bits(outlier_activations(M, K, seed=9))
+    xq, sx = oracle.quant_rows(x)
+    W = (np.zeros((N, K), np.int8) if zero_acc
+         else rng.integers(-127, 128, (N, K), dtype=np.int8))
+    sw = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    edge = np.array([0x0000, 0x8000, 0x0001, 0x8001, 0x007F, 0x807F, 0x0080, 0x8080, 0x7F7F,
+                     0xFF7F, 0x3F80, 0xBF80], np.uint16)
+    b = _rand_bf16(rng, (N,), 0.02)
+    b[: 4 * len(edge)] = np.tile(edge, 4)
+    R = _rand_bf16(rng, (M, N))
+    pick = rng.random((M, N)) < 0.3
+    R[pick] = rng.choice(np.r_[edge, [0x7F80, 0xFF80]].astype(np.uint16), pick.sum())
+    # biases stay finite, so no sum is inf + -inf
+    want = oracle.linear(xq, sx, W, sw, b, _lib.EPI_BIAS_RESID, R)
+    got = from_dev_bf16(ops.linear(to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw), to_dev_bf16(b),
+                                   _lib.EPI_BIAS_RESID, R=to_dev_bf16(R)))
+    np.testing.assert_array_equal(got, want)
+
+
+def test_linear_qkv_scatter_prefill(cuda):
+    """Packed QKV GEMM of a prefill (token-major tiles): 3 sequences of 100
+    tokens each written to Q and to K/V cache rows pos0[b] + t; tiles of 32
+    rows straddle sequences."""
+    rng = np.random.default_rng(12)
+    B, T, d, C = 3, 100, 768, 256
+    x = oracle.bf16_bits(outlier_activations(B * T, d, seed=5))
+    xq, sx = oracle.quant_rows(x)
+    W = rng.integers(-127, 128, (3 * d, d), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, 3 * d).astype(np.float32)
+    b = _rand_bf16(rng, (3 * d,), 0.02)
+    want = oracle.linear(xq, sx, W, sw, b, oracle.EPI_BIAS)
+    pos = rng.integers(0, C - T, B).astype(np.int32)
+    Q = torch.zeros((B * T, d), dtype=torch.bfloat16, device=cuda)
+    Kc = torch.zeros((B, C, d), dtype=torch.bfloat16, device=cuda)
+    Vc = torch.zeros((B, C, d), dtype=torch.bfloat16, device=cuda)
+    ops.linear_qkv(to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw), to_dev_bf16(b), Q, Kc, Vc,
+                   C * d, T, to_dev(pos))
+    q, k, v = from_dev_bf16(Q), from_dev_bf16(Kc), from_dev_bf16(Vc)
+    np.testing.assert_array_equal(q, want[:, :d])
+    for i in range(B):
+        rows = slice(i * T, (i + 1) * T)
+        np.testing.assert_array_equal(k[i, pos[i]:pos[i] + T], want[rows, d:2 * d])
+        np.testing.assert_array_equal(v[i, pos[i]:pos[i] + T], want[rows, 2 * d:])
+        other = np.r_[0:pos[i], pos[i] + T:C]
+        assert not k[i, other].any() and not v[i, other].any()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 3072, 768), (64, 5120, 1280), (512, 3072, 768),
+                                   (333, 320, 768)])
 def test_linear_gelu_within_one_ulp(cuda, M, N, K):
     """GELU uses CUDA's tanhf on the GPU and the C library's on the CPU:
     at most 1 bf16 ulp apart, almost always identical."""
