@@ -41,6 +41,7 @@ constexpr int kCBox = 128;      // K bytes per stage
 constexpr int kCThreads = 256;  // 8 warps
 constexpr int kCMaxStages = 8;
 constexpr int kCMaxCluster = 8;  // portable cluster size
+constexpr int kCPre = 2;         // reduction groups per thread with preloaded epilogue inputs
 
 struct ClusterGemmArgs : LinearArgs {
   int BN;       // tokens per tile (multiple of 32, <= 128)
@@ -69,6 +70,12 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 // Address of this CTA's shared-memory word `p` in cluster CTA `rank`.
 __device__ __forceinline__ uint32_t dsmem_addr(const void *p, uint32_t rank) {
   uint32_t out;
@@ -89,8 +96,8 @@ __device__ __forceinline__ int4 ld_dsmem_v4(uint32_t addr) {
 struct Epi4In {
   float sx;
   float sw[4];
-  float b[4];
-  float r[4];
+  uint2 b;  // 4 bf16 biases
+  uint2 r;  // 4 bf16 residual values
 };
 
 template <int EPI>
@@ -103,20 +110,8 @@ __device__ __forceinline__ Epi4In load4(const ClusterGemmArgs &a, int m, int n) 
   in.sw[1] = sw.y;
   in.sw[2] = sw.z;
   in.sw[3] = sw.w;
-  if (EPI >= EPI_BIAS && EPI <= EPI_QKV) {
-    const uint2 b = __ldg(reinterpret_cast<const uint2 *>(a.bias + n));
-    in.b[0] = __uint_as_float(b.x << 16);
-    in.b[1] = __uint_as_float(b.x & 0xffff0000u);
-    in.b[2] = __uint_as_float(b.y << 16);
-    in.b[3] = __uint_as_float(b.y & 0xffff0000u);
-  }
-  if (EPI == EPI_RESID) {
-    const uint2 r = *reinterpret_cast<const uint2 *>(a.R + (int64_t)m * a.ldr + n);
-    in.r[0] = __uint_as_float(r.x << 16);
-    in.r[1] = __uint_as_float(r.x & 0xffff0000u);
-    in.r[2] = __uint_as_float(r.y << 16);
-    in.r[3] = __uint_as_float(r.y & 0xffff0000u);
-  }
+  if (EPI >= EPI_BIAS && EPI <= EPI_QKV) in.b = __ldg(reinterpret_cast<const uint2 *>(a.bias + n));
+  if (EPI == EPI_RESID) in.r = *reinterpret_cast<const uint2 *>(a.R + (int64_t)m * a.ldr + n);
   return in;
 }
 
@@ -129,22 +124,30 @@ __device__ __forceinline__ void store4(const ClusterGemmArgs &a, int m, int n, c
     *reinterpret_cast<int4 *>(s32_row(a, m) + n) = acc;
     return;
   }
-  uint16_t o[4];
+  // dequant_bf of the 4 channels as two paired bf16 conversions, then the
+  // bias / residual additions of bf16 values as bf16x2 additions (bit-identical
+  // to the fp32 additions rounded to bf16; see add_bf2)
+  uint32_t t2[2], o2[2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float t = dequant_bf(v[i], in.sw[i], in.sx);
+  for (int h = 0; h < 2; ++h)
+    t2[h] = pack_bf2(__fmul_rn(__fmul_rn((float)v[2 * h], in.sw[2 * h]), in.sx),
+                     __fmul_rn(__fmul_rn((float)v[2 * h + 1], in.sw[2 * h + 1]), in.sx));
+  const uint32_t b2[2] = {in.b.x, in.b.y}, r2[2] = {in.r.x, in.r.y};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
     if (EPI == EPI_DEQUANT) {
-      o[i] = f2bf(t);
+      o2[h] = t2[h];
     } else if (EPI == EPI_BIAS || EPI == EPI_QKV) {
-      o[i] = f2bf(__fadd_rn(t, in.b[i]));
+      o2[h] = add_bf2(t2[h], b2[h]);
     } else if (EPI == EPI_RESID) {
-      o[i] = f2bf(__fadd_rn(in.r[i], add_bf(t, in.b[i])));
+      o2[h] = add_bf2(r2[h], add_bf2(t2[h], b2[h]));
     } else {  // EPI_GELU
-      o[i] = f2bf(gelu_tanh(add_bf(t, in.b[i])));
+      const uint32_t u = add_bf2(t2[h], b2[h]);
+      o2[h] = pack_bf2(gelu_tanh(__uint_as_float(u << 16)),
+                       gelu_tanh(__uint_as_float(u & 0xffff0000u)));
     }
   }
-  const uint2 packed = make_uint2((uint32_t)o[0] | ((uint32_t)o[1] << 16),
-                                  (uint32_t)o[2] | ((uint32_t)o[3] << 16));
+  const uint2 packed = make_uint2(o2[0], o2[1]);
   uint16_t *dst;
   if (EPI == EPI_QKV) {
     const int seg = n / a.dseg, col = n - seg * a.dseg;
@@ -161,8 +164,10 @@ __device__ __forceinline__ void store4(const ClusterGemmArgs &a, int m, int n, c
   *reinterpret_cast<uint2 *>(dst) = packed;
 }
 
+// At most 128 registers a thread: the CTA must fit on an SM beside the CTAs
+// of the kernel before it, so that the weight boxes stream during its tail.
 template <int EPI>
-__global__ void __launch_bounds__(kCThreads, 1)
+__global__ void __launch_bounds__(kCThreads, 2)
     gemm_cm_cluster_kernel(const __grid_constant__ CUtensorMap tmW,
                            const __grid_constant__ CUtensorMap tmX, ClusterGemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -211,15 +216,37 @@ __global__ void __launch_bounds__(kCThreads, 1)
   // made the step 15% slower, even when triggered after the MMAs.
 
   int issued = 0;
-  bool have_partial = false;
+  const int pre = min(nkb, stages);
   if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer ----------------
-    const int pre = min(nkb, stages);
     for (int i = 0; i < pre; ++i) {  // weights: independent of the previous kernel
       mbar_arrive_expect_tx(&ctl->full[i], stage_bytes);
       tma_load_2d(smem + (size_t)i * stage_bytes, &tmW, &ctl->full[i], (kb0 + i) * kCBox, n0);
     }
-    pdl_wait();
+  }
+  pdl_wait();  // everything below may read what the previous kernel wrote
+
+  // This thread's share of the reduction: groups (token, 4 channels)
+  // g = g0 + threadIdx.x + i * kCThreads of slice `rank`. Their epilogue
+  // inputs (per-token scale, channel scales, bias, residual) are loaded now,
+  // so they arrive while the MMAs run.
+  const int groups = BN * (kCBM / 4);
+  const int g0 = (int)((long long)groups * rank / a.ksplit);
+  const int g1 = (int)((long long)groups * (rank + 1) / a.ksplit);
+  const bool preloaded = g1 - g0 <= kCPre * kCThreads;  // else the plain loop below
+  Epi4In pin[kCPre];
+#pragma unroll
+  for (int i = 0; i < kCPre; ++i) {
+    pin[i] = Epi4In{};
+    const int g = g0 + (int)threadIdx.x + i * kCThreads;
+    if (preloaded && g < g1) {
+      const int m = g >> 5, n = n0 + (g & 31) * 4;
+      if (m < a.M && n < a.N) pin[i] = load4<EPI>(a, m, n);
+    }
+  }
+
+  bool have_partial = false;
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
     int stage = 0;
     uint32_t phase = 0;
     for (int i = 0; i < nkb; ++i) {
@@ -271,7 +298,6 @@ __global__ void __launch_bounds__(kCThreads, 1)
     tc_commit(&ctl->tmem_full);  // also completes after an abort: no MMA left running
   } else if (warp >= 4) {
     // ---------------- accumulator -> shared memory ----------------
-    pdl_wait();
     int ok = 1;
     if (lane == 0) ok = mbar_wait(&ctl->tmem_full, 0, abort_flag, a.err, 0x1203);
     ok = __shfl_sync(0xffffffffu, ok, 0) && !*abort_flag;
@@ -290,16 +316,41 @@ __global__ void __launch_bounds__(kCThreads, 1)
       have_partial = true;
     }
   }
-  if (warp < 4) pdl_wait();  // the reduction below reads sX, R, pos0 written earlier
   (void)have_partial;
   tc_fence_before();
   cluster_sync_all();  // every partial tile of the cluster is in shared memory
 
   // ---------------- distributed reduction + epilogue ----------------
-  if (!*abort_flag) {
-    const int groups = BN * (kCBM / 4);  // (token, 4 channels)
-    const int g0 = (int)((long long)groups * rank / a.ksplit);
-    const int g1 = (int)((long long)groups * (rank + 1) / a.ksplit);
+  // All DSMEM reads first; then the CTA tells the cluster it is done reading
+  // (a peer may exit once every CTA has), and the epilogue arithmetic and
+  // stores overlap that barrier. One arrive and one wait for every thread,
+  // outside the branches.
+  const bool run = !*abort_flag;
+  int4 sum[kCPre];
+#pragma unroll
+  for (int i = 0; i < kCPre; ++i) sum[i] = make_int4(0, 0, 0, 0);
+  if (run && preloaded) {
+#pragma unroll
+    for (int i = 0; i < kCPre; ++i) {
+      const int g = g0 + (int)threadIdx.x + i * kCThreads;
+      if (g < g1) {
+        const int32_t *src = partial + (g >> 5) * kCBM + (g & 31) * 4;
+        int4 p[kCMaxCluster];  // all ks loads in flight before the first addition
+#pragma unroll
+        for (int r = 0; r < kCMaxCluster; ++r)
+          if (r < a.ksplit) p[r] = ld_dsmem_v4(dsmem_addr(src, (uint32_t)r));
+#pragma unroll
+        for (int r = 0; r < kCMaxCluster; ++r) {
+          if (r < a.ksplit) {
+            sum[i].x += p[r].x;
+            sum[i].y += p[r].y;
+            sum[i].z += p[r].z;
+            sum[i].w += p[r].w;
+          }
+        }
+      }
+    }
+  } else if (run) {
     for (int g = g0 + (int)threadIdx.x; g < g1; g += kCThreads) {
       const int tok = g >> 5, ch = (g & 31) * 4;
       const int m = tok, n = n0 + ch;
@@ -325,7 +376,16 @@ __global__ void __launch_bounds__(kCThreads, 1)
       if (live) store4<EPI>(a, m, n, sum, in);
     }
   }
-  cluster_sync_all();  // no CTA leaves while another still reads its partial tile
+  cluster_arrive();  // this CTA has read every partial it needs
+  if (run && preloaded) {
+#pragma unroll
+    for (int i = 0; i < kCPre; ++i) {
+      const int g = g0 + (int)threadIdx.x + i * kCThreads;
+      const int m = g >> 5, n = n0 + (g & 31) * 4;
+      if (g < g1 && m < a.M && n < a.N) store4<EPI>(a, m, n, sum[i], pin[i]);
+    }
+  }
+  cluster_wait();  // no CTA leaves while another still reads its partial tile
 
   if (warp == 0 && lane == 0 && *abort_flag) {
     // drain loads that were issued but never consumed by an MMA

@@ -129,13 +129,15 @@ def test_linear_qkv_scatter_split_k(cuda):
 
 
 @pytest.mark.parametrize("zero_acc", [True, False])
-def test_linear_resid_bf16_edge_values(cuda, zero_acc):
+@pytest.mark.parametrize("M", [256, 64])
+def test_linear_resid_bf16_edge_values(cuda, zero_acc, M):
     """Bias and residual additions at the edges of bf16: subnormals, signed
-    zeros, the largest finite values and infinities (token-major tiles). With
-    zero weights every dequantized product is +0, so the sums see the edge
-    values themselves; with random weights tiny biases meet normal values."""
+    zeros, the largest finite values and infinities (token-major tiles at 256
+    tokens, the cluster split-K path at 64). With zero weights every
+    dequantized product is +0, so the sums see the edge values themselves;
+    with random weights tiny biases meet normal values."""
     rng = np.random.default_rng(21 + zero_acc)
-    M, N, K = 256, 512, 128
+    N, K = 512, 128
     x = oracle.bf16_bits(outlier_activations(M, K, seed=9))
     xq, sx = oracle.quant_rows(x)
     W = (np.zeros((N, K), np.int8) if zero_acc
