@@ -117,6 +117,60 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     if (lane == m && m < a.M) gemv_store(a, m, n, acc[m]);
 }
 
+// Single-token path for long rows (M == 1, K > 2048: the W2 projection of a
+// batch-1 decode step): one CTA of 16 warps per SM, each CTA owning a
+// contiguous run of output channels and each warp RPW of them (rows warp,
+// warp + 16, ...). Every warp requests all of its weight rows (16-byte loads
+// into registers) before waiting for the previous kernel, so the GEMV's
+// weight stream is in flight during that kernel's tail (programmatic
+// dependent launch).
+constexpr int kRowsWarps = 16;
+
+template <int NVL, int RPW>
+__global__ void __launch_bounds__(kRowsWarps * 32)
+    gemv_i8_rows_kernel(const int8_t *__restrict__ X, const int8_t *__restrict__ W, GemvArgs a,
+                        int rows) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * rows;
+  const int n_end = min(n0 + rows, a.N);
+  const int kv = a.K >> 4;
+  int4 w[RPW][NVL];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int n = n0 + warp + kRowsWarps * i;
+    const int4 *wrow = reinterpret_cast<const int4 *>(W + (int64_t)n * a.K);
+#pragma unroll
+    for (int u = 0; u < NVL; ++u) {
+      const int v = lane + 32 * u;
+      w[i][u] = (n < n_end && v < kv) ? __ldg(wrow + v) : make_int4(0, 0, 0, 0);
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  int4 x[NVL];
+  const int4 *xrow = reinterpret_cast<const int4 *>(X);
+#pragma unroll
+  for (int u = 0; u < NVL; ++u) {
+    const int v = lane + 32 * u;
+    x[u] = v < kv ? __ldg(xrow + v) : make_int4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int n = n0 + warp + kRowsWarps * i;
+    int acc = 0;
+#pragma unroll
+    for (int u = 0; u < NVL; ++u) {
+      acc = __dp4a(w[i][u].x, x[u].x, acc);
+      acc = __dp4a(w[i][u].y, x[u].y, acc);
+      acc = __dp4a(w[i][u].z, x[u].z, acc);
+      acc = __dp4a(w[i][u].w, x[u].w, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0 && n < n_end) gemv_store(a, 0, n, acc);
+  }
+}
+
 // Scalar fallback for any K / alignment (correctness path, not a hot path).
 __global__ void gemv_i8_scalar_kernel(const int8_t *__restrict__ X, int64_t ldx,
                                       const int8_t *__restrict__ W, GemvArgs a) {
@@ -153,9 +207,44 @@ static int launch_vec_k(const int8_t *X, int64_t ldx, const int8_t *W, const Gem
   return W8A8_ERR_UNSUPPORTED;
 }
 
+template <int NVL, int RPW>
+static int launch_rows(const int8_t *X, const int8_t *W, const GemvArgs &a, int rows,
+                       cudaStream_t s) {
+  const int grid = (a.N + rows - 1) / rows;
+  launch_pdl(gemv_i8_rows_kernel<NVL, RPW>, dim3(grid), dim3(kRowsWarps * 32), 0, s, X, W, a,
+             rows);
+  return check_launch("gemv_i8_rows");
+}
+
+// rows per warp (1..3) x 16-byte weight vectors per lane per row (K / 512,
+// rounded up): a lane holds at most 16 weight vectors (128 registers a
+// thread with 512 threads a CTA, without spilling)
+template <int NVL>
+static int launch_rows_k(const int8_t *X, const int8_t *W, const GemvArgs &a, int rows,
+                         cudaStream_t s) {
+  const int rpw = (rows + kRowsWarps - 1) / kRowsWarps;
+  if (rpw <= 1) return launch_rows<NVL, 1>(X, W, a, rows, s);
+  if (rpw <= 2 && NVL <= 8) return launch_rows<NVL, (NVL <= 8 ? 2 : 1)>(X, W, a, rows, s);
+  return W8A8_ERR_UNSUPPORTED;
+}
+
 int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs &a,
                    cudaStream_t s) {
   const bool vec = (a.K % 16 == 0) && (ldx % 16 == 0) && aligned16(X) && aligned16(W);
+  if (vec && a.M == 1) {
+    int st;
+    DeviceCtx *ctx = device_ctx(&st);
+    if (!ctx) return st;
+    // Long rows (K > 2048) only: measured on GPT-2 large, W2 (1280 x 5120)
+    // takes 5.1 us this way against 7.0 us with 4-warp blocks, while the
+    // K = 1280 projections are faster with the 4-warp blocks below.
+    const int rows = (a.N + ctx->sm_count - 1) / ctx->sm_count;  // one CTA per SM
+    const int nvl = ((a.K >> 4) + 31) / 32;
+    int r = W8A8_ERR_UNSUPPORTED;
+    if (nvl > 4 && nvl <= 8) r = launch_rows_k<8>(X, W, a, rows, s);
+    else if (nvl > 8 && nvl <= 16) r = launch_rows_k<16>(X, W, a, rows, s);
+    if (r != W8A8_ERR_UNSUPPORTED) return r;
+  }
   if (vec && a.M <= 16 && a.K <= 16 * 32 * 16) {
     if (a.M <= 1) return launch_vec_k<1>(X, ldx, W, a, s);
     if (a.M <= 2) return launch_vec_k<2>(X, ldx, W, a, s);

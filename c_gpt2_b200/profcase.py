@@ -9,11 +9,12 @@ size of the large model (d_model 1280, 20 heads, context 1024).
     python -m c_gpt2_b200.profcase linear --m 32768 --n 5120 --k 1280 --epi gelu
     python -m c_gpt2_b200.profcase linear --m 64 --n 5120 --k 1280 --epi gelu
     python -m c_gpt2_b200.profcase decode [--model medium] [--batch 1] [--prompt 512] [--gen 256]
+    python -m c_gpt2_b200.profcase gemv-chain [--model large] [--layers 36]
 
 Every case holds well under 1 GB on the device and exceeds the 126 MB L2 only
 where the workload itself does (the attention KV cache, the prefill
-activations). Prints one line with the CUDA-event time per launch, measured
-after the profiled launches.
+activations, the weights of the GEMV chain). Prints one line with the
+CUDA-event time per launch, measured after the profiled launches.
 """
 from __future__ import annotations
 
@@ -156,6 +157,44 @@ def linear(a) -> None:
           f"{ops_ / us / 1e6:.0f} TOP/s, {byts / us / 1e3:.0f} GB/s algorithmic")
 
 
+def gemv_chain(a) -> None:
+    """The batch-1 decode GEMVs of a model back to back: per layer W_qkv,
+    attn_proj, W1, W2 with their epilogues, each layer with its own weights
+    (708 MB for GPT-2 large: every replay streams them from HBM), one CUDA
+    graph. Per-GEMV time and the HBM bandwidth the weight stream reaches when
+    each GEMV's weight loads overlap the previous launch (programmatic
+    dependent launch), as inside a decode step."""
+    from .quant8 import DIMS
+    dims = DIMS[a.model]
+    d, L = dims.d_model, a.layers
+    g = torch.Generator(device="cuda").manual_seed(0)
+    shapes = [(3 * d, d, "bias"), (d, d, "resid"), (4 * d, d, "gelu"), (d, 4 * d, "resid")]
+    Ws = [[torch.randint(-127, 128, (n, k), dtype=torch.int8, device="cuda", generator=g)
+           for n, k, _ in shapes] for _ in range(L)]
+    xs = {k: torch.randint(-127, 128, (1, k), dtype=torch.int8, device="cuda", generator=g)
+          for k in (d, 4 * d)}
+    sx = torch.full((1,), 1e-3, device="cuda")
+    sws = {n: torch.rand((n,), device="cuda", generator=g) * 0.01 + 1e-3 for n, _, _ in shapes}
+    bs = {n: (torch.randn((n,), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+          for n, _, _ in shapes}
+    R = torch.randn((1, d), device="cuda", generator=g).to(torch.bfloat16)
+    ys = {n: torch.empty((1, n), dtype=torch.bfloat16, device="cuda") for n, _, _ in shapes}
+
+    def run():
+        for layer in range(L):
+            for (n, k, e), W in zip(shapes, Ws[layer]):
+                ops.linear(xs[k], sx, W, sws[n], bs[n], EPI[e],
+                           R=R if e == "resid" else None, out=ys[n])
+
+    run()
+    torch.cuda.synchronize()
+    ms = _replay_ms(_graph(run, 1, False))
+    n_launch = 4 * L
+    wbytes = sum(n * k for n, k, _ in shapes) * L
+    print(f"gemv-chain {a.model} x{L} layers: {1000 * ms / n_launch:.2f} us/GEMV, "
+          f"{wbytes / 1e6:.0f} MB weights in {1000 * ms:.1f} us -> {wbytes / ms / 1e6:.0f} GB/s")
+
+
 def decode(a) -> None:
     """Whole greedy decode steps of the engine (CUDA-graph replays): per-step
     time and the bytes a step must read (int8 weights + bf16 LM head + the KV
@@ -209,6 +248,9 @@ def main(argv=None) -> None:
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--prompt", type=int, default=512)
     p.add_argument("--gen", type=int, default=256)
+    p = sub.add_parser("gemv-chain")
+    p.add_argument("--model", choices=["small", "medium", "large"], default="large")
+    p.add_argument("--layers", type=int, default=36)
     p = sub.add_parser("linear")
     p.add_argument("--m", type=int, required=True)
     p.add_argument("--n", type=int, required=True)
@@ -224,7 +266,8 @@ def main(argv=None) -> None:
         global _FLUSH
         _FLUSH = torch.ones((64 << 20,), dtype=torch.float32, device="cuda")
     {"attention-decode": attention_decode, "attention-prefill": attention_prefill,
-     "layernorm-quant": layernorm_quant, "linear": linear, "decode": decode}[a.case](a)
+     "layernorm-quant": layernorm_quant, "linear": linear, "decode": decode,
+     "gemv-chain": gemv_chain}[a.case](a)
     st = ops.device_error()
     if st:
         raise SystemExit(f"device error word {st}")

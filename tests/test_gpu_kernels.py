@@ -61,7 +61,8 @@ def test_gemm_s32_extreme_values(cuda):
 
 @pytest.mark.parametrize("M,N,K", [(1, 2304, 768), (9, 768, 3072), (16, 2304, 768),
                                    (128, 3072, 768), (300, 768, 3072), (1024, 2304, 768),
-                                   (300, 320, 768), (129, 96, 256)])
+                                   (300, 320, 768), (129, 96, 256), (1, 1280, 5120),
+                                   (1, 200, 3072), (1, 5120, 1280)])
 @pytest.mark.parametrize("epi", [_lib.EPI_DEQUANT, _lib.EPI_BIAS, _lib.EPI_BIAS_RESID])
 def test_linear_epilogues_bit_exact(cuda, M, N, K, epi):
     rng = np.random.default_rng(M + N + K + epi)
