@@ -387,12 +387,13 @@ __device__ __forceinline__ void score_keys(const DecodeArgs &a, int b, int h, in
 // Softmax statistics of a full score row (n entries, bf16) with the
 // reference's 256-slot tree: slot t adds e_j for j = t, t + 256, ... in
 // order, then the slots fold pairwise (s = 128 .. 1). With NT = 128 threads,
-// thread t owns slots t and t + 128 (the first fold is its own addition).
-// Returns (max, 1/sum).
+// thread t owns slots t and t + 128 (the first fold is its own addition);
+// with more than 256, threads 0..255 own the slots and the rest only help
+// with the maximum. s_tree holds 256 floats. Returns (max, 1/sum).
 template <int NT, typename Load>
 __device__ __forceinline__ void row_stats(int n, int tid, Load ld, float *s_red, float *s_tree,
                                           float &mx_out, float &inv_out) {
-  static_assert(NT == 128 || NT == 256, "row_stats: 128 or 256 threads");
+  static_assert(NT == 128 || NT == 256 || NT == 512, "row_stats: 128, 256 or 512 threads");
   const int warp = tid >> 5, lane = tid & 31;
   float mx = -INFINITY;
   for (int j = tid; j < n; j += NT) mx = fmaxf(mx, bf2f(ld(j)));
@@ -404,13 +405,14 @@ __device__ __forceinline__ void row_stats(int n, int tid, Load ld, float *s_red,
 #pragma unroll
   for (int w = 1; w < NT / 32; ++w) mx = fmaxf(mx, s_red[w]);
   float local_sum = 0.0f;
-  for (int j = tid; j < n; j += 256) local_sum += expf(bf2f(ld(j)) - mx);
+  if (tid < 256)
+    for (int j = tid; j < n; j += 256) local_sum += expf(bf2f(ld(j)) - mx);
   if (NT == 128) {
     float hi_sum = 0.0f;
     for (int j = tid + 128; j < n; j += 256) hi_sum += expf(bf2f(ld(j)) - mx);
     local_sum += hi_sum;  // fold s = 128: slot t += slot t + 128
   }
-  s_tree[tid] = local_sum;
+  if (tid < (NT == 128 ? 128 : 256)) s_tree[tid] = local_sum;
   __syncthreads();
   for (int s = (NT == 128 ? 64 : 128); s > 0; s >>= 1) {
     if (tid < s) s_tree[tid] += s_tree[tid + s];
@@ -591,19 +593,18 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
   if (a.Xq) quant_row_when_complete<256>(a, b, tid, s_red, &s_last);
 }
 
-// Whole-row path (enough (b, h) pairs to fill the GPU): one CTA of 128
-// threads per (b, h) keeps the scores in shared memory, so K and V are each
-// read once and the call is one launch. Small CTAs (48 registers, ~8 KB of
-// shared memory) let ten of them share an SM, so a 64-sequence batch of
-// GPT-2 large (1280 pairs) runs as a single wave.
-constexpr int kFusedThreads = 128;
-
-__global__ void __launch_bounds__(kFusedThreads) attention_decode_fused_kernel(DecodeArgs a) {
+// Whole-row path: one CTA per (b, h) keeps the scores in shared memory, so K
+// and V are each read once and the call is one launch. With enough pairs to
+// fill the GPU the CTAs are small (128 threads, 48 registers, ~8 KB of shared
+// memory): ten share an SM and a 64-sequence batch of GPT-2 large (1280
+// pairs) runs as a single wave. With fewer pairs than SMs (small batches)
+// each CTA has 512 threads, so one pair's keys are covered in a few steps.
+template <int NT>
+__global__ void __launch_bounds__(NT) attention_decode_fused_kernel(DecodeArgs a) {
   pdl_wait();
   pdl_launch_dependents();
-  constexpr int NT = kFusedThreads;
   __shared__ float s_red[NT / 32];
-  __shared__ float s_tree[NT];
+  __shared__ float s_tree[NT == 128 ? 128 : 256];
   __shared__ float s_part[NT / 32][kHD];
   __shared__ float s_p[1024];
   __shared__ uint16_t s_s[1024];
@@ -624,14 +625,16 @@ __global__ void __launch_bounds__(kFusedThreads) attention_decode_fused_kernel(D
   if (a.Xq) quant_row_when_complete<NT>(a, b, tid, s_red, &s_flag);
 }
 
-// One CTA per (sequence, head) as soon as the pairs alone cover the SMs (one
-// launch, K and V read once); below that, split the keys so that about two
-// CTAs land on every SM, with at least 128 keys per split. Measured on GPT-2
-// large decode steps: 8 sequences (160 pairs) run 15% faster unsplit than in
-// 2 splits, a single sequence 6% faster in 8 splits than in 16.
+// One CTA per (sequence, head) unless the pairs cover fewer than a quarter of
+// the SMs; then split the keys so that about two CTAs land on every SM, with
+// at least 128 keys per split. Measured on decode steps (prompt 512): GPT-2
+// large with 1 sequence (20 pairs) 1196 us split / 1362 us whole-row, with 4
+// sequences 1755 us split / 1577 us whole-row (512-thread CTAs); GPT-2 medium
+// with 1 sequence 789 / 869 us; 8 sequences of GPT-2 large (160 pairs) 15%
+// faster whole-row than in 2 splits.
 static int decode_splits(int n_seq, int n_head, int max_ctx, int sm_count) {
   const int pairs = n_seq * n_head;
-  if (pairs >= sm_count) return 1;
+  if (4 * pairs >= sm_count) return 1;
   int splits = 1;
   while (pairs * splits < 2 * sm_count && splits * 2 * 128 <= max_ctx) splits *= 2;
   return splits;
@@ -696,7 +699,10 @@ int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
   a.Xq = Xq;
   a.sXq = sXq;
   if (a.splits == 1) {
-    launch_pdl(attention_decode_fused_kernel, dim3(n_seq * n_head), dim3(kFusedThreads), 0, s, a);
+    if (n_seq * n_head >= sm_count)
+      launch_pdl(attention_decode_fused_kernel<128>, dim3(n_seq * n_head), dim3(128), 0, s, a);
+    else
+      launch_pdl(attention_decode_fused_kernel<512>, dim3(n_seq * n_head), dim3(512), 0, s, a);
     return check_launch("attention_decode_fused");
   }
   dim3 grid(n_seq * n_head, a.splits);
