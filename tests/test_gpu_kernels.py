@@ -328,6 +328,20 @@ def test_lm_head_and_greedy(cuda, M):
         assert toks[m] == oracle.greedy(got[m])
 
 
+def test_greedy_probability_rounding_ties(cuda):
+    """Logits from a few adjacent bf16 values near the top: many entries share
+    the largest bf16 probability after rounding (also entries whose logits
+    differ), and the first of them must win, as in the reference."""
+    rng = np.random.default_rng(5)
+    V, M = 50257, 8
+    top = oracle.bf16_bits(np.array([0.5], np.float32))[0]
+    vals = (top - np.arange(4, dtype=np.uint16)).astype(np.uint16)
+    lg = rng.choice(vals, (M, V)).astype(np.uint16)
+    lg[:, ::7] = oracle.bf16_bits(np.full((1,), -4.0, np.float32))[0]
+    toks = ops.sample_greedy(to_dev_bf16(lg)).cpu().numpy()
+    assert list(toks) == [oracle.greedy(lg[m]) for m in range(M)]
+
+
 def test_greedy_tie_break_first_index(cuda):
     V = 50257
     x = np.full((2, V), -3.0, np.float32)
