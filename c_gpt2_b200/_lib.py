@@ -86,6 +86,11 @@ SIGNATURES = {
     "gpt2_engine_generate_device": (_i, [_p, _p, _i, _i, _i, _p, _p]),
     "gpt2_engine_prefill": (_i, [_p, _p, _i, _i, _p, _i]),
     "gpt2_engine_decode_steps": (_i, [_p, _i]),
+    "gpt2_engine_slots_begin": (_i, [_p, _i, _p, _i]),
+    "gpt2_engine_slot_prefill": (_i, [_p, _i, _p, _i]),
+    "gpt2_engine_slot_release": (_i, [_p, _i, _p]),
+    "gpt2_engine_slot_tokens": (_i, [_p, _i]),
+    "gpt2_engine_serve": (_i, [_p, _p, _i, _i]),
     "gpt2_engine_copy_logits": (_i, [_p, _p, _i]),
     "gpt2_engine_set_graphs": (_i, [_p, _i]),
     "gpt2_engine_launches_per_decode_step": (_i, [_p]),
@@ -122,6 +127,11 @@ COMPAT_SIGNATURES = {
 class EngineConfig(C.Structure):
     _fields_ = [("d_model", _i), ("n_layer", _i), ("n_head", _i), ("vocab", _i), ("ctx", _i),
                 ("max_batch", _i), ("max_tokens", _i)]
+
+
+class Request(C.Structure):
+    """gpt2_request (include/gpt2_engine.h)."""
+    _fields_ = [("prompt", _p), ("T", _i), ("n_gen", _i), ("out", _p)]
 
 
 class W8A8Error(RuntimeError):

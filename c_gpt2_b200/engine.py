@@ -7,7 +7,7 @@ import os
 import numpy as np
 
 from . import _lib
-from ._lib import EngineConfig, W8A8Error, core
+from ._lib import EngineConfig, Request, W8A8Error, core
 from .quant8 import GPT2Dims
 
 
@@ -91,6 +91,41 @@ class Engine:
 
     def decode_steps(self, steps: int) -> None:
         self._check(core().gpt2_engine_decode_steps(self._h, steps), "gpt2_engine_decode_steps")
+
+    # -- continuous batching ------------------------------------------------
+    def serve(self, requests: list[tuple[np.ndarray, int]], slots: int) -> list[np.ndarray]:
+        """Serve (prompt ids, n_gen) requests over `slots` decode slots, admitted
+        in order as slots free up (gpt2_engine_serve). Returns each request's
+        generated ids."""
+        prompts = [np.ascontiguousarray(p, dtype=np.int32) for p, _ in requests]
+        outs = [np.zeros((n,), dtype=np.int32) for _, n in requests]
+        reqs = (Request * len(requests))()
+        for i, ((_, n), p, o) in enumerate(zip(requests, prompts, outs)):
+            reqs[i] = Request(p.ctypes.data, p.size, n, o.ctypes.data)
+        self._check(core().gpt2_engine_serve(self._h, reqs, len(requests), slots),
+                    "gpt2_engine_serve")
+        return outs
+
+    def slots_begin(self, slots: int, out_d, out_stride: int) -> None:
+        self._check(core().gpt2_engine_slots_begin(self._h, slots, out_d.data_ptr(), out_stride),
+                    "gpt2_engine_slots_begin")
+
+    def slot_prefill(self, slot: int, prompt_d) -> None:
+        self._check(core().gpt2_engine_slot_prefill(self._h, slot, prompt_d.data_ptr(),
+                                                    prompt_d.numel()),
+                    "gpt2_engine_slot_prefill")
+
+    def slot_release(self, slot: int) -> np.ndarray:
+        """The slot's tokens so far; the slot is parked."""
+        n = core().gpt2_engine_slot_tokens(self._h, slot)
+        out = np.zeros((max(n, 0),), dtype=np.int32)
+        self._check(core().gpt2_engine_slot_release(self._h, slot,
+                                                    out.ctypes.data if n > 0 else None),
+                    "gpt2_engine_slot_release")
+        return out
+
+    def slot_tokens(self, slot: int) -> int:
+        return core().gpt2_engine_slot_tokens(self._h, slot)
 
     def logits(self, rows: int) -> np.ndarray:
         """bf16 logits of the last step as float32 [rows, vocab]."""

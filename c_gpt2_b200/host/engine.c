@@ -53,14 +53,19 @@ struct gpt2_engine {
   size_t attn_ws_bytes;
   void *lin_ws; /* split-K workspace of the decode-sized GEMMs (zeroed) */
   size_t lin_ws_bytes;
-  /* current batch */
+  /* current batch: B slots (rows) of the decode step */
   int B;
   int32_t *out;
   int out_stride;
+  /* host mirror of each slot's device counters (len: cache rows filled,
+   * gen: tokens written to its output row); active: the slot holds a
+   * sequence whose tokens are wanted (else it is parked and its steps are
+   * discarded) */
+  int *slot_len, *slot_gen, *slot_active;
   /* decode graph */
   int use_graphs;
   cudaGraphExec_t graph;
-  int graph_B;
+  int graph_B, graph_stride;
   int32_t *graph_out;
 };
 
@@ -171,10 +176,15 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   e->device = device;
   e->use_graphs = 1;
   e->layers = (layer_w *)calloc((size_t)cfg->n_layer, sizeof(layer_w));
-  if (!e->layers) {
+  e->slot_len = (int *)calloc((size_t)cfg->max_batch * 3, sizeof(int));
+  if (!e->layers || !e->slot_len) {
+    free(e->layers);
+    free(e->slot_len);
     free(e);
     return W8A8_ERR_NOMEM;
   }
+  e->slot_gen = e->slot_len + cfg->max_batch;
+  e->slot_active = e->slot_len + 2 * cfg->max_batch;
   int st = w8a8_init(device);
   if (st != W8A8_OK) {
     gpt2_engine_destroy(e);
@@ -254,6 +264,7 @@ void gpt2_engine_destroy(gpt2_engine *e) {
   if (e->Kc) cudaFree(e->Kc);
   if (e->Vc) cudaFree(e->Vc);
   if (e->stream) cudaStreamDestroy(e->stream);
+  free(e->slot_len);
   free(e->layers);
   free(e);
 }
@@ -386,14 +397,16 @@ int gpt2_engine_load_quant8(gpt2_engine *e, const char *path) {
 
 /* One transformer block over M = B*T rows of H (T tokens per sequence,
  * written at cache rows pos0[b] + t; pos0 == NULL means prefill from 0). */
-static int block_forward(gpt2_engine *e, int l, int B, int T, const int32_t *pos0, int first) {
+static int block_forward(gpt2_engine *e, int l, int slot0, int B, int T, const int32_t *pos0,
+                         int first) {
   const gpt2_engine_config *c = &e->cfg;
   const layer_w *w = &e->layers[l];
   const int d = c->d_model, f = 4 * d, M = B * T, Hh = c->n_head;
   const float eps = 1e-5f; /* gpt2.c:627 */
   const int64_t seq_stride = (int64_t)c->n_layer * c->ctx * d;
-  gpt2_bf16_t *Kl = e->Kc + (int64_t)l * c->ctx * d;
-  gpt2_bf16_t *Vl = e->Vc + (int64_t)l * c->ctx * d;
+  /* the caches of slots slot0 .. slot0+B-1 */
+  gpt2_bf16_t *Kl = e->Kc + (int64_t)slot0 * seq_stride + (int64_t)l * c->ctx * d;
+  gpt2_bf16_t *Vl = e->Vc + (int64_t)slot0 * seq_stride + (int64_t)l * c->ctx * d;
   void *s = (void *)e->stream;
   if (!first)
     W8_TRY(e, w8a8_layernorm_quant(e->H, d, M, d, w->ln1_g, w->ln1_b, eps, NULL, 0, e->Xq, e->sX, s));
@@ -418,8 +431,9 @@ static int block_forward(gpt2_engine *e, int l, int B, int T, const int32_t *pos
 }
 
 /* Embedding + all blocks + final LN of the last row of each sequence + LM
- * head + greedy pick appended to the output buffer. */
-static int model_forward(gpt2_engine *e, const int32_t *tokens_d, int B, int T,
+ * head + greedy pick appended to the output rows, for the B sequences in
+ * slots slot0 .. slot0+B-1. */
+static int model_forward(gpt2_engine *e, const int32_t *tokens_d, int slot0, int B, int T,
                          const int32_t *pos0) {
   const gpt2_engine_config *c = &e->cfg;
   const int d = c->d_model, M = B * T;
@@ -429,15 +443,16 @@ static int model_forward(gpt2_engine *e, const int32_t *tokens_d, int B, int T,
   W8_TRY(e, w8a8_embed_layernorm_quant(e->wte, e->wpe, tokens_d, M, T, pos0, d, e->H, w0->ln1_g,
                                        w0->ln1_b, eps, NULL, e->Xq, e->sX, s));
   for (int l = 0; l < c->n_layer; ++l) {
-    int st = block_forward(e, l, B, T, pos0, l == 0);
+    int st = block_forward(e, l, slot0, B, T, pos0, l == 0);
     if (st) return st;
   }
   /* final LayerNorm on the last token of every sequence (gpt2.c:2150-2157) */
   W8_TRY(e, w8a8_layernorm_quant(e->H + (int64_t)(T - 1) * d, (int64_t)T * d, B, d, e->lnf_g,
                                  e->lnf_b, eps, e->Xf, d, NULL, NULL, s));
   W8_TRY(e, w8a8_lm_head(e->Xf, d, B, d, e->wte, c->vocab, e->logits, c->vocab, s));
-  W8_TRY(e, w8a8_sample_greedy(e->logits, c->vocab, B, c->vocab, e->next, e->out,
-                               e->out_stride, e->gen, s));
+  W8_TRY(e, w8a8_sample_greedy(e->logits, c->vocab, B, c->vocab, e->next + slot0,
+                               e->out + (int64_t)slot0 * e->out_stride, e->out_stride,
+                               e->gen + slot0, s));
   return W8A8_OK;
 }
 
@@ -464,23 +479,93 @@ int gpt2_engine_prefill(gpt2_engine *e, const int32_t *prompts_d, int B, int T,
   if (B <= 0 || T <= 0 || B > c->max_batch || (size_t)B * T > (size_t)c->max_tokens ||
       T > c->ctx)
     return fail(e, W8A8_ERR_INVALID, "batch %d x %d exceeds engine limits", B, T);
+  if (out_stride < 1) return fail(e, W8A8_ERR_INVALID, "output stride %d", out_stride);
   e->B = B;
   e->out = out_tokens_d;
   e->out_stride = out_stride;
   /* reset per-sequence state: gen = 0, len = T (after this prefill) */
   CUDA_TRY(e, cudaMemsetAsync(e->gen, 0, (size_t)B * 4, e->stream));
-  int st = model_forward(e, prompts_d, B, T, NULL);
+  int st = model_forward(e, prompts_d, 0, B, T, NULL);
   if (st) return st;
   CUDA_TRY(e, cudaMemsetAsync(e->len, 0, (size_t)B * 4, e->stream));
   W8_TRY(e, w8a8_advance_positions(e->len, e->len, B, T, (void *)e->stream));
+  for (int b = 0; b < B; ++b) {
+    e->slot_len[b] = T;
+    e->slot_gen[b] = 1;
+    e->slot_active[b] = 1;
+  }
   return W8A8_OK;
+}
+
+/* ---- continuous batching: requests admitted into and released from slots ---- */
+
+/* Put slot b back to position 0 with an empty output row (device and host
+ * mirror). A parked slot keeps stepping with the others; its tokens are
+ * discarded and its cache rows are scratch. */
+static int park_slot(gpt2_engine *e, int b) {
+  CUDA_TRY(e, cudaMemsetAsync(e->len + b, 0, 4, e->stream));
+  CUDA_TRY(e, cudaMemsetAsync(e->gen + b, 0, 4, e->stream));
+  CUDA_TRY(e, cudaMemsetAsync(e->next + b, 0, 4, e->stream));
+  e->slot_len[b] = 0;
+  e->slot_gen[b] = 0;
+  e->slot_active[b] = 0;
+  return W8A8_OK;
+}
+
+int gpt2_engine_slots_begin(gpt2_engine *e, int B, int32_t *out_tokens_d, int out_stride) {
+  if (!e || !out_tokens_d) return W8A8_ERR_INVALID;
+  if (!e->loaded) return fail(e, W8A8_ERR_INVALID, "weights not loaded");
+  if (B <= 0 || B > e->cfg.max_batch || out_stride < 1)
+    return fail(e, W8A8_ERR_INVALID, "%d slots, output stride %d", B, out_stride);
+  e->B = B;
+  e->out = out_tokens_d;
+  e->out_stride = out_stride;
+  for (int b = 0; b < B; ++b) {
+    int st = park_slot(e, b);
+    if (st) return st;
+  }
+  return W8A8_OK;
+}
+
+int gpt2_engine_slot_prefill(gpt2_engine *e, int slot, const int32_t *prompt_d, int T) {
+  if (!e || !prompt_d) return W8A8_ERR_INVALID;
+  if (!e->loaded) return fail(e, W8A8_ERR_INVALID, "weights not loaded");
+  if (e->B <= 0 || slot < 0 || slot >= e->B)
+    return fail(e, W8A8_ERR_INVALID, "slot %d outside the %d slots", slot, e->B);
+  if (T <= 0 || T > e->cfg.ctx || T > e->cfg.max_tokens)
+    return fail(e, W8A8_ERR_INVALID, "prompt of %d tokens", T);
+  CUDA_TRY(e, cudaMemsetAsync(e->gen + slot, 0, 4, e->stream));
+  int st = model_forward(e, prompt_d, slot, 1, T, NULL);
+  if (st) return st;
+  CUDA_TRY(e, cudaMemsetAsync(e->len + slot, 0, 4, e->stream));
+  W8_TRY(e, w8a8_advance_positions(e->len + slot, e->len + slot, 1, T, (void *)e->stream));
+  e->slot_len[slot] = T;
+  e->slot_gen[slot] = 1;
+  e->slot_active[slot] = 1;
+  return W8A8_OK;
+}
+
+int gpt2_engine_slot_release(gpt2_engine *e, int slot, int32_t *host_tokens) {
+  if (!e || e->B <= 0 || slot < 0 || slot >= e->B) return W8A8_ERR_INVALID;
+  if (host_tokens && e->slot_active[slot] && e->slot_gen[slot] > 0) {
+    CUDA_TRY(e, cudaMemcpyAsync(host_tokens, e->out + (int64_t)slot * e->out_stride,
+                                (size_t)e->slot_gen[slot] * 4, cudaMemcpyDeviceToHost,
+                                e->stream));
+    CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+  }
+  return park_slot(e, slot);
+}
+
+int gpt2_engine_slot_tokens(const gpt2_engine *e, int slot) {
+  if (!e || e->B <= 0 || slot < 0 || slot >= e->B || !e->slot_active[slot]) return -1;
+  return e->slot_gen[slot];
 }
 
 /* One decode step: token next[b] at position len[b]. */
 static int decode_step_launches(gpt2_engine *e) {
   const int B = e->B;
   W8_TRY(e, w8a8_advance_positions(e->nctx, e->len, B, 1, (void *)e->stream));
-  int st = model_forward(e, e->next, B, 1, e->len);
+  int st = model_forward(e, e->next, 0, B, 1, e->len);
   if (st) return st;
   W8_TRY(e, w8a8_advance_positions(e->len, e->len, B, 1, (void *)e->stream));
   return W8A8_OK;
@@ -490,6 +575,25 @@ int gpt2_engine_decode_steps(gpt2_engine *e, int steps) {
   if (!e) return W8A8_ERR_INVALID;
   if (steps <= 0) return W8A8_OK;
   if (e->B <= 0) return fail(e, W8A8_ERR_INVALID, "decode before prefill");
+  if (steps > e->cfg.ctx || steps > e->out_stride)
+    return fail(e, W8A8_ERR_INVALID, "%d steps at once", steps);
+  /* every slot steps: a sequence may not outgrow its cache or output row;
+   * a parked slot that would is parked again at position 0 */
+  for (int b = 0; b < e->B; ++b) {
+    const int over = e->slot_len[b] + steps > e->cfg.ctx || e->slot_gen[b] + steps > e->out_stride;
+    if (over && e->slot_active[b])
+      return fail(e, W8A8_ERR_INVALID, "slot %d: %d cache rows / %d tokens + %d steps exceed "
+                  "ctx %d / %d", b, e->slot_len[b], e->slot_gen[b], steps, e->cfg.ctx,
+                  e->out_stride);
+    if (over) {
+      int st = park_slot(e, b);
+      if (st) return st;
+    }
+  }
+  for (int b = 0; b < e->B; ++b) {
+    e->slot_len[b] += steps;
+    e->slot_gen[b] += steps;
+  }
   if (!e->use_graphs) {
     for (int i = 0; i < steps; ++i) {
       int st = decode_step_launches(e);
@@ -497,7 +601,8 @@ int gpt2_engine_decode_steps(gpt2_engine *e, int steps) {
     }
     return W8A8_OK;
   }
-  if (!e->graph || e->graph_B != e->B || e->graph_out != e->out) {
+  if (!e->graph || e->graph_B != e->B || e->graph_out != e->out ||
+      e->graph_stride != e->out_stride) {
     if (e->graph) {
       cudaGraphExecDestroy(e->graph);
       e->graph = NULL;
@@ -518,6 +623,7 @@ int gpt2_engine_decode_steps(gpt2_engine *e, int steps) {
     if (ce != cudaSuccess) return fail(e, W8A8_ERR_CUDA, "instantiate: %s", cudaGetErrorString(ce));
     e->graph_B = e->B;
     e->graph_out = e->out;
+    e->graph_stride = e->out_stride;
   }
   for (int i = 0; i < steps; ++i) CUDA_TRY(e, cudaGraphLaunch(e->graph, e->stream));
   return W8A8_OK;
@@ -567,6 +673,73 @@ int gpt2_engine_generate(gpt2_engine *e, const int32_t *prompts, int B, int T, i
   int derr = w8a8_device_error(1);
   if (derr) return fail(e, W8A8_ERR_DEVICE, "device error word 0x%x", derr);
   return W8A8_OK;
+}
+
+/* Continuous-batching loop over `slots` slots: admit requests in order into
+ * free slots (one prefill each), run decode steps until the next request is
+ * complete, hand its tokens back and admit the next. */
+int gpt2_engine_serve(gpt2_engine *e, gpt2_request *reqs, int n_req, int slots) {
+  if (!e || (!reqs && n_req > 0) || n_req < 0) return W8A8_ERR_INVALID;
+  if (!e->loaded) return fail(e, W8A8_ERR_INVALID, "weights not loaded");
+  const gpt2_engine_config *c = &e->cfg;
+  if (slots <= 0 || slots > c->max_batch)
+    return fail(e, W8A8_ERR_INVALID, "%d slots (max_batch %d)", slots, c->max_batch);
+  for (int i = 0; i < n_req; ++i) {
+    const gpt2_request *r = &reqs[i];
+    if (!r->prompt || !r->out || r->T <= 0 || r->n_gen <= 0 || r->T > c->max_tokens ||
+        r->T + r->n_gen - 1 > c->ctx)
+      return fail(e, W8A8_ERR_INVALID, "request %d: %d prompt + %d new tokens", i, r->T,
+                  r->n_gen);
+    for (int t = 0; t < r->T; ++t)
+      if (r->prompt[t] < 0 || r->prompt[t] >= c->vocab)
+        return fail(e, W8A8_ERR_INVALID, "request %d: token %d outside the vocabulary", i,
+                    r->prompt[t]);
+  }
+  int st = gpt2_engine_slots_begin(e, slots, e->out_default, c->ctx);
+  if (st) return st;
+  int *owner = (int *)malloc((size_t)slots * sizeof(int));
+  if (!owner) return fail(e, W8A8_ERR_NOMEM, "serve: host memory");
+  for (int b = 0; b < slots; ++b) owner[b] = -1;
+  int next_req = 0, done = 0;
+  while (done < n_req && !st) {
+    /* admit into every free slot */
+    for (int b = 0; b < slots && next_req < n_req && !st; ++b) {
+      if (owner[b] >= 0) continue;
+      const gpt2_request *r = &reqs[next_req];
+      if (cudaMemcpyAsync(e->tokens_in, r->prompt, (size_t)r->T * 4, cudaMemcpyHostToDevice,
+                          e->stream) != cudaSuccess) {
+        st = fail(e, W8A8_ERR_CUDA, "serve: prompt copy");
+        break;
+      }
+      /* tokens_in is reused by the next admission only after this prefill
+       * (one stream) */
+      st = gpt2_engine_slot_prefill(e, b, e->tokens_in, r->T);
+      owner[b] = next_req++;
+    }
+    if (st) break;
+    /* steps until the first active request is complete */
+    int steps = c->ctx;
+    for (int b = 0; b < slots; ++b)
+      if (owner[b] >= 0) {
+        const int left = reqs[owner[b]].n_gen - e->slot_gen[b];
+        if (left < steps) steps = left;
+      }
+    if (steps > 0) st = gpt2_engine_decode_steps(e, steps);
+    if (st) break;
+    for (int b = 0; b < slots && !st; ++b) {
+      if (owner[b] < 0 || e->slot_gen[b] < reqs[owner[b]].n_gen) continue;
+      st = gpt2_engine_slot_release(e, b, reqs[owner[b]].out);
+      owner[b] = -1;
+      ++done;
+    }
+  }
+  free(owner);
+  if (!st) {
+    CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+    const int derr = w8a8_device_error(1);
+    if (derr) return fail(e, W8A8_ERR_DEVICE, "device error word 0x%x", derr);
+  }
+  return st;
 }
 
 int gpt2_engine_copy_logits(gpt2_engine *e, gpt2_bf16_t *host, int rows) {

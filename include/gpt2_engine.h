@@ -74,6 +74,39 @@ int gpt2_engine_prefill(gpt2_engine *e, const int32_t *prompts_d, int B, int T,
                         int32_t *out_tokens_d, int out_stride);
 int gpt2_engine_decode_steps(gpt2_engine *e, int steps);
 
+/* Continuous batching (serving requests of different lengths; the
+ * reference serves one sequence per process, gpt2.c:2026-2036).
+ * The decode step runs over B slots; each slot holds one sequence or is
+ * parked (it steps at position 0 and its tokens are discarded). A slot's
+ * sequence produces exactly the tokens it would produce in any other batch
+ * of B slots: every row of every kernel is computed on its own.
+ *   slots_begin:  B slots (B <= max_batch), all parked; slot b writes its
+ *                 tokens to out_tokens_d[b*out_stride ...] (device memory).
+ *   slot_prefill: prefill prompt_d[0..T) (device ids in [0, vocab), not
+ *                 checked) into slot `slot`, writing its first token; the
+ *                 other slots keep their state.
+ *   decode_steps: every slot steps (as above); fails when an active slot
+ *                 would pass ctx cache rows or out_stride tokens.
+ *   slot_release: copy the slot's tokens so far to host_tokens (NULL: drop
+ *                 them; synchronous) and park the slot.
+ *   slot_tokens:  tokens the slot's sequence has produced, -1 if parked. */
+int gpt2_engine_slots_begin(gpt2_engine *e, int B, int32_t *out_tokens_d, int out_stride);
+int gpt2_engine_slot_prefill(gpt2_engine *e, int slot, const int32_t *prompt_d, int T);
+int gpt2_engine_slot_release(gpt2_engine *e, int slot, int32_t *host_tokens);
+int gpt2_engine_slot_tokens(const gpt2_engine *e, int slot);
+
+/* One request of gpt2_engine_serve: T host prompt ids -> n_gen new ids. */
+typedef struct {
+  const int32_t *prompt;
+  int T;
+  int n_gen;
+  int32_t *out;  /* host, n_gen ids */
+} gpt2_request;
+/* Serve n_req requests over `slots` slots (continuous batching): requests
+ * are admitted in order as slots free up; each gets the tokens it would get
+ * alone at this slot count. Checks every id; synchronous. */
+int gpt2_engine_serve(gpt2_engine *e, gpt2_request *reqs, int n_req, int slots);
+
 /* Copy the logits of the last step ([B, vocab] bf16) to host memory. */
 int gpt2_engine_copy_logits(gpt2_engine *e, gpt2_bf16_t *host, int rows);
 /* Enable (default) or disable CUDA-graph replay of decode steps. */

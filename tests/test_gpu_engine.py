@@ -137,3 +137,74 @@ def test_engine_rejects_out_of_vocabulary_prompt(cuda, tiny_image):
     with pytest.raises(W8A8Error):
         eng.generate(P, 4)
     eng.close()
+
+
+def _requests(seed: int, n: int):
+    rng = np.random.default_rng(seed)
+    out = []
+    for i in range(n):
+        T = int(rng.integers(3, 40))
+        out.append((rng.integers(0, TINY.vocab, T).astype(np.int32), int(rng.integers(1, 25))))
+    return out
+
+
+def test_serve_continuous_batching_matches_oracle(cuda, tiny_image):
+    """Continuous batching: 7 requests of different prompt lengths and token
+    budgets over 3 slots, admitted as slots free up. Every request's stream
+    equals the oracle's stream for that prompt alone."""
+    reqs = _requests(21, 7)
+    eng = Engine(TINY, max_batch=4, max_tokens=64)
+    eng.load_quant8(tiny_image)
+    outs = eng.serve(reqs, slots=3)
+    for (p, n), got in zip(reqs, outs):
+        assert got.shape == (n,)
+        assert_same_stream_up_to_ties(got, tiny_image, TINY, p, n)
+    eng.close()
+
+
+def test_serve_independent_of_admission_order(cuda, tiny_image):
+    """A request's tokens do not depend on which requests share the decode
+    steps with it, nor on its slot: served in reverse order the outputs are
+    bit-identical. A later batch generate() (other output stride) is
+    unaffected by the serving graph."""
+    reqs = _requests(22, 6)
+    eng = Engine(TINY, max_batch=4, max_tokens=64)
+    eng.load_quant8(tiny_image)
+    fwd = eng.serve(reqs, slots=3)
+    rev = eng.serve(reqs[::-1], slots=3)[::-1]
+    for a, b in zip(fwd, rev):
+        np.testing.assert_array_equal(a, b)
+    P = prompts(3, 16, TINY.vocab, seed=4)
+    after = eng.generate(P, 12)
+    fresh = Engine(TINY, max_batch=4, max_tokens=64)
+    fresh.load_quant8(tiny_image)
+    np.testing.assert_array_equal(after, fresh.generate(P, 12))
+    eng.close()
+    fresh.close()
+
+
+def test_slot_api_bounds(cuda, tiny_image):
+    """Slot calls: a released slot returns its tokens and can be reused; a
+    sequence may not step past its output row or ctx; bad slots are refused."""
+    from c_gpt2_b200._lib import W8A8Error
+    eng = Engine(TINY, max_batch=2, max_tokens=64)
+    eng.load_quant8(tiny_image)
+    out = torch.zeros((2, 8), dtype=torch.int32, device=cuda)
+    eng.slots_begin(2, out, 8)
+    p = torch.from_numpy(prompts(1, 10, TINY.vocab, seed=3)[0]).to(cuda)
+    eng.slot_prefill(1, p)
+    assert eng.slot_tokens(1) == 1 and eng.slot_tokens(0) == -1
+    eng.decode_steps(4)
+    assert eng.slot_tokens(1) == 5
+    with pytest.raises(W8A8Error):
+        eng.decode_steps(4)            # slot 1 would write 9 tokens into a row of 8
+    toks = eng.slot_release(1)
+    want = eng.generate(prompts(1, 10, TINY.vocab, seed=3), 5)[0]
+    np.testing.assert_array_equal(toks, want)
+    eng.slots_begin(2, out, 8)
+    with pytest.raises(W8A8Error):
+        eng.slot_prefill(2, p)         # no slot 2
+    long = torch.from_numpy(prompts(1, TINY.ctx + 1, TINY.vocab, seed=3)[0]).to(cuda)
+    with pytest.raises(W8A8Error):
+        eng.slot_prefill(0, long)      # longer than ctx
+    eng.close()
