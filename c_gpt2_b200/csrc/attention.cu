@@ -593,6 +593,110 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
   if (a.Xq) quant_row_when_complete<256>(a, b, tid, s_red, &s_last);
 }
 
+// Split path as one launch: the `splits` CTAs of a (b, h) pair form a thread-
+// block cluster; CTA r owns keys [r*kps, (r+1)*kps) of the row (kps =
+// keys_per_split) and everything the two-kernel form exchanges through the
+// workspace moves through distributed shared memory instead:
+//   scores of its keys (own shared memory) -> its maximum -> the row maximum
+//   (every CTA reads all CTAs' maxima) -> e_j = expf(S_j - max) of its keys ->
+//   the reference's 256-slot sums (slot t adds e_j, j = t, t + 256, ... in
+//   order, read from the CTA holding each j; CTA r sums slots
+//   r*256/splits ..) stored in CTA 0 -> every CTA folds the 256 slots with the
+//   same tree -> P of its keys -> its P.V partial -> CTA 0 adds the partials
+//   in rank order, rounds, stores (and quantizes the sequence's row when it
+//   is the last of its heads).
+// The same operations on the same key ranges as the two kernels above, so the
+// same bits, in one launch with no global round trip between the phases.
+__global__ void __launch_bounds__(256) attention_decode_cluster_kernel(DecodeArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ uint16_t s_s[1024];  // scores of this CTA's keys
+  __shared__ float s_e[1024];     // their exponentials, then their P
+  __shared__ float s_red[8];
+  __shared__ float s_tree[256];
+  __shared__ float s_slots[256];  // CTA 0: the 256 slot sums
+  __shared__ float s_part[8][kHD];
+  __shared__ float s_o[kHD];      // this CTA's P.V partial
+  __shared__ float s_cmax;
+  __shared__ int s_flag;
+  const uint32_t r = cluster_ctarank();
+  const int S = a.splits, kps = a.keys_per_split;
+  const int bh = blockIdx.x / S;
+  const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
+  const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
+  const int j0 = (int)r * kps, j1 = min(n, j0 + kps);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // scores of this CTA's keys
+  score_keys(a, b, h, j0, j1, warp, 8, lane, [&](int j, uint16_t sv) { s_s[j - j0] = sv; });
+  __syncthreads();
+  // row maximum
+  float mx = -INFINITY;
+  for (int j = j0 + tid; j < j1; j += 256) mx = fmaxf(mx, bf2f(s_s[j - j0]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) s_red[warp] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float m = s_red[0];
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, s_red[w]);
+    s_cmax = m;
+  }
+  cluster_sync_all();
+  if (tid == 0) {
+    float m = ld_dsmem_f32(dsmem_addr(&s_cmax, 0));
+    for (int q = 1; q < S; ++q) m = fmaxf(m, ld_dsmem_f32(dsmem_addr(&s_cmax, (uint32_t)q)));
+    s_red[0] = m;
+  }
+  __syncthreads();
+  mx = s_red[0];
+  for (int j = j0 + tid; j < j1; j += 256) s_e[j - j0] = expf(bf2f(s_s[j - j0]) - mx);
+  cluster_sync_all();
+  // slot sums, in order, over the cluster
+  const int per = 256 / S;  // slots per CTA (S <= 8: at most 8 slots' worth of... per >= 32)
+  if (tid < per) {
+    const int t = (int)r * per + tid;
+    float acc = 0.0f;
+    int q = 0, off = t;  // e_j lives in CTA q at offset off (kps >= 128: q steps by <= 2)
+    while (off >= kps) {
+      off -= kps;
+      ++q;
+    }
+    for (int j = t; j < n; j += 256) {
+      acc += ld_dsmem_f32(dsmem_addr(&s_e[off], (uint32_t)q));
+      off += 256;
+      while (off >= kps) {
+        off -= kps;
+        ++q;
+      }
+    }
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dsmem_addr(&s_slots[t], 0)), "f"(acc)
+                 : "memory");
+  }
+  cluster_sync_all();
+  s_tree[tid] = ld_dsmem_f32(dsmem_addr(&s_slots[tid], 0));
+  __syncthreads();
+  for (int s = 128; s > 0; s >>= 1) {
+    if (tid < s) s_tree[tid] += s_tree[tid + s];
+    __syncthreads();
+  }
+  const float inv_sum = 1.0f / s_tree[0];
+  for (int j = j0 + tid; j < j1; j += 256)
+    s_e[j - j0] = bf2f(f2bf(bf2f(f2bf(s_e[j - j0])) * inv_sum));
+  __syncthreads();
+  const float o = pv_range<256>(a, b, h, j0, j1, s_e, s_part, tid);
+  if (tid < kHD) s_o[tid] = o;
+  cluster_sync_all();
+  if (r == 0) {
+    if (tid < kHD) {
+      float tot = 0.f;
+      for (int q = 0; q < S; ++q) tot += ld_dsmem_f32(dsmem_addr(&s_o[tid], (uint32_t)q));
+      a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(tot);
+    }
+    if (a.Xq) quant_row_when_complete<256>(a, b, tid, s_red, &s_flag);
+  }
+  cluster_sync_all();  // no CTA leaves while CTA 0 still reads its partial
+}
+
 // Whole-row path: one CTA per (b, h) keeps the scores in shared memory, so K
 // and V are each read once and the call is one launch. With enough pairs to
 // fill the GPU the CTAs are small (128 threads, 48 registers, ~8 KB of shared
@@ -657,7 +761,10 @@ int decode_workspace_reset(void *ws, size_t ws_bytes, cudaStream_t s) {
 }
 
 int decode_launches(int n_seq, int n_head, int max_ctx, int sm_count) {
-  return decode_splits(n_seq, n_head, max_ctx, sm_count) == 1 ? 1 : 2;
+  const int splits = decode_splits(n_seq, n_head, max_ctx, sm_count);
+  if (splits == 1) return 1;
+  const int kps = (max_ctx + splits - 1) / splits;
+  return (kps <= 1024 && kps >= 128 && splits <= 8) ? 1 : 2;  // cluster form: one launch
 }
 
 size_t decode_workspace_bytes(int n_seq, int n_head, int max_ctx, int splits) {
@@ -704,6 +811,27 @@ int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
     else
       launch_pdl(attention_decode_fused_kernel<512>, dim3(n_seq * n_head), dim3(512), 0, s, a);
     return check_launch("attention_decode_fused");
+  }
+  if (a.keys_per_split <= 1024 && a.keys_per_split >= 128 && a.splits <= 8) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_seq * n_head * a.splits);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)a.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, attention_decode_cluster_kernel, a) != cudaSuccess) {
+      cudaGetLastError();
+      return W8A8_ERR_CUDA;
+    }
+    return check_launch("attention_decode_cluster");
   }
   dim3 grid(n_seq * n_head, a.splits);
   launch_pdl(attention_decode_scores_kernel, dim3(grid), dim3(256), 0, s, a);
