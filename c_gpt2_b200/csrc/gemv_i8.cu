@@ -1,11 +1,13 @@
-// HBM-streaming INT8 GEMV for decode (1..15 tokens) and the CUDA-core
-// fallback for shapes the TMA path cannot take (K % 16 != 0, unaligned rows).
+// HBM-streaming INT8 GEMV for decode (the engine sends it single tokens; the
+// API takes up to 16) and the CUDA-core fallback for shapes the TMA path
+// cannot take (K % 16 != 0, unaligned rows).
 //
 // One warp owns one output channel n: it holds W[n, :] in registers (16-byte
 // loads, all in flight at once), multiplies against the token rows with dp4a,
-// and reduces across lanes. A block
-// holds 4 warps; the grid covers N/4 blocks, so even the 768-row projections
-// of GPT-2 small spread over more blocks than the B200 has SMs. Exact integer
+// and reduces across lanes. A block holds 4 warps; the grid covers N/4
+// blocks, so even the 768-row projections of GPT-2 small spread over more
+// blocks than the B200 has SMs. Single tokens with rows longer than 2048
+// bytes take 16-warp CTAs, one per SM (gemv_i8_rows_kernel). Exact integer
 // accumulation: results are identical to the tensor-core path, and the same
 // fused epilogues apply.
 #include "common.cuh"

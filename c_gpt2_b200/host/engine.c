@@ -3,14 +3,16 @@
  *
  * Per layer, the reference runs 3 quant+GEMM+dequant triplets for Q/K/V, 3
  * bias adds, H x (QK^T, softmax, PV), concat, and 5 more launch groups for
- * the projection / MLP (gpt2.c:1124-1330). Here a layer is 9 launches:
+ * the projection / MLP (gpt2.c:1124-1330). Here a prefill layer is 9
+ * launches:
  *
  *   LN1+quant -> QKV GEMM (dequant, bias, scatter into Q and the KV cache)
  *   -> attention -> quant -> proj GEMM (dequant, bias, residual)
  *   -> LN2+quant -> W1 GEMM (dequant, bias, GELU) -> quant
  *   -> W2 GEMM (dequant, bias, residual)
  *
- * with the first LN1 fused into the embedding gather. Each intermediate is
+ * and a decode layer 8 (the attention kernel quantizes its own output), with
+ * the first LN1 fused into the embedding gather. Each intermediate is
  * rounded to bf16 where the reference rounds it, so every output element is
  * the reference's value for the same inputs (see gpt2_w8a8.h).
  */
