@@ -102,11 +102,13 @@ def test_linear_split_k_bit_exact(cuda, M, N, K, epi):
     assert not ws.any(), "workspace not returned to zero"
 
 
-def test_linear_qkv_scatter_split_k(cuda):
+@pytest.mark.parametrize("B", [20, 8, 3])
+def test_linear_qkv_scatter_split_k(cuda, B):
     """Packed QKV GEMM writing Q rows and K/V cache rows at per-sequence
-    positions (decode: one token per sequence), with split-K."""
-    rng = np.random.default_rng(11)
-    B, d, C = 20, 768, 64
+    positions (decode: one token per sequence), split over K, at batch sizes
+    20, 8 and 3."""
+    rng = np.random.default_rng(11 + B)
+    d, C = 768, 64
     x = oracle.bf16_bits(outlier_activations(B, d, seed=4))
     xq, sx = oracle.quant_rows(x)
     W = rng.integers(-127, 128, (3 * d, d), dtype=np.int8)
