@@ -349,7 +349,7 @@ __device__ __forceinline__ void load_q8(const DecodeArgs &a, int b, int h, int p
 // S_j = bf16(0.125 * q.k_j) for keys [j0, j1), written through `emit(j, s)`.
 // 8 lanes cover one 128-byte key row (16 bytes each), a warp 4 keys per
 // step; each lane keeps 4 row loads in flight.
-template <typename Emit>
+template <int U = 4, typename Emit>
 __device__ __forceinline__ void score_keys(const DecodeArgs &a, int b, int h, int j0, int j1,
                                            int warp, int nwarps, int lane, Emit emit) {
   const int sub = lane >> 3, part = lane & 7;
@@ -357,7 +357,8 @@ __device__ __forceinline__ void score_keys(const DecodeArgs &a, int b, int h, in
   load_q8(a, b, h, part, q);
   const uint16_t *Kb = a.Kc + (int64_t)b * a.seq_stride + h * kHD + part * 8;
   const int step = nwarps * 4;
-  constexpr int U = 4;
+  // U row loads in flight per lane (any U: each score is computed alone)
+  
   for (int jb = j0 + warp * 4; jb < j1; jb += step * U) {
     uint4 kv[U];
 #pragma unroll
@@ -425,7 +426,7 @@ __device__ __forceinline__ void row_stats(int n, int tid, Load ld, float *s_red,
 // Partial O = sum_{j in [j0, j1)} P_j V_j over NT threads: 8 lanes per
 // 128-byte V row (8 dims each), 4 rows per warp step, 4 steps in flight.
 // Returns this thread's share for dim `tid` (< 64) after the block reduction.
-template <int NT>
+template <int NT, int U = 4>
 __device__ __forceinline__ float pv_range(const DecodeArgs &a, int b, int h, int j0, int j1,
                                           const float *p, float (*s_part)[kHD], int tid) {
   const int warp = tid >> 5, lane = tid & 31;
@@ -434,7 +435,9 @@ __device__ __forceinline__ float pv_range(const DecodeArgs &a, int b, int h, int
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   const uint16_t *Vb = a.Vc + (int64_t)b * a.seq_stride + h * kHD + part * 8;
-  constexpr int U = 4;
+  // U rows in flight per lane: each lane still adds its rows (j = j0 + warp*4 + sub
+  // + NT/8 * k, k = 0, 1, ...) in increasing order, so U does not change the result
+  
   constexpr int kRows = NT / 8;  // V rows per step over the block
   for (int jb = j0 + warp * 4 + sub; jb < j1; jb += kRows * U) {
     uint4 vv[U];
@@ -703,7 +706,7 @@ __global__ void __launch_bounds__(256) attention_decode_cluster_kernel(DecodeArg
 // memory): ten share an SM and a 64-sequence batch of GPT-2 large (1280
 // pairs) runs as a single wave. With fewer pairs than SMs (small batches)
 // each CTA has 512 threads, so one pair's keys are covered in a few steps.
-template <int NT>
+template <int NT, int U>
 __global__ void __launch_bounds__(NT) attention_decode_fused_kernel(DecodeArgs a) {
   pdl_wait();
   pdl_launch_dependents();
@@ -717,14 +720,14 @@ __global__ void __launch_bounds__(NT) attention_decode_fused_kernel(DecodeArgs a
   const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
   const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
   const int tid = threadIdx.x;
-  score_keys(a, b, h, 0, n, tid >> 5, NT / 32, tid & 31, [&](int j, uint16_t s) { s_s[j] = s; });
+  score_keys<U>(a, b, h, 0, n, tid >> 5, NT / 32, tid & 31, [&](int j, uint16_t s) { s_s[j] = s; });
   __syncthreads();
   float mx, inv_sum;
   row_stats<NT>(n, tid, [&](int j) { return s_s[j]; }, s_red, s_tree, mx, inv_sum);
   for (int j = tid; j < n; j += NT)
     s_p[j] = bf2f(f2bf(bf2f(f2bf(expf(bf2f(s_s[j]) - mx))) * inv_sum));
   __syncthreads();
-  const float o = pv_range<NT>(a, b, h, 0, n, s_p, s_part, tid);
+  const float o = pv_range<NT, U>(a, b, h, 0, n, s_p, s_part, tid);
   if (tid < kHD) a.O[(int64_t)b * a.ldo + h * kHD + tid] = f2bf(o);
   if (a.Xq) quant_row_when_complete<NT>(a, b, tid, s_red, &s_flag);
 }
@@ -806,10 +809,13 @@ int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
   a.Xq = Xq;
   a.sXq = sXq;
   if (a.splits == 1) {
-    if (n_seq * n_head >= sm_count)
-      launch_pdl(attention_decode_fused_kernel<128>, dim3(n_seq * n_head), dim3(128), 0, s, a);
+    const int pairs = n_seq * n_head;
+    if (pairs >= 8 * sm_count)
+      launch_pdl(attention_decode_fused_kernel<128, 4>, dim3(pairs), dim3(128), 0, s, a);
+    else if (pairs >= 4 * sm_count)
+      launch_pdl(attention_decode_fused_kernel<256, 4>, dim3(pairs), dim3(256), 0, s, a);
     else
-      launch_pdl(attention_decode_fused_kernel<512>, dim3(n_seq * n_head), dim3(512), 0, s, a);
+      launch_pdl(attention_decode_fused_kernel<512, 4>, dim3(pairs), dim3(512), 0, s, a);
     return check_launch("attention_decode_fused");
   }
   if (a.keys_per_split <= 1024 && a.keys_per_split >= 128 && a.splits <= 8) {
