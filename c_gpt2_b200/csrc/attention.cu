@@ -597,8 +597,8 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
 }
 
 // Split path as one launch: the `splits` CTAs of a (b, h) pair form a thread-
-// block cluster; CTA r owns keys [r*kps, (r+1)*kps) of the row (kps =
-// keys_per_split) and everything the two-kernel form exchanges through the
+// block cluster; CTA r owns keys [r*kps, (r+1)*kps) of the pair's n keys (kps
+// = ceil(n / splits)) and everything the two-kernel form exchanges through the
 // workspace moves through distributed shared memory instead:
 //   scores of its keys (own shared memory) -> its maximum -> the row maximum
 //   (every CTA reads all CTAs' maxima) -> e_j = expf(S_j - max) of its keys ->
@@ -608,8 +608,8 @@ __global__ void __launch_bounds__(256) attention_decode_pv_kernel(DecodeArgs a) 
 //   same tree -> P of its keys -> its P.V partial -> CTA 0 adds the partials
 //   in rank order, rounds, stores (and quantizes the sequence's row when it
 //   is the last of its heads).
-// The same operations on the same key ranges as the two kernels above, so the
-// same bits, in one launch with no global round trip between the phases.
+// The same operations as the two kernels above (which split by max_ctx), in
+// one launch with no global round trip between the phases.
 __global__ void __launch_bounds__(256) attention_decode_cluster_kernel(DecodeArgs a) {
   pdl_wait();
   pdl_launch_dependents();
@@ -623,10 +623,12 @@ __global__ void __launch_bounds__(256) attention_decode_cluster_kernel(DecodeArg
   __shared__ float s_cmax;
   __shared__ int s_flag;
   const uint32_t r = cluster_ctarank();
-  const int S = a.splits, kps = a.keys_per_split;
+  const int S = a.splits;
   const int bh = blockIdx.x / S;
   const int b = bh / a.n_head, h = bh - (bh / a.n_head) * a.n_head;
   const int n = a.n_ctx ? a.n_ctx[b] : a.max_ctx;
+  // the pair's own keys split evenly (at most keys_per_split <= 1024 each)
+  const int kps = max(1, (n + S - 1) / S);
   const int j0 = (int)r * kps, j1 = min(n, j0 + kps);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // scores of this CTA's keys
@@ -655,11 +657,11 @@ __global__ void __launch_bounds__(256) attention_decode_cluster_kernel(DecodeArg
   for (int j = j0 + tid; j < j1; j += 256) s_e[j - j0] = expf(bf2f(s_s[j - j0]) - mx);
   cluster_sync_all();
   // slot sums, in order, over the cluster
-  const int per = 256 / S;  // slots per CTA (S <= 8: at most 8 slots' worth of... per >= 32)
+  const int per = 256 / S;  // slots per CTA (S <= 8: per >= 32)
   if (tid < per) {
     const int t = (int)r * per + tid;
     float acc = 0.0f;
-    int q = 0, off = t;  // e_j lives in CTA q at offset off (kps >= 128: q steps by <= 2)
+    int q = 0, off = t;  // e_j lives in CTA q at offset off
     while (off >= kps) {
       off -= kps;
       ++q;
