@@ -71,6 +71,7 @@ struct __align__(16) SmemCtl {
   int consumed;    // k-iterations consumed by the MMA thread (for abort drain)
   int last_flag;   // split-K: this CTA holds the last partial of the tile
   int vote[2][kEpiWarps];
+  uint64_t rbar[kEpiWarps][3];  // residual slots of each epilogue warp (RT mode)
 };
 
 // ---------------------------------------------------------------------------
@@ -224,6 +225,11 @@ constexpr int kWarpStageBytes = 32 * kStageRowBytes;  // 1 KiB output / residual
 constexpr int kParamBytes = 64 * 4 + 64 * 2;
 constexpr int kWarpEpiBytes = kWarpStageBytes + 2 * kParamBytes;
 constexpr int kEpiStageBytes = kEpiWarps * kWarpEpiBytes;  // 28 KiB
+// Residual by TMA (RT mode, residual GEMMs with short K): per warp three 1 KiB
+// residual slots, then the output buffer and the parameter buffers.
+constexpr int kRSlots = 3;
+constexpr int kWarpEpiBytesRT = 5 * 1024;
+constexpr int kEpiStageBytesRT = kEpiWarps * kWarpEpiBytesRT;  // 80 KiB
 
 // Byte offset of 16-byte half h of row r in a warp's buffer. The half is
 // flipped on rows 4..7 of every 8, which makes both access patterns below
@@ -364,25 +370,56 @@ __device__ __forceinline__ void tm_row_info(const GemmArgs &a, const TmTile &g, 
   if (EPI == EPI_QKV) kv = qkv_row_offset<EPI>(a, m);
 }
 
-template <int EPI>
+// RT mode: lane 0 requests item j's 32 x 16 residual block into a slot by TMA
+// (the 32-byte swizzle lays it out as stage_off does); an item without
+// columns (a partial tile) completes the slot's phase without data.
+__device__ __forceinline__ void tm_issue_resid(const CUtensorMap *tmRb, uint64_t *bar,
+                                               uint32_t slot, const TmTile &g, int quarter,
+                                               int group, int j) {
+  if (!((j >> 1) ? g.live1 : g.live0)) {
+    mbar_arrive(bar);
+    return;
+  }
+  mbar_arrive_expect_tx(bar, (uint32_t)kWarpStageBytes);
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(slot),
+      "l"(tmRb), "r"(smem_u32(bar)), "r"(g.b0 + tm_item_col(group, j)), "r"(g.a0 + 32 * quarter)
+      : "memory");
+}
+
+template <int EPI, bool RT>
 __device__ __forceinline__ void epilogue_tm(const GemmArgs &a, SmemCtl *ctl, uint32_t tmem_base,
-                                            uint32_t stage, int quarter, int group, int lane,
-                                            volatile int *abort_flag, bool vec_params) {
+                                            uint32_t wbase, int e, int lane,
+                                            volatile int *abort_flag, bool vec_params,
+                                            const CUtensorMap *tmRb) {
+  const int quarter = (e + kEpiWarp0) & 3, group = e >> 2;
   const int total_units = a.a_tiles * a.b_tiles;
+  // output (and, without RT, residual) buffer; RT: the residual slots first
+  const uint32_t stage = RT ? wbase + (uint32_t)(kRSlots * kWarpStageBytes) : wbase;
   const uint32_t params = stage + kWarpStageBytes;  // two buffers of kParamBytes
   int acc = 0;
   uint32_t acc_phase = 0;
   // residual pieces of the next two items (items run 0..3 within a tile,
-  // then on to the CTA's next tile)
+  // then on to the CTA's next tile); RT: items issued / consumed
   uint4 rp[2], rq[2];
+  int r_issued = 0, r_used = 0;
   float sx_next = 0.f;
   int64_t kv_next = 0;
   TmTile gn = {};
   if ((int)blockIdx.x < total_units) {
     gn = tm_tile(a, blockIdx.x, quarter, group, lane);
     tm_load_params<EPI>(a, gn, group, lane, params, vec_params);
-    tm_load_resid<EPI>(a, gn, group, 0, rp);
-    tm_load_resid<EPI>(a, gn, group, 1, rq);
+    if (RT) {
+      if (lane == 0)
+        for (int j = 0; j < 2; ++j)
+          tm_issue_resid(tmRb, &ctl->rbar[e][j], wbase + (uint32_t)(j * kWarpStageBytes), gn,
+                         quarter, group, j);
+      r_issued = 2;
+    } else {
+      tm_load_resid<EPI>(a, gn, group, 0, rp);
+      tm_load_resid<EPI>(a, gn, group, 1, rq);
+    }
     tm_row_info<EPI>(a, gn, quarter, lane, sx_next, kv_next);
   }
   int iter = 0;
@@ -424,18 +461,33 @@ __device__ __forceinline__ void epilogue_tm(const GemmArgs &a, SmemCtl *ctl, uin
       uint32_t bias2[8];
       if (live) {
         tmem_ld_32x32b_x16(t_row + (uint32_t)jcol, r);
-        if (EPI == EPI_RESID) {  // this item's residual pieces into the row buffer
+        if (EPI == EPI_RESID && !RT) {  // this item's residual pieces into the row buffer
 #pragma unroll
           for (int i = 0; i < 2; ++i)
             st_shared_v4(stage + stage_off((lane >> 1) + 16 * i, lane & 1), rp[i]);
         }
       }
-      rp[0] = rq[0];
-      rp[1] = rq[1];
-      if (j < 2)
-        tm_load_resid<EPI>(a, g, group, j + 2, rq);
-      else if (has_next)
-        tm_load_resid<EPI>(a, gn, group, j - 2, rq);
+      if (RT) {
+        // refill the slot read by the previous item with the item two ahead:
+        // every lane's reads of it before the asynchronous write
+        if (j < 2 || has_next) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int q = r_issued % kRSlots;
+            tm_issue_resid(tmRb, &ctl->rbar[e][q], wbase + (uint32_t)(q * kWarpStageBytes),
+                           j < 2 ? g : gn, quarter, group, j < 2 ? j + 2 : j - 2);
+          }
+          ++r_issued;
+        }
+      } else {
+        rp[0] = rq[0];
+        rp[1] = rq[1];
+        if (j < 2)
+          tm_load_resid<EPI>(a, g, group, j + 2, rq);
+        else if (has_next)
+          tm_load_resid<EPI>(a, gn, group, j - 2, rq);
+      }
       if (live) {
         const uint32_t pi = (uint32_t)(32 * (j >> 1) + 16 * (j & 1));  // column in the buffer
 #pragma unroll
@@ -462,9 +514,19 @@ __device__ __forceinline__ void epilogue_tm(const GemmArgs &a, SmemCtl *ctl, uin
         tc_fence_before();
         mbar_arrive(&ctl->tmem_empty[acc]);
       }
-      if (!live) continue;
       uint4 rown[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-      if (EPI == EPI_RESID) {  // the residual of this lane's own row
+      if (RT) {  // this item's slot (its phase completes even for an item without columns)
+        const int q = r_used % kRSlots;
+        mbar_wait(&ctl->rbar[e][q], (uint32_t)((r_used / kRSlots) & 1), nullptr, a.err, 0x1108);
+        ++r_used;
+        if (live) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            rown[h] = ld_shared_v4(wbase + (uint32_t)(q * kWarpStageBytes) + stage_off(lane, h));
+        }
+      }
+      if (!live) continue;
+      if (EPI == EPI_RESID && !RT) {  // the residual of this lane's own row
         __syncwarp();
 #pragma unroll
         for (int h = 0; h < 2; ++h) rown[h] = ld_shared_v4(stage + stage_off(lane, h));
@@ -523,12 +585,19 @@ __device__ __forceinline__ void epilogue_tm(const GemmArgs &a, SmemCtl *ctl, uin
     }
   }
   cp_async_wait_all();  // no copy into shared memory outlives the loop
+  if (RT) {             // nor a residual load (only after an abort are any left)
+    for (; r_used < r_issued; ++r_used)
+      mbar_wait(&ctl->rbar[e][r_used % kRSlots], (uint32_t)((r_used / kRSlots) & 1), nullptr,
+                a.err, 0x1109);
+    __syncwarp();
+  }
 }
 
-template <int KIND, int EPI, bool CM>
+template <int KIND, int EPI, bool CM, bool RT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmR, GemmArgs a) {
+                   const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmRb,
+                   GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int BN = a.BN;
@@ -539,7 +608,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // [stages][A box | B box] | token-major bf16: epilogue buffers | SmemCtl
   constexpr bool kStaged = !CM && EPI != EPI_S32;
   uint8_t *epi_stage = smem + (size_t)stages * stage_bytes;
-  SmemCtl *ctl = reinterpret_cast<SmemCtl *>(epi_stage + (kStaged ? kEpiStageBytes : 0));
+  SmemCtl *ctl = reinterpret_cast<SmemCtl *>(
+      epi_stage + (kStaged ? (RT ? kEpiStageBytesRT : kEpiStageBytes) : 0));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -557,6 +627,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ctl->tmem_empty[i], kEpiThreads);
     }
     mbar_init(&ctl->drain, 1);
+    if (RT)
+      for (int w = 0; w < kEpiWarps; ++w)
+        for (int q = 0; q < kRSlots; ++q) mbar_init(&ctl->rbar[w][q], 1);
     ctl->abort_flag = 0;
     ctl->consumed = 0;
     fence_barrier_init();
@@ -564,6 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (!CM && EPI == EPI_RESID) prefetch_tmap(&tmR);
+    if (RT) prefetch_tmap(&tmRb);
   }
   if (warp == 1) {
     tmem_alloc(&ctl->tmem_base, tmem_cols);
@@ -701,8 +775,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue (token-major, bf16) ----------------
     pdl_wait();
     const int e = warp - kEpiWarp0;
-    epilogue_tm<EPI>(a, ctl, tmem_base, smem_u32(epi_stage) + (uint32_t)(e * kWarpEpiBytes),
-                     warp & 3, e >> 2, lane, abort_flag, a.vec_params != 0);
+    epilogue_tm<EPI, RT>(a, ctl, tmem_base,
+                         smem_u32(epi_stage) + (uint32_t)(e * (RT ? kWarpEpiBytesRT : kWarpEpiBytes)),
+                         e, lane, abort_flag, a.vec_params != 0, &tmRb);
   } else if (warp >= kEpiWarp0) {
     // ---------------- epilogue ----------------
     pdl_wait();
@@ -826,7 +901,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 static int round_up32(int x) { return (x + 31) & ~31; }
 
-template <int KIND, int EPI, bool CM>
+template <int KIND, int EPI, bool CM, bool RT = false>
 static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const LinearArgs &la,
                      cudaStream_t stream) {
   int st;
@@ -838,8 +913,9 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   const int esz = KIND == 0 ? 1 : 2;
   const CUtensorMapDataType dt =
       KIND == 0 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  CUtensorMap tmA, tmB, tmR;
+  CUtensorMap tmA, tmB, tmR, tmRb;
   memset(&tmR, 0, sizeof(tmR));
+  memset(&tmRb, 0, sizeof(tmRb));
   if (CM) {  // A = weights, B = tokens
     a.BN = M >= 256 ? 256 : round_up32(M < 32 ? 32 : M);
     st = make_tmap_2d(&tmA, W, dt, (uint64_t)N, (uint64_t)K, (uint64_t)K * esz, kBoxBytes / esz,
@@ -862,12 +938,18 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
     a.b_tiles = (N + a.BN - 1) / a.BN;
     if (EPI == EPI_RESID) {  // L2 prefetch of the residual, one 128 x BN box per tile
       st = make_tmap_2d(&tmR, la.R, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)M, (uint64_t)N,
-                        (uint64_t)la.ldr * 2, (uint32_t)a.BN, kBM, false);
+                        (uint64_t)la.ldr * 2, (uint32_t)a.BN, kBM, 0);
+      if (st) return st;
+    }
+    if (RT) {  // the epilogue's 32-row x 16-channel residual blocks
+      st = make_tmap_2d(&tmRb, la.R, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)M, (uint64_t)N,
+                        (uint64_t)la.ldr * 2, 16, 32, 32);
       if (st) return st;
     }
   }
   const int stage_bytes = (kBM + a.BN) * kBoxBytes;
-  const int epi_bytes = (!CM && EPI != EPI_S32) ? kEpiStageBytes : 0;
+  const int epi_bytes =
+      (!CM && EPI != EPI_S32) ? (RT ? kEpiStageBytesRT : kEpiStageBytes) : 0;
   const int budget = 227 * 1024 - 1024 - epi_bytes - (int)sizeof(SmemCtl) - 64;
   a.stages = budget / stage_bytes;
   if (a.stages > 8) a.stages = 8;
@@ -903,14 +985,15 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return W8A8_ERR_CUDA;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<KIND, EPI, CM>,
+    if (cudaFuncSetAttribute(gemm_tc_kernel<KIND, EPI, CM, RT>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
       return W8A8_ERR_CUDA;
     attr_set[dev] = true;
   }
   const int units = tiles0 * a.ksplit;
   const int grid = units < ctx->sm_count ? units : ctx->sm_count;
-  launch_pdl(gemm_tc_kernel<KIND, EPI, CM>, dim3(grid), dim3(kThreads), smem, stream, tmA, tmB, tmR,
+  launch_pdl(gemm_tc_kernel<KIND, EPI, CM, RT>, dim3(grid), dim3(kThreads), smem, stream, tmA, tmB,
+             tmR, tmRb,
              a);
   return check_launch("gemm_tc");
 }
@@ -946,7 +1029,14 @@ static bool token_major_ok(const LinearArgs &a) {
 template <int EPI>
 static int launch_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,
                      cudaStream_t s) {
-  if (token_major_ok(a)) return launch_tc<0, EPI, false>(W, X, ldx, a, s);
+  if (token_major_ok(a)) {
+    // Residual GEMMs with short K (attn_proj): residual blocks by TMA into
+    // per-warp slots; the slots leave room for three pipeline stages, enough
+    // where the residual loads, not the operand loads, set the pace.
+    if (EPI == EPI_RESID && (a.K + kBoxBytes - 1) / kBoxBytes <= 16)
+      return launch_tc<0, EPI, false, EPI == EPI_RESID>(W, X, ldx, a, s);
+    return launch_tc<0, EPI, false>(W, X, ldx, a, s);
+  }
   // Decode: too few 128-channel tiles to occupy the GPU; split K over a
   // cluster and reduce in distributed shared memory.
   int st;

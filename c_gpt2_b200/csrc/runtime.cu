@@ -95,7 +95,7 @@ DeviceCtx *device_ctx(int *status) {
 
 int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, uint64_t rows,
                  uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows,
-                 bool swizzle128) {
+                 int swizzle_bytes) {
   if (!g_encode && resolve_encoder() != W8A8_OK) return W8A8_ERR_CUDA;
   if (!aligned16(base) || (row_pitch_bytes & 15u) || rows == 0 || cols == 0)
     return W8A8_ERR_INVALID;
@@ -105,7 +105,9 @@ int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, 
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? W8A8_OK : W8A8_ERR_INVALID;
 }

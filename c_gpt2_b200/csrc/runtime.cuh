@@ -24,11 +24,12 @@ DeviceCtx *device_ctx(int *status);
 // 2-D row-major tensor map: `rows` x `cols` elements, row pitch in bytes,
 // box of box_cols x box_rows, 128-byte swizzle, out-of-bounds reads as zero.
 // 2-D tensor map over a row-major matrix; boxes of box_rows x box_cols,
-// written to shared memory with the 128-byte swizzle unless swizzle128 is
-// false (maps used only for L2 prefetches).
+// written to shared memory with the 128-byte swizzle (the MMA operands), the
+// 32-byte swizzle (swizzle_bytes = 32: 16-byte halves of 32-byte rows swapped
+// on rows 4..7 of every 8) or none (0: maps used only for L2 prefetches).
 int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, uint64_t rows,
                  uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows,
-                 bool swizzle128 = true);
+                 int swizzle_bytes = 128);
 
 // Whether kernels are launched with programmatic stream serialization
 // (W8A8_PDL=0 in the environment turns it off).
