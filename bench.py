@@ -201,7 +201,10 @@ def kernel_rooflines(count: int, peaks: dict, dev) -> dict:
     512-token decode phase). Algorithmic bytes = K and V rows read + q + o.
 
     prefill INT8 GEMM: the MLP up-projection of GPT-2 large over this rank's
-    B x 512 prompt tokens (N = 5120, K = 1280), 2*M*N*K operations.
+    B x 512 prompt tokens (N = 5120, K = 1280), 2*M*N*K operations; and the
+    four prefill GEMMs of a layer together (W_qkv with the bias epilogue,
+    attn_proj and W2 with bias + residual, W1 with bias + GELU), each timed
+    alone, reported as their summed operations over their summed times.
     """
     import torch
     from c_gpt2_b200 import _lib, ops
@@ -231,6 +234,24 @@ def kernel_rooflines(count: int, peaks: dict, dev) -> dict:
     gms = time_kernel(lambda: ops.linear(xq, sx, W, sw, b, _lib.EPI_BIAS_GELU, out=y), 20, stream)
     tops = 2.0 * M * N * Kd / (gms * 1e-3) / 1e12
     int8_peak = 2.0 * peaks["bf16_tflops"]
+    del xq, W, y
+    # the other three prefill GEMMs of a layer, each with inputs beyond L2
+    per = {"w1": (round(gms, 4), 2.0 * M * N * Kd)}
+    for name, n_out, k_in, epi in (("w_qkv", 3 * d, d, _lib.EPI_BIAS),
+                                   ("attn_proj", d, d, _lib.EPI_BIAS_RESID),
+                                   ("w2", d, 4 * d, _lib.EPI_BIAS_RESID)):
+        x_ = torch.randint(-127, 128, (M, k_in), dtype=torch.int8, device=dev)
+        w_ = torch.randint(-127, 128, (n_out, k_in), dtype=torch.int8, device=dev)
+        sw_ = torch.rand((n_out,), device=dev) * 0.01 + 1e-3
+        b_ = (torch.randn((n_out,), device=dev) * 0.02).to(torch.bfloat16)
+        r_ = (torch.randn((M, n_out), device=dev).to(torch.bfloat16)
+              if epi == _lib.EPI_BIAS_RESID else None)
+        y_ = torch.empty((M, n_out), dtype=torch.bfloat16, device=dev)
+        t_ = time_kernel(lambda: ops.linear(x_, sx, w_, sw_, b_, epi, R=r_, out=y_), 20, stream)
+        per[name] = (round(t_, 4), 2.0 * M * n_out * k_in)
+        del x_, w_, r_, y_
+    all_ms = sum(t for t, _ in per.values())
+    all_tops = sum(o for _, o in per.values()) / (all_ms * 1e-3) / 1e12
     return {
         "attention": {"ms": ms, "bytes": attn_bytes, "gbs": attn_gbs, "seqs": B},
         "gemm": {"workload": f"W1 prefill GEMM M={M} N={N} K={Kd} (+dequant, bias, GELU)",
@@ -239,6 +260,12 @@ def kernel_rooflines(count: int, peaks: dict, dev) -> dict:
                  "peak_note": f"2 x {peaks['source']} bf16 dense (INT8 runs the tensor pipe "
                               "at twice the bf16 rate)",
                  "frac": round(tops / int8_peak, 4)},
+        "gemm_layer": {"workload": f"the four prefill GEMMs of one GPT-2 large layer at M={M} "
+                                   "(W_qkv bias, attn_proj bias+residual, W1 bias+GELU, "
+                                   "W2 bias+residual), each timed alone",
+                       "ms": round(all_ms, 4), "tops": round(all_tops, 1),
+                       "frac": round(all_tops / int8_peak, 4),
+                       "ms_per_gemm": {k: t for k, (t, _) in per.items()}},
     }
 
 
@@ -364,6 +391,7 @@ def main() -> None:
                          "algorithmic_bytes": int(roof["attention"]["bytes"]),
                          "peak_source": peaks["source"]},
             "gemm": roof["gemm"],
+            "gemm_layer": roof["gemm_layer"],
             "cpu_baseline": cpu,
             "clocks": clk,
             "gpu_launches": int(launches),
