@@ -68,6 +68,8 @@ SIGNATURES = {
                                          _p, _p, _sz, _p]),
     "w8a8_lm_head": (_i, [_p, _i64, _i, _i, _p, _i, _p, _i64, _p]),
     "w8a8_sample_greedy": (_i, [_p, _i64, _i, _i, _p, _p, _i64, _p, _p]),
+    "w8a8_sample_topk": (_i, [_p, _i64, _i, _i, _f, _i, _p, _i64, _p, _p, _p, _i64, _p, _p,
+                              _i64, _p]),
     "w8a8_advance_positions": (_i, [_p, _p, _i, _i, _p]),
     "w8a8_ref_embeddings": (_i, [_p, _p, _p, _p, _i, _i, _i, _p]),
     "w8a8_ref_add_bias": (_i, [_p, _i, _i, _p, _p]),
@@ -93,6 +95,8 @@ SIGNATURES = {
     "gpt2_engine_serve": (_i, [_p, _p, _i, _i]),
     "gpt2_engine_copy_logits": (_i, [_p, _p, _i]),
     "gpt2_engine_set_graphs": (_i, [_p, _i]),
+    "gpt2_engine_set_sampling": (_i, [_p, _f, _i]),
+    "gpt2_engine_set_draws": (_i, [_p, _i, _p, _i]),
     "gpt2_engine_launches_per_decode_step": (_i, [_p]),
     "gpt2_engine_launches_per_prefill": (_i, [_p]),
     "gpt2_engine_stream": (_p, [_p]),
@@ -131,7 +135,7 @@ class EngineConfig(C.Structure):
 
 class Request(C.Structure):
     """gpt2_request (include/gpt2_engine.h)."""
-    _fields_ = [("prompt", _p), ("T", _i), ("n_gen", _i), ("out", _p)]
+    _fields_ = [("prompt", _p), ("T", _i), ("n_gen", _i), ("out", _p), ("draws", _p)]
 
 
 class W8A8Error(RuntimeError):

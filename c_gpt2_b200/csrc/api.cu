@@ -380,6 +380,25 @@ extern "C" int w8a8_sample_greedy(const gpt2_bf16_t *logits, int64_t ldl, int M,
                               (cudaStream_t)stream);
 }
 
+extern "C" int w8a8_sample_topk(const gpt2_bf16_t *logits, int64_t ldl, int M, int V,
+                                float temperature, int top_k, const float *rnd,
+                                int64_t rnd_stride, const int32_t *rnd_pos, int32_t *out_tokens,
+                                int32_t *append_to, int64_t append_stride, int32_t *append_pos,
+                                gpt2_bf16_t *probs_out, int64_t ldp, void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!logits || !out_tokens || M < 0 || V <= 0 || ldl < V) return W8A8_ERR_INVALID;
+  if (append_to && !append_pos) return W8A8_ERR_INVALID;
+  if (!(temperature > 0.0f))  // gpt2.c:2212: greedy when the temperature is not positive
+    return w8a8_sample_greedy(logits, ldl, M, V, out_tokens, append_to, append_stride, append_pos,
+                              stream);
+  if (!rnd || rnd_stride < 0 || (probs_out && ldp < V)) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  return launch_topk_sample(logits, ldl, M, V, temperature, top_k, rnd, rnd_stride, rnd_pos,
+                            out_tokens, append_to, append_stride, append_pos, probs_out, ldp,
+                            (cudaStream_t)stream);
+}
+
 extern "C" int w8a8_advance_positions(int32_t *dst, const int32_t *src, int n, int delta,
                                       void *stream) {
   if (n == 0) return W8A8_OK;

@@ -132,5 +132,9 @@ int launch_greedy_sample(const uint16_t *logits, int64_t ldl, int M, int V, int3
                          int32_t *append_to, int64_t append_stride, int32_t *append_pos,
                          cudaStream_t s);
 int launch_advance(int32_t *dst, const int32_t *src, int n, int delta, cudaStream_t s);
+int launch_topk_sample(const uint16_t *logits, int64_t ldl, int M, int V, float temperature,
+                       int k, const float *rnd, int64_t rnd_stride, const int32_t *rnd_pos,
+                       int32_t *out, int32_t *append_to, int64_t append_stride,
+                       int32_t *append_pos, uint16_t *probs_out, int64_t ldp, cudaStream_t s);
 
 }  // namespace w8a8

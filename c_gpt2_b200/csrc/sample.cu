@@ -289,4 +289,250 @@ int launch_advance(int32_t *dst, const int32_t *src, int n, int delta, cudaStrea
   return check_launch("advance");
 }
 
+// ---- top-k sampling at a temperature (gpt2.c:130-180, gpt2.c:2223-2245) ----
+//
+// The reference, per generated token: probs = softmax_cuda(logits, T) in bf16
+// (cuda/softmax.cu:24-92); copies them to the host; sorts (probability, index)
+// pairs by descending probability with qsort; sums the first k probabilities
+// in that order in fp32; divides each of them by the sum into bf16 (or sets
+// every one to bf16(1/k) if the sum is 0); draws r = rand()/RAND_MAX; adds
+// the renormalised probabilities in order in fp32 and takes the first token
+// whose running sum exceeds r, else the k-th.
+//
+// One CTA per row does all of it on the GPU. The probabilities are non-negative
+// bf16 values at most 1.0, so their bit patterns 0 .. 0x3F80 order them: a
+// histogram over those 16257 keys replaces the sort. Every sum depends only on
+// the sequence of probability VALUES in sorted order, which ties do not change,
+// so the fp32 sums are the reference's to the bit; warp 0 walks the non-empty
+// keys from the top and adds each key's value once per token that has it.
+// Which of several equal-probability tokens comes first is what qsort leaves
+// unspecified; here it is the lowest index (also at the k-th place).
+constexpr int kTopkThreads = 256;
+constexpr int kTopkBins = 0x3F81;  // keys of +0.0 .. 1.0
+constexpr size_t kTopkHistBytes = ((size_t)kTopkBins * 4 + 15) / 16 * 16;
+constexpr int kTopkMaxVocab = 81920;
+
+__device__ __forceinline__ int topk_key(uint16_t p) { return p <= 0x3F80 ? (int)p : 0x3F80; }
+
+__global__ void __launch_bounds__(kTopkThreads)
+    topk_sample_kernel(const uint16_t *__restrict__ logits, int64_t ldl, int V, float inv_temp,
+                       int k, const float *__restrict__ rnd, int64_t rnd_stride,
+                       const int32_t *__restrict__ rnd_pos, int32_t *__restrict__ out,
+                       int32_t *__restrict__ append_to, int64_t append_stride,
+                       int32_t *__restrict__ append_pos, uint16_t *__restrict__ probs_out,
+                       int64_t ldp) {
+  extern __shared__ __align__(16) uint8_t tk_smem[];
+  uint32_t *hist = reinterpret_cast<uint32_t *>(tk_smem);                // [kTopkBins]
+  uint16_t *p16 = reinterpret_cast<uint16_t *>(tk_smem + kTopkHistBytes);  // [V]
+  __shared__ float s_red[kTopkThreads];
+  __shared__ uint32_t s_scan[kTopkThreads];
+  __shared__ int s_thr_key, s_take, s_sel_key, s_sel_rank, s_tok;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint16_t *x = logits + (int64_t)row * ldl;
+  for (int b = tid; b < kTopkBins; b += kTopkThreads) hist[b] = 0;
+  if (tid == 0) {
+    s_tok = 0;
+    s_thr_key = 0;
+    s_take = 1;
+  }
+
+  // 1. row maximum of x * (1/T)
+  float mx = -INFINITY;
+  for (int j = tid; j < V; j += kTopkThreads) mx = fmaxf(mx, bf2f(x[j]) * inv_temp);
+  s_red[tid] = mx;
+  __syncthreads();
+  for (int s = kTopkThreads / 2; s > 0; s >>= 1) {
+    if (tid < s) s_red[tid] = fmaxf(s_red[tid], s_red[tid + s]);
+    __syncthreads();
+  }
+  mx = s_red[0];
+  __syncthreads();
+  // 2. exponentials (kept as bf16, as the reference stores them) and the
+  //    256-slot sum tree of softmax.cu:62-82 (slot t adds j = t, t+256, ...)
+  float acc = 0.0f;
+  for (int j = tid; j < V; j += kTopkThreads) {
+    const float e = expf(__fmaf_rn(bf2f(x[j]), inv_temp, -mx));
+    p16[j] = f2bf(e);
+    acc += e;
+  }
+  s_red[tid] = acc;
+  __syncthreads();
+  for (int s = kTopkThreads / 2; s > 0; s >>= 1) {
+    if (tid < s) s_red[tid] += s_red[tid + s];
+    __syncthreads();
+  }
+  const float inv_sum = 1.0f / s_red[0];
+  // 3. bf16 probabilities and the histogram of their keys (each thread
+  //    rewrites only the entries it wrote in step 2)
+  for (int j0 = 0; j0 < V; j0 += kTopkThreads) {
+    const int j = j0 + tid;
+    int key = -1;
+    if (j < V) {
+      const uint16_t p = f2bf(bf2f(p16[j]) * inv_sum);
+      p16[j] = p;
+      if (probs_out) probs_out[(int64_t)row * ldp + j] = p;
+      key = topk_key(p);
+    }
+    const uint32_t peers = __match_any_sync(0xffffffffu, key);
+    if (key >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[key], (uint32_t)__popc(peers));
+  }
+  __syncthreads();
+
+  // 4. the k-th key from the top: thread t sums keys [64t, 64t+64); a scan
+  //    over the threads in descending key order gives the count above each
+  //    chunk, and the one chunk where the count reaches k is walked key by key
+  constexpr int kChunk = (kTopkBins + kTopkThreads - 1) / kTopkThreads;
+  const int c_lo = tid * kChunk, c_hi = min(kTopkBins, c_lo + kChunk);
+  uint32_t mine = 0;
+  for (int b = c_lo; b < c_hi; ++b) mine += hist[b];
+  s_scan[kTopkThreads - 1 - tid] = mine;
+  __syncthreads();
+  for (int off = 1; off < kTopkThreads; off <<= 1) {
+    const uint32_t v = s_scan[tid] + (tid >= off ? s_scan[tid - off] : 0u);
+    __syncthreads();
+    s_scan[tid] = v;
+    __syncthreads();
+  }
+  const uint32_t above = s_scan[kTopkThreads - 1 - tid] - mine;  // tokens in higher chunks
+  if (above < (uint32_t)k && above + mine >= (uint32_t)k) {
+    uint32_t cnt = above;
+    for (int b = c_hi - 1; b >= c_lo; --b) {
+      if (cnt + hist[b] >= (uint32_t)k) {
+        s_thr_key = b;
+        s_take = k - (int)cnt;
+        break;
+      }
+      cnt += hist[b];
+    }
+  }
+  __syncthreads();
+
+  // 5. warp 0: fp32 sum of the k probabilities in descending order, their
+  //    renormalised bf16 values, and the draw (lanes run in lock step and
+  //    hold the same values)
+  if (warp == 0) {
+    const int thr = s_thr_key, take = s_take;
+    float sum = 0.0f;
+    for (int b0 = kTopkBins - 1; b0 >= thr; b0 -= 32) {
+      const int b = b0 - lane;
+      const uint32_t h = b > thr ? hist[b] : (b == thr ? (uint32_t)take : 0u);
+      uint32_t nz = __ballot_sync(0xffffffffu, h != 0);
+      while (nz) {
+        const int l = __ffs(nz) - 1;  // lowest lane = highest key
+        nz &= nz - 1;
+        const uint32_t n = __shfl_sync(0xffffffffu, h, l);
+        const float pv = bf2f((uint16_t)(b0 - l));
+        for (uint32_t i = 0; i < n; ++i) {
+          const float ns = sum + pv;
+          if (ns == sum) break;  // adding pv again changes nothing
+          sum = ns;
+        }
+      }
+    }
+    const bool uniform = !(sum > 0.0f);
+    const float q_uniform = bf2f(f2bf(__fdiv_rn(1.0f, (float)k)));
+    const float r = rnd[(int64_t)row * rnd_stride + (rnd_pos ? rnd_pos[row] : 0)];
+    int sel_key = thr, sel_rank = take - 1;  // no running sum above r: the k-th token
+    float cum = 0.0f;
+    bool done = false;
+    for (int b0 = kTopkBins - 1; b0 >= thr && !done; b0 -= 32) {
+      const int b = b0 - lane;
+      const uint32_t h = b > thr ? hist[b] : (b == thr ? (uint32_t)take : 0u);
+      uint32_t nz = __ballot_sync(0xffffffffu, h != 0);
+      while (nz && !done) {
+        const int l = __ffs(nz) - 1;
+        nz &= nz - 1;
+        const uint32_t n = __shfl_sync(0xffffffffu, h, l);
+        const float q = uniform ? q_uniform : bf2f(f2bf(__fdiv_rn(bf2f((uint16_t)(b0 - l)), sum)));
+        for (uint32_t i = 0; i < n; ++i) {
+          const float nc = cum + q;
+          if (r < nc) {
+            sel_key = b0 - l;
+            sel_rank = (int)i;
+            done = true;
+            break;
+          }
+          // Later terms are no larger than q, so a running sum that q no
+          // longer moves stays at or below r: the k-th token is taken.
+          if (nc == cum) {
+            done = true;
+            break;
+          }
+          cum = nc;
+        }
+      }
+    }
+    if (lane == 0) {
+      s_sel_key = sel_key;
+      s_sel_rank = sel_rank;
+    }
+  }
+  __syncthreads();
+
+  // 6. the token: the sel_rank-th (from 0) index, in ascending order, whose
+  //    key is sel_key; thread t counts over its contiguous share of the row
+  const int sel_key = s_sel_key, sel_rank = s_sel_rank;
+  const int per = (V + kTopkThreads - 1) / kTopkThreads;
+  const int j_lo = min(V, tid * per), j_hi = min(V, j_lo + per);
+  uint32_t cnt = 0;
+  for (int j = j_lo; j < j_hi; ++j) cnt += topk_key(p16[j]) == sel_key;
+  s_scan[tid] = cnt;
+  __syncthreads();
+  for (int off = 1; off < kTopkThreads; off <<= 1) {
+    const uint32_t v = s_scan[tid] + (tid >= off ? s_scan[tid - off] : 0u);
+    __syncthreads();
+    s_scan[tid] = v;
+    __syncthreads();
+  }
+  const uint32_t before = s_scan[tid] - cnt;
+  if (before <= (uint32_t)sel_rank && (uint32_t)sel_rank < before + cnt) {
+    uint32_t c = before;
+    for (int j = j_lo; j < j_hi; ++j) {
+      if (topk_key(p16[j]) == sel_key) {
+        if (c == (uint32_t)sel_rank) {
+          s_tok = j;
+          break;
+        }
+        ++c;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const int tok = s_tok;
+    out[row] = tok;
+    if (append_to) {
+      const int p = append_pos[row];
+      append_to[(int64_t)row * append_stride + p] = tok;
+      append_pos[row] = p + 1;
+    }
+  }
+}
+
+int launch_topk_sample(const uint16_t *logits, int64_t ldl, int M, int V, float temperature,
+                       int k, const float *rnd, int64_t rnd_stride, const int32_t *rnd_pos,
+                       int32_t *out, int32_t *append_to, int64_t append_stride,
+                       int32_t *append_pos, uint16_t *probs_out, int64_t ldp, cudaStream_t s) {
+  if (V > kTopkMaxVocab) return W8A8_ERR_UNSUPPORTED;
+  const size_t smem = kTopkHistBytes + ((size_t)V * 2 + 15) / 16 * 16;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(topk_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(kTopkHistBytes + (size_t)kTopkMaxVocab * 2)) != cudaSuccess)
+      return W8A8_ERR_CUDA;
+    attr_set[dev] = true;
+  }
+  if (k < 1) k = 1;  // gpt2.c:1963-1968 clamps top_k to [1, vocab]
+  if (k > V) k = V;
+  const float inv_temp = 1.0f / temperature;  // IEEE division, as softmax.cu:32 on the device
+  launch_pdl(topk_sample_kernel, dim3(M), dim3(kTopkThreads), smem, s, logits, ldl, V, inv_temp,
+             k, rnd, rnd_stride, rnd_pos, out, append_to, append_stride, append_pos, probs_out,
+             ldp);
+  return check_launch("topk_sample");
+}
+
 }  // namespace w8a8

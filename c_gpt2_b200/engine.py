@@ -93,15 +93,22 @@ class Engine:
         self._check(core().gpt2_engine_decode_steps(self._h, steps), "gpt2_engine_decode_steps")
 
     # -- continuous batching ------------------------------------------------
-    def serve(self, requests: list[tuple[np.ndarray, int]], slots: int) -> list[np.ndarray]:
-        """Serve (prompt ids, n_gen) requests over `slots` decode slots, admitted
-        in order as slots free up (gpt2_engine_serve). Returns each request's
-        generated ids."""
-        prompts = [np.ascontiguousarray(p, dtype=np.int32) for p, _ in requests]
-        outs = [np.zeros((n,), dtype=np.int32) for _, n in requests]
+    def serve(self, requests: list[tuple], slots: int) -> list[np.ndarray]:
+        """Serve (prompt ids, n_gen) or (prompt ids, n_gen, draws) requests over
+        `slots` decode slots, admitted in order as slots free up
+        (gpt2_engine_serve); draws (n_gen floats in [0, 1]) are used when top-k
+        sampling is on. Returns each request's generated ids."""
+        prompts = [np.ascontiguousarray(r[0], dtype=np.int32) for r in requests]
+        outs = [np.zeros((r[1],), dtype=np.int32) for r in requests]
+        draws = [np.ascontiguousarray(r[2], dtype=np.float32) if len(r) > 2 else None
+                 for r in requests]
+        for r, dr in zip(requests, draws):
+            if dr is not None and dr.size != r[1]:
+                raise ValueError("a request's draws must number its n_gen")
         reqs = (Request * len(requests))()
-        for i, ((_, n), p, o) in enumerate(zip(requests, prompts, outs)):
-            reqs[i] = Request(p.ctypes.data, p.size, n, o.ctypes.data)
+        for i, (r, p, o, dr) in enumerate(zip(requests, prompts, outs, draws)):
+            reqs[i] = Request(p.ctypes.data, p.size, r[1], o.ctypes.data,
+                              dr.ctypes.data if dr is not None else None)
         self._check(core().gpt2_engine_serve(self._h, reqs, len(requests), slots),
                     "gpt2_engine_serve")
         return outs
@@ -133,6 +140,17 @@ class Engine:
         self._check(core().gpt2_engine_copy_logits(self._h, raw.ctypes.data, rows),
                     "gpt2_engine_copy_logits")
         return (raw.astype(np.uint32) << 16).view(np.float32)
+
+    def set_sampling(self, temperature: float, top_k: int = 40) -> None:
+        """temperature <= 0: greedy (default); else top-k sampling at that temperature."""
+        self._check(core().gpt2_engine_set_sampling(self._h, float(temperature), int(top_k)),
+                    "gpt2_engine_set_sampling")
+
+    def set_draws(self, slot: int, draws) -> None:
+        """Slot `slot`'s draws in [0, 1], one per token from its first on."""
+        d = np.ascontiguousarray(draws, dtype=np.float32)
+        self._check(core().gpt2_engine_set_draws(self._h, slot, d.ctypes.data if d.size else None,
+                                                 d.size), "gpt2_engine_set_draws")
 
     def set_graphs(self, enable: bool) -> None:
         self._check(core().gpt2_engine_set_graphs(self._h, 1 if enable else 0),

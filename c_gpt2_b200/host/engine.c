@@ -64,6 +64,11 @@ struct gpt2_engine {
    * sequence whose tokens are wanted (else it is parked and its steps are
    * discarded) */
   int *slot_len, *slot_gen, *slot_active;
+  /* sampling: temperature <= 0 greedy, else top-k at that temperature with
+   * the draws of slot b in rnd[b*ctx ...], indexed by the slot's output count */
+  float temperature;
+  int top_k;
+  float *rnd;
   /* decode graph */
   int use_graphs;
   cudaGraphExec_t graph;
@@ -208,7 +213,7 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   /* activations */
   e->attn_ws_bytes = w8a8_attention_decode_workspace_size((int)Bm, cfg->n_head, (int)C);
   e->lin_ws_bytes = w8a8_linear_workspace_size((int)Bm, 4 * (int)d);
-  size_t off = 0, sizes[14];
+  size_t off = 0, sizes[15];
   sizes[0] = Mt * d * 2;        /* H */
   sizes[1] = Mt * d * 2;        /* R1 */
   sizes[2] = Mt * d * 2;        /* Q */
@@ -223,8 +228,9 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   sizes[11] = Bm * 4 * (size_t)C; /* default output buffer */
   sizes[12] = e->attn_ws_bytes;
   sizes[13] = e->lin_ws_bytes;
-  size_t offs[14];
-  for (int i = 0; i < 14; ++i) {
+  sizes[14] = Bm * C * 4;       /* sampling draws [max_batch][ctx] */
+  size_t offs[15];
+  for (int i = 0; i < 15; ++i) {
     offs[i] = off;
     off += ALIGN_UP(sizes[i], 256);
   }
@@ -250,6 +256,8 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   e->out_default = (int32_t *)(a + offs[11]);
   e->attn_ws = a + offs[12];
   e->lin_ws = a + offs[13];
+  e->rnd = (float *)(a + offs[14]);
+  e->top_k = 40;
   if (cudaMemset(e->ablob, 0, off) != cudaSuccess) {
     gpt2_engine_destroy(e);
     return W8A8_ERR_CUDA;
@@ -452,9 +460,17 @@ static int model_forward(gpt2_engine *e, const int32_t *tokens_d, int slot0, int
   W8_TRY(e, w8a8_layernorm_quant(e->H + (int64_t)(T - 1) * d, (int64_t)T * d, B, d, e->lnf_g,
                                  e->lnf_b, eps, e->Xf, d, NULL, NULL, s));
   W8_TRY(e, w8a8_lm_head(e->Xf, d, B, d, e->wte, c->vocab, e->logits, c->vocab, s));
-  W8_TRY(e, w8a8_sample_greedy(e->logits, c->vocab, B, c->vocab, e->next + slot0,
-                               e->out + (int64_t)slot0 * e->out_stride, e->out_stride,
-                               e->gen + slot0, s));
+  /* gpt2.c:2176-2245: greedy at temperature <= 0, else top-k sampling; the
+   * draw of a slot's i-th token is rnd[slot][i] (i = its output count) */
+  if (e->temperature > 0.0f)
+    W8_TRY(e, w8a8_sample_topk(e->logits, c->vocab, B, c->vocab, e->temperature, e->top_k,
+                               e->rnd + (int64_t)slot0 * c->ctx, c->ctx, e->gen + slot0,
+                               e->next + slot0, e->out + (int64_t)slot0 * e->out_stride,
+                               e->out_stride, e->gen + slot0, NULL, 0, s));
+  else
+    W8_TRY(e, w8a8_sample_greedy(e->logits, c->vocab, B, c->vocab, e->next + slot0,
+                                 e->out + (int64_t)slot0 * e->out_stride, e->out_stride,
+                                 e->gen + slot0, s));
   return W8A8_OK;
 }
 
@@ -713,6 +729,15 @@ int gpt2_engine_serve(gpt2_engine *e, gpt2_request *reqs, int n_req, int slots) 
         st = fail(e, W8A8_ERR_CUDA, "serve: prompt copy");
         break;
       }
+      /* the request's draws (zeros if it brings none) into the slot's row */
+      if (e->temperature > 0.0f) {
+        st = r->draws ? gpt2_engine_set_draws(e, b, r->draws, r->n_gen)
+                      : (cudaMemsetAsync(e->rnd + (int64_t)b * c->ctx, 0, (size_t)c->ctx * 4,
+                                         e->stream) == cudaSuccess ? W8A8_OK
+                                                                    : fail(e, W8A8_ERR_CUDA,
+                                                                           "serve: draws"));
+        if (st) break;
+      }
       /* tokens_in is reused by the next admission only after this prefill
        * (one stream) */
       st = gpt2_engine_slot_prefill(e, b, e->tokens_in, r->T);
@@ -749,6 +774,29 @@ int gpt2_engine_copy_logits(gpt2_engine *e, gpt2_bf16_t *host, int rows) {
   CUDA_TRY(e, cudaMemcpyAsync(host, e->logits, (size_t)rows * e->cfg.vocab * 2,
                               cudaMemcpyDeviceToHost, e->stream));
   CUDA_TRY(e, cudaStreamSynchronize(e->stream));
+  return W8A8_OK;
+}
+
+int gpt2_engine_set_sampling(gpt2_engine *e, float temperature, int top_k) {
+  if (!e) return W8A8_ERR_INVALID;
+  if (temperature != temperature) return fail(e, W8A8_ERR_INVALID, "temperature is NaN");
+  e->temperature = temperature;
+  e->top_k = top_k;
+  /* the captured decode step holds the sampler and its arguments */
+  if (e->graph) {
+    cudaGraphExecDestroy(e->graph);
+    e->graph = NULL;
+  }
+  return W8A8_OK;
+}
+
+int gpt2_engine_set_draws(gpt2_engine *e, int slot, const float *draws, int n) {
+  if (!e || slot < 0 || slot >= e->cfg.max_batch || n < 0 || n > e->cfg.ctx || (n > 0 && !draws))
+    return W8A8_ERR_INVALID;
+  if (n == 0) return W8A8_OK;
+  /* stream-ordered: steps already queued read the slot's previous draws */
+  CUDA_TRY(e, cudaMemcpyAsync(e->rnd + (int64_t)slot * e->cfg.ctx, draws, (size_t)n * 4,
+                              cudaMemcpyHostToDevice, e->stream));
   return W8A8_OK;
 }
 

@@ -264,6 +264,20 @@ def sample_greedy(logits):
     return out
 
 
+def sample_topk(logits, temperature, top_k, rnd, probs_out=None):
+    """Top-k sampling at a temperature, one draw per row (``rnd`` float32 [M]
+    on the device, each in [0, 1]); ``probs_out`` optionally receives the bf16
+    probabilities. A temperature <= 0 gives the greedy token."""
+    M, V = logits.shape
+    out = torch.empty((M,), dtype=torch.int32, device=logits.device)
+    check(core().w8a8_sample_topk(_ptr(logits), logits.stride(0), M, V, float(temperature),
+                                  int(top_k), _ptr(rnd), 1, None, _ptr(out), None, 0, None,
+                                  _ptr(probs_out) if probs_out is not None else None,
+                                  probs_out.stride(0) if probs_out is not None else 0,
+                                  _stream()), "w8a8_sample_topk")
+    return out
+
+
 # ---- reference-shaped element-wise operations (in place where the reference is) ----
 
 def ref_softmax(a, rows, cols, stride, out, temperature=1.0, causal=0):

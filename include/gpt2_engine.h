@@ -6,7 +6,7 @@
  * kernels of gpt2_w8a8.h: it loads the reference's quant8.bin weight file,
  * keeps W_qkv packed, holds one reference-layout KV cache ([L][ctx][d] bf16)
  * per resident sequence, runs prefill for a batch of equal-length prompts,
- * then greedy decode with one CUDA graph per decode step. Sequences are
+ * then greedy (or top-k sampled) decode with one CUDA graph per decode step. Sequences are
  * independent: each sequence's tokens are those it would produce alone.
  *
  * Device memory is allocated once in gpt2_engine_create / load (the
@@ -69,7 +69,7 @@ int gpt2_engine_generate_device(gpt2_engine *e, const int32_t *prompts_d, int B,
  * prompt ids must lie in [0, vocab) (not checked);
  * prefill resets the batch, fills the KV caches and writes the first token
  * of each sequence to out_tokens_d[b*out_stride]; decode_steps runs `steps`
- * further greedy steps, appending tokens after those already produced. */
+ * further steps, appending tokens after those already produced. */
 int gpt2_engine_prefill(gpt2_engine *e, const int32_t *prompts_d, int B, int T,
                         int32_t *out_tokens_d, int out_stride);
 int gpt2_engine_decode_steps(gpt2_engine *e, int steps);
@@ -100,12 +100,24 @@ typedef struct {
   const int32_t *prompt;
   int T;
   int n_gen;
-  int32_t *out;  /* host, n_gen ids */
+  int32_t *out;        /* host, n_gen ids */
+  const float *draws;  /* host, n_gen draws for top-k sampling (NULL: all 0) */
 } gpt2_request;
 /* Serve n_req requests over `slots` slots (continuous batching): requests
  * are admitted in order as slots free up; each gets the tokens it would get
  * alone at this slot count. Checks every id; synchronous. */
 int gpt2_engine_serve(gpt2_engine *e, gpt2_request *reqs, int n_req, int slots);
+
+/* Sampling of every following prefill and decode step (gpt2.c:2176-2245).
+ * temperature <= 0 (the default): greedy. Otherwise top-k sampling at that
+ * temperature (w8a8_sample_topk; top_k clamped to [1, vocab], default 40):
+ * slot b's i-th token (i from 0; the prefill writes i = 0) is drawn with the
+ * i-th value set by gpt2_engine_set_draws for slot b (0 where none was set).
+ * The reference draws (float)rand() / RAND_MAX for each token (gpt2.c:2231). */
+int gpt2_engine_set_sampling(gpt2_engine *e, float temperature, int top_k);
+/* draws[0..n) (host memory, n <= ctx) become slot `slot`'s draws from its
+ * first token on; ordered on the engine stream after the work queued so far. */
+int gpt2_engine_set_draws(gpt2_engine *e, int slot, const float *draws, int n);
 
 /* Copy the logits of the last step ([B, vocab] bf16) to host memory. */
 int gpt2_engine_copy_logits(gpt2_engine *e, gpt2_bf16_t *host, int rows);

@@ -200,6 +200,26 @@ int w8a8_sample_greedy(const gpt2_bf16_t *logits, int64_t ldl, int M, int V,
                        int32_t *out_tokens, int32_t *append_to, int64_t append_stride,
                        int32_t *append_pos, void *stream);
 
+/* ---- top-k sampling at a temperature (gpt2.c:130-180 top_k_sample,
+ * gpt2.c:2223-2245 the draw) ----
+ * Per row m: probs = softmax(logits / temperature) in the reference's bf16
+ * rounding order (softmax.cu:24-92); the top_k largest probabilities (top_k
+ * clamped to [1, V] as gpt2.c:1963-1968 clamps it), summed in fp32 in
+ * descending order and each divided by that sum into bf16 (all bf16(1/top_k)
+ * if the sum is 0); r = rnd[m*rnd_stride + (rnd_pos ? rnd_pos[m] : 0)], the
+ * caller's draw in [0, 1] ((float)rand() / RAND_MAX in the reference); the
+ * token is the first of the sorted top_k whose fp32 running sum exceeds r,
+ * else the top_k-th. Among equal probabilities the lower index sorts first
+ * (the reference's qsort leaves that order unspecified). A temperature that
+ * is not positive gives the greedy token (w8a8_sample_greedy; rnd unused).
+ * probs_out (optional, [M, ldp]) receives the bf16 probabilities. Appends to
+ * append_to / append_pos as w8a8_sample_greedy does. V <= 81920, else
+ * W8A8_ERR_UNSUPPORTED. */
+int w8a8_sample_topk(const gpt2_bf16_t *logits, int64_t ldl, int M, int V, float temperature,
+                     int top_k, const float *rnd, int64_t rnd_stride, const int32_t *rnd_pos,
+                     int32_t *out_tokens, int32_t *append_to, int64_t append_stride,
+                     int32_t *append_pos, gpt2_bf16_t *probs_out, int64_t ldp, void *stream);
+
 /* dst[i] = src[i] + delta for i < n (device arrays; dst may equal src). */
 int w8a8_advance_positions(int32_t *dst, const int32_t *src, int n, int delta, void *stream);
 

@@ -35,6 +35,9 @@ def lib() -> C.CDLL:
         l.orc_lm_head.argtypes = [p, i, p, i, p]
         l.orc_greedy.argtypes = [p, i]
         l.orc_greedy.restype = i
+        l.orc_top_k.argtypes = [p, i, i, p, p]
+        l.orc_sample_topk.argtypes = [p, i, i, f]
+        l.orc_sample_topk.restype = i
         l.orc_generate.argtypes = [p, sz, i, i, i, i, i, p, i, i, p, p]
         l.orc_generate.restype = i
         _lib = l
@@ -124,6 +127,23 @@ def lm_head(xf, wte) -> np.ndarray:
 def greedy(logits) -> int:
     x = _c(logits, np.uint16)
     return int(lib().orc_greedy(x.ctypes.data, x.size))
+
+
+def top_k(probs, k):
+    """gpt2.c:130-180: (indices [k], renormalised bf16 probabilities [k]) of one
+    row of bf16 probabilities; equal probabilities in ascending index order."""
+    p = _c(probs, np.uint16)
+    kk = min(max(int(k), 1), p.size)
+    idx = np.empty((kk,), np.int32)
+    q = np.empty((kk,), np.uint16)
+    lib().orc_top_k(p.ctypes.data, p.size, int(k), idx.ctypes.data, q.ctypes.data)
+    return idx, q
+
+
+def sample_topk(probs, k, r) -> int:
+    """gpt2.c:2223-2245: the token drawn with r in [0, 1] from one row of bf16 probabilities."""
+    p = _c(probs, np.uint16)
+    return int(lib().orc_sample_topk(p.ctypes.data, p.size, int(k), float(r)))
 
 
 def generate(image: bytes, dims, prompt, n_gen: int):

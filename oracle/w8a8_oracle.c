@@ -257,6 +257,68 @@ int orc_greedy(const uint16_t *logits, int V) {
   return tok;
 }
 
+/* ---- top-k sampling: gpt2.c:130-180 (top_k_sample) and the draw of
+ * gpt2.c:2223-2245. (probability, index) pairs sorted by descending
+ * probability; the reference's qsort (compareTokenProbs, gpt2.c:102-113)
+ * leaves the order of equal probabilities unspecified, this sort puts the
+ * lower index first. k is clamped to [1, V] as gpt2.c:1963-1968 does. ---- */
+typedef struct {
+  float prob;
+  int index;
+} orc_tokprob;
+
+static int cmp_tokprob(const void *a, const void *b) {
+  const orc_tokprob *x = (const orc_tokprob *)a, *y = (const orc_tokprob *)b;
+  if (x->prob < y->prob) return 1;
+  if (x->prob > y->prob) return -1;
+  return (x->index > y->index) - (x->index < y->index);
+}
+
+/* idx[k], q[k] (bf16): the top k tokens and their renormalised probabilities */
+void orc_top_k(const uint16_t *probs, int V, int k, int *idx, uint16_t *q) {
+  if (k < 1) k = 1;
+  if (k > V) k = V;
+  orc_tokprob *t = (orc_tokprob *)malloc((size_t)V * sizeof(orc_tokprob));
+  for (int i = 0; i < V; ++i) {
+    t[i].prob = orc_bf2f(probs[i]);
+    t[i].index = i;
+  }
+  qsort(t, (size_t)V, sizeof(orc_tokprob), cmp_tokprob);
+  float sum = 0.0f;
+  for (int i = 0; i < k; ++i) {
+    idx[i] = t[i].index;
+    q[i] = orc_f2bf(t[i].prob);
+    sum += t[i].prob;
+  }
+  if (sum > 0.0f) {
+    for (int i = 0; i < k; ++i) q[i] = orc_f2bf(orc_bf2f(q[i]) / sum);
+  } else {
+    for (int i = 0; i < k; ++i) q[i] = orc_f2bf(1.0f / (float)k);
+  }
+  free(t);
+}
+
+/* the token drawn with r from the bf16 probabilities of one row */
+int orc_sample_topk(const uint16_t *probs, int V, int k, float r) {
+  if (k < 1) k = 1;
+  if (k > V) k = V;
+  int *idx = (int *)malloc((size_t)k * sizeof(int));
+  uint16_t *q = (uint16_t *)malloc((size_t)k * 2);
+  orc_top_k(probs, V, k, idx, q);
+  int tok = idx[k - 1];
+  float cum = 0.0f;
+  for (int i = 0; i < k; ++i) {
+    cum += orc_bf2f(q[i]);
+    if (r < cum) {
+      tok = idx[i];
+      break;
+    }
+  }
+  free(idx);
+  free(q);
+  return tok;
+}
+
 /* ---------------------------------------------------------------------------
  * Whole-model greedy generation from a quant8 image (one sequence), following
  * the INT8 GPU forward of gpt2.c:1124-1330 and the token loop 2094-2247.

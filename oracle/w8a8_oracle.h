@@ -26,6 +26,8 @@ void orc_attention(const uint16_t *Q, const uint16_t *K, const uint16_t *V, int 
                    int n_head, uint16_t *O);
 void orc_lm_head(const uint16_t *xf, int d, const uint16_t *wte, int V, uint16_t *logits);
 int orc_greedy(const uint16_t *logits, int V);
+void orc_top_k(const uint16_t *probs, int V, int k, int *idx, uint16_t *q);
+int orc_sample_topk(const uint16_t *probs, int V, int k, float r);
 int orc_generate(const uint8_t *image, size_t bytes, int d, int L, int H, int vocab, int ctx,
                  const int32_t *prompt, int T, int n_gen, int32_t *out, uint16_t *last_logits);
 
