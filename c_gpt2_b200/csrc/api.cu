@@ -391,7 +391,8 @@ extern "C" int w8a8_sample_topk(const gpt2_bf16_t *logits, int64_t ldl, int M, i
   if (!(temperature > 0.0f))  // gpt2.c:2212: greedy when the temperature is not positive
     return w8a8_sample_greedy(logits, ldl, M, V, out_tokens, append_to, append_stride, append_pos,
                               stream);
-  if (!rnd || rnd_stride < 0 || (probs_out && ldp < V)) return W8A8_ERR_INVALID;
+  if (!rnd || rnd_stride < 0 || (probs_out && ldp < V) || ((uintptr_t)logits & 1))
+    return W8A8_ERR_INVALID;
   int st = ready();
   if (st) return st;
   return launch_topk_sample(logits, ldl, M, V, temperature, top_k, rnd, rnd_stride, rnd_pos,

@@ -322,25 +322,43 @@ __global__ void __launch_bounds__(kTopkThreads)
                        int32_t *__restrict__ append_pos, uint16_t *__restrict__ probs_out,
                        int64_t ldp) {
   extern __shared__ __align__(16) uint8_t tk_smem[];
-  uint32_t *hist = reinterpret_cast<uint32_t *>(tk_smem);                // [kTopkBins]
-  uint16_t *p16 = reinterpret_cast<uint16_t *>(tk_smem + kTopkHistBytes);  // [V]
+  uint32_t *hist = reinterpret_cast<uint32_t *>(tk_smem);  // [kTopkBins]
   __shared__ float s_red[kTopkThreads];
   __shared__ uint32_t s_scan[kTopkThreads];
-  __shared__ int s_thr_key, s_take, s_sel_key, s_sel_rank, s_tok;
+  __shared__ int s_thr_key, s_take, s_top_key, s_sel_key, s_sel_rank, s_tok, s_first;
   pdl_wait();
   pdl_launch_dependents();
   const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint16_t *x = logits + (int64_t)row * ldl;
+  // The row (logits, then exponentials, then probabilities) in shared memory
+  // at the same position modulo 16 bytes as in global memory (rows start on
+  // 2-byte boundaries), so that the copy moves aligned 16-byte vectors.
+  const int shift = (int)(((uintptr_t)x & 15) >> 1);
+  uint16_t *p16 = reinterpret_cast<uint16_t *>(tk_smem + kTopkHistBytes) + shift;  // [V]
   for (int b = tid; b < kTopkBins; b += kTopkThreads) hist[b] = 0;
   if (tid == 0) {
     s_tok = 0;
     s_thr_key = 0;
     s_take = 1;
+    s_top_key = 0;
+    s_first = 0x7fffffff;
   }
+  {
+    const int head = min(V, (8 - shift) & 7);  // elements before the first 16-byte boundary
+    const int nvec = (V - head) >> 3;
+    for (int j = tid; j < head; j += kTopkThreads) p16[j] = x[j];
+    const uint4 *xv = reinterpret_cast<const uint4 *>(x + head);
+    uint4 *sv = reinterpret_cast<uint4 *>(p16 + head);
+#pragma unroll 4
+    for (int i = tid; i < nvec; i += kTopkThreads) sv[i] = __ldg(xv + i);
+    for (int j = head + nvec * 8 + tid; j < V; j += kTopkThreads) p16[j] = x[j];
+  }
+  __syncthreads();
 
   // 1. row maximum of x * (1/T)
   float mx = -INFINITY;
-  for (int j = tid; j < V; j += kTopkThreads) mx = fmaxf(mx, bf2f(x[j]) * inv_temp);
+#pragma unroll 4
+  for (int j = tid; j < V; j += kTopkThreads) mx = fmaxf(mx, bf2f(p16[j]) * inv_temp);
   s_red[tid] = mx;
   __syncthreads();
   for (int s = kTopkThreads / 2; s > 0; s >>= 1) {
@@ -352,8 +370,9 @@ __global__ void __launch_bounds__(kTopkThreads)
   // 2. exponentials (kept as bf16, as the reference stores them) and the
   //    256-slot sum tree of softmax.cu:62-82 (slot t adds j = t, t+256, ...)
   float acc = 0.0f;
+#pragma unroll 4
   for (int j = tid; j < V; j += kTopkThreads) {
-    const float e = expf(__fmaf_rn(bf2f(x[j]), inv_temp, -mx));
+    const float e = expf(__fmaf_rn(bf2f(p16[j]), inv_temp, -mx));
     p16[j] = f2bf(e);
     acc += e;
   }
@@ -365,19 +384,22 @@ __global__ void __launch_bounds__(kTopkThreads)
   }
   const float inv_sum = 1.0f / s_red[0];
   // 3. bf16 probabilities and the histogram of their keys (each thread
-  //    rewrites only the entries it wrote in step 2)
-  for (int j0 = 0; j0 < V; j0 += kTopkThreads) {
-    const int j = j0 + tid;
-    int key = -1;
-    if (j < V) {
-      const uint16_t p = f2bf(bf2f(p16[j]) * inv_sum);
-      p16[j] = p;
-      if (probs_out) probs_out[(int64_t)row * ldp + j] = p;
-      key = topk_key(p);
-    }
-    const uint32_t peers = __match_any_sync(0xffffffffu, key);
-    if (key >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[key], (uint32_t)__popc(peers));
+  //    rewrites only the entries it wrote in step 2; lanes of a warp mostly
+  //    hold different keys, and those that share one are serialised by the
+  //    shared-memory atomic); s_top_key: the largest key present
+  int top_key = 0;
+#pragma unroll 4
+  for (int j = tid; j < V; j += kTopkThreads) {
+    const uint16_t p = f2bf(bf2f(p16[j]) * inv_sum);
+    p16[j] = p;
+    if (probs_out) probs_out[(int64_t)row * ldp + j] = p;
+    const int key = topk_key(p);
+    atomicAdd(&hist[key], 1u);
+    top_key = max(top_key, key);
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) top_key = max(top_key, __shfl_xor_sync(0xffffffffu, top_key, o));
+  if (lane == 0) atomicMax(&s_top_key, top_key);
   __syncthreads();
 
   // 4. the k-th key from the top: thread t sums keys [64t, 64t+64); a scan
@@ -385,8 +407,17 @@ __global__ void __launch_bounds__(kTopkThreads)
   //    chunk, and the one chunk where the count reaches k is walked key by key
   constexpr int kChunk = (kTopkBins + kTopkThreads - 1) / kTopkThreads;
   const int c_lo = tid * kChunk, c_hi = min(kTopkBins, c_lo + kChunk);
+  // (each lane starts at its own offset in its chunk: chunks are 64 words
+  // apart, so lanes reading the same offset would all hit one bank)
   uint32_t mine = 0;
-  for (int b = c_lo; b < c_hi; ++b) mine += hist[b];
+  const int c_n = max(0, c_hi - c_lo);
+  if (c_n > 0) {
+    const int o = lane % c_n;
+    for (int i = 0; i < c_n; ++i) {
+      const int b = i + o < c_n ? i + o : i + o - c_n;
+      mine += hist[c_lo + b];
+    }
+  }
   s_scan[kTopkThreads - 1 - tid] = mine;
   __syncthreads();
   for (int off = 1; off < kTopkThreads; off <<= 1) {
@@ -410,12 +441,13 @@ __global__ void __launch_bounds__(kTopkThreads)
   __syncthreads();
 
   // 5. warp 0: fp32 sum of the k probabilities in descending order, their
-  //    renormalised bf16 values, and the draw (lanes run in lock step and
-  //    hold the same values)
+  //    renormalised bf16 values, and the draw. Lanes hold 32 keys at a time
+  //    (lane l: key b0 - l), from the largest present key down, and run the
+  //    additions in lock step with the same values.
   if (warp == 0) {
-    const int thr = s_thr_key, take = s_take;
+    const int thr = s_thr_key, take = s_take, top = max(s_top_key, thr);
     float sum = 0.0f;
-    for (int b0 = kTopkBins - 1; b0 >= thr; b0 -= 32) {
+    for (int b0 = top; b0 >= thr; b0 -= 32) {
       const int b = b0 - lane;
       const uint32_t h = b > thr ? hist[b] : (b == thr ? (uint32_t)take : 0u);
       uint32_t nz = __ballot_sync(0xffffffffu, h != 0);
@@ -424,9 +456,20 @@ __global__ void __launch_bounds__(kTopkThreads)
         nz &= nz - 1;
         const uint32_t n = __shfl_sync(0xffffffffu, h, l);
         const float pv = bf2f((uint16_t)(b0 - l));
-        for (uint32_t i = 0; i < n; ++i) {
+        // sum += pv, n times, in order; once an addition leaves the sum
+        // unchanged every later one of pv does too
+        uint32_t i = 0;
+        for (; i + 4 <= n; i += 4) {
+          const float a1 = sum + pv, a2 = a1 + pv, a3 = a2 + pv, a4 = a3 + pv;
+          sum = a4;
+          if (a4 == a3) {
+            i = n;
+            break;
+          }
+        }
+        for (; i < n; ++i) {
           const float ns = sum + pv;
-          if (ns == sum) break;  // adding pv again changes nothing
+          if (ns == sum) break;
           sum = ns;
         }
       }
@@ -437,16 +480,37 @@ __global__ void __launch_bounds__(kTopkThreads)
     int sel_key = thr, sel_rank = take - 1;  // no running sum above r: the k-th token
     float cum = 0.0f;
     bool done = false;
-    for (int b0 = kTopkBins - 1; b0 >= thr && !done; b0 -= 32) {
+    for (int b0 = top; b0 >= thr && !done; b0 -= 32) {
       const int b = b0 - lane;
       const uint32_t h = b > thr ? hist[b] : (b == thr ? (uint32_t)take : 0u);
+      // each lane's renormalised value, bf16(p / sum), for its own key
+      const float q_l =
+          uniform ? q_uniform : bf2f(f2bf(__fdiv_rn(bf2f((uint16_t)max(b, 0)), sum)));
       uint32_t nz = __ballot_sync(0xffffffffu, h != 0);
       while (nz && !done) {
         const int l = __ffs(nz) - 1;
         nz &= nz - 1;
         const uint32_t n = __shfl_sync(0xffffffffu, h, l);
-        const float q = uniform ? q_uniform : bf2f(f2bf(__fdiv_rn(bf2f((uint16_t)(b0 - l)), sum)));
-        for (uint32_t i = 0; i < n; ++i) {
+        const float q = __shfl_sync(0xffffffffu, q_l, l);
+        // cum += q, n times; the first running sum above r picks the token.
+        // Later terms are no larger than q, so a running sum that q no
+        // longer moves stays at or below r: the k-th token is taken.
+        uint32_t i = 0;
+        for (; i + 4 <= n; i += 4) {
+          const float c1 = cum + q, c2 = c1 + q, c3 = c2 + q, c4 = c3 + q;
+          if (r < c4) {
+            sel_key = b0 - l;
+            sel_rank = (int)i + (r < c1 ? 0 : r < c2 ? 1 : r < c3 ? 2 : 3);
+            done = true;
+            break;
+          }
+          if (c4 == c3) {
+            done = true;
+            break;
+          }
+          cum = c4;
+        }
+        for (; i < n && !done; ++i) {
           const float nc = cum + q;
           if (r < nc) {
             sel_key = b0 - l;
@@ -454,8 +518,6 @@ __global__ void __launch_bounds__(kTopkThreads)
             done = true;
             break;
           }
-          // Later terms are no larger than q, so a running sum that q no
-          // longer moves stays at or below r: the k-th token is taken.
           if (nc == cum) {
             done = true;
             break;
@@ -472,30 +534,56 @@ __global__ void __launch_bounds__(kTopkThreads)
   __syncthreads();
 
   // 6. the token: the sel_rank-th (from 0) index, in ascending order, whose
-  //    key is sel_key; thread t counts over its contiguous share of the row
+  //    key is sel_key. Rank 0 (every drawn probability that no other token
+  //    shares): the first such index, each thread stopping at its own first
+  //    one. Otherwise thread t counts over its contiguous share of the row, a
+  //    scan over the threads finds the share holding the wanted one, and that
+  //    thread walks its share.
   const int sel_key = s_sel_key, sel_rank = s_sel_rank;
-  const int per = (V + kTopkThreads - 1) / kTopkThreads;
-  const int j_lo = min(V, tid * per), j_hi = min(V, j_lo + per);
-  uint32_t cnt = 0;
-  for (int j = j_lo; j < j_hi; ++j) cnt += topk_key(p16[j]) == sel_key;
-  s_scan[tid] = cnt;
-  __syncthreads();
-  for (int off = 1; off < kTopkThreads; off <<= 1) {
-    const uint32_t v = s_scan[tid] + (tid >= off ? s_scan[tid - off] : 0u);
+  if (sel_rank == 0) {
+    // (eight entries per round, so that the loads are in flight together; the
+    // thread holding the match is usually the only one that stops early)
+    int first = 0x7fffffff;
+    for (int j0 = tid; j0 < V && first == 0x7fffffff; j0 += 8 * kTopkThreads) {
+      int key[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u * kTopkThreads;
+        key[u] = j < V ? topk_key(p16[j]) : -1;
+      }
+#pragma unroll
+      for (int u = 7; u >= 0; --u)
+        if (key[u] == sel_key) first = j0 + u * kTopkThreads;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+    if (lane == 0) atomicMin(&s_first, first);
     __syncthreads();
-    s_scan[tid] = v;
+    if (tid == 0 && s_first < V) s_tok = s_first;
+  } else {
+    const int per = (V + kTopkThreads - 1) / kTopkThreads;
+    const int j_lo = min(V, tid * per), j_hi = min(V, j_lo + per);
+    uint32_t cnt = 0;
+    for (int j = j_lo; j < j_hi; ++j) cnt += topk_key(p16[j]) == sel_key;
+    s_scan[tid] = cnt;
     __syncthreads();
-  }
-  const uint32_t before = s_scan[tid] - cnt;
-  if (before <= (uint32_t)sel_rank && (uint32_t)sel_rank < before + cnt) {
-    uint32_t c = before;
-    for (int j = j_lo; j < j_hi; ++j) {
-      if (topk_key(p16[j]) == sel_key) {
-        if (c == (uint32_t)sel_rank) {
-          s_tok = j;
-          break;
+    for (int off = 1; off < kTopkThreads; off <<= 1) {
+      const uint32_t v = s_scan[tid] + (tid >= off ? s_scan[tid - off] : 0u);
+      __syncthreads();
+      s_scan[tid] = v;
+      __syncthreads();
+    }
+    const uint32_t before = s_scan[tid] - cnt;
+    if (before <= (uint32_t)sel_rank && (uint32_t)sel_rank < before + cnt) {
+      uint32_t c = before;
+      for (int j = j_lo; j < j_hi; ++j) {
+        if (topk_key(p16[j]) == sel_key) {
+          if (c == (uint32_t)sel_rank) {
+            s_tok = j;
+            break;
+          }
+          ++c;
         }
-        ++c;
       }
     }
   }
@@ -516,13 +604,14 @@ int launch_topk_sample(const uint16_t *logits, int64_t ldl, int M, int V, float 
                        int32_t *out, int32_t *append_to, int64_t append_stride,
                        int32_t *append_pos, uint16_t *probs_out, int64_t ldp, cudaStream_t s) {
   if (V > kTopkMaxVocab) return W8A8_ERR_UNSUPPORTED;
-  const size_t smem = kTopkHistBytes + ((size_t)V * 2 + 15) / 16 * 16;
+  const size_t smem = kTopkHistBytes + ((size_t)(V + 8) * 2 + 15) / 16 * 16;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
     if (cudaFuncSetAttribute(topk_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(kTopkHistBytes + (size_t)kTopkMaxVocab * 2)) != cudaSuccess)
+                             (int)(kTopkHistBytes + (size_t)(kTopkMaxVocab + 8) * 2)) !=
+        cudaSuccess)
       return W8A8_ERR_CUDA;
     attr_set[dev] = true;
   }
