@@ -385,8 +385,163 @@ int gpt2_engine_load_quant8_memory(gpt2_engine *e, const void *data, size_t byte
   return W8A8_OK;
 }
 
+/* ---- the quant8.json manifest (tools/offline_quant/src/writer.py:72-124) ----
+ * A flat JSON object written by json.dump(indent=2); only the fields below
+ * are read, each once, so a key search suffices. */
+static const char *mf_skip_ws(const char *p) {
+  while (*p == ' ' || *p == '\t' || *p == '\n' || *p == '\r') ++p;
+  return p;
+}
+
+static const char *mf_value(const char *text, const char *key) {
+  char pat[64];
+  snprintf(pat, sizeof pat, "\"%s\"", key);
+  const char *p = strstr(text, pat);
+  if (!p) return NULL;
+  p = mf_skip_ws(p + strlen(pat));
+  return *p == ':' ? mf_skip_ws(p + 1) : NULL;
+}
+
+/* the string at p (no escapes) into out; returns the position after it */
+static const char *mf_string(const char *p, char *out, size_t cap) {
+  if (!p || *p != '"') return NULL;
+  size_t n = 0;
+  for (++p; *p && *p != '"'; ++p) {
+    if (*p == '\\' || n + 1 >= cap) return NULL;
+    out[n++] = *p;
+  }
+  if (*p != '"') return NULL;
+  out[n] = 0;
+  return p + 1;
+}
+
+static int mf_string_is(const char *text, const char *key, const char *want) {
+  char buf[128];
+  return mf_string(mf_value(text, key), buf, sizeof buf) && strcmp(buf, want) == 0;
+}
+
+static int mf_list_is(const char *text, const char *key, const char *const *want, int n) {
+  const char *p = mf_value(text, key);
+  if (!p || *p != '[') return 0;
+  p = mf_skip_ws(p + 1);
+  for (int i = 0; i < n; ++i) {
+    char buf[64];
+    p = mf_string(p, buf, sizeof buf);
+    if (!p || strcmp(buf, want[i]) != 0) return 0;
+    p = mf_skip_ws(p);
+    if (i + 1 < n) {
+      if (*p != ',') return 0;
+      p = mf_skip_ws(p + 1);
+    }
+  }
+  return *p == ']';
+}
+
+/* num / den rounded half to even (Python's round, writer.py:90-96) */
+static long long div_round_even(long long num, long long den) {
+  long long q = num / den, r = num % den;
+  if (2 * r > den || (2 * r == den && (q & 1))) ++q;
+  return q;
+}
+
+int gpt2_quant8_check_manifest(const gpt2_engine_config *cfg, const char *text, char *err,
+                               size_t err_len) {
+  char tmp[8];
+  if (!err || err_len == 0) {
+    err = tmp;
+    err_len = sizeof tmp;
+  }
+  err[0] = 0;
+  if (!cfg || !text) {
+    snprintf(err, err_len, "no configuration or manifest text");
+    return W8A8_ERR_INVALID;
+  }
+  static const char *const quantized[] = {"W_qkv", "attn_proj", "W1", "W2"};
+  static const char *const preserved[] = {"wte", "wpe", "ln1_gamma", "ln1_beta", "b_qkv",
+                                          "attn_proj_bias", "ln2_gamma", "ln2_beta", "b1", "b2",
+                                          "lnf_gamma", "lnf_beta"};
+  if (!mf_string_is(text, "scheme", "int8_per_channel_symmetric") ||
+      !mf_string_is(text, "scale_convention", "amax/127") ||
+      !mf_string_is(text, "scale_dtype", "fp32")) {
+    snprintf(err, err_len, "not per-channel symmetric int8 with fp32 amax/127 scales");
+    return W8A8_ERR_INVALID;
+  }
+  if (!mf_list_is(text, "quantized_tensors", quantized, 4) ||
+      !mf_list_is(text, "preserved_tensors", preserved, 12)) {
+    snprintf(err, err_len, "tensor lists differ from the quant8.bin layout");
+    return W8A8_ERR_INVALID;
+  }
+  /* model name where the dimensions are a GPT-2 size (reader.py:36-43) */
+  static const struct { int d, L, H; const char *name; } sizes[] = {
+      {768, 12, 12, "gpt2-small"}, {1024, 24, 16, "gpt2-medium"}, {1280, 36, 20, "gpt2-large"}};
+  for (int i = 0; i < 3; ++i)
+    if (cfg->d_model == sizes[i].d && cfg->n_layer == sizes[i].L && cfg->n_head == sizes[i].H &&
+        !mf_string_is(text, "model", sizes[i].name)) {
+      snprintf(err, err_len, "model is not %s", sizes[i].name);
+      return W8A8_ERR_INVALID;
+    }
+  /* memory summary (writer.py:72-96): unpadded tensor bytes */
+  const long long d = cfg->d_model, f = 4 * d, L = cfg->n_layer;
+  const long long preserved_b =
+      4 * ((long long)cfg->vocab * d + (long long)cfg->ctx * d + 2 * d + L * (9 * d + f));
+  const long long quant_b = L * (4 * d * d + 2 * f * d);
+  const long long scale_b = 4 * L * (5 * d + f);
+  const long long mib = 1024 * 1024;
+  const struct { const char *key; long long want; } summary[] = {
+      {"source_fp32_total_mb", div_round_even(preserved_b + 4 * quant_b, mib)},
+      {"quantized_int8_mb", div_round_even(quant_b, mib)},
+      {"preserved_fp32_mb", div_round_even(preserved_b, mib)},
+      {"scale_overhead_kb", div_round_even(scale_b, 1024)},
+      {"artifact_total_mb", div_round_even(preserved_b + quant_b + scale_b, mib)}};
+  for (int i = 0; i < 5; ++i) {
+    const char *p = mf_value(text, summary[i].key);
+    char *end = NULL;
+    const long long v = p ? strtoll(p, &end, 10) : -1;
+    if (!p || end == p || v != summary[i].want) {
+      snprintf(err, err_len, "memory_summary.%s is not %lld", summary[i].key, summary[i].want);
+      return W8A8_ERR_INVALID;
+    }
+  }
+  return W8A8_OK;
+}
+
+/* The manifest beside a quant8 file (X.bin -> X.json), checked when present. */
+static int check_sibling_manifest(gpt2_engine *e, const char *path) {
+  const size_t n = strlen(path);
+  char *jpath = (char *)malloc(n + 6);
+  if (!jpath) return fail(e, W8A8_ERR_NOMEM, "host memory");
+  memcpy(jpath, path, n + 1);
+  if (n >= 4 && strcmp(jpath + n - 4, ".bin") == 0) jpath[n - 4] = 0;
+  strcat(jpath, ".json");
+  FILE *fp = fopen(jpath, "rb");
+  if (!fp) {
+    free(jpath);
+    return W8A8_OK;  /* no manifest: the reference's loader needs none either */
+  }
+  enum { kMax = 1 << 16 };
+  char *text = (char *)malloc(kMax + 1);
+  size_t got = text ? fread(text, 1, kMax + 1, fp) : 0;
+  fclose(fp);
+  int st = W8A8_OK;
+  if (!text) {
+    st = fail(e, W8A8_ERR_NOMEM, "host memory");
+  } else if (got > kMax) {
+    st = fail(e, W8A8_ERR_INVALID, "%s: larger than %d bytes", jpath, kMax);
+  } else {
+    text[got] = 0;
+    char why[160];
+    if (gpt2_quant8_check_manifest(&e->cfg, text, why, sizeof why) != W8A8_OK)
+      st = fail(e, W8A8_ERR_INVALID, "%s: %s", jpath, why);
+  }
+  free(text);
+  free(jpath);
+  return st;
+}
+
 int gpt2_engine_load_quant8(gpt2_engine *e, const char *path) {
   if (!e || !path) return W8A8_ERR_INVALID;
+  int mst = check_sibling_manifest(e, path);
+  if (mst) return mst;
   FILE *fp = fopen(path, "rb");
   if (!fp) return fail(e, W8A8_ERR_IO, "cannot open %s", path);
   size_t need = gpt2_engine_quant8_bytes(&e->cfg);

@@ -7,6 +7,10 @@
 * INT8 ``quant8.bin`` — the same order with the four GEMM weights replaced by
   an int8 block followed by its fp32 per-output-channel scale, every block
   zero-padded to 16 bytes (tools/offline_quant/src/writer.py:34-69).
+* ``quant8.json`` — the manifest written beside it
+  (tools/offline_quant/src/writer.py:72-124): scheme, scale convention, the
+  quantized and preserved tensor names and a memory summary, all determined
+  by the model's dimensions.
 
 Per-channel symmetric quantization follows
 tools/offline_quant/src/quantizer.py:52-64: scale = amax/127 per output row
@@ -14,6 +18,8 @@ tools/offline_quant/src/quantizer.py:52-64: scale = amax/127 per output row
 """
 from __future__ import annotations
 
+import json
+import os
 from dataclasses import dataclass
 from typing import BinaryIO, Iterable, Iterator
 
@@ -22,6 +28,12 @@ import numpy as np
 INT8_MAX = 127
 ALIGNMENT = 16
 QUANTIZED = ("W_qkv", "attn_proj", "W1", "W2")
+PRESERVED = ("wte", "wpe", "ln1_gamma", "ln1_beta", "b_qkv", "attn_proj_bias",
+             "ln2_gamma", "ln2_beta", "b1", "b2", "lnf_gamma", "lnf_beta")
+MANIFEST_TOOL_VERSION = "0.1"
+MANIFEST_SCHEME = "int8_per_channel_symmetric"
+MANIFEST_SCALE_CONVENTION = "amax/127"
+MANIFEST_SCALE_DTYPE = "fp32"
 
 
 @dataclass(frozen=True)
@@ -42,6 +54,20 @@ DIMS = {
     "medium": GPT2Dims(1024, 24, 16),
     "large": GPT2Dims(1280, 36, 20),
 }
+
+
+# the reference's model names and FP32 weight files (tools/offline_quant/src/reader.py:36-43,
+# include/model_config.h:14,22,30)
+WEIGHTS_FILES = {"small": "gpt2_c_weights.bin", "medium": "gpt2_medium_c_weights.bin",
+                 "large": "gpt2_large_c_weights.bin"}
+
+
+def model_name(dims: GPT2Dims) -> str | None:
+    for name, known in DIMS.items():
+        if (known.d_model, known.n_layer, known.n_head) == (dims.d_model, dims.n_layer,
+                                                            dims.n_head):
+            return name
+    return None
 
 
 def tensor_layout(dims: GPT2Dims) -> list[tuple[str, tuple[int, ...]]]:
@@ -142,3 +168,69 @@ def read_quant8(data: bytes | memoryview, dims: GPT2Dims) -> dict[str, np.ndarra
         else:
             out[name] = take(count, np.float32).reshape(shape)
     return out
+
+
+# ---- the quant8.json manifest (tools/offline_quant/src/writer.py:72-124) ----
+
+def memory_summary(dims: GPT2Dims) -> dict[str, int]:
+    """writer.py:72-96: byte counts of the unpadded tensors, rounded (Python's
+    round, half to even) to MiB / KiB."""
+    d, f, L = dims.d_model, dims.d_ff, dims.n_layer
+    preserved = 4 * (dims.vocab * d + dims.ctx * d + 2 * d + L * (2 * d + 3 * d + d + 2 * d + f + d))
+    quantized = L * (3 * d * d + d * d + f * d + d * f)
+    scales = 4 * L * (3 * d + d + f + d)
+    mib = 1024 * 1024
+    return {
+        "source_fp32_total_mb": round((preserved + 4 * quantized) / mib),
+        "quantized_int8_mb": round(quantized / mib),
+        "preserved_fp32_mb": round(preserved / mib),
+        "scale_overhead_kb": round(scales / 1024),
+        "artifact_total_mb": round((preserved + quantized + scales) / mib),
+    }
+
+
+def build_manifest(dims: GPT2Dims, name: str | None = None,
+                   weights_filename: str | None = None) -> dict:
+    """writer.py:99-111 for a model of these dimensions; name and weights file
+    default to the reference's for GPT-2 small / medium / large."""
+    name = name or model_name(dims)
+    if name is None:
+        raise ValueError("dimensions of no GPT-2 size: give the model name")
+    weights_filename = weights_filename or WEIGHTS_FILES[name]
+    return {
+        "tool_version": MANIFEST_TOOL_VERSION,
+        "model": f"gpt2-{name}",
+        "scheme": MANIFEST_SCHEME,
+        "scale_convention": MANIFEST_SCALE_CONVENTION,
+        "scale_dtype": MANIFEST_SCALE_DTYPE,
+        "source_weights_path": f"weights/{weights_filename}",
+        "quantized_tensors": list(QUANTIZED),
+        "preserved_tensors": list(PRESERVED),
+        "memory_summary": memory_summary(dims),
+    }
+
+
+def manifest_text(manifest: dict) -> str:
+    """The file's text as writer.py:120-122 writes it."""
+    return json.dumps(manifest, indent=2) + "\n"
+
+
+def write_manifest(path: str | os.PathLike, dims: GPT2Dims, name: str | None = None,
+                   weights_filename: str | None = None) -> None:
+    with open(path, "w") as f:
+        f.write(manifest_text(build_manifest(dims, name, weights_filename)))
+
+
+def check_manifest(manifest: dict, dims: GPT2Dims) -> None:
+    """Raise ValueError unless the manifest describes this scheme and a model
+    of these dimensions (the model name, where it names a GPT-2 size, and the
+    memory summary)."""
+    want = {"scheme": MANIFEST_SCHEME, "scale_convention": MANIFEST_SCALE_CONVENTION,
+            "scale_dtype": MANIFEST_SCALE_DTYPE, "quantized_tensors": list(QUANTIZED),
+            "preserved_tensors": list(PRESERVED), "memory_summary": memory_summary(dims)}
+    for key, value in want.items():
+        if manifest.get(key) != value:
+            raise ValueError(f"quant8 manifest: {key} is {manifest.get(key)!r}, expected {value!r}")
+    name = model_name(dims)
+    if name is not None and manifest.get("model") != f"gpt2-{name}":
+        raise ValueError(f"quant8 manifest: model {manifest.get('model')!r} for GPT-2 {name}")

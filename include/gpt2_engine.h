@@ -48,6 +48,16 @@ void gpt2_engine_destroy(gpt2_engine *e);
  * FP32 tensors are rounded to bf16 (round-to-nearest-even) as the
  * reference's loader does (gpt2.c:1613-1628). */
 int gpt2_engine_load_quant8(gpt2_engine *e, const char *path);
+/* The manifest the reference's writer puts beside the file
+ * (gpt2_<size>_quant8.json, tools/offline_quant/src/writer.py:72-124):
+ * gpt2_engine_load_quant8(path) reads X.json for X.bin when it exists and
+ * refuses the load unless it describes per-channel symmetric int8 weights with
+ * fp32 amax/127 scales, the quant8.bin tensor lists, the model named by a GPT-2
+ * size's dimensions and the memory summary of this configuration.
+ * gpt2_quant8_check_manifest runs that check on a manifest's text (host only):
+ * W8A8_OK, or W8A8_ERR_INVALID with the reason in err. */
+int gpt2_quant8_check_manifest(const gpt2_engine_config *cfg, const char *json_text, char *err,
+                               size_t err_len);
 int gpt2_engine_load_quant8_memory(gpt2_engine *e, const void *data, size_t bytes);
 /* Bytes of a quant8.bin for this configuration. */
 size_t gpt2_engine_quant8_bytes(const gpt2_engine_config *cfg);

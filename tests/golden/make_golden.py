@@ -10,6 +10,10 @@ Runs only where the reference tree is mounted (REF_ROOT, default
   quant8_tiny.json    SHA-256 and size of the quant8.bin the reference's
                       writer (tools/offline_quant/src/writer.py:50-69)
                       produces for tiny seeded weights
+  quant8_manifests.json  the text of the quant8.json manifest the reference's
+                      writer (tools/offline_quant/src/writer.py:99-124) writes
+                      for GPT-2 small / medium / large and the tiny model
+                      (it depends on tensor sizes only: zero-filled tensors)
   ref_fp32_small.npz  the reference's CPU FP32 build (oracle/_ref, gpt2.c)
                       on GPT-2 small, seed-0 weights, a 32-token prompt of
                       seed-0 ids: the 64-token greedy stream and the logits
@@ -103,6 +107,32 @@ def make_quant8_tiny(quantizer, reader, writer) -> None:
     (HERE / "quant8_tiny.json").write_text(json.dumps(meta, indent=2) + "\n")
 
 
+def make_quant8_manifests(quantizer, reader, writer) -> None:
+    def zeros_weights(cfg, vocab, ctx):
+        d, f = cfg.d_model, 4 * cfg.d_model
+        z = lambda *shape: np.zeros(shape, np.float32)
+        qt = lambda o, i: quantizer.QuantizedTensor(int8=np.zeros((o, i), np.int8), scale=z(o))
+        layers = [quantizer.QuantizedLayer(
+            ln1_gamma=z(d), ln1_beta=z(d), W_qkv=qt(3 * d, d), b_qkv=z(3 * d),
+            attn_proj=qt(d, d), attn_proj_bias=z(d), ln2_gamma=z(d), ln2_beta=z(d),
+            W1=qt(f, d), b1=z(f), W2=qt(d, f), b2=z(d)) for _ in range(cfg.num_layers)]
+        return quantizer.QuantizedWeights(config=cfg, wte=z(vocab, d), wpe=z(ctx, d),
+                                          layers=layers, lnf_gamma=z(d), lnf_beta=z(d))
+
+    out = {}
+    cases = [(name, cfg, reader.VOCAB_SIZE, reader.CTX_LEN)
+             for name, cfg in reader.MODEL_CONFIGS.items()]
+    cases.append(("tiny", reader.ModelConfig("tiny", TINY["d_model"], TINY["n_layer"],
+                                             TINY["n_head"], "tiny.bin"),
+                  TINY["vocab"], TINY["ctx"]))
+    for name, cfg, vocab, ctx in cases:
+        buf = io.StringIO()  # as writer.write_quantized writes the file (writer.py:120-122)
+        json.dump(writer.build_manifest(zeros_weights(cfg, vocab, ctx)), buf, indent=2)
+        buf.write("\n")
+        out[name] = buf.getvalue()
+    (HERE / "quant8_manifests.json").write_text(json.dumps(out, indent=1) + "\n")
+
+
 def make_ref_fp32_small() -> None:
     from c_gpt2_b200.quant8 import DIMS
     from c_gpt2_b200.synthetic import prompts, write_weight_files
@@ -129,6 +159,7 @@ def main() -> None:
     quantizer, reader, writer = reference_quant_modules()
     make_weight_quant(quantizer)
     make_quant8_tiny(quantizer, reader, writer)
+    make_quant8_manifests(quantizer, reader, writer)
     if not args.skip_ref_run:
         make_ref_fp32_small()
 

@@ -85,3 +85,77 @@ def test_synthetic_is_seeded():
     x = outlier_activations(16, 768, seed=1)
     big = np.abs(x).max(axis=0) > 10
     assert 1 <= big.sum() <= 8  # 1% of 768 channels scaled x20
+
+
+# ---- the quant8.json manifest (tools/offline_quant/src/writer.py:72-124) ----
+
+MANIFESTS = json.loads((GOLDEN / "quant8_manifests.json").read_text())
+TINY_GOLDEN = GPT2Dims(d_model=64, n_layer=2, n_head=1, vocab=100, ctx=16)
+
+
+def _manifest_cases():
+    from c_gpt2_b200 import quant8
+    yield "small", DIMS["small"], quant8.build_manifest(DIMS["small"])
+    yield "medium", DIMS["medium"], quant8.build_manifest(DIMS["medium"])
+    yield "large", DIMS["large"], quant8.build_manifest(DIMS["large"])
+    yield "tiny", TINY_GOLDEN, quant8.build_manifest(TINY_GOLDEN, "tiny", "tiny.bin")
+
+
+def test_manifest_matches_reference_writer(tmp_path):
+    """The text the reference's writer writes, byte for byte."""
+    from c_gpt2_b200 import quant8
+    for name, dims, m in _manifest_cases():
+        assert quant8.manifest_text(m) == MANIFESTS[name], name
+        quant8.check_manifest(json.loads(MANIFESTS[name]), dims)
+    path = tmp_path / "gpt2_large_quant8.json"
+    quant8.write_manifest(path, DIMS["large"])
+    assert path.read_text() == MANIFESTS["large"]
+
+
+def _spoiled(text):
+    """Manifests that must be refused: one field changed each."""
+    m = json.loads(text)
+    out = []
+    for key, value in (("scheme", "int8_per_tensor"), ("scale_convention", "amax/128"),
+                       ("scale_dtype", "fp16")):
+        out.append({**m, key: value})
+    out.append({**m, "quantized_tensors": m["quantized_tensors"][::-1]})
+    out.append({**m, "preserved_tensors": m["preserved_tensors"][:-1]})
+    ms = dict(m["memory_summary"])
+    ms["scale_overhead_kb"] += 1
+    out.append({**m, "memory_summary": ms})
+    return out
+
+
+def test_manifest_check_refuses_mismatches():
+    from c_gpt2_b200 import quant8
+    for m in _spoiled(MANIFESTS["large"]):
+        with pytest.raises(ValueError):
+            quant8.check_manifest(m, DIMS["large"])
+    with pytest.raises(ValueError):  # a small model's manifest for the large model
+        quant8.check_manifest(json.loads(MANIFESTS["small"]), DIMS["large"])
+    with pytest.raises(ValueError):
+        quant8.check_manifest({**json.loads(MANIFESTS["large"]), "model": "gpt2-xl"},
+                              DIMS["large"])
+
+
+def test_engine_manifest_check_in_c():
+    """gpt2_quant8_check_manifest (the engine loader's check; host code only)."""
+    import ctypes as C
+    from c_gpt2_b200._lib import EngineConfig, W8A8_ERR_INVALID, W8A8_OK, core
+
+    def check(dims, text):
+        cfg = EngineConfig(dims.d_model, dims.n_layer, dims.n_head, dims.vocab, dims.ctx, 1, 1)
+        err = C.create_string_buffer(160)
+        st = core().gpt2_quant8_check_manifest(C.byref(cfg), text.encode(), err, 160)
+        return st, err.value.decode()
+
+    for name, dims, _ in _manifest_cases():
+        assert check(dims, MANIFESTS[name]) == (W8A8_OK, ""), name
+    for m in _spoiled(MANIFESTS["large"]):
+        st, why = check(DIMS["large"], json.dumps(m, indent=2))
+        assert st == W8A8_ERR_INVALID and why
+    assert check(DIMS["large"], MANIFESTS["small"])[0] == W8A8_ERR_INVALID
+    assert check(DIMS["large"], MANIFESTS["large"].replace("gpt2-large", "gpt2-xl"))[0] \
+        == W8A8_ERR_INVALID
+    assert check(DIMS["large"], "{}")[0] == W8A8_ERR_INVALID

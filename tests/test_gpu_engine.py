@@ -208,3 +208,29 @@ def test_slot_api_bounds(cuda, tiny_image):
     with pytest.raises(W8A8Error):
         eng.slot_prefill(0, long)      # longer than ctx
     eng.close()
+
+
+def test_load_from_path_checks_manifest(cuda, tiny_image, tmp_path):
+    """gpt2_engine_load_quant8(X.bin) reads the manifest X.json the reference's
+    writer puts beside it (writer.py:114-124) and refuses one that does not
+    describe this model; without a manifest the file loads as before."""
+    import json
+
+    from c_gpt2_b200 import quant8
+    from c_gpt2_b200._lib import W8A8Error
+
+    bin_path = tmp_path / "gpt2_tiny_quant8.bin"
+    bin_path.write_bytes(tiny_image)
+    P = prompts(2, 8, TINY.vocab, seed=4)
+    eng = Engine(TINY, max_batch=2, max_tokens=2 * 8)
+    eng.load_quant8(str(bin_path))  # no manifest
+    want = eng.generate(P, 6)
+    quant8.write_manifest(tmp_path / "gpt2_tiny_quant8.json", TINY, "tiny", "tiny.bin")
+    eng.load_quant8(str(bin_path))
+    np.testing.assert_array_equal(eng.generate(P, 6), want)
+    m = quant8.build_manifest(TINY, "tiny", "tiny.bin")
+    m["memory_summary"] = dict(m["memory_summary"], scale_overhead_kb=999)
+    (tmp_path / "gpt2_tiny_quant8.json").write_text(quant8.manifest_text(m))
+    with pytest.raises(W8A8Error, match="memory_summary"):
+        eng.load_quant8(str(bin_path))
+    eng.close()
