@@ -1,7 +1,8 @@
 """Regenerate the golden fixtures of tests/golden/ from the reference itself.
 
 Runs only where the reference tree is mounted (REF_ROOT, default
-/root/reference); the GPU box never runs it. Outputs:
+/root/reference); the tests read the fixtures it wrote and never run it.
+Outputs:
 
   weight_quant.npz    the reference's per-channel quantizer
                       (tools/offline_quant/src/quantizer.py:52-64) applied to
