@@ -276,6 +276,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-split", type=int, choices=[1, 2], default=1,
+                    help="decode each step as one chain of kernels or two concurrent chains")
     args = ap.parse_args()
 
     from c_gpt2_b200.dp import dist_env, max_over_ranks, shard
@@ -303,6 +305,7 @@ def main() -> None:
     img = quant8_image_gpu(dims, seed=0, device=dev)
     eng = Engine(dims, max_batch=count, max_tokens=count * PROMPT, device=local)
     eng.load_quant8(img)
+    eng.set_decode_split(args.decode_split)
     del img
     P = prompts(N_SEQ, PROMPT, dims.vocab, seed=0)[first:first + count]
     pd = torch.from_numpy(np.ascontiguousarray(P)).to(dev)
@@ -376,7 +379,7 @@ def main() -> None:
             "dtype": "int8", "data": "synthetic",
             "config": {"workload": WORKLOAD, "model": "gpt2-large", "n_seq": N_SEQ,
                        "prompt_len": PROMPT, "gen_len": GEN, "seq_per_gpu": N_SEQ // world,
-                       "parallelism": f"dp{world}",
+                       "parallelism": f"dp{world}", "decode_chains": args.decode_split,
                        "l2": "inputs larger than L2 (929 MB weights + 12 GB KV cache per step)"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": int(count * PROMPT * 4),

@@ -152,6 +152,11 @@ class Engine:
         self._check(core().gpt2_engine_set_draws(self._h, slot, d.ctypes.data if d.size else None,
                                                  d.size), "gpt2_engine_set_draws")
 
+    def set_decode_split(self, halves: int) -> None:
+        """Decode steps as one chain over all slots (1) or two concurrent chains (2)."""
+        self._check(core().gpt2_engine_set_decode_split(self._h, int(halves)),
+                    "gpt2_engine_set_decode_split")
+
     def set_graphs(self, enable: bool) -> None:
         self._check(core().gpt2_engine_set_graphs(self._h, 1 if enable else 0),
                     "gpt2_engine_set_graphs")

@@ -55,6 +55,11 @@ struct gpt2_engine {
   size_t attn_ws_bytes;
   void *lin_ws; /* split-K workspace of the decode-sized GEMMs (zeroed) */
   size_t lin_ws_bytes;
+  /* the second half of a split decode step: its own stream and workspaces */
+  cudaStream_t stream2;
+  cudaEvent_t ev_fork, ev_join;
+  void *attn_ws2, *lin_ws2;
+  int decode_split; /* 1: one chain of B rows; 2: two chains of B/2 rows on two streams */
   /* current batch: B slots (rows) of the decode step */
   int B;
   int32_t *out;
@@ -72,7 +77,7 @@ struct gpt2_engine {
   /* decode graph */
   int use_graphs;
   cudaGraphExec_t graph;
-  int graph_B, graph_stride;
+  int graph_B, graph_stride, graph_split;
   int32_t *graph_out;
 };
 
@@ -197,7 +202,10 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
     gpt2_engine_destroy(e);
     return st;
   }
-  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess) {
+  if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&e->stream2, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming) != cudaSuccess) {
     gpt2_engine_destroy(e);
     return W8A8_ERR_CUDA;
   }
@@ -213,7 +221,7 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   /* activations */
   e->attn_ws_bytes = w8a8_attention_decode_workspace_size((int)Bm, cfg->n_head, (int)C);
   e->lin_ws_bytes = w8a8_linear_workspace_size((int)Bm, 4 * (int)d);
-  size_t off = 0, sizes[15];
+  size_t off = 0, sizes[17];
   sizes[0] = Mt * d * 2;        /* H */
   sizes[1] = Mt * d * 2;        /* R1 */
   sizes[2] = Mt * d * 2;        /* Q */
@@ -229,8 +237,10 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   sizes[12] = e->attn_ws_bytes;
   sizes[13] = e->lin_ws_bytes;
   sizes[14] = Bm * C * 4;       /* sampling draws [max_batch][ctx] */
-  size_t offs[15];
-  for (int i = 0; i < 15; ++i) {
+  sizes[15] = e->attn_ws_bytes; /* second decode half */
+  sizes[16] = e->lin_ws_bytes;
+  size_t offs[17];
+  for (int i = 0; i < 17; ++i) {
     offs[i] = off;
     off += ALIGN_UP(sizes[i], 256);
   }
@@ -257,7 +267,10 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   e->attn_ws = a + offs[12];
   e->lin_ws = a + offs[13];
   e->rnd = (float *)(a + offs[14]);
+  e->attn_ws2 = a + offs[15];
+  e->lin_ws2 = a + offs[16];
   e->top_k = 40;
+  e->decode_split = 1;
   if (cudaMemset(e->ablob, 0, off) != cudaSuccess) {
     gpt2_engine_destroy(e);
     return W8A8_ERR_CUDA;
@@ -274,6 +287,9 @@ void gpt2_engine_destroy(gpt2_engine *e) {
   if (e->Kc) cudaFree(e->Kc);
   if (e->Vc) cudaFree(e->Vc);
   if (e->stream) cudaStreamDestroy(e->stream);
+  if (e->stream2) cudaStreamDestroy(e->stream2);
+  if (e->ev_fork) cudaEventDestroy(e->ev_fork);
+  if (e->ev_join) cudaEventDestroy(e->ev_join);
   free(e->slot_len);
   free(e->layers);
   free(e);
@@ -560,10 +576,41 @@ int gpt2_engine_load_quant8(gpt2_engine *e, const char *path) {
 
 /* ---- forward passes ---- */
 
+/* The activation buffers, workspaces and stream one forward pass uses. A
+ * split decode step runs its two halves at the same time on two streams:
+ * each half uses the buffer rows of its own slots and its own workspaces. */
+typedef struct {
+  gpt2_bf16_t *H, *R1, *Q, *ATT, *X1, *Xf, *logits;
+  int8_t *Xq;
+  float *sX;
+  void *attn_ws, *lin_ws;
+  void *s;
+} act_view;
+
+/* Rows row0.. of every activation buffer; half 1 takes the second workspaces
+ * and stream. */
+static act_view view_at(gpt2_engine *e, int row0, int half) {
+  const int64_t d = e->cfg.d_model, f = 4 * d;
+  act_view v;
+  v.H = e->H + row0 * d;
+  v.R1 = e->R1 + row0 * d;
+  v.Q = e->Q + row0 * d;
+  v.ATT = e->ATT + row0 * d;
+  v.X1 = e->X1 + row0 * f;
+  v.Xf = e->Xf + row0 * d;
+  v.logits = e->logits + (int64_t)row0 * e->cfg.vocab;
+  v.Xq = e->Xq + row0 * f; /* rows of up to 4d int8 */
+  v.sX = e->sX + row0;
+  v.attn_ws = half ? e->attn_ws2 : e->attn_ws;
+  v.lin_ws = half ? e->lin_ws2 : e->lin_ws;
+  v.s = (void *)(half ? e->stream2 : e->stream);
+  return v;
+}
+
 /* One transformer block over M = B*T rows of H (T tokens per sequence,
  * written at cache rows pos0[b] + t; pos0 == NULL means prefill from 0). */
-static int block_forward(gpt2_engine *e, int l, int slot0, int B, int T, const int32_t *pos0,
-                         int first) {
+static int block_forward(gpt2_engine *e, const act_view *v, int l, int slot0, int B, int T,
+                         const int32_t *pos0, int first) {
   const gpt2_engine_config *c = &e->cfg;
   const layer_w *w = &e->layers[l];
   const int d = c->d_model, f = 4 * d, M = B * T, Hh = c->n_head;
@@ -572,61 +619,69 @@ static int block_forward(gpt2_engine *e, int l, int slot0, int B, int T, const i
   /* the caches of slots slot0 .. slot0+B-1 */
   gpt2_bf16_t *Kl = e->Kc + (int64_t)slot0 * seq_stride + (int64_t)l * c->ctx * d;
   gpt2_bf16_t *Vl = e->Vc + (int64_t)slot0 * seq_stride + (int64_t)l * c->ctx * d;
-  void *s = (void *)e->stream;
+  void *s = v->s;
+  const size_t lwb = e->lin_ws_bytes;
   if (!first)
-    W8_TRY(e, w8a8_layernorm_quant(e->H, d, M, d, w->ln1_g, w->ln1_b, eps, NULL, 0, e->Xq, e->sX, s));
-  W8_TRY(e, w8a8_linear_qkv(e->Xq, e->sX, M, d, w->Wqkv, w->sWqkv, w->bqkv, e->Q, d, Kl, Vl,
-                            seq_stride, T, pos0, e->lin_ws, e->lin_ws_bytes, s));
+    W8_TRY(e, w8a8_layernorm_quant(v->H, d, M, d, w->ln1_g, w->ln1_b, eps, NULL, 0, v->Xq, v->sX, s));
+  W8_TRY(e, w8a8_linear_qkv(v->Xq, v->sX, M, d, w->Wqkv, w->sWqkv, w->bqkv, v->Q, d, Kl, Vl,
+                            seq_stride, T, pos0, v->lin_ws, lwb, s));
   if (pos0 == NULL)
-    W8_TRY(e, w8a8_attention_prefill(e->Q, d, Kl, Vl, seq_stride, B, T, Hh, 64, e->ATT, d, s));
+    W8_TRY(e, w8a8_attention_prefill(v->Q, d, Kl, Vl, seq_stride, B, T, Hh, 64, v->ATT, d, s));
   else  /* decode: the attention kernel also quantizes its output rows */
-    W8_TRY(e, w8a8_attention_decode_quant(e->Q, d, Kl, Vl, seq_stride, B, e->nctx, c->ctx, Hh, 64,
-                                          e->ATT, d, e->Xq, e->sX, e->attn_ws, e->attn_ws_bytes,
-                                          s));
-  if (pos0 == NULL) W8_TRY(e, w8a8_quant_rows(e->ATT, d, M, d, e->Xq, e->sX, s));
-  W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, d, w->Wproj, w->sWproj, w->bproj, d, W8A8_EPI_BIAS_RESID,
-                        e->H, d, e->R1, d, e->lin_ws, e->lin_ws_bytes, s));
-  W8_TRY(e, w8a8_layernorm_quant(e->R1, d, M, d, w->ln2_g, w->ln2_b, eps, NULL, 0, e->Xq, e->sX, s));
-  W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, d, w->W1, w->sW1, w->b1, f, W8A8_EPI_BIAS_GELU, NULL, 0,
-                        e->X1, f, e->lin_ws, e->lin_ws_bytes, s));
-  W8_TRY(e, w8a8_quant_rows(e->X1, f, M, f, e->Xq, e->sX, s));
-  W8_TRY(e, w8a8_linear(e->Xq, e->sX, M, f, w->W2, w->sW2, w->b2, d, W8A8_EPI_BIAS_RESID, e->R1, d,
-                        e->H, d, e->lin_ws, e->lin_ws_bytes, s));
+    W8_TRY(e, w8a8_attention_decode_quant(v->Q, d, Kl, Vl, seq_stride, B, e->nctx + slot0, c->ctx,
+                                          Hh, 64, v->ATT, d, v->Xq, v->sX, v->attn_ws,
+                                          e->attn_ws_bytes, s));
+  if (pos0 == NULL) W8_TRY(e, w8a8_quant_rows(v->ATT, d, M, d, v->Xq, v->sX, s));
+  W8_TRY(e, w8a8_linear(v->Xq, v->sX, M, d, w->Wproj, w->sWproj, w->bproj, d, W8A8_EPI_BIAS_RESID,
+                        v->H, d, v->R1, d, v->lin_ws, lwb, s));
+  W8_TRY(e, w8a8_layernorm_quant(v->R1, d, M, d, w->ln2_g, w->ln2_b, eps, NULL, 0, v->Xq, v->sX, s));
+  W8_TRY(e, w8a8_linear(v->Xq, v->sX, M, d, w->W1, w->sW1, w->b1, f, W8A8_EPI_BIAS_GELU, NULL, 0,
+                        v->X1, f, v->lin_ws, lwb, s));
+  W8_TRY(e, w8a8_quant_rows(v->X1, f, M, f, v->Xq, v->sX, s));
+  W8_TRY(e, w8a8_linear(v->Xq, v->sX, M, f, w->W2, w->sW2, w->b2, d, W8A8_EPI_BIAS_RESID, v->R1, d,
+                        v->H, d, v->lin_ws, lwb, s));
   return W8A8_OK;
 }
 
 /* Embedding + all blocks + final LN of the last row of each sequence + LM
  * head + greedy pick appended to the output rows, for the B sequences in
  * slots slot0 .. slot0+B-1. */
-static int model_forward(gpt2_engine *e, const int32_t *tokens_d, int slot0, int B, int T,
-                         const int32_t *pos0) {
+static int model_forward(gpt2_engine *e, const act_view *v, const int32_t *tokens_d, int slot0,
+                         int B, int T, const int32_t *pos0) {
   const gpt2_engine_config *c = &e->cfg;
   const int d = c->d_model, M = B * T;
   const float eps = 1e-5f;
-  void *s = (void *)e->stream;
+  void *s = v->s;
   const layer_w *w0 = &e->layers[0];
-  W8_TRY(e, w8a8_embed_layernorm_quant(e->wte, e->wpe, tokens_d, M, T, pos0, d, e->H, w0->ln1_g,
-                                       w0->ln1_b, eps, NULL, e->Xq, e->sX, s));
+  W8_TRY(e, w8a8_embed_layernorm_quant(e->wte, e->wpe, tokens_d, M, T, pos0, d, v->H, w0->ln1_g,
+                                       w0->ln1_b, eps, NULL, v->Xq, v->sX, s));
   for (int l = 0; l < c->n_layer; ++l) {
-    int st = block_forward(e, l, slot0, B, T, pos0, l == 0);
+    int st = block_forward(e, v, l, slot0, B, T, pos0, l == 0);
     if (st) return st;
   }
   /* final LayerNorm on the last token of every sequence (gpt2.c:2150-2157) */
-  W8_TRY(e, w8a8_layernorm_quant(e->H + (int64_t)(T - 1) * d, (int64_t)T * d, B, d, e->lnf_g,
-                                 e->lnf_b, eps, e->Xf, d, NULL, NULL, s));
-  W8_TRY(e, w8a8_lm_head(e->Xf, d, B, d, e->wte, c->vocab, e->logits, c->vocab, s));
+  W8_TRY(e, w8a8_layernorm_quant(v->H + (int64_t)(T - 1) * d, (int64_t)T * d, B, d, e->lnf_g,
+                                 e->lnf_b, eps, v->Xf, d, NULL, NULL, s));
+  W8_TRY(e, w8a8_lm_head(v->Xf, d, B, d, e->wte, c->vocab, v->logits, c->vocab, s));
   /* gpt2.c:2176-2245: greedy at temperature <= 0, else top-k sampling; the
    * draw of a slot's i-th token is rnd[slot][i] (i = its output count) */
   if (e->temperature > 0.0f)
-    W8_TRY(e, w8a8_sample_topk(e->logits, c->vocab, B, c->vocab, e->temperature, e->top_k,
+    W8_TRY(e, w8a8_sample_topk(v->logits, c->vocab, B, c->vocab, e->temperature, e->top_k,
                                e->rnd + (int64_t)slot0 * c->ctx, c->ctx, e->gen + slot0,
                                e->next + slot0, e->out + (int64_t)slot0 * e->out_stride,
                                e->out_stride, e->gen + slot0, NULL, 0, s));
   else
-    W8_TRY(e, w8a8_sample_greedy(e->logits, c->vocab, B, c->vocab, e->next + slot0,
+    W8_TRY(e, w8a8_sample_greedy(v->logits, c->vocab, B, c->vocab, e->next + slot0,
                                  e->out + (int64_t)slot0 * e->out_stride, e->out_stride,
                                  e->gen + slot0, s));
   return W8A8_OK;
+}
+
+/* A decode step of B slots runs as one chain, or (decode_split 2, B >= 2) as
+ * two chains of ceil(B/2) and floor(B/2) slots on two streams. */
+static int decode_halves(const gpt2_engine *e, int B) { return e->decode_split == 2 && B >= 2 ? 2 : 1; }
+static int decode_half_rows(const gpt2_engine *e, int B, int h) {
+  return decode_halves(e, B) == 1 ? B : (h == 0 ? (B + 1) / 2 : B / 2);
 }
 
 int gpt2_engine_launches_per_decode_step(const gpt2_engine *e) {
@@ -634,9 +689,14 @@ int gpt2_engine_launches_per_decode_step(const gpt2_engine *e) {
    * kernels, output quantization fused), attn_proj, LN2, W1, quant, W2; then
    * nctx, final LN, LM head, sample, len advance */
   if (!e) return 0;
-  const int attn = w8a8_attention_decode_launches(e->B > 0 ? e->B : e->cfg.max_batch,
-                                                  e->cfg.n_head, e->cfg.ctx);
-  return 1 + e->cfg.n_layer * (7 + attn) - 1 + 1 + 3 + 1;
+  const int B = e->B > 0 ? e->B : e->cfg.max_batch;
+  int n = 0;
+  for (int h = 0; h < decode_halves(e, B); ++h) {
+    const int rows = decode_half_rows(e, B, h);
+    const int attn = w8a8_attention_decode_launches(rows, e->cfg.n_head, e->cfg.ctx);
+    n += 1 + e->cfg.n_layer * (7 + attn) - 1 + 1 + 3 + 1;
+  }
+  return n;
 }
 
 int gpt2_engine_launches_per_prefill(const gpt2_engine *e) {
@@ -658,7 +718,8 @@ int gpt2_engine_prefill(gpt2_engine *e, const int32_t *prompts_d, int B, int T,
   e->out_stride = out_stride;
   /* reset per-sequence state: gen = 0, len = T (after this prefill) */
   CUDA_TRY(e, cudaMemsetAsync(e->gen, 0, (size_t)B * 4, e->stream));
-  int st = model_forward(e, prompts_d, 0, B, T, NULL);
+  const act_view v = view_at(e, 0, 0);
+  int st = model_forward(e, &v, prompts_d, 0, B, T, NULL);
   if (st) return st;
   CUDA_TRY(e, cudaMemsetAsync(e->len, 0, (size_t)B * 4, e->stream));
   W8_TRY(e, w8a8_advance_positions(e->len, e->len, B, T, (void *)e->stream));
@@ -708,7 +769,8 @@ int gpt2_engine_slot_prefill(gpt2_engine *e, int slot, const int32_t *prompt_d, 
   if (T <= 0 || T > e->cfg.ctx || T > e->cfg.max_tokens)
     return fail(e, W8A8_ERR_INVALID, "prompt of %d tokens", T);
   CUDA_TRY(e, cudaMemsetAsync(e->gen + slot, 0, 4, e->stream));
-  int st = model_forward(e, prompt_d, slot, 1, T, NULL);
+  const act_view v = view_at(e, 0, 0);
+  int st = model_forward(e, &v, prompt_d, slot, 1, T, NULL);
   if (st) return st;
   CUDA_TRY(e, cudaMemsetAsync(e->len + slot, 0, 4, e->stream));
   W8_TRY(e, w8a8_advance_positions(e->len + slot, e->len + slot, 1, T, (void *)e->stream));
@@ -734,14 +796,36 @@ int gpt2_engine_slot_tokens(const gpt2_engine *e, int slot) {
   return e->slot_gen[slot];
 }
 
-/* One decode step: token next[b] at position len[b]. */
+/* One decode step of slots slot0 .. slot0+B-1: token next[b] at position len[b]. */
+static int decode_chain(gpt2_engine *e, const act_view *v, int slot0, int B) {
+  W8_TRY(e, w8a8_advance_positions(e->nctx + slot0, e->len + slot0, B, 1, v->s));
+  int st = model_forward(e, v, e->next + slot0, slot0, B, 1, e->len + slot0);
+  if (st) return st;
+  W8_TRY(e, w8a8_advance_positions(e->len + slot0, e->len + slot0, B, 1, v->s));
+  return W8A8_OK;
+}
+
+/* One decode step of all B slots: one chain on the engine stream, or two
+ * independent chains (every row of every kernel is computed on its own) on
+ * the engine stream and the second stream, forked from and joined back to
+ * the engine stream, so that one half's latency-bound GEMMs run while the
+ * other half's attention streams its KV cache. */
 static int decode_step_launches(gpt2_engine *e) {
   const int B = e->B;
-  W8_TRY(e, w8a8_advance_positions(e->nctx, e->len, B, 1, (void *)e->stream));
-  int st = model_forward(e, e->next, 0, B, 1, e->len);
-  if (st) return st;
-  W8_TRY(e, w8a8_advance_positions(e->len, e->len, B, 1, (void *)e->stream));
-  return W8A8_OK;
+  if (decode_halves(e, B) == 1) {
+    const act_view v = view_at(e, 0, 0);
+    return decode_chain(e, &v, 0, B);
+  }
+  const int b0 = decode_half_rows(e, B, 0), b1 = decode_half_rows(e, B, 1);
+  CUDA_TRY(e, cudaEventRecord(e->ev_fork, e->stream));
+  CUDA_TRY(e, cudaStreamWaitEvent(e->stream2, e->ev_fork, 0));
+  const act_view v0 = view_at(e, 0, 0), v1 = view_at(e, b0, 1);
+  int st = decode_chain(e, &v0, 0, b0);
+  if (!st) st = decode_chain(e, &v1, b0, b1);
+  /* join even after an error, so that a capture in progress ends cleanly */
+  cudaEventRecord(e->ev_join, e->stream2);
+  cudaStreamWaitEvent(e->stream, e->ev_join, 0);
+  return st;
 }
 
 int gpt2_engine_decode_steps(gpt2_engine *e, int steps) {
@@ -775,7 +859,7 @@ int gpt2_engine_decode_steps(gpt2_engine *e, int steps) {
     return W8A8_OK;
   }
   if (!e->graph || e->graph_B != e->B || e->graph_out != e->out ||
-      e->graph_stride != e->out_stride) {
+      e->graph_stride != e->out_stride || e->graph_split != e->decode_split) {
     if (e->graph) {
       cudaGraphExecDestroy(e->graph);
       e->graph = NULL;
@@ -797,6 +881,7 @@ int gpt2_engine_decode_steps(gpt2_engine *e, int steps) {
     e->graph_B = e->B;
     e->graph_out = e->out;
     e->graph_stride = e->out_stride;
+    e->graph_split = e->decode_split;
   }
   for (int i = 0; i < steps; ++i) CUDA_TRY(e, cudaGraphLaunch(e->graph, e->stream));
   return W8A8_OK;
@@ -952,6 +1037,12 @@ int gpt2_engine_set_draws(gpt2_engine *e, int slot, const float *draws, int n) {
   /* stream-ordered: steps already queued read the slot's previous draws */
   CUDA_TRY(e, cudaMemcpyAsync(e->rnd + (int64_t)slot * e->cfg.ctx, draws, (size_t)n * 4,
                               cudaMemcpyHostToDevice, e->stream));
+  return W8A8_OK;
+}
+
+int gpt2_engine_set_decode_split(gpt2_engine *e, int halves) {
+  if (!e || (halves != 1 && halves != 2)) return W8A8_ERR_INVALID;
+  e->decode_split = halves;
   return W8A8_OK;
 }
 

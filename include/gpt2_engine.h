@@ -131,6 +131,10 @@ int gpt2_engine_set_draws(gpt2_engine *e, int slot, const float *draws, int n);
 
 /* Copy the logits of the last step ([B, vocab] bf16) to host memory. */
 int gpt2_engine_copy_logits(gpt2_engine *e, gpt2_bf16_t *host, int rows);
+/* Decode steps as one chain of kernels over all B slots (1, the default) or
+ * as two independent chains over the first ceil(B/2) and the other slots,
+ * run at the same time on two streams (2). Tokens are the same either way. */
+int gpt2_engine_set_decode_split(gpt2_engine *e, int halves);
 /* Enable (default) or disable CUDA-graph replay of decode steps. */
 int gpt2_engine_set_graphs(gpt2_engine *e, int enable);
 /* Kernel launches per decode step (for launch accounting). */

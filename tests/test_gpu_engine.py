@@ -234,3 +234,34 @@ def test_load_from_path_checks_manifest(cuda, tiny_image, tmp_path):
     with pytest.raises(W8A8Error, match="memory_summary"):
         eng.load_quant8(str(bin_path))
     eng.close()
+
+
+def test_decode_split_gives_the_same_tokens(cuda, tiny_image):
+    """Two concurrent decode chains (gpt2_engine_set_decode_split(2)) give every
+    sequence the tokens of one chain: graphed and eager, an odd batch, top-k
+    sampling and continuous batching."""
+    P = prompts(5, 12, TINY.vocab, seed=21)
+    eng = Engine(TINY, max_batch=8, max_tokens=8 * 12)
+    eng.load_quant8(tiny_image)
+    one = eng.generate(P, 20)
+    eng.set_decode_split(2)
+    np.testing.assert_array_equal(eng.generate(P, 20), one)
+    eng.set_graphs(False)
+    np.testing.assert_array_equal(eng.generate(P, 20), one)
+    eng.set_graphs(True)
+    R = np.random.default_rng(3).random((5, 20), dtype=np.float32)
+    eng.set_sampling(0.9, 40)
+    for b in range(5):
+        eng.set_draws(b, R[b])
+    sampled2 = eng.generate(P, 20)
+    eng.set_decode_split(1)
+    np.testing.assert_array_equal(eng.generate(P, 20), sampled2)
+    reqs = [(P[i][: 6 + i], 8 + i, R[i][: 8 + i]) for i in range(5)]
+    served1 = eng.serve(reqs, slots=3)
+    eng.set_decode_split(2)
+    served2 = eng.serve(reqs, slots=3)
+    for a, b in zip(served1, served2):
+        np.testing.assert_array_equal(a, b)
+    with pytest.raises(RuntimeError):
+        eng.set_decode_split(3)
+    eng.close()
