@@ -10,6 +10,7 @@ size of the large model (d_model 1280, 20 heads, context 1024).
     python -m c_gpt2_b200.profcase linear --m 64 --n 5120 --k 1280 --epi gelu
     python -m c_gpt2_b200.profcase decode [--model medium] [--batch 1] [--prompt 512] [--gen 256]
     python -m c_gpt2_b200.profcase gemv-chain [--model large] [--layers 36]
+    python -m c_gpt2_b200.profcase sample [--rows 64] [--top-k 40] [--temperature 0.8]
 
 Every case holds well under 1 GB on the device and exceeds the 126 MB L2 only
 where the workload itself does (the attention KV cache, the prefill
@@ -228,6 +229,29 @@ def decode(a) -> None:
           f" MB -> {gbs:.0f} GB/s")
 
 
+def sample(a) -> None:
+    """The next-token pick of a decode step over rows x 50257 bf16 logits
+    (N(0, 3)): greedy at temperature <= 0, else top-k sampling."""
+    V = 50257
+    g = torch.Generator(device="cuda").manual_seed(0)
+    logits = (3 * torch.randn((a.rows, V), device="cuda", generator=g)).to(torch.bfloat16)
+    rnd = torch.rand((a.rows,), device="cuda", generator=g)
+
+    def run():
+        if a.temperature > 0:
+            ops.sample_topk(logits, a.temperature, a.top_k, rnd)
+        else:
+            ops.sample_greedy(logits)
+
+    for _ in range(a.launches):
+        run()
+    torch.cuda.synchronize()
+    us = _time(run, a.timed)
+    what = f"top-{a.top_k} at T={a.temperature}" if a.temperature > 0 else "greedy"
+    print(f"sample {what}, {a.rows} rows x {V}: {us:.2f} us/launch, "
+          f"{a.rows * V * 2 / us / 1e3:.0f} GB/s of logits")
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     sub = ap.add_subparsers(dest="case", required=True)
@@ -256,6 +280,10 @@ def main(argv=None) -> None:
     p.add_argument("--n", type=int, required=True)
     p.add_argument("--k", type=int, required=True)
     p.add_argument("--epi", choices=sorted(EPI), default="bias")
+    p = sub.add_parser("sample")
+    p.add_argument("--rows", type=int, default=64)
+    p.add_argument("--top-k", type=int, default=40)
+    p.add_argument("--temperature", type=float, default=0.8)
     for p in sub.choices.values():
         p.add_argument("--launches", type=int, default=3, help="launches before timing")
         p.add_argument("--timed", type=int, default=20, help="launches timed after them")
@@ -267,7 +295,7 @@ def main(argv=None) -> None:
         _FLUSH = torch.ones((64 << 20,), dtype=torch.float32, device="cuda")
     {"attention-decode": attention_decode, "attention-prefill": attention_prefill,
      "layernorm-quant": layernorm_quant, "linear": linear, "decode": decode,
-     "gemv-chain": gemv_chain}[a.case](a)
+     "gemv-chain": gemv_chain, "sample": sample}[a.case](a)
     st = ops.device_error()
     if st:
         raise SystemExit(f"device error word {st}")
