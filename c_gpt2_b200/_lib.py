@@ -110,7 +110,7 @@ COMPAT_SYMBOLS = [
     "embeddings_cuda", "layernorm_cuda", "add_bias_cuda", "softmax_cuda", "casual_masking_cuda",
     "gelu_cuda", "concat_heads_cuda", "add_2d_cuda", "per_token_quant_cuda",
     "dequant_int32_to_bf16_cuda", "dot_2d_int8_fused_cuda", "attention_prefill_cuda",
-    "attention_decode_cuda", "lm_head_greedy_cuda",
+    "attention_decode_cuda", "lm_head_greedy_cuda", "lm_head_topk_cuda",
 ]
 COMPAT_SIGNATURES = {
     "embeddings_cuda": [_p, _p, _p, _p, _i, _i],
@@ -127,6 +127,7 @@ COMPAT_SIGNATURES = {
     "attention_prefill_cuda": [_p, _p, _p, _i, _p],
     "attention_decode_cuda": [_p, _p, _p, _i, _p, _p, _sz],
     "lm_head_greedy_cuda": [_p, _p, _p, _p],
+    "lm_head_topk_cuda": [_p, _p, _p, _f, _i, _p, _p],
 }
 
 

@@ -139,3 +139,13 @@ void lm_head_greedy_cuda(const act_t *xf, const weight_t *wte, act_t *logits, in
                            0, NULL, NULL),
         "lm_head_greedy_cuda (sample)", 1, vocab_size);
 }
+
+void lm_head_topk_cuda(const act_t *xf, const weight_t *wte, act_t *logits, float temperature,
+                       int top_k, const float *r_d, int *token_d) {
+  check(w8a8_lm_head((const gpt2_bf16_t *)xf, d_model, 1, d_model, (const gpt2_bf16_t *)wte,
+                     vocab_size, (gpt2_bf16_t *)logits, vocab_size, NULL),
+        "lm_head_topk_cuda (lm head)", 1, vocab_size);
+  check(w8a8_sample_topk((const gpt2_bf16_t *)logits, vocab_size, 1, vocab_size, temperature,
+                         top_k, r_d, 0, NULL, token_d, NULL, 0, NULL, NULL, 0, NULL),
+        "lm_head_topk_cuda (sample)", 1, vocab_size);
+}

@@ -93,6 +93,14 @@ void attention_decode_cuda(act_t *Q_d, act_t *k_cache_layer, act_t *v_cache_laye
  * *token_d (device int). wte is the untransposed embedding table. */
 void lm_head_greedy_cuda(const act_t *xf, const weight_t *wte, act_t *logits, int *token_d);
 
+/* The same LM head, then the token of gpt2.c:2223-2245 at temperature > 0:
+ * top_k_sample (gpt2.c:130-180; top_k clamped to [1, vocab]) and the draw with
+ * *r_d, a device float holding the host's (float)rand() / RAND_MAX. Among
+ * equal probabilities the lower index comes first (the reference's qsort
+ * leaves that order unspecified). temperature <= 0: the greedy token. */
+void lm_head_topk_cuda(const act_t *xf, const weight_t *wte, act_t *logits, float temperature,
+                       int top_k, const float *r_d, int *token_d);
+
 #ifdef __cplusplus
 }
 #endif

@@ -166,3 +166,33 @@ def test_topk_rejects_bad_arguments(cuda):
                                 o.data_ptr(), None, 0, None, None, 0, s) == _lib.W8A8_ERR_INVALID
     assert lib.w8a8_sample_topk(x.data_ptr(), 90000, 0, 50257, 1.0, 40, r.data_ptr(), 1, None,
                                 o.data_ptr(), None, 0, None, None, 0, s) == 0
+
+
+def test_reference_abi_lm_head_picks(cuda):
+    """lm_head_greedy_cuda and lm_head_topk_cuda (include/cuda_kernels.h, the
+    per-size drop-in library) give the LM head's logits and the token that the
+    runtime ABI's w8a8_lm_head + sampler give on the same buffers."""
+    lib = _lib.compat("small")
+    d, V = 768, 50257
+    rng = np.random.default_rng(12)
+    xf = to_dev_bf16(oracle.bf16_bits(rng.standard_normal(d).astype(np.float32)))
+    wte = to_dev_bf16(oracle.bf16_bits(rng.standard_normal((V, d)).astype(np.float32) * 0.08))
+    want_logits = ops.lm_head(xf[None], wte)
+    logits = torch.zeros((V,), dtype=torch.bfloat16, device="cuda:0")
+    tok = torch.full((1,), -1, dtype=torch.int32, device="cuda:0")
+    lib.lm_head_greedy_cuda(xf.data_ptr(), wte.data_ptr(), logits.data_ptr(), tok.data_ptr())
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(from_dev_bf16(logits), from_dev_bf16(want_logits[0]))
+    assert tok.item() == ops.sample_greedy(want_logits).item()
+    for temp, k, r in ((0.8, 40, 0.3), (1.3, 1000, 0.77), (0.6, 1, 0.5), (0.0, 40, 0.5)):
+        r_d = torch.tensor([r], dtype=torch.float32, device="cuda:0")
+        logits.zero_()
+        lib.lm_head_topk_cuda(xf.data_ptr(), wte.data_ptr(), logits.data_ptr(), temp, k,
+                              r_d.data_ptr(), tok.data_ptr())
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(from_dev_bf16(logits), from_dev_bf16(want_logits[0]))
+        probs = torch.zeros((1, V), dtype=torch.bfloat16, device="cuda:0")
+        want = ops.sample_topk(want_logits, temp, k, r_d, probs_out=probs).item()
+        assert tok.item() == want, (temp, k, r)
+        if temp > 0:
+            assert want == oracle.sample_topk(from_dev_bf16(probs)[0], k, r)
