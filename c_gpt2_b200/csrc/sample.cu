@@ -312,6 +312,9 @@ constexpr int kTopkBins = 0x3F81;  // keys of +0.0 .. 1.0
 constexpr size_t kTopkHistBytes = ((size_t)kTopkBins * 4 + 15) / 16 * 16;
 constexpr int kTopkMaxVocab = 81920;
 
+// (A row whose logits hold NaN or infinities gives probabilities outside
+// [0, 1]; they count as 1.0, so every index stays in range and the token is
+// some id in [0, V).)
 __device__ __forceinline__ int topk_key(uint16_t p) { return p <= 0x3F80 ? (int)p : 0x3F80; }
 
 __global__ void __launch_bounds__(kTopkThreads)
