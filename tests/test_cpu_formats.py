@@ -159,3 +159,23 @@ def test_engine_manifest_check_in_c():
     assert check(DIMS["large"], MANIFESTS["large"].replace("gpt2-large", "gpt2-xl"))[0] \
         == W8A8_ERR_INVALID
     assert check(DIMS["large"], "{}")[0] == W8A8_ERR_INVALID
+
+
+def test_engine_manifest_check_any_json_layout():
+    """The C check reads the fields wherever json.dump puts them: compact
+    separators, reordered keys and CRLF line ends are the same manifest;
+    an escaped string is refused rather than misread."""
+    import ctypes as C
+    from c_gpt2_b200._lib import EngineConfig, W8A8_ERR_INVALID, W8A8_OK, core
+
+    dims = DIMS["medium"]
+    cfg = EngineConfig(dims.d_model, dims.n_layer, dims.n_head, dims.vocab, dims.ctx, 1, 1)
+    m = json.loads(MANIFESTS["medium"])
+    texts = [json.dumps(m, separators=(",", ":")),
+             json.dumps(dict(reversed(list(m.items()))), indent=4),
+             MANIFESTS["medium"].replace("\n", "\r\n")]
+    for t in texts:
+        assert core().gpt2_quant8_check_manifest(C.byref(cfg), t.encode(), None, 0) == W8A8_OK
+    bad = MANIFESTS["medium"].replace('"amax/127"', '"amax\\/127"')
+    assert core().gpt2_quant8_check_manifest(C.byref(cfg), bad.encode(), None, 0) \
+        == W8A8_ERR_INVALID
