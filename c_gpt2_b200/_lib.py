@@ -99,6 +99,7 @@ SIGNATURES = {
     "gpt2_engine_set_sampling": (_i, [_p, _f, _i]),
     "gpt2_quant8_check_manifest": (_i, [_p, C.c_char_p, C.c_char_p, C.c_size_t]),
     "gpt2_engine_set_draws": (_i, [_p, _i, _p, _i]),
+    "gpt2_reference_draws": (_i, [C.c_uint, _p, _i]),
     "gpt2_engine_launches_per_decode_step": (_i, [_p]),
     "gpt2_engine_launches_per_prefill": (_i, [_p]),
     "gpt2_engine_stream": (_p, [_p]),

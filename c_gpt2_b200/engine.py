@@ -157,6 +157,16 @@ class Engine:
         self._check(core().gpt2_engine_set_decode_split(self._h, int(halves)),
                     "gpt2_engine_set_decode_split")
 
+    @staticmethod
+    def reference_draws(n: int, seed: int = 1) -> np.ndarray:
+        """(float)rand() / RAND_MAX for n calls of glibc's rand() after srand(seed):
+        the reference's draws (gpt2.c:2231; it never seeds: seed 1)."""
+        out = np.zeros((n,), dtype=np.float32)
+        st = core().gpt2_reference_draws(seed, out.ctypes.data if n else None, n)
+        if st != _lib.W8A8_OK:
+            raise ValueError(f"gpt2_reference_draws: status {st}")
+        return out
+
     def set_graphs(self, enable: bool) -> None:
         self._check(core().gpt2_engine_set_graphs(self._h, 1 if enable else 0),
                     "gpt2_engine_set_graphs")

@@ -1030,6 +1030,24 @@ int gpt2_engine_set_sampling(gpt2_engine *e, float temperature, int top_k) {
   return W8A8_OK;
 }
 
+int gpt2_reference_draws(unsigned seed, float *out, int n) {
+  if (n < 0 || (n > 0 && !out)) return W8A8_ERR_INVALID;
+  /* glibc's rand() is random() on a 128-byte TYPE_3 state; initstate_r with a
+   * 128-byte buffer and the same seed gives the same sequence without
+   * touching the process's own generator */
+  char state[128];
+  struct random_data rd;
+  memset(&rd, 0, sizeof rd);
+  memset(state, 0, sizeof state);
+  if (initstate_r(seed, state, sizeof state, &rd) != 0) return W8A8_ERR_INVALID;
+  for (int i = 0; i < n; ++i) {
+    int32_t v;
+    random_r(&rd, &v);
+    out[i] = (float)v / RAND_MAX;  /* gpt2.c:2231 */
+  }
+  return W8A8_OK;
+}
+
 int gpt2_engine_set_draws(gpt2_engine *e, int slot, const float *draws, int n) {
   if (!e || slot < 0 || slot >= e->cfg.max_batch || n < 0 || n > e->cfg.ctx || (n > 0 && !draws))
     return W8A8_ERR_INVALID;

@@ -128,6 +128,11 @@ int gpt2_engine_set_sampling(gpt2_engine *e, float temperature, int top_k);
 /* draws[0..n) (host memory, n <= ctx) become slot `slot`'s draws from its
  * first token on; ordered on the engine stream after the work queued so far. */
 int gpt2_engine_set_draws(gpt2_engine *e, int slot, const float *draws, int n);
+/* The draws of the reference's sampling loop for one sequence: out[i] =
+ * (float)rand() / RAND_MAX at the i-th call of glibc's rand() after
+ * srand(seed) (gpt2.c:2231; the reference never seeds, which is seed 1),
+ * from a private generator state (the process's rand() is not touched). */
+int gpt2_reference_draws(unsigned seed, float *out, int n);
 
 /* Copy the logits of the last step ([B, vocab] bf16) to host memory. */
 int gpt2_engine_copy_logits(gpt2_engine *e, gpt2_bf16_t *host, int rows);

@@ -108,3 +108,26 @@ def test_top_k_clamps_k():
     assert oracle.sample_topk(p, 0, 0.5) == oracle.sample_topk(p, 1, 0.5) == 99
     i_all, _ = oracle.top_k(p, 10**6)
     assert len(i_all) == 100
+
+
+def test_reference_draws_are_glibc_rand():
+    """gpt2_reference_draws reproduces the reference's r = (float)rand() /
+    RAND_MAX (gpt2.c:2231) from its own generator state."""
+    from c_gpt2_b200.engine import Engine
+
+    libc = C.CDLL(None)
+    for seed in (1, 7, 123456789):
+        libc.srand(seed)
+        want = np.array([np.float32(libc.rand()) / np.float32(2147483647) for _ in range(2000)],
+                        np.float32)
+        got = Engine.reference_draws(2000, seed)
+        np.testing.assert_array_equal(got, want)
+        assert got.min() >= 0.0 and got.max() <= 1.0
+    # the process's own rand() stream is untouched by the helper
+    libc.srand(5)
+    a = [libc.rand() for _ in range(3)]
+    libc.srand(5)
+    libc.rand()
+    Engine.reference_draws(10, 5)
+    assert [libc.rand(), libc.rand()] == a[1:]
+    assert Engine.reference_draws(0).size == 0
