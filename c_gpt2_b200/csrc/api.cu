@@ -127,6 +127,32 @@ extern "C" int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, cons
   return dispatch_linear(Xq, K, W, a, (cudaStream_t)stream);
 }
 
+namespace w8a8 {
+
+// Workspace bytes w8a8_linear would read for these operands given one: nonzero
+// only where its dispatch ends in the channel-major tcgen05 GEMM split over K
+// (a few tokens whose operands the cluster kernel cannot take). The GEMV, the
+// token-major GEMM and the cluster GEMM read none. 0 for arguments that
+// w8a8_linear refuses, which it then reports itself.
+size_t linear_workspace_used(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W,
+                             const float *sW, const gpt2_bf16_t *bias, int N, int epilogue,
+                             const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy) {
+  int epi;
+  switch (epilogue) {
+    case W8A8_EPI_DEQUANT: epi = EPI_DEQUANT; break;
+    case W8A8_EPI_BIAS: epi = EPI_BIAS; break;
+    case W8A8_EPI_BIAS_RESID: epi = EPI_RESID; break;
+    case W8A8_EPI_BIAS_GELU: epi = EPI_GELU; break;
+    default: return 0;
+  }
+  if (M <= 0 || N <= 0 || K <= 0 || ready() != W8A8_OK) return 0;
+  if (!(M >= kTcMinM && tc_ok_i8(Xq, K, W, K))) return 0;  // GEMV
+  LinearArgs a = make_args(epi, M, N, K, sX, sW, bias, R, ldr, Y, ldy);
+  return gemm_i8_workspace_used(Xq, K, a);
+}
+
+}  // namespace w8a8
+
 extern "C" size_t w8a8_linear_workspace_size(int M, int N) {
   if (M <= 0 || N <= 0) return 0;
   return linear_workspace_bytes(M, N);

@@ -832,7 +832,7 @@ int launch_attention_decode(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     if (cudaLaunchKernelEx(&cfg, attention_decode_cluster_kernel, a) != cudaSuccess) {

@@ -450,7 +450,7 @@ static int launch_cluster(const int8_t *W, const int8_t *X, int64_t ldx, const L
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   if (cudaLaunchKernelEx(&cfg, gemm_cm_cluster_kernel<EPI>, tmW, tmX, a) != cudaSuccess) {

@@ -901,6 +901,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 static int round_up32(int x) { return (x + 31) & ~31; }
 
+// Token tile of the channel-major orientation (weights as the MMA's M = 128
+// operand, the tokens as its N).
+static int cm_token_tile(int M) { return M >= 256 ? 256 : round_up32(M < 32 ? 32 : M); }
+
+// K splits of a channel-major int8 GEMM given a workspace: when the output
+// tiles alone cannot occupy the GPU, about one (tile, K range) unit per SM.
+// Returns 1 (no split, the workspace is not read) otherwise; *kb_per is the
+// number of 128-byte K blocks per split.
+static int cm_ksplit(int M, int N, int K, int sm_count, int *kb_per) {
+  const int kblocks = (K + kBoxBytes - 1) / kBoxBytes;
+  const int BN = cm_token_tile(M);
+  const int tiles0 = ((N + kBM - 1) / kBM) * ((M + BN - 1) / BN);
+  *kb_per = kblocks;
+  if (2 * tiles0 > sm_count || kblocks <= 1) return 1;
+  int ks = sm_count / tiles0;
+  if (ks > kblocks) ks = kblocks;
+  const int per = (kblocks + ks - 1) / ks;
+  const int splits = (kblocks + per - 1) / per;
+  if (splits > 1) *kb_per = per;
+  return splits;
+}
+
 template <int KIND, int EPI, bool CM, bool RT = false>
 static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const LinearArgs &la,
                      cudaStream_t stream) {
@@ -917,7 +939,7 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   memset(&tmR, 0, sizeof(tmR));
   memset(&tmRb, 0, sizeof(tmRb));
   if (CM) {  // A = weights, B = tokens
-    a.BN = M >= 256 ? 256 : round_up32(M < 32 ? 32 : M);
+    a.BN = cm_token_tile(M);
     st = make_tmap_2d(&tmA, W, dt, (uint64_t)N, (uint64_t)K, (uint64_t)K * esz, kBoxBytes / esz,
                       kBM);
     if (st) return st;
@@ -964,20 +986,15 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   a.ws = nullptr;
   a.tickets = nullptr;
   const int tiles0 = a.a_tiles * a.b_tiles;
-  if (CM && KIND == 0 && la.workspace && 2 * tiles0 <= ctx->sm_count && a.kblocks > 1 &&
+  if (CM && KIND == 0 && la.workspace &&
       la.workspace_bytes >= linear_workspace_bytes(M, N)) {
     // Too few output tiles to occupy the GPU (decode): split K so that about
     // one unit lands on every SM.
-    int ks = ctx->sm_count / tiles0;
-    if (ks > a.kblocks) ks = a.kblocks;
-    a.kb_per = (a.kblocks + ks - 1) / ks;
-    a.ksplit = (a.kblocks + a.kb_per - 1) / a.kb_per;
+    a.ksplit = cm_ksplit(M, N, K, ctx->sm_count, &a.kb_per);
     if (a.ksplit > 1) {
       uint8_t *w = (uint8_t *)la.workspace;
       a.ws = (int32_t *)w;
       a.tickets = (int *)(w + (((size_t)M * N * 4 + 255) & ~(size_t)255));
-    } else {
-      a.kb_per = a.kblocks;
     }
   }
   static bool attr_set[64] = {};  // per template instantiation and device
@@ -1003,17 +1020,6 @@ size_t linear_workspace_bytes(int M, int N) {
   return (((size_t)M * N * 4 + 255) & ~(size_t)255) + tiles * 4;
 }
 
-// W8A8_CLUSTER_GEMM=0 in the environment keeps decode GEMMs on the
-// global-workspace split-K path (for comparison).
-static bool getenv_cluster_on() {
-  static int on = -1;
-  if (on < 0) {
-    const char *v = getenv("W8A8_CLUSTER_GEMM");
-    on = (v && v[0] == '0') ? 0 : 1;
-  }
-  return on == 1;
-}
-
 // Token-major needs whole 32-column chunks and 16-byte aligned output rows.
 static bool token_major_ok(const LinearArgs &a) {
   if (a.M <= kBM || (a.N & 31)) return false;
@@ -1024,6 +1030,13 @@ static bool token_major_ok(const LinearArgs &a) {
       (!aligned16(a.Kc) || !aligned16(a.Vc) || (a.dseg & 31) || (a.seq_stride % 8)))
     return false;
   return true;
+}
+
+// Decode-sized GEMMs whose 128-channel tiles cannot occupy the GPU take the
+// cluster split-K kernel when its operand rules hold.
+static bool takes_cluster(const LinearArgs &a, const void *X, int64_t ldx, int sm_count) {
+  const int tiles = (a.N + kBM - 1) / kBM;
+  return 2 * tiles <= sm_count && cluster_gemm_ok(a, X, ldx);
 }
 
 template <int EPI>
@@ -1042,10 +1055,17 @@ static int launch_i8(const int8_t *W, const int8_t *X, int64_t ldx, const Linear
   int st;
   DeviceCtx *ctx = device_ctx(&st);
   if (!ctx) return st;
-  const int tiles = (a.N + kBM - 1) / kBM;
-  if (2 * tiles <= ctx->sm_count && cluster_gemm_ok(a, X, ldx) && getenv_cluster_on())
-    return gemm_cluster_i8(W, X, ldx, a, s);
+  if (takes_cluster(a, X, ldx, ctx->sm_count)) return gemm_cluster_i8(W, X, ldx, a, s);
   return launch_tc<0, EPI, true>(W, X, ldx, a, s);
+}
+
+size_t gemm_i8_workspace_used(const int8_t *X, int64_t ldx, const LinearArgs &a) {
+  if (token_major_ok(a)) return 0;
+  int st, kb_per;
+  DeviceCtx *ctx = device_ctx(&st);
+  if (!ctx || takes_cluster(a, X, ldx, ctx->sm_count)) return 0;
+  if (cm_ksplit(a.M, a.N, a.K, ctx->sm_count, &kb_per) <= 1) return 0;
+  return linear_workspace_bytes(a.M, a.N);
 }
 
 int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,

@@ -90,12 +90,20 @@ struct ReduceArgs {
 // gemm_tc.cu
 int gemm_tc_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,
                cudaStream_t stream);
+// Workspace bytes gemm_tc_i8 reads for these operands (a.workspace set):
+// nonzero only where it takes the channel-major kernel split over K.
+size_t gemm_i8_workspace_used(const int8_t *X, int64_t ldx, const LinearArgs &a);
 int gemm_tc_bf16(const uint16_t *W, const uint16_t *X, int64_t ldx, const LinearArgs &a,
                  cudaStream_t stream);
 // gemm_cluster.cu: decode-sized GEMMs (M <= 128) with split-K in a cluster
 bool cluster_gemm_ok(const LinearArgs &a, const void *X, int64_t ldx);
 int gemm_cluster_i8(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &a,
                     cudaStream_t stream);
+// api.cu: workspace bytes w8a8_linear reads for these operands (0 where the
+// chosen kernel reads none)
+size_t linear_workspace_used(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W,
+                             const float *sW, const uint16_t *bias, int N, int epilogue,
+                             const uint16_t *R, int64_t ldr, uint16_t *Y, int64_t ldy);
 // gemv_i8.cu
 int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const LinearArgs &a,
                    cudaStream_t s);

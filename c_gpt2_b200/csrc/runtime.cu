@@ -5,10 +5,6 @@
 
 #include "runtime.cuh"
 
-#include <mutex>
-#include <utility>
-#include <vector>
-
 namespace w8a8 {
 
 // One error word per device. Kernels record the first failure here (bounded
@@ -16,35 +12,6 @@ namespace w8a8 {
 __device__ int g_device_error;
 
 static DeviceCtx g_ctx[64];
-
-void prefer_max_carveout(const void *func) {
-  static std::mutex mu;
-  static std::vector<std::pair<int, const void *>> done;
-  static int mode = -1;  // off unless W8A8_CARVEOUT=1
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return;
-  std::lock_guard<std::mutex> lock(mu);
-  if (mode < 0) {
-    const char *v = getenv("W8A8_CARVEOUT");
-    mode = (v && v[0] == '1') ? 1 : 0;
-  }
-  if (!mode) return;
-  for (const auto &d : done)
-    if (d.first == dev && d.second == func) return;
-  if (cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-    cudaGetLastError();  // a refused hint is not an error of the launch that follows
-  done.emplace_back(dev, func);
-}
-
-bool pdl_enabled() {
-  static int enabled = -1;
-  if (enabled < 0) {
-    const char *v = getenv("W8A8_PDL");
-    enabled = (v && v[0] == '0') ? 0 : 1;
-  }
-  return enabled == 1;
-}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,

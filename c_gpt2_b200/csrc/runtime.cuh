@@ -31,23 +31,11 @@ int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, 
                  uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows,
                  int swizzle_bytes = 128);
 
-// Whether kernels are launched with programmatic stream serialization
-// (W8A8_PDL=0 in the environment turns it off).
-bool pdl_enabled();
-
-// With W8A8_CARVEOUT=1 in the environment, give `func` the largest
-// shared-memory carveout, once per kernel and device, so that an SM never
-// changes its L1/shared split between two kernels (the tensor-core GEMM needs
-// ~200 KB of shared memory per CTA). Off by default: measured slower, since
-// the kernels that stream the KV cache lose their L1.
-void prefer_max_carveout(const void *func);
-
 // Launch `kernel` with programmatic dependent launch allowed: it may begin
 // while the preceding kernel of the stream finishes (see pdl_wait()).
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                              cudaStream_t stream, Args &&...args) {
-  prefer_max_carveout(reinterpret_cast<const void *>(kernel));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -55,7 +43,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);

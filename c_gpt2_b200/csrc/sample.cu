@@ -269,7 +269,7 @@ int launch_greedy_sample(const uint16_t *logits, int64_t ldl, int M, int V, int3
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     if (cudaLaunchKernelEx(&cfg, greedy_sample_cluster_kernel, logits, ldl, V, C, out, append_to,

@@ -106,14 +106,17 @@ int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W
  * No counterpart in the reference. For callers that cannot allocate device
  * memory (a host that sizes all device memory once at start-up, a plugin whose
  * host owns the allocator, a path that must not pay cudaMalloc's implicit
- * synchronisation): the split-K scratch comes from a fixed array compiled into
- * this library (W8A8_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the
- * library until exit). Shapes whose scratch would exceed it, i.e.
- * M*N*4 bytes plus one 4-byte counter per 128 x 32 output tile, return
- * W8A8_ERR_UNSUPPORTED. Nothing is allocated. The first call on a device
- * looks up the array's device address and must come before any stream capture.
- * All calls share the array: calls whose GPU work overlaps race and must be
- * serialised by the caller. Same arguments and results as w8a8_linear. */
+ * synchronisation). Where w8a8_linear would split a few-token GEMM over K into
+ * a caller's workspace (operands the cluster kernel cannot take), this entry
+ * point uses a fixed array compiled into this library instead
+ * (W8A8_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the library until
+ * exit), clearing the part it uses first; such shapes needing more than the
+ * array, i.e. M*N*4 bytes plus one 4-byte counter per 128 x 32 output tile,
+ * return W8A8_ERR_UNSUPPORTED. Every other shape runs as w8a8_linear with no
+ * workspace. Nothing is allocated. The first call on a device looks up the
+ * array's device address and must come before any stream capture. All calls
+ * share the array: calls whose GPU work overlaps race and must be serialised
+ * by the caller. Same arguments and results as w8a8_linear. */
 #define W8A8_NOALLOC_SCRATCH_BYTES (4u << 20)
 int w8a8_linear_noalloc(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W,
                         const float *sW, const gpt2_bf16_t *bias, int N, int epilogue,

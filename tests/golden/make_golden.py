@@ -1,7 +1,7 @@
 """Regenerate the golden fixtures of tests/golden/ from the reference itself.
 
-Runs only where the reference tree is mounted (REF_ROOT, default
-/root/reference); the tests read the fixtures it wrote and never run it.
+Runs only where the reference tree is mounted (its root in the REF_ROOT
+environment variable); the tests read the fixtures it wrote and never run it.
 Outputs:
 
   weight_quant.npz    the reference's per-channel quantizer
