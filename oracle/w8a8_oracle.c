@@ -15,12 +15,19 @@
  * expf/tanhf (C library versions here). The cuBLAS GEMMs of the reference
  * (INT8 -> exact integers; bf16 attention and LM head -> fp32 sums in an
  * unspecified order) are restated as sequential sums.
+ *
+ * Loops over independent output elements (rows, channels, heads, vocabulary
+ * entries) are spread over a small pthread pool (ORC_THREADS, default: the
+ * online CPUs); every element is still computed by the same sequential
+ * expression, so results do not depend on the thread count.
  */
 #include "w8a8_oracle.h"
 
 #include <math.h>
+#include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 /* fmaf() is a slow library call on a plain x86-64 build; the hot loops are
  * cloned for CPUs with an FMA unit (same IEEE results either way). */
@@ -29,6 +36,95 @@
 #else
 #define ORC_HOT
 #endif
+
+/* ---- parallel for over [0, n): a persistent pthread pool ----
+ * fn(ctx, lo, hi) runs on contiguous chunks; the calling thread takes chunk 0.
+ * One region at a time (a mutex); a forked child rebuilds the pool. */
+typedef void (*orc_range_fn)(void *ctx, long lo, long hi);
+
+#define ORC_MAX_THREADS 64
+static struct {
+  pthread_mutex_t region, mu;
+  pthread_cond_t go, done;
+  int nthreads;
+  pid_t pid;
+  unsigned long gen;
+  int pending;
+  orc_range_fn fn;
+  void *ctx;
+  long n, chunk;
+} g_pool = {PTHREAD_MUTEX_INITIALIZER, PTHREAD_MUTEX_INITIALIZER, PTHREAD_COND_INITIALIZER,
+            PTHREAD_COND_INITIALIZER, 0, 0, 0, 0, NULL, NULL, 0, 0};
+
+static void pool_run_chunk(int i) {
+  const long lo = (long)i * g_pool.chunk;
+  long hi = lo + g_pool.chunk;
+  if (hi > g_pool.n) hi = g_pool.n;
+  if (lo < hi) g_pool.fn(g_pool.ctx, lo, hi);
+}
+
+static void *pool_worker(void *arg) {
+  const int id = (int)(long)arg;
+  unsigned long seen = 0;
+  pthread_mutex_lock(&g_pool.mu);
+  for (;;) {
+    while (g_pool.gen == seen) pthread_cond_wait(&g_pool.go, &g_pool.mu);
+    seen = g_pool.gen;
+    pthread_mutex_unlock(&g_pool.mu);
+    pool_run_chunk(id);
+    pthread_mutex_lock(&g_pool.mu);
+    if (--g_pool.pending == 0) pthread_cond_signal(&g_pool.done);
+  }
+  return NULL;
+}
+
+static void pool_start(void) {
+  int t = 0;
+  const char *env = getenv("ORC_THREADS");
+  if (env) t = atoi(env);
+  if (t <= 0) t = (int)sysconf(_SC_NPROCESSORS_ONLN);
+  if (t < 1) t = 1;
+  if (t > ORC_MAX_THREADS) t = ORC_MAX_THREADS;
+  g_pool.nthreads = 1;
+  g_pool.gen = 0;
+  g_pool.pid = getpid();
+  pthread_attr_t attr;
+  pthread_attr_init(&attr);
+  pthread_attr_setdetachstate(&attr, PTHREAD_CREATE_DETACHED);
+  for (int i = 1; i < t; ++i) {
+    pthread_t th;
+    if (pthread_create(&th, &attr, pool_worker, (void *)(long)i) != 0) break;
+    g_pool.nthreads = i + 1;
+  }
+  pthread_attr_destroy(&attr);
+}
+
+/* min_work: elements below which one thread does it all */
+static void orc_parallel(long n, long min_work, orc_range_fn fn, void *ctx) {
+  if (n <= 0) return;
+  pthread_mutex_lock(&g_pool.region);
+  if (g_pool.pid != getpid()) pool_start();
+  const int workers = g_pool.nthreads;
+  if (workers == 1 || n < min_work) {
+    pthread_mutex_unlock(&g_pool.region);
+    fn(ctx, 0, n);
+    return;
+  }
+  pthread_mutex_lock(&g_pool.mu);
+  g_pool.fn = fn;
+  g_pool.ctx = ctx;
+  g_pool.n = n;
+  g_pool.chunk = (n + workers - 1) / workers;
+  g_pool.pending = workers - 1;
+  g_pool.gen++;
+  pthread_cond_broadcast(&g_pool.go);
+  pthread_mutex_unlock(&g_pool.mu);
+  pool_run_chunk(0);
+  pthread_mutex_lock(&g_pool.mu);
+  while (g_pool.pending > 0) pthread_cond_wait(&g_pool.done, &g_pool.mu);
+  pthread_mutex_unlock(&g_pool.mu);
+  pthread_mutex_unlock(&g_pool.region);
+}
 
 /* ---- bf16 ---- */
 float orc_bf2f(uint16_t v) {
@@ -48,9 +144,20 @@ uint16_t orc_f2bf(float f) {
 static float rbf(float f) { return orc_bf2f(orc_f2bf(f)); }
 
 /* ---- per-token quantization: cuda/activation_quant.cu:54-91 ---- */
-void orc_quant_rows(const uint16_t *x, int M, int K, int8_t *xq, float *sx) {
-  for (int m = 0; m < M; ++m) {
-    const uint16_t *row = x + (size_t)m * K;
+typedef struct {
+  const uint16_t *x;
+  int K;
+  int8_t *xq;
+  float *sx;
+} quant_job;
+
+static void quant_range(void *ctx, long m0, long m1) {
+  const quant_job *j = (const quant_job *)ctx;
+  const int K = j->K;
+  for (long m = m0; m < m1; ++m) {
+    const uint16_t *row = j->x + (size_t)m * K;
+    int8_t *xq = j->xq;
+    float *sx = j->sx;
     float amax = 0.0f;
     for (int k = 0; k < K; ++k) amax = fmaxf(amax, fabsf(orc_bf2f(row[k])));
     const float scale = amax > 0.0f ? amax / 127.0f : 1.0f;
@@ -66,17 +173,35 @@ void orc_quant_rows(const uint16_t *x, int M, int K, int8_t *xq, float *sx) {
   }
 }
 
+void orc_quant_rows(const uint16_t *x, int M, int K, int8_t *xq, float *sx) {
+  quant_job j = {x, K, xq, sx};
+  orc_parallel(M, 2, quant_range, &j);
+}
+
 /* ---- INT8 GEMM: the cublasGemmEx call of gpt2.c:404-415 ---- */
-ORC_HOT void orc_gemm_s32(const int8_t *xq, int M, int K, const int8_t *W, int N, int32_t *Y) {
-  for (int m = 0; m < M; ++m) {
-    const int8_t *a = xq + (size_t)m * K;
-    for (int n = 0; n < N; ++n) {
-      const int8_t *b = W + (size_t)n * K;
-      int32_t acc = 0;
-      for (int k = 0; k < K; ++k) acc += (int32_t)a[k] * (int32_t)b[k];
-      Y[(size_t)m * N + n] = acc;
-    }
+ORC_HOT static int32_t dot_i8(const int8_t *a, const int8_t *b, int K) {
+  int32_t acc = 0;
+  for (int k = 0; k < K; ++k) acc += (int32_t)a[k] * (int32_t)b[k];
+  return acc;
+}
+
+typedef struct {
+  const int8_t *xq, *W;
+  int M, K, N;
+  int32_t *Y;
+} gemm_job;
+
+static void gemm_range(void *ctx, long i0, long i1) {
+  const gemm_job *j = (const gemm_job *)ctx;
+  for (long i = i0; i < i1; ++i) {
+    const long m = i / j->N, n = i % j->N;
+    j->Y[i] = dot_i8(j->xq + (size_t)m * j->K, j->W + (size_t)n * j->K, j->K);
   }
+}
+
+void orc_gemm_s32(const int8_t *xq, int M, int K, const int8_t *W, int N, int32_t *Y) {
+  gemm_job j = {xq, W, M, K, N, Y};
+  orc_parallel((long)M * N, 4096, gemm_range, &j);
 }
 
 /* dequant_int32_to_bf16_kernel (activation_quant.cu:128-130) */
@@ -93,14 +218,25 @@ float orc_gelu(float val) {
 /* ---- fused linear epilogues:
  * dequant (activation_quant.cu:129) -> add_bias (add_bias.cu:14)
  * -> add_2d residual (add_2d.cu:14) or gelu (gelu.cu:12-16) ---- */
-void orc_linear(const int8_t *xq, const float *sx, int M, int K, const int8_t *W,
-                const float *sw, const uint16_t *bias, int N, int epi, const uint16_t *R,
-                uint16_t *Y) {
-  int32_t *acc = (int32_t *)malloc((size_t)N * sizeof(int32_t));
-  for (int m = 0; m < M; ++m) {
-    orc_gemm_s32(xq + (size_t)m * K, 1, K, W, N, acc);
-    for (int n = 0; n < N; ++n) {
-      float t = dequant(acc[n], sw[n], sx[m]);
+typedef struct {
+  const int8_t *xq, *W;
+  const float *sx, *sw;
+  const uint16_t *bias, *R;
+  int K, N, epi;
+  uint16_t *Y;
+} linear_job;
+
+static void linear_range(void *ctx, long i0, long i1) {
+  const linear_job *j = (const linear_job *)ctx;
+  const int K = j->K, N = j->N, epi = j->epi;
+  const float *sx = j->sx, *sw = j->sw;
+  const uint16_t *bias = j->bias, *R = j->R;
+  uint16_t *Y = j->Y;
+  for (long i = i0; i < i1; ++i) {
+    {
+      const long m = i / N, n = i % N;
+      const int32_t acc = dot_i8(j->xq + (size_t)m * K, j->W + (size_t)n * K, K);
+      float t = dequant(acc, sw[n], sx[m]);
       float out;
       if (epi == ORC_EPI_DEQUANT) {
         out = t;
@@ -116,7 +252,13 @@ void orc_linear(const int8_t *xq, const float *sx, int M, int K, const int8_t *W
       Y[(size_t)m * N + n] = orc_f2bf(out);
     }
   }
-  free(acc);
+}
+
+void orc_linear(const int8_t *xq, const float *sx, int M, int K, const int8_t *W,
+                const float *sw, const uint16_t *bias, int N, int epi, const uint16_t *R,
+                uint16_t *Y) {
+  linear_job j = {xq, W, sx, sw, bias, R, K, N, epi, Y};
+  orc_parallel((long)M * N, 4096, linear_range, &j);
 }
 
 /* ---- LayerNorm: cuda/layernorm.cu:23-77 ----
@@ -129,10 +271,21 @@ static float tree1024(float *s) {
   return s[0];
 }
 
-ORC_HOT void orc_layernorm(const uint16_t *x, int M, int d, const uint16_t *gamma,
-                   const uint16_t *beta, float eps, uint16_t *y) {
-  float s[1024];
-  for (int m = 0; m < M; ++m) {
+typedef struct {
+  const uint16_t *x, *gamma, *beta;
+  int d;
+  float eps;
+  uint16_t *y;
+} ln_job;
+
+ORC_HOT static void ln_range(void *ctx, long m0, long m1) {
+  const ln_job *j = (const ln_job *)ctx;
+  const uint16_t *x = j->x, *gamma = j->gamma, *beta = j->beta;
+  const int d = j->d;
+  const float eps = j->eps;
+  uint16_t *y = j->y;
+  for (long m = m0; m < m1; ++m) {
+    float s[1024];
     const uint16_t *row = x + (size_t)m * d;
     for (int t = 0; t < 1024; ++t) {
       float sum = 0.0f;
@@ -155,6 +308,12 @@ ORC_HOT void orc_layernorm(const uint16_t *x, int M, int d, const uint16_t *gamm
       y[(size_t)m * d + i] = orc_f2bf(fmaf(normalized, orc_bf2f(gamma[i]), orc_bf2f(beta[i])));
     }
   }
+}
+
+void orc_layernorm(const uint16_t *x, int M, int d, const uint16_t *gamma, const uint16_t *beta,
+                   float eps, uint16_t *y) {
+  ln_job j = {x, gamma, beta, d, eps, y};
+  orc_parallel(M, 2, ln_range, &j);
 }
 
 /* ---- softmax row: cuda/softmax.cu:31-91 (temperature t, 256-thread tree) ----
@@ -203,27 +362,53 @@ ORC_HOT static void attend_row(const uint16_t *q, const uint16_t *K, const uint1
   }
 }
 
-/* Causal attention for rows [q0, q0+nq) of one sequence whose K/V cache rows
- * are [0, q0+nq). Q/O rows have stride d; K/V rows stride d. */
-void orc_attention(const uint16_t *Q, const uint16_t *K, const uint16_t *V, int q0, int nq,
-                   int n_head, uint16_t *O) {
-  const int d = n_head * 64;
-  const int nmax = q0 + nq;
+typedef struct {
+  const uint16_t *Q, *K, *V;
+  int q0, nq, n_head;
+  uint16_t *O;
+} attn_job;
+
+/* work item w: head w % n_head of row r = w / n_head taken in the order
+ * 0, nq-1, 1, nq-2, ..., so that every contiguous chunk of items mixes short
+ * and long causal rows */
+static void attn_range(void *ctx, long w0, long w1) {
+  const attn_job *j = (const attn_job *)ctx;
+  const int d = j->n_head * 64;
+  const int nmax = j->q0 + j->nq;
   uint16_t *srow = (uint16_t *)malloc((size_t)nmax * 2);
   uint16_t *prow = (uint16_t *)malloc((size_t)nmax * 2);
-  for (int i = 0; i < nq; ++i)
-    for (int h = 0; h < n_head; ++h)
-      attend_row(Q + (size_t)i * d + h * 64, K + h * 64, V + h * 64, d, q0 + i + 1,
-                 O + (size_t)i * d + h * 64, srow, prow);
+  for (long w = w0; w < w1; ++w) {
+    const int h = (int)(w % j->n_head), r = (int)(w / j->n_head);
+    const int i = (r & 1) ? j->nq - 1 - r / 2 : r / 2;
+    attend_row(j->Q + (size_t)i * d + h * 64, j->K + h * 64, j->V + h * 64, d, j->q0 + i + 1,
+               j->O + (size_t)i * d + h * 64, srow, prow);
+  }
   free(srow);
   free(prow);
 }
 
+/* Causal attention for rows [q0, q0+nq) of one sequence whose K/V cache rows
+ * are [0, q0+nq). Q/O rows have stride d; K/V rows stride d. */
+void orc_attention(const uint16_t *Q, const uint16_t *K, const uint16_t *V, int q0, int nq,
+                   int n_head, uint16_t *O) {
+  attn_job j = {Q, K, V, q0, nq, n_head, O};
+  orc_parallel((long)nq * n_head, 2, attn_range, &j);
+}
+
 /* ---- LM head: gpt2.c:2160 (bf16 GEMM, fp32 sums) ---- */
-ORC_HOT void orc_lm_head(const uint16_t *xf, int d, const uint16_t *wte, int V, uint16_t *logits) {
-  /* eight vocabulary rows at a time: independent sums, each still in k order */
-  int v = 0;
-  for (; v + 8 <= V; v += 8) {
+typedef struct {
+  const uint16_t *xf, *wte;
+  int d;
+  uint16_t *logits;
+} lm_job;
+
+/* blocks [b0, b1) of eight vocabulary rows */
+ORC_HOT static void lm_range(void *ctx, long b0, long b1) {
+  const lm_job *j = (const lm_job *)ctx;
+  const uint16_t *xf = j->xf, *wte = j->wte;
+  const int d = j->d;
+  uint16_t *logits = j->logits;
+  for (long v = 8 * b0; v < 8 * b1; v += 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int k = 0; k < d; ++k) {
       const float x = orc_bf2f(xf[k]);
@@ -231,7 +416,14 @@ ORC_HOT void orc_lm_head(const uint16_t *xf, int d, const uint16_t *wte, int V, 
     }
     for (int r = 0; r < 8; ++r) logits[v + r] = orc_f2bf(acc[r]);
   }
-  for (; v < V; ++v) {
+}
+
+ORC_HOT void orc_lm_head(const uint16_t *xf, int d, const uint16_t *wte, int V, uint16_t *logits) {
+  /* eight vocabulary rows at a time: independent sums, each still in k order */
+  const int V8 = V & ~7;
+  lm_job j = {xf, wte, d, logits};
+  orc_parallel(V8 / 8, 64, lm_range, &j);
+  for (int v = V8; v < V; ++v) {
     const uint16_t *w = wte + (size_t)v * d;
     float acc = 0.0f;
     for (int k = 0; k < d; ++k) acc = fmaf(orc_bf2f(xf[k]), orc_bf2f(w[k]), acc);
@@ -339,6 +531,15 @@ static uint16_t *to_bf16(const float *src, size_t n) {
 
 int orc_generate(const uint8_t *image, size_t bytes, int d, int L, int H, int vocab, int ctx,
                  const int32_t *prompt, int T, int n_gen, int32_t *out, uint16_t *last_logits) {
+  return orc_generate_steps(image, bytes, d, L, H, vocab, ctx, prompt, T, n_gen, out, last_logits,
+                            NULL);
+}
+
+/* As orc_generate; step_logits (optional, [n_gen][vocab] bf16) receives the
+ * logits every generated token was picked from. */
+int orc_generate_steps(const uint8_t *image, size_t bytes, int d, int L, int H, int vocab,
+                       int ctx, const int32_t *prompt, int T, int n_gen, int32_t *out,
+                       uint16_t *last_logits, uint16_t *step_logits) {
   if (T <= 0 || n_gen <= 0 || T + n_gen - 1 > ctx || d != H * 64) return -1;
   const int f = 4 * d;
   size_t off = 0;
@@ -441,6 +642,7 @@ int orc_generate(const uint8_t *image, size_t bytes, int d, int L, int H, int vo
     /* final LN on the last row, LM head, greedy (gpt2.c:2150-2222) */
     orc_layernorm(h + (size_t)(nrows - 1) * d, 1, d, gf, bf, eps, xf);
     orc_lm_head(xf, d, wte, vocab, logits);
+    if (step_logits) memcpy(step_logits + (size_t)g * vocab, logits, (size_t)vocab * 2);
     const int tok = orc_greedy(logits, vocab);
     out[g] = tok;
     toks[cur] = tok;
