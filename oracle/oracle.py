@@ -40,6 +40,10 @@ def lib() -> C.CDLL:
         l.orc_sample_topk.restype = i
         l.orc_generate.argtypes = [p, sz, i, i, i, i, i, p, i, i, p, p]
         l.orc_generate.restype = i
+        l.orc_generate_steps.argtypes = [p, sz, i, i, i, i, i, p, i, i, p, p, p]
+        l.orc_generate_steps.restype = i
+        l.orc_set_sum_order.argtypes = [i]
+        l.orc_set_sum_order.restype = None
         _lib = l
     return _lib
 
@@ -157,4 +161,28 @@ def generate(image: bytes, dims, prompt, n_gen: int):
                             logits.ctypes.data)
     if st != 0:
         raise RuntimeError(f"orc_generate failed ({st})")
+    return out, logits
+
+
+def generate_steps(image, dims, prompt, n_gen: int, sum_order: int = 0):
+    """Greedy stream of one sequence with the bf16 logits every token was
+    picked from: (tokens [n_gen], logits bits [n_gen, vocab]).
+
+    sum_order 1 adds the fp32 sums the reference leaves to cuBLAS (attention
+    dot products and P.V, LM head) in descending instead of ascending index
+    order: an equally valid reading of the reference, for measuring how far
+    two valid orders drift apart."""
+    buf = np.frombuffer(image, dtype=np.uint8)
+    p = _c(prompt, np.int32)
+    out = np.empty((n_gen,), np.int32)
+    logits = np.empty((n_gen, dims.vocab), np.uint16)
+    lib().orc_set_sum_order(sum_order)
+    try:
+        st = lib().orc_generate_steps(buf.ctypes.data, buf.nbytes, dims.d_model, dims.n_layer,
+                                      dims.n_head, dims.vocab, dims.ctx, p.ctypes.data, p.size,
+                                      n_gen, out.ctypes.data, None, logits.ctypes.data)
+    finally:
+        lib().orc_set_sum_order(0)
+    if st != 0:
+        raise RuntimeError(f"orc_generate_steps failed ({st})")
     return out, logits

@@ -346,18 +346,32 @@ void orc_softmax_row(const uint16_t *in, int n, float temperature, uint16_t *out
 /* ---- attention of one query row over keys [0, n) of one head:
  * gpt2.c:1191-1203 / 1205-1217 (S = bf16(alpha*q.k), alpha = 1/sqrt(64);
  * softmax_cuda; O = bf16(P.V)); sums in key/dim order with fmaf ---- */
+/* Order of the fp32 sums the reference leaves to cuBLAS (the attention dot
+ * products and P.V, the LM head): 0 = ascending index (the oracle), 1 =
+ * descending. The second order is just as valid a reading of the reference;
+ * the tests use it to measure how far two valid orders drift apart. */
+static int g_sum_order = 0;
+void orc_set_sum_order(int order) { g_sum_order = order ? 1 : 0; }
+
 ORC_HOT static void attend_row(const uint16_t *q, const uint16_t *K, const uint16_t *V, int64_t ld, int n,
                        uint16_t *o, uint16_t *srow, uint16_t *prow) {
+  const int rev = g_sum_order;
   for (int j = 0; j < n; ++j) {
     const uint16_t *k = K + (int64_t)j * ld;
     float acc = 0.0f;
-    for (int c = 0; c < 64; ++c) acc = fmaf(orc_bf2f(q[c]), orc_bf2f(k[c]), acc);
+    for (int i = 0; i < 64; ++i) {
+      const int c = rev ? 63 - i : i;
+      acc = fmaf(orc_bf2f(q[c]), orc_bf2f(k[c]), acc);
+    }
     srow[j] = orc_f2bf(acc * 0.125f);
   }
   orc_softmax_row(srow, n, 1.0f, prow);
   for (int c = 0; c < 64; ++c) {
     float acc = 0.0f;
-    for (int j = 0; j < n; ++j) acc = fmaf(orc_bf2f(prow[j]), orc_bf2f(V[(int64_t)j * ld + c]), acc);
+    for (int i = 0; i < n; ++i) {
+      const int j = rev ? n - 1 - i : i;
+      acc = fmaf(orc_bf2f(prow[j]), orc_bf2f(V[(int64_t)j * ld + c]), acc);
+    }
     o[c] = orc_f2bf(acc);
   }
 }
@@ -408,9 +422,11 @@ ORC_HOT static void lm_range(void *ctx, long b0, long b1) {
   const uint16_t *xf = j->xf, *wte = j->wte;
   const int d = j->d;
   uint16_t *logits = j->logits;
+  const int rev = g_sum_order;
   for (long v = 8 * b0; v < 8 * b1; v += 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int k = 0; k < d; ++k) {
+    for (int i = 0; i < d; ++i) {
+      const int k = rev ? d - 1 - i : i;
       const float x = orc_bf2f(xf[k]);
       for (int r = 0; r < 8; ++r) acc[r] = fmaf(x, orc_bf2f(wte[(size_t)(v + r) * d + k]), acc[r]);
     }
@@ -426,7 +442,10 @@ ORC_HOT void orc_lm_head(const uint16_t *xf, int d, const uint16_t *wte, int V, 
   for (int v = V8; v < V; ++v) {
     const uint16_t *w = wte + (size_t)v * d;
     float acc = 0.0f;
-    for (int k = 0; k < d; ++k) acc = fmaf(orc_bf2f(xf[k]), orc_bf2f(w[k]), acc);
+    for (int i = 0; i < d; ++i) {
+      const int k = g_sum_order ? d - 1 - i : i;
+      acc = fmaf(orc_bf2f(xf[k]), orc_bf2f(w[k]), acc);
+    }
     logits[v] = orc_f2bf(acc);
   }
 }

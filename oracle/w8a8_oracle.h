@@ -30,6 +30,7 @@ void orc_top_k(const uint16_t *probs, int V, int k, int *idx, uint16_t *q);
 int orc_sample_topk(const uint16_t *probs, int V, int k, float r);
 int orc_generate(const uint8_t *image, size_t bytes, int d, int L, int H, int vocab, int ctx,
                  const int32_t *prompt, int T, int n_gen, int32_t *out, uint16_t *last_logits);
+void orc_set_sum_order(int order);
 int orc_generate_steps(const uint8_t *image, size_t bytes, int d, int L, int H, int vocab,
                        int ctx, const int32_t *prompt, int T, int n_gen, int32_t *out,
                        uint16_t *last_logits, uint16_t *step_logits);
