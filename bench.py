@@ -7,6 +7,11 @@ GPUs of one node (64/N sequences per rank, strong scaling, no collective on
 the data path). Weights: GPT-2 large architecture, random N(0, 0.02) init,
 per-output-channel INT8 (synthetic; no checkpoint is available offline).
 
+Outside the timed region, a second leg runs the GPT-2 large W8A8 prefill of
+32 x 1024 tokens tensor-parallel over all ranks (`tp_prefill` in the JSON
+line: device time, and bit-equality of its tokens and logits with the
+single-GPU engine's prefill of the same batch).
+
 One step = the whole job on a rank's shard: batched prefill of its prompts,
 then 511 greedy decode steps (CUDA-graph replays). `value` = generated
 tokens of all ranks / max-over-ranks device time (CUDA events on the
@@ -269,6 +274,89 @@ def kernel_rooflines(count: int, peaks: dict, dev) -> dict:
     }
 
 
+# Tensor-parallel prefill leg (GPT-2 large, 32 prompts x 1024 tokens, split
+# over every rank of the run).
+TP_SEQ, TP_TOK = 32, 1024
+
+
+def tp_prefill_leg(args, rank: int, world: int, local: int, dev) -> dict | None:
+    """GPT-2 large W8A8 prefill of 32 x 1024 tokens, tensor-parallel over the
+    run's ranks (W_qkv and W1 column-split, attn_proj and W2 row-split; int32
+    reduce-scatter + int8 all-gather + fp32 max all-reduce over NCCL), timed
+    on the device (max over ranks), and its next tokens and logits compared
+    bit for bit with the single-GPU engine's prefill of the same batch, which
+    rank 0 also times. Every rank takes the same collective steps."""
+    import torch
+    import torch.distributed as dist
+    from c_gpt2_b200.dp import max_over_ranks
+    from c_gpt2_b200.engine import Engine
+    from c_gpt2_b200.quant8 import DIMS, read_quant8
+    from c_gpt2_b200.synthetic import prompts, quant8_image_gpu
+    from c_gpt2_b200.tp import TPPlan, TPPrefill, shard_weights
+
+    dims = DIMS["large"]
+    img = quant8_image_gpu(dims, seed=0, device=dev)
+    P = torch.from_numpy(prompts(TP_SEQ, TP_TOK, dims.vocab, seed=0)).to(dev)
+    plan = TPPlan.make(dims, world)
+    shard = shard_weights(read_quant8(img, dims), plan, rank, dev)
+    tp = TPPrefill(plan, shard, rank)
+    for _ in range(args.warmup):
+        tp.run(P)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        nxt, logits = tp.run(P)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
+    full = logits
+    if world > 1:
+        full = torch.empty((TP_SEQ, dims.vocab), dtype=logits.dtype, device=dev)
+        dist.all_gather_into_tensor(full, logits.contiguous())
+    tp.close()
+    del shard, tp
+    out = None
+    if rank == 0:
+        eng = Engine(dims, max_batch=TP_SEQ, max_tokens=TP_SEQ * TP_TOK, device=local)
+        eng.load_quant8(img)
+        one = torch.empty((TP_SEQ,), dtype=torch.int32, device=dev)
+        es = torch.cuda.ExternalStream(eng.stream_handle, device=dev)
+        for _ in range(args.warmup):
+            eng.prefill(P, one, 1)
+        torch.cuda.synchronize()
+        e0.record(es)
+        for _ in range(args.steps):
+            eng.prefill(P, one, 1)
+        e1.record(es)
+        torch.cuda.synchronize()
+        ms1 = e0.elapsed_time(e1) / args.steps
+        want = eng.logits(TP_SEQ)
+        eng.close()
+        got = (full.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+               .astype(np.uint32) << 16).view(np.float32)
+        same_tok = bool(np.array_equal(nxt.cpu().numpy(), one.cpu().numpy()))
+        same_logits = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+        M = TP_SEQ * TP_TOK
+        gemm_ops = 2.0 * M * 12 * dims.d_model ** 2 * dims.n_layer
+        out = {"workload": f"gpt2-large W8A8 prefill {TP_SEQ} x {TP_TOK} tokens, "
+                           f"tensor-parallel tp{world} (heads per rank "
+                           f"{[h1 - h0 for h0, h1 in plan.heads]})",
+               "tp": world, "ms": round(ms, 3), "tok_per_s": round(M / (ms / 1e3), 1),
+               "gemm_tops_effective": round(gemm_ops / (ms / 1e3) / 1e12, 1),
+               "ms_1gpu_engine": round(ms1, 3), "vs_1gpu": round(ms1 / ms, 3),
+               "bitexact": same_tok and same_logits, "tokens_equal": same_tok,
+               "logits_equal": same_logits,
+               "exchange": "int32 reduce-scatter + int8 all-gather + fp32 max all-reduce (NCCL)"}
+    if world > 1:
+        dist.barrier()
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -276,6 +364,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp-prefill", action="store_true",
+                    help="skip the tensor-parallel 32 x 1024 prefill leg")
     ap.add_argument("--decode-split", type=int, choices=[1, 2], default=1,
                     help="decode each step as one chain of kernels or two concurrent chains")
     args = ap.parse_args()
@@ -355,6 +445,7 @@ def main() -> None:
 
     roof = kernel_rooflines(count, peaks, dev)
     achieved = roof["attention"]["gbs"]
+    tp_line = None if args.no_tp_prefill else tp_prefill_leg(args, rank, world, local, dev)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -395,6 +486,7 @@ def main() -> None:
                          "peak_source": peaks["source"]},
             "gemm": roof["gemm"],
             "gemm_layer": roof["gemm_layer"],
+            "tp_prefill": tp_line,
             "cpu_baseline": cpu,
             "clocks": clk,
             "gpu_launches": int(launches),

@@ -155,7 +155,12 @@ class Collectives:
         if self.world == 1:
             return
         m = full.shape[0] // world
-        dist.all_gather_into_tensor(full, full[rank * m:(rank + 1) * m].clone(), group=self.group)
+        own = full[rank * m:(rank + 1) * m]
+        # NCCL gathers in place when the input is this rank's chunk of the
+        # output; other backends get a copy of the chunk
+        if dist.get_backend(self.group) != "nccl":
+            own = own.clone()
+        dist.all_gather_into_tensor(full, own, group=self.group)
 
     def reduce_scatter_sum(self, out: torch.Tensor, full: torch.Tensor) -> None:
         if self.world == 1:
