@@ -15,7 +15,9 @@
 #define REF_CTX 1024
 
 int gpt2_reference_main(int argc, char **argv);
+#ifndef REF_NO_LOGITS
 extern float logits[REF_CTX][REF_VOCAB];
+#endif
 
 int main(int argc, char **argv) {
   const char *dump = NULL;
@@ -33,11 +35,16 @@ int main(int argc, char **argv) {
   args[n] = NULL;
   int rc = gpt2_reference_main(n, args);
   free(args);
+#ifdef REF_NO_LOGITS
+  if (dump) return 5; /* GPU builds: the logits live on the device */
+#endif
   if (rc == 0 && dump) {
     if (row < 0 || row >= REF_CTX) return 3;
     FILE *fp = fopen(dump, "wb");
     if (!fp) return 4;
+#ifndef REF_NO_LOGITS
     fwrite(logits[row], sizeof(float), REF_VOCAB, fp);
+#endif
     fclose(fp);
   }
   return rc;

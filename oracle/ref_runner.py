@@ -1,7 +1,9 @@
-"""Run the reference's own CPU FP32 build (oracle/_ref/gpt2_ref_<size>) on
-seeded synthetic weights and prompt ids. TEST INFRASTRUCTURE ONLY: used by
-tests/, the smoke check and bench.py's CPU-baseline leg as the checker and
-baseline, never by the product path.
+"""Run the reference's own CPU FP32 build (oracle/_ref/gpt2_ref_<size>), and
+the GPU builds of its gpt2.c (the reference's INT8 GPU build, and gpt2.c on
+this repository's library), on seeded synthetic weights and prompt ids. TEST
+INFRASTRUCTURE ONLY: used by tests/, the smoke check, c_gpt2_b200.profcase's
+reference legs and bench.py's CPU-baseline leg as the checker and baseline,
+never by the product path.
 
 The reference reads weights from the relative path weights/<file>
 (include/model_config.h:14,22,30) and tokenizes over TCP 127.0.0.1:65432
@@ -27,10 +29,24 @@ REF_DIR = HERE / "_ref"
 PORT = 65432
 WEIGHT_FILES = {"small": "gpt2_c_weights.bin", "medium": "gpt2_medium_c_weights.bin",
                 "large": "gpt2_large_c_weights.bin"}
+# the INT8 GPU builds read the quant8.bin instead (include/model_config.h:15,23,31)
+QUANT8_FILES = {"small": "gpt2_small_quant8.bin", "medium": "gpt2_medium_quant8.bin",
+                "large": "gpt2_large_quant8.bin"}
+# GPU builds of gpt2.c (oracle/Makefile):
+#   gpu_int8    the reference's INT8 GPU build: its cuda/*.cu kernels + cuBLAS
+#   ourkernels  the same gpt2.c object on this repository's libcuda_kernels
+#   dropin      gpt2.c with its GPU layer and pick on this repository's entry
+#               points (no cuBLAS)
+GPU_BUILDS = {"gpu_int8": "gpt2_gpu_int8_{}", "ourkernels": "gpt2_gpu_ourkernels_{}",
+              "dropin": "gpt2_dropin_{}"}
 
 
 def ref_binary(size: str) -> Path:
     return REF_DIR / f"gpt2_ref_{size}"
+
+
+def gpu_binary(build: str, size: str) -> Path:
+    return REF_DIR / GPU_BUILDS[build].format(size)
 
 
 class FakeTokenizer:
@@ -93,14 +109,30 @@ class FakeTokenizer:
 def run_reference(size: str, fp32_weights: Path, prompt_ids, n_gen: int,
                   dump_logits_row: int | None = None, threads: int | None = None,
                   timeout: float = 3600.0) -> dict:
-    """Run the reference once; returns {"tokens", "perf", "logits", "wall_s"}."""
-    exe = ref_binary(size)
+    """Run the reference's CPU FP32 build once; returns {"tokens", "perf",
+    "logits", "wall_s"}."""
+    return _run(ref_binary(size), WEIGHT_FILES[size], fp32_weights, prompt_ids, n_gen,
+                dump_logits_row, threads, timeout)
+
+
+def run_gpu_build(build: str, size: str, quant8_weights: Path, prompt_ids, n_gen: int,
+                  temperature: float = 0.0, top_k: int = 40, timeout: float = 1800.0) -> dict:
+    """Run one GPU build of gpt2.c (GPU_BUILDS) on a quant8.bin; returns
+    {"tokens", "perf", "wall_s"}. At temperature > 0 the reference draws with
+    its own unseeded rand()."""
+    return _run(gpu_binary(build, size), QUANT8_FILES[size], quant8_weights, prompt_ids, n_gen,
+                None, None, timeout, temperature=temperature, top_k=top_k)
+
+
+def _run(exe: Path, weight_name: str, weights: Path, prompt_ids, n_gen: int,
+         dump_logits_row: int | None, threads: int | None, timeout: float,
+         temperature: float = 0.0, top_k: int | None = None) -> dict:
     if not exe.exists():
         raise FileNotFoundError(f"{exe} missing: run `make -C oracle ref`")
     with tempfile.TemporaryDirectory() as td:
         td = Path(td)
         (td / "weights").mkdir()
-        os.symlink(Path(fp32_weights).resolve(), td / "weights" / WEIGHT_FILES[size])
+        os.symlink(Path(weights).resolve(), td / "weights" / weight_name)
         (td / "logs").mkdir()
         env = dict(os.environ)
         n = threads or os.cpu_count() or 1
@@ -108,8 +140,11 @@ def run_reference(size: str, fp32_weights: Path, prompt_ids, n_gen: int,
         cmd = [str(exe)]
         if dump_logits_row is not None:
             cmd += ["--dump-logits", str(td / "logits.f32"), str(dump_logits_row)]
-        cmd += ["--prompt", "synthetic prompt", "--temperature", "0", "--no-stream",
-                "--req_out_tokens", str(n_gen), "--json_out_file", str(td / "perf.json")]
+        cmd += ["--prompt", "synthetic prompt", "--temperature", repr(float(temperature)),
+                "--no-stream", "--req_out_tokens", str(n_gen),
+                "--json_out_file", str(td / "perf.json")]
+        if top_k is not None:
+            cmd += ["--top_k", str(top_k)]
         tok = FakeTokenizer(prompt_ids)
         try:
             t0 = time.perf_counter()
