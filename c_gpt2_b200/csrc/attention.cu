@@ -25,6 +25,7 @@
 // P.V; the last split to finish (ticket counter, no waiting) adds the partials
 // in split order and rounds.
 #include "common.cuh"
+#include "kernels.cuh"
 #include "runtime.cuh"
 
 namespace w8a8 {
@@ -284,6 +285,8 @@ __global__ void __launch_bounds__(kPrefillThreads)
 int launch_attention_prefill(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
                              const uint16_t *Vc, int64_t seq_stride, int n_seq, int T, int n_head,
                              uint16_t *O, int64_t ldo, cudaStream_t s) {
+  if (attention_prefill_tc_ok(Q, ldq, Kc, Vc, seq_stride, T, n_head))
+    return launch_attention_prefill_tc(Q, ldq, Kc, Vc, seq_stride, n_seq, T, n_head, O, ldo, s);
   PrefillArgs a;
   a.Q = Q;
   a.ldq = ldq;

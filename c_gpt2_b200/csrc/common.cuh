@@ -243,6 +243,47 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory descriptor for an MN-major operand tile with the 128-byte
+// swizzle: each 128-byte row holds 64 consecutive 16-bit elements along M/N
+// (one swizzle atom), rows are consecutive K indices, 8-row groups 1024 bytes
+// apart (SBO). Used for a [K rows][64] tile read as the N = 64 side.
+__device__ __forceinline__ uint64_t make_sw128_mn_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;            // leading byte offset: next 64-wide atom (only one here)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: next 8 K rows
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// tcgen05.st of 32 lanes x 32 columns (thread i writes lane base + i).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 3D TMA load (box {x, y, 1} at coordinates x, y, z).
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const void *tmap, uint64_t *bar, int x,
+                                            int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // Instruction descriptor (dense, K-major A and B).
 //   c_format: 1 = F32, 2 = S32 ; ab_format: kind::i8 -> 1 (signed),
 //   kind::f16 -> 1 (bf16).
@@ -250,6 +291,11 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_format, uint32_t ab
                                                   int n) {
   return (c_format << 4) | (ab_format << 7) | (ab_format << 10) | ((uint32_t)(n >> 3) << 17) |
          ((uint32_t)(m >> 4) << 24);
+}
+// The same with an MN-major B operand (bit 16: B transposed).
+__host__ __device__ constexpr uint32_t make_idesc_bmn(uint32_t c_format, uint32_t ab_format, int m,
+                                                      int n) {
+  return make_idesc(c_format, ab_format, m, n) | (1u << 16);
 }
 
 // ---------------------------------------------------------------------------

@@ -124,6 +124,12 @@ int launch_quant_rows_amax(const uint16_t *X, int64_t ldx, int M, int K, const f
                            cudaStream_t s);
 int launch_reduce_layernorm_quant(const ReduceArgs &a, int M, cudaStream_t s);
 // attention.cu
+// attention_tc.cu: tcgen05 prefill attention (head_dim 64, T <= 1024)
+bool attention_prefill_tc_ok(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
+                             const uint16_t *Vc, int64_t seq_stride, int T, int n_head);
+int launch_attention_prefill_tc(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
+                                const uint16_t *Vc, int64_t seq_stride, int n_seq, int T,
+                                int n_head, uint16_t *O, int64_t ldo, cudaStream_t stream);
 int launch_attention_prefill(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
                              const uint16_t *Vc, int64_t seq_stride, int n_seq, int T, int n_head,
                              uint16_t *O, int64_t ldo, cudaStream_t s);

@@ -79,6 +79,23 @@ int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, 
   return r == CUDA_SUCCESS ? W8A8_OK : W8A8_ERR_INVALID;
 }
 
+int make_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, uint64_t planes,
+                 uint64_t rows, uint64_t cols, uint64_t row_pitch_bytes,
+                 uint64_t plane_pitch_bytes, uint32_t box_cols, uint32_t box_rows) {
+  if (!g_encode && resolve_encoder() != W8A8_OK) return W8A8_ERR_CUDA;
+  if (!aligned16(base) || (row_pitch_bytes & 15u) || (plane_pitch_bytes & 15u) || rows == 0 ||
+      cols == 0 || planes == 0)
+    return W8A8_ERR_INVALID;
+  cuuint64_t dims[3] = {cols, rows, planes};
+  cuuint64_t strides[2] = {row_pitch_bytes, plane_pitch_bytes};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? W8A8_OK : W8A8_ERR_INVALID;
+}
+
 }  // namespace w8a8
 
 using namespace w8a8;

@@ -30,6 +30,11 @@ DeviceCtx *device_ctx(int *status);
 int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, uint64_t rows,
                  uint64_t cols, uint64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows,
                  int swizzle_bytes = 128);
+// [planes][rows][cols] view (cols contiguous), box {box_cols, box_rows, 1},
+// 128-byte swizzle; elements outside the extents read as zero.
+int make_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, uint64_t planes,
+                 uint64_t rows, uint64_t cols, uint64_t row_pitch_bytes,
+                 uint64_t plane_pitch_bytes, uint32_t box_cols, uint32_t box_rows);
 
 // Launch `kernel` with programmatic dependent launch allowed: it may begin
 // while the preceding kernel of the stream finishes (see pdl_wait()).

@@ -259,7 +259,7 @@ def _attn_tolerance(got, want):
 
 
 @pytest.mark.parametrize("n_seq,T,H", [(1, 1, 1), (1, 37, 2), (2, 64, 12), (3, 130, 4),
-                                       (1, 512, 16), (1, 1024, 2)])
+                                       (1, 512, 16), (1, 1024, 2), (2, 1000, 3), (4, 256, 20)])
 def test_attention_prefill(cuda, n_seq, T, H):
     rng = np.random.default_rng(T * 13 + H)
     Q, K, V = _attn_case(rng, n_seq, T, H)
