@@ -25,6 +25,11 @@
 //            keeps the reference's order and each thread holds 32 slot sums
 //            at a time. Recomputing S costs tensor-core time the kernel has
 //            to spare; storing it would not fit on chip at 1024 keys.
+// The softmax warps first scale the Q tile by 0.125 in shared memory (exact:
+// a power of two), so S = bf16(acc) needs no multiply; scores stay packed as
+// bf16x2 until an exponential needs them, and only the diagonal key tile
+// (kt == query tile) pays for the causal mask. P is double-buffered when the
+// key tiles leave room for a second buffer (prompts up to 512 tokens).
 // Every wait is bounded and records an error instead of hanging.
 #include "common.cuh"
 #include "runtime.cuh"
@@ -51,11 +56,11 @@ constexpr uint32_t kTmemSlots = 320;     // 4 x 32 columns: slot sums of the eve
 constexpr uint32_t kTmemCols = 512;
 
 struct AttnCtl {
-  uint64_t q_full;
+  uint64_t q_full, q_ready;
   uint64_t k_full[kAMaxKT];
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, p_empty;
+  uint64_t p_full[2], p_empty[2];
   uint64_t o_full;
   uint64_t drain;
   uint32_t tmem_base;
@@ -66,26 +71,26 @@ struct AttnCtl {
 
 struct AttnTcArgs {
   int T, n_qt;
+  int p_bufs;     // 1 or 2 P buffers
   uint16_t *O;
   int64_t ldo;
   int vec_store;  // O rows 16-byte aligned
   int *err;
 };
 
-// Bounded wait by all lanes of a warp on the same phase.
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                          int *err, int code) {
-  return mbar_wait(bar, parity, abort_flag, err, code);
-}
-
-// One key tile's 32 scores of this thread: S = bf16(0.125 * acc) as floats.
-__device__ __forceinline__ void scores32(const uint32_t (&v)[32], float (&s)[32]) {
+// One key tile's 32 scores of this thread as bf16 pairs: S = bf16(acc) (the
+// 0.125 is in Q already).
+__device__ __forceinline__ void scores_bf2(const uint32_t (&v)[32], uint32_t (&p)[16]) {
 #pragma unroll
-  for (int c = 0; c < 32; c += 2) {
-    s[c] = __uint_as_float(v[c]) * 0.125f;
-    s[c + 1] = __uint_as_float(v[c + 1]) * 0.125f;
-    round_bf2(s[c], s[c + 1]);
-  }
+  for (int c = 0; c < 16; ++c)
+    p[c] = pack_bf2(__uint_as_float(v[2 * c]), __uint_as_float(v[2 * c + 1]));
+}
+__device__ __forceinline__ float lo_f(uint32_t p) { return __uint_as_float(p << 16); }
+__device__ __forceinline__ float hi_f(uint32_t p) { return __uint_as_float(p & 0xffff0000u); }
+__device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
 
 }  // namespace
@@ -105,20 +110,21 @@ __global__ void __launch_bounds__(kAThreads, 1)
   uint8_t *sK = sQ + kATile;
   uint8_t *sV = sK + (size_t)a.n_qt * kATile;
   uint8_t *sP = sV + 2 * kATile;
-  AttnCtl *ctl = reinterpret_cast<AttnCtl *>(sP + kAP);
+  AttnCtl *ctl = reinterpret_cast<AttnCtl *>(sP + (size_t)a.p_bufs * kAP);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     mbar_init(&ctl->q_full, 1);
+    mbar_init(&ctl->q_ready, 1);
     for (int i = 0; i < kAMaxKT; ++i) mbar_init(&ctl->k_full[i], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ctl->v_full[i], 1);
       mbar_init(&ctl->v_empty[i], 1);
       mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->s_empty[i], kSoftWarps);
+      mbar_init(&ctl->p_full[i], kSoftWarps);
+      mbar_init(&ctl->p_empty[i], 1);
     }
-    mbar_init(&ctl->p_full, kSoftWarps);
-    mbar_init(&ctl->p_empty, 1);
     mbar_init(&ctl->o_full, 1);
     mbar_init(&ctl->drain, 1);
     ctl->abort_flag = 0;
@@ -172,7 +178,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
       const uint32_t idO = make_idesc_bmn(1, 1, kAQ, 64);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV),
                      p_addr = smem_u32(sP);
-      bool ok = mbar_wait(&ctl->q_full, 0, abort_flag, a.err, 0x1403);
+      bool ok = mbar_wait(&ctl->q_ready, 0, abort_flag, a.err, 0x1403);
       tc_fence_after();
       int sidx = 0;
       uint32_t k_seen = 0;
@@ -204,16 +210,19 @@ __global__ void __launch_bounds__(kAThreads, 1)
       for (int kt = 0; kt < n_kt && ok; ++kt) {
         if (kt + 1 < n_kt && !(ok = issue_s(kt + 1))) break;
         const int vb = kt & 1;
-        if (!(ok = mbar_wait(&ctl->p_full, kt & 1, abort_flag, a.err, 0x1406))) break;
+        const int pb = a.p_bufs == 2 ? (kt & 1) : 0;
+        const uint32_t pph = (uint32_t)((a.p_bufs == 2 ? kt >> 1 : kt) & 1);
+        if (!(ok = mbar_wait(&ctl->p_full[pb], pph, abort_flag, a.err, 0x1406))) break;
         if (!(ok = mbar_wait(&ctl->v_full[vb], (kt >> 1) & 1, abort_flag, a.err, 0x1407))) break;
         tc_fence_after();
         const uint32_t vbase = v_addr + (uint32_t)vb * kATile;
+        const uint32_t pbase = p_addr + (uint32_t)pb * kAP;
 #pragma unroll
         for (int ks = 0; ks < kAK / 16; ++ks)
           tc_mma_bf16(tmem + kTmemO,
-                      make_sw128_desc(p_addr + (uint32_t)(ks >> 2) * kATile + 32 * (ks & 3)),
+                      make_sw128_desc(pbase + (uint32_t)(ks >> 2) * kATile + 32 * (ks & 3)),
                       make_sw128_mn_desc(vbase + (uint32_t)ks * 2048), idO, (kt > 0) || (ks > 0));
-        tc_commit(&ctl->p_empty);
+        tc_commit(&ctl->p_empty[pb]);
         tc_commit(&ctl->v_empty[vb]);
       }
       if (ok) {
@@ -231,9 +240,25 @@ __global__ void __launch_bounds__(kAThreads, 1)
     const int qpos = q0 + r;
     const uint32_t trow = tmem + ((uint32_t)(qd * 32) << 16);
     const int col0 = cq * 32;          // this thread's columns of each key tile
+    // Q *= 0.125 in place (exact for bf16: a power of two), then the MMA may start
+    {
+      mbar_wait(&ctl->q_full, 0, abort_flag, a.err, 0x140C);
+      uint4 *q4 = reinterpret_cast<uint4 *>(sQ) + threadIdx.x * 2;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        uint4 v = q4[i];
+        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = pack_bf2(lo_f(w[j]) * 0.125f, hi_f(w[j]) * 0.125f);
+        q4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      named_barrier_sync(kSoftBar, kSoftThreads);
+      if (threadIdx.x == 0) mbar_arrive(&ctl->q_ready);
+    }
     int sidx = 0;
     // Wait for the next score tile, copy this thread's 32 columns, release it.
-    auto next_scores = [&](float (&s)[32]) {
+    auto next_scores = [&](uint32_t (&p)[16]) {
       const int buf = sidx & 1;
       mbar_wait(&ctl->s_full[buf], (sidx >> 1) & 1, abort_flag, a.err, 0x1409);
       tc_fence_after();
@@ -244,19 +269,28 @@ __global__ void __launch_bounds__(kAThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->s_empty[buf]);
       ++sidx;
-      scores32(v, s);
+      scores_bf2(v, p);
     };
 
     // ---- pass 1: row maximum ----
+    uint32_t mx2 = 0xff80ff80u;  // (-inf, -inf)
     float m = -INFINITY;
     for (int kt = 0; kt < n_kt; ++kt) {
-      float s[32];
-      next_scores(s);
-      const int lim = qpos - (kt * kAK + col0);  // columns c <= lim are causal
+      uint32_t p[16];
+      next_scores(p);
+      if (kt < qt) {  // below the diagonal: every key is visible
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if (c <= lim) m = fmaxf(m, s[c]);
+        for (int c = 0; c < 16; ++c) mx2 = bf2_max(mx2, p[c]);
+      } else {
+        const int lim = qpos - (kt * kAK + col0);  // columns c <= lim are causal
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float x = (c & 1) ? hi_f(p[c >> 1]) : lo_f(p[c >> 1]);
+          if (c <= lim) m = fmaxf(m, x);
+        }
+      }
     }
+    m = fmaxf(m, fmaxf(lo_f(mx2), hi_f(mx2)));
     ctl->row_max[cq][r] = m;
     named_barrier_sync(kSoftBar, kSoftThreads);
     m = fmaxf(fmaxf(ctl->row_max[0][r], ctl->row_max[1][r]),
@@ -268,12 +302,22 @@ __global__ void __launch_bounds__(kAThreads, 1)
 #pragma unroll
       for (int c = 0; c < 32; ++c) sl[c] = 0.0f;
       for (int kt = par; kt < n_kt; kt += 2) {
-        float s[32];
-        next_scores(s);
-        const int lim = qpos - (kt * kAK + col0);
+        uint32_t p[16];
+        next_scores(p);
+        if (kt < qt) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if (c <= lim) sl[c] = sl[c] + expf(s[c] - m);
+          for (int c = 0; c < 16; ++c) {
+            sl[2 * c] = sl[2 * c] + expf(lo_f(p[c]) - m);
+            sl[2 * c + 1] = sl[2 * c + 1] + expf(hi_f(p[c]) - m);
+          }
+        } else {
+          const int lim = qpos - (kt * kAK + col0);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float x = (c & 1) ? hi_f(p[c >> 1]) : lo_f(p[c >> 1]);
+            if (c <= lim) sl[c] = sl[c] + expf(x - m);
+          }
+        }
       }
       if (par == 0) {  // park the even slots in TMEM
         uint32_t u[32];
@@ -292,7 +336,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
       for (int c = 0; c < 32; ++c) sl[c] = __uint_as_float(u[c]) + sl[c];
     }
     // h = 64 and h = 32 across the four threads of a row, through shared
-    // memory (the P buffer, unused until pass 3)
+    // memory (the first P buffer, unused until pass 3)
     float *xs = reinterpret_cast<float *>(sP);  // [2][32][128]
     if (cq >= 2) {
 #pragma unroll
@@ -322,20 +366,30 @@ __global__ void __launch_bounds__(kAThreads, 1)
     const float inv = ctl->row_inv[r];
 
     // ---- pass 3: P into shared memory (128-byte swizzle), one tile at a time ----
-    uint8_t *prow = sP + (size_t)(cq >> 1) * kATile + (size_t)r * 128;
     for (int kt = 0; kt < n_kt; ++kt) {
-      float s[32];
-      next_scores(s);
-      const int lim = qpos - (kt * kAK + col0);
+      uint32_t p[16];
+      next_scores(p);
       uint32_t pk[16];
+      if (kt < qt) {
 #pragma unroll
-      for (int c = 0; c < 32; c += 2) {
-        float p0 = 0.0f, p1 = 0.0f;
-        if (c <= lim) p0 = round_bf(expf(s[c] - m)) * inv;
-        if (c + 1 <= lim) p1 = round_bf(expf(s[c + 1] - m)) * inv;
-        pk[c >> 1] = pack_bf2(p0, p1);
+        for (int c = 0; c < 16; ++c) {
+          const uint32_t e2 = pack_bf2(expf(lo_f(p[c]) - m), expf(hi_f(p[c]) - m));
+          pk[c] = pack_bf2(lo_f(e2) * inv, hi_f(e2) * inv);
+        }
+      } else {
+        const int lim = qpos - (kt * kAK + col0);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          float p0 = 0.0f, p1 = 0.0f;
+          if (2 * c <= lim) p0 = round_bf(expf(lo_f(p[c]) - m)) * inv;
+          if (2 * c + 1 <= lim) p1 = round_bf(expf(hi_f(p[c]) - m)) * inv;
+          pk[c] = pack_bf2(p0, p1);
+        }
       }
-      if (kt > 0) mbar_wait(&ctl->p_empty, (kt - 1) & 1, abort_flag, a.err, 0x140A);
+      const int pb = a.p_bufs == 2 ? (kt & 1) : 0;
+      const int use = a.p_bufs == 2 ? kt >> 1 : kt;  // earlier fills of this buffer
+      if (use > 0) mbar_wait(&ctl->p_empty[pb], (uint32_t)((use - 1) & 1), abort_flag, a.err, 0x140A);
+      uint8_t *prow = sP + (size_t)pb * kAP + (size_t)(cq >> 1) * kATile + (size_t)r * 128;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int unit = ((cq & 1) * 4 + i) ^ (r & 7);
@@ -344,7 +398,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ctl->p_full);
+      if (lane == 0) mbar_arrive(&ctl->p_full[pb]);
     }
 
     // ---- O: this thread's 16 head dims of its row ----
@@ -408,7 +462,9 @@ int launch_attention_prefill_tc(const uint16_t *Q, int64_t ldq, const uint16_t *
   a.ldo = ldo;
   a.vec_store = aligned16(O) && ldo % 8 == 0;
   a.err = ctx->err;
-  size_t smem = 1024 + (size_t)kATile * (1 + a.n_qt + 2) + kAP + sizeof(AttnCtl);
+  const size_t base = 1024 + (size_t)kATile * (1 + a.n_qt + 2) + sizeof(AttnCtl);
+  a.p_bufs = base + 2 * kAP <= 227 * 1024 ? 2 : 1;
+  size_t smem = base + (size_t)a.p_bufs * kAP;
   // at least half of the SM's shared memory: one CTA per SM, which owns all
   // 512 TMEM columns
   if (smem < 116 * 1024) smem = 116 * 1024;
