@@ -96,6 +96,7 @@ SIGNATURES = {
     "gpt2_engine_copy_logits": (_i, [_p, _p, _i]),
     "gpt2_engine_set_graphs": (_i, [_p, _i]),
     "gpt2_engine_set_decode_split": (_i, [_p, _i]),
+    "w8a8_last_cuda_error": (C.c_char_p, []),
     "gpt2_engine_set_sampling": (_i, [_p, _f, _i]),
     "gpt2_quant8_check_manifest": (_i, [_p, C.c_char_p, C.c_char_p, C.c_size_t]),
     "gpt2_engine_set_draws": (_i, [_p, _i, _p, _i]),

@@ -13,6 +13,10 @@ __device__ int g_device_error;
 
 static DeviceCtx g_ctx[64];
 
+// The CUDA error of the calling thread's last failed launch.
+static thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+void note_cuda_error(cudaError_t e) { g_last_cuda_error = e; }
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -105,6 +109,10 @@ extern "C" int w8a8_init(int device) {
   int st;
   DeviceCtx *c = device_ctx(&st);
   return c ? W8A8_OK : st;
+}
+
+extern "C" const char *w8a8_last_cuda_error(void) {
+  return g_last_cuda_error == cudaSuccess ? "no error" : cudaGetErrorString(g_last_cuda_error);
 }
 
 extern "C" const char *w8a8_status_string(int status) {

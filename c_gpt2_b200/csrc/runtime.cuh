@@ -54,10 +54,15 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// Remember the CUDA error behind a W8A8_ERR_CUDA (w8a8_last_cuda_error).
+void note_cuda_error(cudaError_t e);
+
 inline int check_launch(const char *what) {
   cudaError_t e = cudaGetLastError();
   (void)what;
-  return e == cudaSuccess ? W8A8_OK : W8A8_ERR_CUDA;
+  if (e == cudaSuccess) return W8A8_OK;
+  note_cuda_error(e);
+  return W8A8_ERR_CUDA;
 }
 
 __host__ __device__ inline bool aligned16(const void *p) { return (((uintptr_t)p) & 15u) == 0; }

@@ -57,6 +57,8 @@ typedef uint16_t gpt2_bf16_t;
  * Call once per device (with that device current) before stream capture. */
 int w8a8_init(int device);
 const char *w8a8_status_string(int status);
+/* The CUDA error behind the calling thread's last W8A8_ERR_CUDA from a launch. */
+const char *w8a8_last_cuda_error(void);
 /* Returns the first error code a kernel recorded on the current device since
  * the last reset (0 = none); `reset` != 0 clears it. Synchronises the device. */
 int w8a8_device_error(int reset);
