@@ -431,6 +431,388 @@ __global__ void __launch_bounds__(kAThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Prompts up to 512 tokens (at most four key tiles): the exponentials fit on
+// chip. Pass 2 writes bf16(e_j) for every key tile into shared memory, laid
+// out as the P operand, so pass 3 is P_j = bf16(float(bf16(e_j)) * inv) in
+// place: no third S = Q K^T and no second expf. The K tiles are dead after
+// pass 2, and the V tiles are loaded into their space.
+//   shared memory: Q 16 KB | K tiles, then V tiles, 16 KB each | E / P tiles,
+//   32 KB each (128 rows x 128 keys bf16 as two 64-key 128-byte-swizzle atoms)
+//   TMEM: S buffers 0-255, O 256-319, slot sums 320-447, exchange 448-511
+// Every rounding point and sum order is the three-pass kernel's.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kEMaxKT = 4;
+constexpr uint32_t kTmemX = 448;  // cross-thread exchange columns (64)
+
+struct AttnCtlE {
+  uint64_t q_full, q_ready;
+  uint64_t k_full[kEMaxKT], v_full[kEMaxKT], p_full[kEMaxKT];
+  uint64_t s_full[2], s_empty[2];
+  uint64_t k_dead, o_full, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// this thread's 16-byte units of row r in a P-layout tile: keys [32*cq, +32)
+__device__ __forceinline__ uint4 *p_unit(uint8_t *tile, int r, int cq, int i) {
+  const int unit = ((cq & 1) * 4 + i) ^ (r & 7);
+  return reinterpret_cast<uint4 *>(tile + (size_t)(cq >> 1) * kATile + (size_t)r * 128 +
+                                   unit * 16);
+}
+
+// Exchange through TMEM columns of this thread's lane: other warps of the
+// same lane quadrant read what a warp wrote after a named barrier.
+__device__ __forceinline__ void xchg_barrier() {
+  tc_fence_before();
+  named_barrier_sync(kSoftBar, kSoftThreads);
+  tc_fence_after();
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kAThreads, 1)
+    attention_prefill_tc_e_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                  const __grid_constant__ CUtensorMap tmK,
+                                  const __grid_constant__ CUtensorMap tmV, AttnTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int qt = a.n_qt - 1 - (int)blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qt * kAQ;
+  const int nk = min(q0 + kAQ, a.T);
+  const int n_kt = (nk + kAK - 1) / kAK;
+  uint8_t *sQ = smem;
+  uint8_t *sKV = sQ + kATile;                          // [n_qt] K tiles, then V tiles
+  uint8_t *sE = sKV + (size_t)a.n_qt * kATile;         // [n_qt] E / P tiles
+  AttnCtlE *ctl = reinterpret_cast<AttnCtlE *>(sE + (size_t)a.n_qt * kAP);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&ctl->q_full, 1);
+    mbar_init(&ctl->q_ready, 1);
+    for (int i = 0; i < kEMaxKT; ++i) {
+      mbar_init(&ctl->k_full[i], 1);
+      mbar_init(&ctl->v_full[i], 1);
+      mbar_init(&ctl->p_full[i], kSoftWarps);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->s_full[i], 1);
+      mbar_init(&ctl->s_empty[i], kSoftWarps);
+    }
+    mbar_init(&ctl->k_dead, 1);
+    mbar_init(&ctl->o_full, 1);
+    mbar_init(&ctl->drain, 1);
+    ctl->abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&ctl->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  volatile int *abort_flag = &ctl->abort_flag;
+  pdl_wait();  // Q, K and V are the previous kernel's output
+
+  if (warp == kTmaWarp) {
+    // ---------------- TMA ----------------
+    if (lane == 0) {
+      int v_issued = 0;
+      mbar_arrive_expect_tx(&ctl->q_full, kATile);
+      tma_load_3d(sQ, &tmQ, &ctl->q_full, h * 64, q0, b);
+      for (int kt = 0; kt < n_kt; ++kt) {
+        mbar_arrive_expect_tx(&ctl->k_full[kt], kATile);
+        tma_load_3d(sKV + (size_t)kt * kATile, &tmK, &ctl->k_full[kt], h * 64, kt * kAK, b);
+      }
+      // the V tiles, once no MMA reads the K tiles any more
+      if (mbar_wait(&ctl->k_dead, 0, abort_flag, a.err, 0x1421)) {
+        for (int kt = 0; kt < n_kt; ++kt, ++v_issued) {
+          mbar_arrive_expect_tx(&ctl->v_full[kt], kATile);
+          tma_load_3d(sKV + (size_t)kt * kATile, &tmV, &ctl->v_full[kt], h * 64, kt * kAK, b);
+        }
+      }
+      if (*abort_flag) {
+        // no bulk copy may still be writing shared memory when the CTA exits
+        mbar_wait(&ctl->q_full, 0, nullptr, a.err, 0x1422);
+        for (int kt = 0; kt < n_kt; ++kt) mbar_wait(&ctl->k_full[kt], 0, nullptr, a.err, 0x1422);
+        for (int kt = 0; kt < v_issued; ++kt) mbar_wait(&ctl->v_full[kt], 0, nullptr, a.err, 0x1422);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idS = make_idesc(1, 1, kAQ, kAK);
+      const uint32_t idO = make_idesc_bmn(1, 1, kAQ, 64);
+      const uint32_t q_addr = smem_u32(sQ), kv_addr = smem_u32(sKV), e_addr = smem_u32(sE);
+      bool ok = mbar_wait(&ctl->q_ready, 0, abort_flag, a.err, 0x1423);
+      tc_fence_after();
+      int sidx = 0;
+      uint32_t k_seen = 0;
+      auto issue_s = [&](int kt) -> bool {
+        const int buf = sidx & 1;
+        if (!mbar_wait(&ctl->s_empty[buf], ((sidx >> 1) & 1) ^ 1, abort_flag, a.err, 0x1424))
+          return false;
+        if (!(k_seen & (1u << kt))) {
+          if (!mbar_wait(&ctl->k_full[kt], 0, abort_flag, a.err, 0x1425)) return false;
+          k_seen |= 1u << kt;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + kTmemS + (uint32_t)(buf * kAK);
+        const uint32_t kb = kv_addr + (uint32_t)kt * kATile;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_bf16(d, make_sw128_desc(q_addr + 32 * k), make_sw128_desc(kb + 32 * k), idS,
+                      k > 0);
+        tc_commit(&ctl->s_full[buf]);
+        ++sidx;
+        return true;
+      };
+      for (int kt = 0; kt < n_kt && ok; ++kt) ok = issue_s(kt);
+      for (int par = 0; par < 2 && ok; ++par)
+        for (int kt = par; kt < n_kt && ok; kt += 2) ok = issue_s(kt);
+      tc_commit(&ctl->k_dead);  // completes once every S MMA has read its K tile
+      for (int kt = 0; kt < n_kt && ok; ++kt) {
+        if (!(ok = mbar_wait(&ctl->p_full[kt], 0, abort_flag, a.err, 0x1426))) break;
+        if (!(ok = mbar_wait(&ctl->v_full[kt], 0, abort_flag, a.err, 0x1427))) break;
+        tc_fence_after();
+        const uint32_t vbase = kv_addr + (uint32_t)kt * kATile;
+        const uint32_t pbase = e_addr + (uint32_t)kt * kAP;
+#pragma unroll
+        for (int ks = 0; ks < kAK / 16; ++ks)
+          tc_mma_bf16(tmem + kTmemO,
+                      make_sw128_desc(pbase + (uint32_t)(ks >> 2) * kATile + 32 * (ks & 3)),
+                      make_sw128_mn_desc(vbase + (uint32_t)ks * 2048), idO, (kt > 0) || (ks > 0));
+      }
+      if (ok) {
+        tc_commit(&ctl->o_full);
+      } else {
+        tc_commit(&ctl->drain);
+        mbar_wait(&ctl->drain, 0, nullptr, a.err, 0x1428);
+      }
+    }
+  } else {
+    // ---------------- softmax warps ----------------
+    const int qd = warp & 3, cq = warp >> 2;
+    const int r = qd * 32 + lane;
+    const int qpos = q0 + r;
+    const uint32_t trow = tmem + ((uint32_t)(qd * 32) << 16);
+    const int col0 = cq * 32;
+    {  // Q *= 0.125 in place (exact), then the MMA may start
+      mbar_wait(&ctl->q_full, 0, abort_flag, a.err, 0x1429);
+      uint4 *q4 = reinterpret_cast<uint4 *>(sQ) + threadIdx.x * 2;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        uint4 v = q4[i];
+        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = pack_bf2(lo_f(w[j]) * 0.125f, hi_f(w[j]) * 0.125f);
+        q4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      named_barrier_sync(kSoftBar, kSoftThreads);
+      if (threadIdx.x == 0) mbar_arrive(&ctl->q_ready);
+    }
+    int sidx = 0;
+    auto next_scores = [&](uint32_t (&pp)[16]) {
+      const int buf = sidx & 1;
+      mbar_wait(&ctl->s_full[buf], (sidx >> 1) & 1, abort_flag, a.err, 0x142A);
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(trow + kTmemS + (uint32_t)(buf * kAK + col0), v);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->s_empty[buf]);
+      ++sidx;
+      scores_bf2(v, pp);
+    };
+
+    // ---- pass 1: row maximum ----
+    uint32_t mx2 = 0xff80ff80u;
+    float m = -INFINITY;
+    for (int kt = 0; kt < n_kt; ++kt) {
+      uint32_t pp[16];
+      next_scores(pp);
+      if (kt < qt) {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) mx2 = bf2_max(mx2, pp[c]);
+      } else {
+        const int lim = qpos - (kt * kAK + col0);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float x = (c & 1) ? hi_f(pp[c >> 1]) : lo_f(pp[c >> 1]);
+          if (c <= lim) m = fmaxf(m, x);
+        }
+      }
+    }
+    m = fmaxf(m, fmaxf(lo_f(mx2), hi_f(mx2)));
+    tmem_st_32x32b_x1(trow + kTmemX + (uint32_t)cq, __float_as_uint(m));
+    tmem_st_wait();
+    xchg_barrier();
+    {
+      uint32_t mm[4];
+      tmem_ld_32x32b_x4(trow + kTmemX, mm);
+      tmem_ld_wait();
+      m = fmaxf(fmaxf(__uint_as_float(mm[0]), __uint_as_float(mm[1])),
+                fmaxf(__uint_as_float(mm[2]), __uint_as_float(mm[3])));
+    }
+    xchg_barrier();  // every lane has read the maxima before the columns are reused
+
+    // ---- pass 2: slot sums and bf16(e) into the E tiles ----
+    float sl[32];
+    for (int par = 0; par < 2; ++par) {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) sl[c] = 0.0f;
+      for (int kt = par; kt < n_kt; kt += 2) {
+        uint32_t pp[16];
+        next_scores(pp);
+        uint8_t *tile = sE + (size_t)kt * kAP;
+        // keys past the row's own position (diagonal tile only) give e = 0
+        const int lim = kt < qt ? 31 : qpos - (kt * kAK + col0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // one 16-byte unit (8 keys) at a time
+          uint32_t e2[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int c = 4 * i + j;
+            float e0 = 0.0f, e1 = 0.0f;
+            if (2 * c <= lim) {
+              e0 = expf(lo_f(pp[c]) - m);
+              sl[2 * c] = sl[2 * c] + e0;
+            }
+            if (2 * c + 1 <= lim) {
+              e1 = expf(hi_f(pp[c]) - m);
+              sl[2 * c + 1] = sl[2 * c + 1] + e1;
+            }
+            e2[j] = pack_bf2(e0, e1);
+          }
+          *p_unit(tile, r, cq, i) = make_uint4(e2[0], e2[1], e2[2], e2[3]);
+        }
+      }
+      if (par == 0) {
+        uint32_t u[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) u[c] = __float_as_uint(sl[c]);
+        tmem_st_32x32b_x32(trow + kTmemSlots + (uint32_t)col0, u);
+        tmem_st_wait();
+      }
+    }
+    {  // fold h = 128, thread-local
+      uint32_t u[32];
+      tmem_ld_32x32b_x32(trow + kTmemSlots + (uint32_t)col0, u);
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) sl[c] = __uint_as_float(u[c]) + sl[c];
+    }
+    // h = 64 (thread cq + 2 -> cq) and h = 32 (thread 1 -> 0) through TMEM
+    if (cq >= 2) {
+      uint32_t u[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) u[c] = __float_as_uint(sl[c]);
+      tmem_st_32x32b_x32(trow + kTmemX + (uint32_t)(32 * (cq - 2)), u);
+      tmem_st_wait();
+    }
+    xchg_barrier();
+    if (cq < 2) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t u[16];
+        tmem_ld_32x32b_x16(trow + kTmemX + (uint32_t)(32 * cq + 16 * half), u);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 16; ++c) sl[16 * half + c] = sl[16 * half + c] + __uint_as_float(u[c]);
+      }
+    }
+    xchg_barrier();
+    if (cq == 1) {
+      uint32_t u[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) u[c] = __float_as_uint(sl[c]);
+      tmem_st_32x32b_x32(trow + kTmemX, u);
+      tmem_st_wait();
+    }
+    xchg_barrier();
+    if (cq == 0) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t u[16];
+        tmem_ld_32x32b_x16(trow + kTmemX + (uint32_t)(16 * half), u);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 16; ++c) sl[16 * half + c] = sl[16 * half + c] + __uint_as_float(u[c]);
+      }
+#pragma unroll
+      for (int hh = 16; hh > 0; hh >>= 1)
+#pragma unroll
+        for (int c = 0; c < hh; ++c) sl[c] = sl[c] + sl[c + hh];
+      tmem_st_32x32b_x1(trow + kTmemX + 32u, __float_as_uint(1.0f / sl[0]));
+      tmem_st_wait();
+    }
+    xchg_barrier();
+    float inv;
+    {
+      uint32_t u[4];
+      tmem_ld_32x32b_x4(trow + kTmemX + 32u, u);
+      tmem_ld_wait();
+      inv = __uint_as_float(u[0]);
+    }
+
+    // ---- pass 3: P = bf16(bf16(e) * inv) in place ----
+    for (int kt = 0; kt < n_kt; ++kt) {
+      uint8_t *tile = sE + (size_t)kt * kAP;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 *u = p_unit(tile, r, cq, i);
+        uint4 v = *u;
+        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = pack_bf2(lo_f(w[j]) * inv, hi_f(w[j]) * inv);
+        *u = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->p_full[kt]);
+    }
+
+    // ---- O: this thread's 16 head dims of its row ----
+    const bool ok = mbar_wait(&ctl->o_full, 0, abort_flag, a.err, 0x142B);
+    tc_fence_after();
+    uint32_t o[16];
+    tmem_ld_32x32b_x16(trow + kTmemO + (uint32_t)(16 * cq), o);
+    tmem_ld_wait();
+    if (ok && !*abort_flag && qpos < a.T) {
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        w[i] = pack_bf2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
+      uint16_t *dst = a.O + ((int64_t)b * a.T + qpos) * a.ldo + h * 64 + 16 * cq;
+      if (a.vec_store) {
+        reinterpret_cast<uint4 *>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4 *>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) reinterpret_cast<uint32_t *>(dst)[i] = w[i];
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 bool attention_prefill_tc_ok(const uint16_t *Q, int64_t ldq, const uint16_t *Kc,
                              const uint16_t *Vc, int64_t seq_stride, int T, int n_head) {
   return T >= 1 && T <= kAMaxKT * kAK && n_head >= 1 && aligned16(Q) && aligned16(Kc) &&
@@ -462,24 +844,40 @@ int launch_attention_prefill_tc(const uint16_t *Q, int64_t ldq, const uint16_t *
   a.ldo = ldo;
   a.vec_store = aligned16(O) && ldo % 8 == 0;
   a.err = ctx->err;
-  const size_t base = 1024 + (size_t)kATile * (1 + a.n_qt + 2) + sizeof(AttnCtl);
-  a.p_bufs = base + 2 * kAP <= 227 * 1024 ? 2 : 1;
-  size_t smem = base + (size_t)a.p_bufs * kAP;
-  // at least half of the SM's shared memory: one CTA per SM, which owns all
-  // 512 TMEM columns
-  if (smem < 116 * 1024) smem = 116 * 1024;
-  static bool attr[64] = {};
+  a.p_bufs = 1;
+  static bool attr[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return W8A8_ERR_CUDA;
-  if (!attr[dev]) {
+  const dim3 grid(a.n_qt, n_head, n_seq);
+  if (a.n_qt <= kEMaxKT) {
+    // exponentials kept on chip: Q | K, then V | E tiles
+    size_t smem = 1024 + (size_t)kATile * (1 + a.n_qt) + (size_t)kAP * a.n_qt + sizeof(AttnCtlE);
+    // at least half of the SM's shared memory: one CTA per SM, which owns all
+    // 512 TMEM columns
+    if (smem < 116 * 1024) smem = 116 * 1024;
+    if (!attr[dev][1]) {
+      if (cudaFuncSetAttribute(attention_prefill_tc_e_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
+          cudaSuccess)
+        return W8A8_ERR_CUDA;
+      attr[dev][1] = true;
+    }
+    launch_pdl(attention_prefill_tc_e_kernel, grid, dim3(kAThreads), smem, stream, tmQ, tmK, tmV,
+               a);
+    return check_launch("attention_prefill_tc_e");
+  }
+  const size_t base = 1024 + (size_t)kATile * (1 + a.n_qt + 2) + sizeof(AttnCtl);
+  a.p_bufs = base + 2 * kAP <= 227 * 1024 ? 2 : 1;
+  size_t smem = base + (size_t)a.p_bufs * kAP;
+  if (smem < 116 * 1024) smem = 116 * 1024;
+  if (!attr[dev][0]) {
     if (cudaFuncSetAttribute(attention_prefill_tc_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
         cudaSuccess)
       return W8A8_ERR_CUDA;
-    attr[dev] = true;
+    attr[dev][0] = true;
   }
-  dim3 grid(a.n_qt, n_head, n_seq);
   launch_pdl(attention_prefill_tc_kernel, grid, dim3(kAThreads), smem, stream, tmQ, tmK, tmV, a);
   return check_launch("attention_prefill_tc");
 }
