@@ -38,6 +38,11 @@ SIGNATURES = {
     "w8a8_gemm_s32": (_i, [_p, _i, _i, _p, _i, _p, _p]),
     "w8a8_linear": (_i, [_p, _p, _i, _i, _p, _p, _p, _i, _i, _p, _i64, _p, _i64, _p, _sz, _p]),
     "w8a8_linear_workspace_size": (_sz, [_i, _i]),
+    "w8a8_absmax_record_floats": (_sz, [_i, _i]),
+    "w8a8_linear_absmax": (_i, [_p, _p, _i, _i, _p, _p, _p, _i, _i, _p, _i64, _p, _i64, _p, _sz,
+                                _p, _p, _sz, _p]),
+    "w8a8_linear_from_bf16": (_i, [_p, _i64, _p, _i, _i, _i, _p, _p, _p, _i, _i, _p, _i64, _p,
+                                   _i64, _p, _p, _p, _sz, _p]),
     "w8a8_linear_noalloc": (_i, [_p, _p, _i, _i, _p, _p, _p, _i, _i, _p, _i64, _p, _i64, _p]),
     "w8a8_linear_qkv": (_i, [_p, _p, _i, _i, _p, _p, _p, _p, _i64, _p, _p, _i64, _i, _p, _p,
                              _sz, _p]),

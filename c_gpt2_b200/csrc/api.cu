@@ -127,6 +127,98 @@ extern "C" int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, cons
   return dispatch_linear(Xq, K, W, a, (cudaStream_t)stream);
 }
 
+static int epi_code(int epilogue, int *epi) {
+  switch (epilogue) {
+    case W8A8_EPI_DEQUANT: *epi = EPI_DEQUANT; return W8A8_OK;
+    case W8A8_EPI_BIAS: *epi = EPI_BIAS; return W8A8_OK;
+    case W8A8_EPI_BIAS_RESID: *epi = EPI_RESID; return W8A8_OK;
+    case W8A8_EPI_BIAS_GELU: *epi = EPI_GELU; return W8A8_OK;
+    default: return W8A8_ERR_INVALID;
+  }
+}
+
+// Parts of a row absmax record: one per CTA of the fused kernels (at most
+// one per 4 output channels), or 1 from the separate maxima kernel.
+extern "C" size_t w8a8_absmax_record_floats(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  const size_t parts = (size_t)(N + 3) / 4;
+  return (size_t)M * (parts > 1 ? parts : 1);
+}
+
+extern "C" int w8a8_linear_absmax(const int8_t *Xq, const float *sX, int M, int K,
+                                  const int8_t *W, const float *sW, const gpt2_bf16_t *bias,
+                                  int N, int epilogue, const gpt2_bf16_t *R, int64_t ldr,
+                                  gpt2_bf16_t *Y, int64_t ldy, float *absmax,
+                                  size_t absmax_floats, int *n_part, void *workspace,
+                                  size_t workspace_bytes, void *stream) {
+  if (!n_part) return W8A8_ERR_INVALID;
+  *n_part = 0;
+  if (M == 0 || N == 0) return W8A8_OK;
+  if (!Xq || !sX || !W || !sW || !Y || !absmax || M < 0 || N < 0 || K <= 0 || ldy < N)
+    return W8A8_ERR_INVALID;
+  int epi;
+  if (epi_code(epilogue, &epi)) return W8A8_ERR_INVALID;
+  if (epi != EPI_DEQUANT && !bias) return W8A8_ERR_INVALID;
+  if (epi == EPI_RESID && (!R || ldr < N)) return W8A8_ERR_INVALID;
+  if (absmax_floats < w8a8_absmax_record_floats(M, N)) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  LinearArgs a = make_args(epi, M, N, K, sX, sW, bias, R, ldr, Y, ldy);
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  a.amax_out = absmax;
+  const cudaStream_t s = (cudaStream_t)stream;
+  int parts = 0;
+  st = M == 1 ? gemv_absmax(Xq, K, W, a, &parts, s) : W8A8_ERR_UNSUPPORTED;
+  if (st == W8A8_OK) {
+    *n_part = parts;
+    return W8A8_OK;
+  }
+  if (st != W8A8_ERR_UNSUPPORTED) return st;
+  // any other shape: the GEMM, then the maxima of its output rows
+  a.amax_out = nullptr;
+  st = dispatch_linear(Xq, K, W, a, s);
+  if (st) return st;
+  float *out[1] = {absmax};
+  st = launch_row_amax(Y, ldy, M, N, out, 1, s);
+  if (st == W8A8_OK) *n_part = 1;
+  return st;
+}
+
+extern "C" int w8a8_linear_from_bf16(const gpt2_bf16_t *X, int64_t ldx, const float *absmax,
+                                     int n_part, int M, int K, const int8_t *W, const float *sW,
+                                     const gpt2_bf16_t *bias, int N, int epilogue,
+                                     const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y,
+                                     int64_t ldy, int8_t *Xq, float *sX, void *workspace,
+                                     size_t workspace_bytes, void *stream) {
+  if (M == 0 || N == 0) return W8A8_OK;
+  if (!X || !absmax || n_part < 1 || !W || !sW || !Y || !Xq || !sX || M < 0 || N < 0 || K <= 0 ||
+      K % 8 || ldx < K || ldy < N)
+    return W8A8_ERR_INVALID;
+  int epi;
+  if (epi_code(epilogue, &epi)) return W8A8_ERR_INVALID;
+  if (epi != EPI_DEQUANT && !bias) return W8A8_ERR_INVALID;
+  if (epi == EPI_RESID && (!R || ldr < N)) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  LinearArgs a = make_args(epi, M, N, K, sX, sW, bias, R, ldr, Y, ldy);
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  a.Xb = X;
+  a.ldxb = ldx;
+  a.amax_in = absmax;
+  a.n_part = n_part;
+  const cudaStream_t s = (cudaStream_t)stream;
+  st = M == 1 ? gemv_from_bf16(W, a, s) : W8A8_ERR_UNSUPPORTED;
+  if (st != W8A8_ERR_UNSUPPORTED) return st;
+  // any other shape: the quantization kernel, then the GEMM on its rows
+  st = launch_quant_rows_amax(X, ldx, M, K, absmax, n_part, M, Xq, K, sX, s);
+  if (st) return st;
+  a.Xb = nullptr;
+  a.amax_in = nullptr;
+  return dispatch_linear(Xq, K, W, a, s);
+}
+
 namespace w8a8 {
 
 // Workspace bytes w8a8_linear would read for these operands given one: nonzero

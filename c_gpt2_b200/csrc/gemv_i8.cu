@@ -21,30 +21,33 @@ typedef LinearArgs GemvArgs;
 
 constexpr int kGemvWarps = 4;
 
-__device__ __forceinline__ void gemv_store(const GemvArgs &a, int m, int n, int32_t acc) {
+// Stores output (m, n); returns the stored bf16 value as a float (0 for
+// int32 outputs). sX: the per-token scales (a.sX, or the kernel's own).
+__device__ __forceinline__ float gemv_store(const GemvArgs &a, const float *sX, int m, int n,
+                                           int32_t acc) {
   float sw = (a.epi != 0) ? a.sW[n] : 0.f;
-  float sx = (a.epi != 0) ? a.sX[m] : 0.f;
+  float sx = (a.epi != 0) ? sX[m] : 0.f;
+  uint16_t *yp = reinterpret_cast<uint16_t *>(a.Y) + (int64_t)m * a.ldy + n;
   switch (a.epi) {
     case 0:
       s32_row(a, m)[n] = acc;
-      break;
+      return 0.0f;
     case 1:
-      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(dequant_bf(acc, sw, sx));
-      break;
+      *yp = f2bf(dequant_bf(acc, sw, sx));
+      return bf2f(*yp);
     case 2:
-      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] =
-          f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bf2f(a.bias[n])));
-      break;
+      *yp = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bf2f(a.bias[n])));
+      return bf2f(*yp);
     case 3: {
       float y = add_bf(dequant_bf(acc, sw, sx), bf2f(a.bias[n]));
       float r = bf2f(a.R[(int64_t)m * a.ldr + n]);
-      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(__fadd_rn(r, y));
-      break;
+      *yp = f2bf(__fadd_rn(r, y));
+      return bf2f(*yp);
     }
     case 4: {
       float y = add_bf(dequant_bf(acc, sw, sx), bf2f(a.bias[n]));
-      reinterpret_cast<uint16_t *>(a.Y)[(int64_t)m * a.ldy + n] = f2bf(gelu_tanh(y));
-      break;
+      *yp = f2bf(gelu_tanh(y));
+      return bf2f(*yp);
     }
     default: {  // QKV scatter
       uint16_t v = f2bf(__fadd_rn(dequant_bf(acc, sw, sx), bf2f(a.bias[n])));
@@ -57,7 +60,7 @@ __device__ __forceinline__ void gemv_store(const GemvArgs &a, int m, int n, int3
         uint16_t *base = seg == 1 ? a.Kc : a.Vc;
         base[(int64_t)b * a.seq_stride + (int64_t)p * a.dseg + col] = v;
       }
-      break;
+      return bf2f(v);
     }
   }
 }
@@ -68,26 +71,30 @@ __device__ __forceinline__ void gemv_store(const GemvArgs &a, int m, int n, int3
 // they are requested before waiting for it (programmatic dependent launch):
 // the weight stream overlaps the previous kernel's tail, and only the small
 // activation rows (L2-resident, shared by the block's warps through L1) are
-// read after the wait.
-template <int MT, int NVL>
+// read after the wait. AMAX: the block also writes its row maxima of |Y|
+// (the row absmax record, one part per block).
+template <int MT, int NVL, bool AMAX>
 __global__ void __launch_bounds__(kGemvWarps * 32)
     gemv_i8_vec_kernel(const int8_t *__restrict__ X, int64_t ldx, const int8_t *__restrict__ W,
                        GemvArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n = blockIdx.x * kGemvWarps + warp;
   const int kv = a.K >> 4;  // 16-byte vectors per row
+  __shared__ unsigned s_amax[AMAX ? MT : 1];
+  if (AMAX) {
+    if (threadIdx.x < MT) s_amax[threadIdx.x] = 0u;
+    __syncthreads();
+  }
   int4 w[NVL];
-  if (n < a.N) {
-    const int4 *wrow = reinterpret_cast<const int4 *>(W + (int64_t)n * a.K);
+  const int4 *wrow = reinterpret_cast<const int4 *>(W + (int64_t)n * a.K);
 #pragma unroll
-    for (int u = 0; u < NVL; ++u) {
-      const int v = lane + 32 * u;
-      w[u] = v < kv ? __ldg(wrow + v) : make_int4(0, 0, 0, 0);
-    }
+  for (int u = 0; u < NVL; ++u) {
+    const int v = lane + 32 * u;
+    w[u] = (n < a.N && v < kv) ? __ldg(wrow + v) : make_int4(0, 0, 0, 0);
   }
   pdl_wait();
   pdl_launch_dependents();
-  if (n >= a.N) return;
+  if (!AMAX && n >= a.N) return;
   int acc[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = 0;
@@ -115,8 +122,17 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   }
   // lane m stores token m (spreads the epilogue over the warp)
 #pragma unroll
-  for (int m = 0; m < MT; ++m)
-    if (lane == m && m < a.M) gemv_store(a, m, n, acc[m]);
+  for (int m = 0; m < MT; ++m) {
+    if (lane == m && m < a.M && n < a.N) {
+      const float y = gemv_store(a, a.sX, m, n, acc[m]);
+      if (AMAX) atomicMax(&s_amax[m], __float_as_uint(fabsf(y)));
+    }
+  }
+  if (AMAX) {
+    __syncthreads();
+    if ((int)threadIdx.x < a.M)
+      a.amax_out[(int64_t)blockIdx.x * a.M + threadIdx.x] = __uint_as_float(s_amax[threadIdx.x]);
+  }
 }
 
 // Single-token path for long rows (M == 1, K > 2048: the W2 projection of a
@@ -126,9 +142,14 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
 // into registers) before waiting for the previous kernel, so the GEMV's
 // weight stream is in flight during that kernel's tail (programmatic
 // dependent launch).
+//
+// FROM_BF16: the token row arrives as bf16 (a.Xb) with the row absmax record
+// (a.amax_in, a.n_part parts); the CTA quantizes it once into shared memory
+// with the reference's per-token rule (cuda/activation_quant.cu:37-110).
 constexpr int kRowsWarps = 16;
+constexpr int kRowsMaxK = 16 * 32 * 16;  // NVL <= 16 vectors of 16 bytes a lane
 
-template <int NVL, int RPW>
+template <int NVL, int RPW, bool FROM_BF16>
 __global__ void __launch_bounds__(kRowsWarps * 32)
     gemv_i8_rows_kernel(const int8_t *__restrict__ X, const int8_t *__restrict__ W, GemvArgs a,
                         int rows) {
@@ -149,12 +170,55 @@ __global__ void __launch_bounds__(kRowsWarps * 32)
   }
   pdl_wait();
   pdl_launch_dependents();
+  __shared__ __align__(16) int8_t xs[FROM_BF16 ? kRowsMaxK : 16];
+  __shared__ float s_red[kRowsWarps];
+  __shared__ float s_sx[1];
+  if (FROM_BF16) {
+    constexpr int kT = kRowsWarps * 32;
+    constexpr int kU = kRowsMaxK / 16 / kT;  // 16-element units per thread
+    uint4 xb[kU][2];
+#pragma unroll
+    for (int j = 0; j < kU; ++j) {  // the row's loads first: they overlap the maxima
+      const int u = (int)threadIdx.x + j * kT;
+      if (u * 16 < a.K) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.Xb + 16 * u);
+        xb[j][0] = src[0];
+        xb[j][1] = src[1];
+      }
+    }
+    // the record's parts: the first 4 per thread in flight together
+    float pv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int p = (int)threadIdx.x + j * kT;
+      pv[j] = p < a.n_part ? a.amax_in[p] : 0.0f;
+    }
+    float mx = fmaxf(fmaxf(pv[0], pv[1]), fmaxf(pv[2], pv[3]));
+    for (int p = (int)threadIdx.x + 4 * kT; p < a.n_part; p += kT) mx = fmaxf(mx, a.amax_in[p]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    mx = s_red[0];
+#pragma unroll
+    for (int i = 1; i < kRowsWarps; ++i) mx = fmaxf(mx, s_red[i]);
+    const float sc = quant_scale(mx), inv = __fdiv_rn(1.0f, sc);
+    if (threadIdx.x == 0) s_sx[0] = sc;
+#pragma unroll
+    for (int j = 0; j < kU; ++j) {
+      const int u = (int)threadIdx.x + j * kT;
+      if (u * 16 < a.K) *reinterpret_cast<uint4 *>(xs + 16 * u) = quant16(xb[j][0], xb[j][1], inv);
+    }
+    __syncthreads();
+  }
   int4 x[NVL];
-  const int4 *xrow = reinterpret_cast<const int4 *>(X);
 #pragma unroll
   for (int u = 0; u < NVL; ++u) {
     const int v = lane + 32 * u;
-    x[u] = v < kv ? __ldg(xrow + v) : make_int4(0, 0, 0, 0);
+    if (FROM_BF16)
+      x[u] = v < kv ? reinterpret_cast<const int4 *>(xs)[v] : make_int4(0, 0, 0, 0);
+    else
+      x[u] = v < kv ? __ldg(reinterpret_cast<const int4 *>(X) + v) : make_int4(0, 0, 0, 0);
   }
 #pragma unroll
   for (int i = 0; i < RPW; ++i) {
@@ -169,7 +233,7 @@ __global__ void __launch_bounds__(kRowsWarps * 32)
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0 && n < n_end) gemv_store(a, 0, n, acc);
+    if (lane == 0 && n < n_end) gemv_store(a, FROM_BF16 ? s_sx : a.sX, 0, n, acc);
   }
 }
 
@@ -187,14 +251,15 @@ __global__ void gemv_i8_scalar_kernel(const int8_t *__restrict__ X, int64_t ldx,
     acc += (int)X[(int64_t)m * ldx + k] * (int)W[(int64_t)n * a.K + k];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) gemv_store(a, m, n, acc);
+  if (lane == 0) gemv_store(a, a.sX, m, n, acc);
 }
 
-template <int MT, int NVL>
+template <int MT, int NVL, bool AMAX = false>
 static int launch_vec(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs &a,
                       cudaStream_t s) {
   dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps);
-  launch_pdl(gemv_i8_vec_kernel<MT, NVL>, dim3(grid), dim3(kGemvWarps * 32), 0, s, X, ldx, W, a);
+  launch_pdl(gemv_i8_vec_kernel<MT, NVL, AMAX>, dim3(grid), dim3(kGemvWarps * 32), 0, s, X, ldx,
+             W, a);
   return check_launch("gemv_i8_vec");
 }
 
@@ -209,24 +274,25 @@ static int launch_vec_k(const int8_t *X, int64_t ldx, const int8_t *W, const Gem
   return W8A8_ERR_UNSUPPORTED;
 }
 
-template <int NVL, int RPW>
+template <int NVL, int RPW, bool FROM_BF16 = false>
 static int launch_rows(const int8_t *X, const int8_t *W, const GemvArgs &a, int rows,
                        cudaStream_t s) {
   const int grid = (a.N + rows - 1) / rows;
-  launch_pdl(gemv_i8_rows_kernel<NVL, RPW>, dim3(grid), dim3(kRowsWarps * 32), 0, s, X, W, a,
-             rows);
+  launch_pdl(gemv_i8_rows_kernel<NVL, RPW, FROM_BF16>, dim3(grid), dim3(kRowsWarps * 32), 0, s,
+             X, W, a, rows);
   return check_launch("gemv_i8_rows");
 }
 
 // rows per warp (1..3) x 16-byte weight vectors per lane per row (K / 512,
 // rounded up): a lane holds at most 16 weight vectors (128 registers a
 // thread with 512 threads a CTA, without spilling)
-template <int NVL>
+template <int NVL, bool FROM_BF16 = false>
 static int launch_rows_k(const int8_t *X, const int8_t *W, const GemvArgs &a, int rows,
                          cudaStream_t s) {
   const int rpw = (rows + kRowsWarps - 1) / kRowsWarps;
-  if (rpw <= 1) return launch_rows<NVL, 1>(X, W, a, rows, s);
-  if (rpw <= 2 && NVL <= 8) return launch_rows<NVL, (NVL <= 8 ? 2 : 1)>(X, W, a, rows, s);
+  if (rpw <= 1) return launch_rows<NVL, 1, FROM_BF16>(X, W, a, rows, s);
+  if (rpw <= 2 && NVL <= 8)
+    return launch_rows<NVL, (NVL <= 8 ? 2 : 1), FROM_BF16>(X, W, a, rows, s);
   return W8A8_ERR_UNSUPPORTED;
 }
 
@@ -258,6 +324,38 @@ int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs
   dim3 grid((a.N + kGemvWarps - 1) / kGemvWarps, a.M);
   launch_pdl(gemv_i8_scalar_kernel, dim3(grid), dim3(kGemvWarps * 32), 0, s, X, ldx, W, a);
   return check_launch("gemv_i8_scalar");
+}
+
+// One token through the 4-warp GEMV with the row absmax record (one part per
+// block); W8A8_ERR_UNSUPPORTED where another kernel would run.
+int gemv_absmax(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs &a, int *n_part,
+                cudaStream_t s) {
+  const bool vec = (a.K % 16 == 0) && (ldx % 16 == 0) && aligned16(X) && aligned16(W);
+  if (!vec || a.M != 1 || !a.amax_out || a.epi == EPI_S32) return W8A8_ERR_UNSUPPORTED;
+  int st;
+  DeviceCtx *ctx = device_ctx(&st);
+  if (!ctx) return st;
+  const int nvl = ((a.K >> 4) + 31) / 32;
+  if (nvl > 4) return W8A8_ERR_UNSUPPORTED;  // long rows take the 16-warp kernel
+  *n_part = (a.N + kGemvWarps - 1) / kGemvWarps;
+  if (nvl <= 2) return launch_vec<1, 2, true>(X, ldx, W, a, s);
+  return launch_vec<1, 4, true>(X, ldx, W, a, s);
+}
+
+// One token with a long bf16 row (K > 2048) through the 16-warp GEMV that
+// quantizes the row itself; W8A8_ERR_UNSUPPORTED elsewhere.
+int gemv_from_bf16(const int8_t *W, const GemvArgs &a, cudaStream_t s) {
+  if (a.M != 1 || !a.Xb || !a.amax_in || a.n_part < 1 || a.K % 16 || a.K > kRowsMaxK ||
+      !aligned16(a.Xb) || !aligned16(W) || a.epi == EPI_S32)
+    return W8A8_ERR_UNSUPPORTED;
+  int st;
+  DeviceCtx *ctx = device_ctx(&st);
+  if (!ctx) return st;
+  const int rows = (a.N + ctx->sm_count - 1) / ctx->sm_count;
+  const int nvl = ((a.K >> 4) + 31) / 32;
+  if (nvl > 4 && nvl <= 8) return launch_rows_k<8, true>(nullptr, W, a, rows, s);
+  if (nvl > 8 && nvl <= 16) return launch_rows_k<16, true>(nullptr, W, a, rows, s);
+  return W8A8_ERR_UNSUPPORTED;
 }
 
 }  // namespace w8a8

@@ -46,7 +46,43 @@ struct LinearArgs {
   // sum slot that this GPU owns in the buffer of the GPU owning row m.
   int32_t *dst[8];
   int rows_per_dst;
+  // Row absmax record of the batch-1 MLP pair (W1 -> W2): a kernel given
+  // amax_out also writes, for each of its CTAs, the largest |Y| of every row
+  // among the outputs that CTA stored: amax_out[cta * M + m] (0 for rows it
+  // did not touch). A kernel given Xb quantizes its bf16 input rows itself
+  // (Xb row stride ldxb, the reference's per-token rule) with the row maxima
+  // of the n_part partials amax_in[part * M + m].
+  float *amax_out;
+  const uint16_t *Xb;
+  int64_t ldxb;
+  const float *amax_in;
+  int n_part;
 };
+
+// The reference's per-token scale of a row whose largest |x| is amax
+// (cuda/activation_quant.cu:75-91), and its quantization of one value.
+__device__ __forceinline__ float quant_scale(float amax) {
+  return amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+}
+__device__ __forceinline__ int quant_value(float x, float inv) {
+  const int q = __float2int_rn(__fmul_rn(x, inv));
+  return q > 127 ? 127 : (q < -127 ? -127 : q);
+}
+// 16 bf16 (two 16-byte vectors) -> 16 int8 with the row's 1 / scale.
+__device__ __forceinline__ uint4 quant16(const uint4 &lo, const uint4 &hi, float inv) {
+  const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int a0 = quant_value(__uint_as_float(w[2 * j] << 16), inv);
+    const int a1 = quant_value(__uint_as_float(w[2 * j] & 0xffff0000u), inv);
+    const int a2 = quant_value(__uint_as_float(w[2 * j + 1] << 16), inv);
+    const int a3 = quant_value(__uint_as_float(w[2 * j + 1] & 0xffff0000u), inv);
+    o[j] = (uint32_t)(a0 & 0xff) | ((uint32_t)(a1 & 0xff) << 8) | ((uint32_t)(a2 & 0xff) << 16) |
+           ((uint32_t)(a3 & 0xff) << 24);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
 
 // Row address of the int32 output of row m (plain or scattered).
 __host__ __device__ inline int32_t *s32_row(const LinearArgs &a, int m) {
@@ -107,6 +143,11 @@ size_t linear_workspace_used(const int8_t *Xq, const float *sX, int M, int K, co
 // gemv_i8.cu
 int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const LinearArgs &a,
                    cudaStream_t s);
+// The batch-1 MLP pair of the row absmax record (LinearArgs::amax_out / Xb):
+// W8A8_ERR_UNSUPPORTED where the operands take a kernel without it.
+int gemv_absmax(const int8_t *X, int64_t ldx, const int8_t *W, const LinearArgs &a, int *n_part,
+                cudaStream_t s);
+int gemv_from_bf16(const int8_t *W, const LinearArgs &a, cudaStream_t s);
 // norm_quant.cu
 int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, float *sX,
                       cudaStream_t s);

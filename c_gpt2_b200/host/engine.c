@@ -59,6 +59,9 @@ struct gpt2_engine {
   cudaStream_t stream2;
   cudaEvent_t ev_fork, ev_join;
   void *attn_ws2, *lin_ws2;
+  /* row absmax records of the decode W1 -> W2 pair (one per half) */
+  float *amax_rec, *amax_rec2;
+  size_t amax_rec_floats;
   int decode_split; /* 1: one chain of B rows; 2: two chains of B/2 rows on two streams */
   /* current batch: B slots (rows) of the decode step */
   int B;
@@ -221,7 +224,8 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   /* activations */
   e->attn_ws_bytes = w8a8_attention_decode_workspace_size((int)Bm, cfg->n_head, (int)C);
   e->lin_ws_bytes = w8a8_linear_workspace_size((int)Bm, 4 * (int)d);
-  size_t off = 0, sizes[17];
+  e->amax_rec_floats = w8a8_absmax_record_floats((int)Bm, 4 * (int)d);
+  size_t off = 0, sizes[19];
   sizes[0] = Mt * d * 2;        /* H */
   sizes[1] = Mt * d * 2;        /* R1 */
   sizes[2] = Mt * d * 2;        /* Q */
@@ -239,8 +243,10 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   sizes[14] = Bm * C * 4;       /* sampling draws [max_batch][ctx] */
   sizes[15] = e->attn_ws_bytes; /* second decode half */
   sizes[16] = e->lin_ws_bytes;
-  size_t offs[17];
-  for (int i = 0; i < 17; ++i) {
+  sizes[17] = e->amax_rec_floats * 4; /* row absmax records */
+  sizes[18] = e->amax_rec_floats * 4;
+  size_t offs[19];
+  for (int i = 0; i < 19; ++i) {
     offs[i] = off;
     off += ALIGN_UP(sizes[i], 256);
   }
@@ -269,6 +275,8 @@ int gpt2_engine_create(const gpt2_engine_config *cfg, int device, gpt2_engine **
   e->rnd = (float *)(a + offs[14]);
   e->attn_ws2 = a + offs[15];
   e->lin_ws2 = a + offs[16];
+  e->amax_rec = (float *)(a + offs[17]);
+  e->amax_rec2 = (float *)(a + offs[18]);
   e->top_k = 40;
   e->decode_split = 1;
   if (cudaMemset(e->ablob, 0, off) != cudaSuccess) {
@@ -584,6 +592,7 @@ typedef struct {
   int8_t *Xq;
   float *sX;
   void *attn_ws, *lin_ws;
+  float *amax; /* row absmax record */
   void *s;
 } act_view;
 
@@ -603,6 +612,7 @@ static act_view view_at(gpt2_engine *e, int row0, int half) {
   v.sX = e->sX + row0;
   v.attn_ws = half ? e->attn_ws2 : e->attn_ws;
   v.lin_ws = half ? e->lin_ws2 : e->lin_ws;
+  v.amax = half ? e->amax_rec2 : e->amax_rec;
   v.s = (void *)(half ? e->stream2 : e->stream);
   return v;
 }
@@ -635,6 +645,18 @@ static int block_forward(gpt2_engine *e, const act_view *v, int l, int slot0, in
   W8_TRY(e, w8a8_linear(v->Xq, v->sX, M, d, w->Wproj, w->sWproj, w->bproj, d, W8A8_EPI_BIAS_RESID,
                         v->H, d, v->R1, d, v->lin_ws, lwb, s));
   W8_TRY(e, w8a8_layernorm_quant(v->R1, d, M, d, w->ln2_g, w->ln2_b, eps, NULL, 0, v->Xq, v->sX, s));
+  if (pos0 != NULL && M == 1) {
+    /* batch-1 decode: W1's epilogue records the row maxima of its GELU output
+     * and W2 quantizes the row itself (no separate quantization launch) */
+    int n_part = 0;
+    W8_TRY(e, w8a8_linear_absmax(v->Xq, v->sX, M, d, w->W1, w->sW1, w->b1, f, W8A8_EPI_BIAS_GELU,
+                                 NULL, 0, v->X1, f, v->amax, e->amax_rec_floats, &n_part,
+                                 v->lin_ws, lwb, s));
+    W8_TRY(e, w8a8_linear_from_bf16(v->X1, f, v->amax, n_part, M, f, w->W2, w->sW2, w->b2, d,
+                                    W8A8_EPI_BIAS_RESID, v->R1, d, v->H, d, v->Xq, v->sX,
+                                    v->lin_ws, lwb, s));
+    return W8A8_OK;
+  }
   W8_TRY(e, w8a8_linear(v->Xq, v->sX, M, d, w->W1, w->sW1, w->b1, f, W8A8_EPI_BIAS_GELU, NULL, 0,
                         v->X1, f, v->lin_ws, lwb, s));
   W8_TRY(e, w8a8_quant_rows(v->X1, f, M, f, v->Xq, v->sX, s));

@@ -7,6 +7,8 @@ function has a counterpart there.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -111,6 +113,46 @@ def linear(Xq, sX, W, sW, bias, epilogue=_lib.EPI_BIAS, R=None, out=None, worksp
     check(core().w8a8_linear(_ptr(Xq), _ptr(sX), M, K, _ptr(W), _ptr(sW), _ptr(bias), N, epilogue,
                              _ptr(R), ldr, _ptr(Y), Y.stride(0), _ptr(workspace), ws_bytes,
                              _stream()), "w8a8_linear")
+    return Y
+
+
+def linear_absmax(Xq, sX, W, sW, bias, epilogue=_lib.EPI_BIAS_GELU, R=None, out=None,
+                  workspace=None):
+    """linear() that also returns the row absmax record of its output:
+    (Y, record [n_part, M] float32) with record.max(0) = max_n |Y[m, n]|."""
+    _need(Xq, torch.int8, "Xq")
+    M, K = Xq.shape
+    N = W.shape[0]
+    Y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=Xq.device)
+    ldr = R.stride(0) if R is not None else 0
+    ws_bytes = workspace.numel() if workspace is not None else 0
+    cap = core().w8a8_absmax_record_floats(M, N)
+    rec = torch.empty(cap, dtype=torch.float32, device=Xq.device)
+    n_part = ctypes.c_int(0)
+    check(core().w8a8_linear_absmax(_ptr(Xq), _ptr(sX), M, K, _ptr(W), _ptr(sW), _ptr(bias), N,
+                                    epilogue, _ptr(R), ldr, _ptr(Y), Y.stride(0), _ptr(rec), cap,
+                                    ctypes.byref(n_part), _ptr(workspace), ws_bytes, _stream()),
+          "w8a8_linear_absmax")
+    return Y, rec[: n_part.value * M].view(n_part.value, M)
+
+
+def linear_from_bf16(X, record, W, sW, bias, epilogue=_lib.EPI_BIAS_RESID, R=None, out=None,
+                     workspace=None, Xq=None, sX=None):
+    """linear() on the per-token quantization of the bf16 rows X, whose row
+    maxima are the parts of `record` ([n_part, M], from linear_absmax)."""
+    _need(X, torch.bfloat16, "X")
+    M, K = X.shape
+    N = W.shape[0]
+    Y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=X.device)
+    Xq = Xq if Xq is not None else torch.empty((M, K), dtype=torch.int8, device=X.device)
+    sX = sX if sX is not None else torch.empty(M, dtype=torch.float32, device=X.device)
+    ldr = R.stride(0) if R is not None else 0
+    ws_bytes = workspace.numel() if workspace is not None else 0
+    check(core().w8a8_linear_from_bf16(_ptr(X), X.stride(0), _ptr(record), record.shape[0], M, K,
+                                       _ptr(W), _ptr(sW), _ptr(bias), N, epilogue, _ptr(R), ldr,
+                                       _ptr(Y), Y.stride(0), _ptr(Xq), _ptr(sX),
+                                       _ptr(workspace), ws_bytes, _stream()),
+          "w8a8_linear_from_bf16")
     return Y
 
 

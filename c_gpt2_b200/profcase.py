@@ -10,6 +10,7 @@ size of the large model (d_model 1280, 20 heads, context 1024).
     python -m c_gpt2_b200.profcase linear --m 64 --n 5120 --k 1280 --epi gelu
     python -m c_gpt2_b200.profcase decode [--model medium] [--batch 1] [--prompt 512] [--gen 256]
     python -m c_gpt2_b200.profcase gemv-chain [--model large] [--layers 36]
+    python -m c_gpt2_b200.profcase mlp-pair [--model large] [--m 64] [--layers 36]
     python -m c_gpt2_b200.profcase sample [--rows 64] [--top-k 40] [--temperature 0.8]
 
 Every case holds well under 1 GB on the device and exceeds the 126 MB L2 only
@@ -20,6 +21,7 @@ CUDA-event time per launch, measured after the profiled launches.
 from __future__ import annotations
 
 import argparse
+import ctypes
 
 import torch
 
@@ -158,6 +160,79 @@ def linear(a) -> None:
           f"{ops_ / us / 1e6:.0f} TOP/s, {byts / us / 1e3:.0f} GB/s algorithmic")
 
 
+def mlp_pair(a) -> None:
+    """The decode MLP pair of a model, W1 (+GELU) then W2 (+residual), for
+    --m tokens over --layers layers of distinct weights (streamed from HBM as
+    in a decode step), in one CUDA graph per variant: W1 -> quant_rows -> W2
+    against the fused pair (W1 with the row absmax record -> W2 quantizing
+    its bf16 input), and each half of both alone."""
+    from .quant8 import DIMS
+    dims = DIMS[a.model]
+    d, L, M = dims.d_model, a.layers, a.m
+    f = 4 * d
+    g = torch.Generator(device="cuda").manual_seed(0)
+    W1 = [torch.randint(-127, 128, (f, d), dtype=torch.int8, device="cuda", generator=g)
+          for _ in range(L)]
+    W2 = [torch.randint(-127, 128, (d, f), dtype=torch.int8, device="cuda", generator=g)
+          for _ in range(L)]
+    sw1 = torch.rand((f,), device="cuda", generator=g) * 1e-3 + 1e-4
+    sw2 = torch.rand((d,), device="cuda", generator=g) * 1e-3 + 1e-4
+    b1 = (torch.randn((f,), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    b2 = (torch.randn((d,), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    xq = torch.randint(-127, 128, (M, d), dtype=torch.int8, device="cuda", generator=g)
+    sx = torch.full((M,), 1e-2, device="cuda")
+    R = torch.randn((M, d), device="cuda", generator=g).to(torch.bfloat16)
+    X1 = torch.empty((M, f), dtype=torch.bfloat16, device="cuda")
+    Y = torch.empty((M, d), dtype=torch.bfloat16, device="cuda")
+    q2 = torch.empty((M, f), dtype=torch.int8, device="cuda")
+    s2 = torch.empty((M,), device="cuda")
+    ws = ops.linear_workspace(M, f, "cuda")
+    lib = _lib.core()
+    cap = lib.w8a8_absmax_record_floats(M, f)
+    rec = torch.empty(cap, dtype=torch.float32, device="cuda")
+    n_part = ctypes.c_int(0)
+    p = ops._ptr
+
+    def w1_plain(i):
+        ops.linear(xq, sx, W1[i], sw1, b1, EPI["gelu"], out=X1, workspace=ws)
+
+    def quant():
+        _lib.check(lib.w8a8_quant_rows(p(X1), f, M, f, p(q2), p(s2), ops._stream()), "quant")
+
+    def w2_plain(i):
+        ops.linear(q2, s2, W2[i], sw2, b2, EPI["resid"], R=R, out=Y, workspace=ws)
+
+    def w1_absmax(i):
+        _lib.check(lib.w8a8_linear_absmax(p(xq), p(sx), M, d, p(W1[i]), p(sw1), p(b1), f,
+                                          EPI["gelu"], None, 0, p(X1), f, p(rec), cap,
+                                          ctypes.byref(n_part), p(ws), ws.numel(),
+                                          ops._stream()), "absmax")
+
+    def w2_bf16(i):
+        _lib.check(lib.w8a8_linear_from_bf16(p(X1), f, p(rec), n_part.value, M, f, p(W2[i]),
+                                             p(sw2), p(b2), d, EPI["resid"], p(R), d, p(Y), d,
+                                             p(q2), p(s2), p(ws), ws.numel(), ops._stream()),
+                   "from_bf16")
+
+    w1_absmax(0)
+    torch.cuda.synchronize()
+    variants = {
+        "W1 -> quant -> W2": lambda: [(w1_plain(i), quant(), w2_plain(i)) for i in range(L)],
+        "W1(absmax) -> W2(bf16 in)": lambda: [(w1_absmax(i), w2_bf16(i)) for i in range(L)],
+        "W1 alone": lambda: [w1_plain(i) for i in range(L)],
+        "W1(absmax) alone": lambda: [w1_absmax(i) for i in range(L)],
+        "quant alone": lambda: [quant() for i in range(L)],
+        "W2 alone": lambda: [w2_plain(i) for i in range(L)],
+        "W2(bf16 in) alone": lambda: [w2_bf16(i) for i in range(L)],
+    }
+    for name, fn in variants.items():
+        fn()
+        torch.cuda.synchronize()
+        ms = _replay_ms(_graph(fn, 1, False))
+        print(f"mlp-pair {a.model} M={M} x{L} layers, {name}: {1000 * ms / L:.2f} us/layer "
+              f"(parts {n_part.value})")
+
+
 def gemv_chain(a) -> None:
     """The batch-1 decode GEMVs of a model back to back: per layer W_qkv,
     attn_proj, W1, W2 with their epilogues, each layer with its own weights
@@ -280,6 +355,10 @@ def main(argv=None) -> None:
     p.add_argument("--n", type=int, required=True)
     p.add_argument("--k", type=int, required=True)
     p.add_argument("--epi", choices=sorted(EPI), default="bias")
+    p = sub.add_parser("mlp-pair")
+    p.add_argument("--model", choices=["small", "medium", "large"], default="large")
+    p.add_argument("--m", type=int, default=64)
+    p.add_argument("--layers", type=int, default=36)
     p = sub.add_parser("sample")
     p.add_argument("--rows", type=int, default=64)
     p.add_argument("--top-k", type=int, default=40)
@@ -295,7 +374,7 @@ def main(argv=None) -> None:
         _FLUSH = torch.ones((64 << 20,), dtype=torch.float32, device="cuda")
     {"attention-decode": attention_decode, "attention-prefill": attention_prefill,
      "layernorm-quant": layernorm_quant, "linear": linear, "decode": decode,
-     "gemv-chain": gemv_chain, "sample": sample}[a.case](a)
+     "gemv-chain": gemv_chain, "sample": sample, "mlp-pair": mlp_pair}[a.case](a)
     st = ops.device_error()
     if st:
         raise SystemExit(f"device error word {st}")

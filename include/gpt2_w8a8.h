@@ -104,6 +104,42 @@ int w8a8_linear(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W
                 const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy,
                 void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- the W1 -> W2 pair with the quantization of W1's output fused ----
+ * The reference quantizes the GELU output per token as a kernel of its own
+ * between the two MLP GEMMs (gpt2.c:1296-1320: gelu_cuda, then
+ * dot_2d_gpu_int8 -> per_token_quant_cuda, cuda/activation_quant.cu:37-110).
+ * Here the first GEMM's epilogue also records each row's largest |y| as
+ * partial maxima (the row absmax record: absmax[part * M + m], one part per
+ * CTA of the kernel that wrote the rows), and the second GEMM quantizes its
+ * bf16 input rows itself with the reference's rule (scale = amax / 127, or 1
+ * for an all-zero row; q = rn(x * (1 / scale)) clamped to +-127): the same
+ * int8 rows and scales as w8a8_quant_rows, without its launch and without
+ * the int8 copy of the rows. Fused for one token (the batch-1 decode GEMVs,
+ * where it saves a launch per layer); other shapes run the separate maxima /
+ * quantization kernels, with the same results: there every output tile of
+ * the second GEMM would quantize the same input columns again, which costs
+ * more than the one quantization launch it saves.
+ *
+ * w8a8_linear_absmax: w8a8_linear (bf16 epilogues only) that also writes the
+ * record into absmax (at least w8a8_absmax_record_floats(M, N) floats) and
+ * its part count into *n_part (host). */
+size_t w8a8_absmax_record_floats(int M, int N);
+int w8a8_linear_absmax(const int8_t *Xq, const float *sX, int M, int K, const int8_t *W,
+                       const float *sW, const gpt2_bf16_t *bias, int N, int epilogue,
+                       const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy,
+                       float *absmax, size_t absmax_floats, int *n_part, void *workspace,
+                       size_t workspace_bytes, void *stream);
+/* w8a8_linear on the per-token quantization of the bf16 rows X (row stride
+ * ldx, K % 8 == 0), whose row maxima are the n_part partials of absmax.
+ * Xq [M][K] / sX [M] receive the quantized rows and scales where the shape
+ * takes the separate quantization kernel; the fused kernels leave them as
+ * they are. */
+int w8a8_linear_from_bf16(const gpt2_bf16_t *X, int64_t ldx, const float *absmax, int n_part,
+                          int M, int K, const int8_t *W, const float *sW,
+                          const gpt2_bf16_t *bias, int N, int epilogue, const gpt2_bf16_t *R,
+                          int64_t ldr, gpt2_bf16_t *Y, int64_t ldy, int8_t *Xq, float *sX,
+                          void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- w8a8_linear without a caller-provided workspace ----
  * No counterpart in the reference. For callers that cannot allocate device
  * memory (a host that sizes all device memory once at start-up, a plugin whose

@@ -413,3 +413,89 @@ def test_embed_layernorm_warp_rows_equal_block_rows(cuda):
         r = slice(s * T, (s + 1) * T)
         assert torch.equal(H[r], h) and torch.equal(Y[r], y)
         assert torch.equal(Xq[r], q) and torch.equal(sX[r], sx)
+
+
+def _cuda_kernels(fn):
+    """Names of the CUDA kernels fn launches."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+
+
+def _mlp_operands(rng, M, d):
+    f = 4 * d
+    x = oracle.bf16_bits(outlier_activations(M, d, seed=M + d))
+    xq, sx = oracle.quant_rows(x)
+    W1 = rng.integers(-127, 128, (f, d), dtype=np.int8)
+    W2 = rng.integers(-127, 128, (d, f), dtype=np.int8)
+    sw1 = rng.uniform(1e-4, 1e-3, f).astype(np.float32)
+    sw2 = rng.uniform(1e-4, 1e-3, d).astype(np.float32)
+    b1 = _rand_bf16(rng, f, 0.02)
+    b2 = _rand_bf16(rng, d, 0.02)
+    R = _rand_bf16(rng, (M, d))
+    dev = [to_dev(xq), to_dev(sx), to_dev(W1), to_dev(sw1), to_dev_bf16(b1), to_dev(W2),
+           to_dev(sw2), to_dev_bf16(b2), to_dev_bf16(R)]
+    return dev
+
+
+@pytest.mark.parametrize("M", [1, 2, 8, 37, 64, 128, 200])
+@pytest.mark.parametrize("d", [768, 1280])
+def test_mlp_pair_fused_quantization(cuda, M, d):
+    """W1 (+GELU) -> W2 with the quantization of W1's output fused
+    (w8a8_linear_absmax -> w8a8_linear_from_bf16) against W1 -> quant_rows
+    -> W2: bit-identical outputs; the record's row maxima are the rows'
+    largest |y|; for one token (the fused GEMVs) no quantization or maxima
+    kernel runs."""
+    rng = np.random.default_rng(M * 5 + d)
+    xq, sx, W1, sw1, b1, W2, sw2, b2, R = _mlp_operands(rng, M, d)
+    ws = ops.linear_workspace(M, 4 * d, cuda)
+    X1 = ops.linear(xq, sx, W1, sw1, b1, _lib.EPI_BIAS_GELU, workspace=ws)
+    q2, s2 = ops.per_token_quant(X1)
+    want = ops.linear(q2, s2, W2, sw2, b2, _lib.EPI_BIAS_RESID, R=R, workspace=ws)
+
+    out = {}
+
+    def fused():
+        X1f, rec = ops.linear_absmax(xq, sx, W1, sw1, b1, _lib.EPI_BIAS_GELU, workspace=ws)
+        out["X1"], out["rec"] = X1f, rec
+        out["Y"] = ops.linear_from_bf16(X1f, rec, W2, sw2, b2, _lib.EPI_BIAS_RESID, R=R,
+                                        workspace=ws)
+
+    names = _cuda_kernels(fused)
+    assert torch.equal(out["X1"].view(torch.int16), X1.view(torch.int16))
+    amax = X1.float().abs().amax(1)
+    assert torch.equal(out["rec"].amax(0), amax)
+    assert torch.equal(out["Y"].view(torch.int16), want.view(torch.int16))
+    quant = [n for n in names if "quant" in n or "amax" in n]
+    if M == 1:
+        assert not quant, names
+        assert len(names) == 2, names
+    assert ops.device_error(reset=True) == 0
+
+
+@pytest.mark.parametrize("M,K,n_part", [(1, 5120, 1), (1, 5120, 7), (3, 3072, 5), (64, 5120, 120),
+                                        (128, 1024, 2), (300, 1024, 3)])
+def test_linear_from_bf16_matches_quant_rows(cuda, M, K, n_part):
+    """The in-kernel quantization against quant_rows on the same bf16 rows:
+    zero rows (scale 1), outlier channels, the row maxima spread over n_part
+    parts (each row's maximum in one part, the others below it)."""
+    rng = np.random.default_rng(M + K + n_part)
+    x = outlier_activations(M, K, seed=M * 3 + K)
+    x[M // 2] = 0.0
+    X = to_dev_bf16(oracle.bf16_bits(x))
+    amax = X.float().abs().amax(1)
+    rec = (amax[None, :] * torch.rand((n_part, M), device=cuda)).contiguous()
+    rec[torch.from_numpy(rng.integers(0, n_part, M)).to(cuda), torch.arange(M, device=cuda)] = amax
+    N = 768
+    W = to_dev(rng.integers(-127, 128, (N, K), dtype=np.int8))
+    sw = to_dev(rng.uniform(1e-4, 1e-3, N).astype(np.float32))
+    b = to_dev_bf16(_rand_bf16(rng, N, 0.02))
+    ws = ops.linear_workspace(M, N, cuda)
+    xq, sx = ops.per_token_quant(X)
+    want = ops.linear(xq, sx, W, sw, b, _lib.EPI_BIAS, workspace=ws)
+    got = ops.linear_from_bf16(X, rec, W, sw, b, _lib.EPI_BIAS, workspace=ws)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    assert ops.device_error(reset=True) == 0
