@@ -499,3 +499,30 @@ def test_linear_from_bf16_matches_quant_rows(cuda, M, K, n_part):
     got = ops.linear_from_bf16(X, rec, W, sw, b, _lib.EPI_BIAS, workspace=ws)
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
     assert ops.device_error(reset=True) == 0
+
+
+def test_prefill_gelu_every_bf16_input(cuda):
+    """The GELU of the prefill GEMM's fused epilogue against the reference-
+    shaped element-wise GELU kernel (cuda/gelu.cu:10-15) for every one of the
+    65536 bf16 inputs, bit for bit. The inputs enter as the biases of a GEMM
+    whose accumulators are zero, so the epilogue's GELU input is each bias
+    exactly."""
+    M, K, N = 256, 16, 1 << 16  # more than 128 tokens: the token-major kernel
+    xq = torch.zeros((M, K), dtype=torch.int8, device=cuda)
+    sx = torch.ones(M, device=cuda)
+    W = torch.ones((N, K), dtype=torch.int8, device=cuda)
+    sw = torch.ones(N, device=cuda)
+    bias = torch.arange(N, dtype=torch.int32).to(torch.int16).view(torch.bfloat16).to(cuda)
+    u = ops.linear(xq, sx, W, sw, bias, _lib.EPI_BIAS)  # the GELU input of each column
+    keep = ~torch.isnan(bias) & (bias.view(torch.int16) != -0x8000)  # 0 + (-0) is +0
+    assert torch.equal(u[0].view(torch.int16)[keep], bias.view(torch.int16)[keep])
+    got = ops.linear(xq, sx, W, sw, bias, _lib.EPI_BIAS_GELU)
+    want = u.clone()
+    ops.ref_gelu(want)
+    g, w = got.view(torch.int16), want.view(torch.int16)
+    both_nan = torch.isnan(got) & torch.isnan(want)
+    bad = (g != w) & ~both_nan
+    assert not bool(bad.any()), [hex(int(b) & 0xffff) for b in bias.view(torch.int16)[bad[0]][:8]]
+    # NaN out for the NaN inputs and for -inf (0.5 * -inf * (1 + -1))
+    assert int(both_nan[0].sum()) == int(torch.isnan(bias).sum()) + 1
+    assert ops.device_error(reset=True) == 0

@@ -196,3 +196,33 @@ def test_reference_abi_lm_head_picks(cuda):
         assert tok.item() == want, (temp, k, r)
         if temp > 0:
             assert want == oracle.sample_topk(from_dev_bf16(probs)[0], k, r)
+
+
+def test_topk_flat_row_ranks_across_the_cluster(cuda):
+    """Every logit equal: one probability key held by all 50257 entries (the
+    largest per-key count), so the drawn rank among equal probabilities runs
+    across the CTAs that share the row; and a row with a single finite
+    maximum among equal floor values."""
+    V = 50257
+    flat = np.zeros((4, V), np.float32)
+    flat[2:, :] = -3.0
+    flat[3, 31337] = 5.0
+    lg = oracle.bf16_bits(flat)
+    for k in (40, 20000, V):
+        r = np.array([0.0, 0.999, 0.5, 0.25], np.float32)
+        toks, probs = _sample(lg, 1.0, k, r)
+        for m in range(4):
+            assert toks[m] == oracle.sample_topk(probs[m], k, r[m]), (k, m)
+
+
+def test_topk_vocab_above_the_cluster_kernel(cuda):
+    """65536..81920 entries take the one-CTA kernel (the cluster kernel's
+    per-key counts are 16 bits wide)."""
+    rng = np.random.default_rng(12)
+    M, V = 2, 70000
+    lg = _logits(rng, M, V, "normal")
+    for k in (40, V):
+        r = rng.random(M, dtype=np.float32)
+        toks, probs = _sample(lg, 0.9, k, r)
+        for m in range(M):
+            assert toks[m] == oracle.sample_topk(probs[m], k, r[m])
