@@ -42,13 +42,20 @@ SCRATCH_BYTES = 4 << 20  # W8A8_NOALLOC_SCRATCH_BYTES of include/gpt2_w8a8.h
 SPLIT_K_KERNEL = re.compile(r"gemm_tc_kernel<0, \d+, true")
 
 
-def _kernels(fn):
-    """Names of the CUDA kernels fn launches."""
-    torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        fn()
+def _kernels(fn, tries=3):
+    """Names of the CUDA kernels fn launches. After many profiler sessions in
+    one process a session can come back with no activity records at all; fn
+    (deterministic) then runs again, up to `tries` times."""
+    names = []
+    for _ in range(tries):
         torch.cuda.synchronize()
-    return [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+        if names:
+            break
+    return names
 
 
 def _operands(M, N, K, epi, seed):
@@ -100,7 +107,7 @@ def test_noalloc_split_k_matches_linear_and_oracle(cuda, M, N, K, epi, pad):
         Y = _out(M, N, pad, cuda)
         st = []
         names = _kernels(lambda: st.append(_noalloc(args, M, K, N, epi, R, Y)))
-        assert st == [_lib.W8A8_OK]
+        assert st and all(x == _lib.W8A8_OK for x in st), st
         np.testing.assert_array_equal(from_dev_bf16(Y), want)
         if call == 0:
             assert any(SPLIT_K_KERNEL.search(n) for n in names), names
@@ -119,7 +126,7 @@ def test_noalloc_shapes_without_split_k(cuda):
         Y = torch.full((M, N), 7.0, dtype=torch.bfloat16, device=cuda)
         st = []
         names = _kernels(lambda: st.append(_noalloc(args, M, K, N, _lib.EPI_BIAS, None, Y)))
-        assert st == [_lib.W8A8_OK]
+        assert st and all(x == _lib.W8A8_OK for x in st), st
         np.testing.assert_array_equal(from_dev_bf16(Y), want)
         assert names and not any(SPLIT_K_KERNEL.search(n) for n in names), names
         assert not any("emset" in n for n in names), names  # no clearing either
