@@ -80,43 +80,61 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// The same sampling with one row spread over a cluster of kSampleCluster CTAs
-// (a decode step's rows are few: at 1-64 rows one CTA per row leaves most
-// SMs idle while each thread evaluates ~200 expf twice). CTA r of the
-// cluster owns entries [r*C, (r+1)*C) of the row, C = ceil(V / kSampleCluster):
-//   1. the row max: each CTA's max, then every CTA the maximum of all eight
-//      (order-independent);
-//   2. e_j = expf(x_j - max) for its entries, kept in its shared memory;
-//   3. the sum in the reference's order: slot t (0..255) adds e_j for
-//      j = t, t + 256, ... in order, reading each e_j from the CTA that holds
-//      it (warp 0 of CTA r runs slots 32r .. 32r+31); the 256 slot sums are
-//      stored in CTA 0, and every CTA folds them with the same tree
-//      (s = 128 .. 1), so every CTA holds the same sum;
+// The same pick with one row spread over a cluster of kSampleCluster CTAs
+// (at 1-64 rows one CTA per row leaves most SMs idle while each thread
+// evaluates ~200 expf). CTA r owns entries [r*C, (r+1)*C) of the row, C a
+// multiple of 256, so that slot t of the sum (entries t, t + 256, ...) meets
+// its entries in CTA order:
+//   1. its logits into shared memory (16-byte loads, all in flight), then
+//      the row maximum (each CTA's, then the largest of all: order-free);
+//   2. fp32 e_j = expf(x_j - max) for its entries, in every CTA at once;
+//   3. the slot sums in the reference's order, passed along the cluster:
+//      CTA r adds its entries of every slot to the running sums CTA r-1 left
+//      in its shared memory (thread t: slot t) and hands them to CTA r+1; the
+//      last CTA folds the 256 slots (s = 128 .. 1) and sends 1 / sum to all;
 //   4. bf16 probabilities of its entries and the first index of their
-//      maximum; CTA 0 picks the first index of the largest over the eight.
-constexpr int kSampleCluster = 8;
+//      maximum; CTA 0 picks the first index of the largest over the cluster.
+constexpr int kSampleCluster = 4;
 constexpr int kSampleThreads = 256;
 
 __global__ void __launch_bounds__(kSampleThreads)
     greedy_sample_cluster_kernel(const uint16_t *__restrict__ logits, int64_t ldl, int V, int C,
                                  int32_t *__restrict__ out, int32_t *__restrict__ append_to,
                                  int64_t append_stride, int32_t *__restrict__ append_pos) {
-  extern __shared__ float s_e[];  // [C] exponentials of this CTA's entries
+  // shared memory: fp32 exponentials [C] | the CTA's logits
+  extern __shared__ __align__(16) uint8_t gs_smem[];
+  float *s_e = reinterpret_cast<float *>(gs_smem);
   __shared__ float s_red[kSampleThreads];
-  __shared__ float s_slots[256];   // CTA 0: the 256 slot sums
-  __shared__ float s_cmax;         // this CTA's row-part maximum
-  __shared__ float s_best;         // this CTA's best probability ...
-  __shared__ int s_best_j;         // ... and its first index
+  __shared__ float s_slots[kSampleThreads];  // running slot sums from the previous CTA
+  __shared__ float s_cmax, s_inv;
+  __shared__ float s_best;  // this CTA's best probability ...
+  __shared__ int s_best_j;  // ... and its first index
+  __shared__ int s_wj[kSampleThreads / 32];
   pdl_wait();
   pdl_launch_dependents();
   const uint32_t r = cluster_ctarank();
   const int row = blockIdx.x / kSampleCluster, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const uint16_t *x = logits + (int64_t)row * ldl;
-  const int j0 = (int)r * C, j1 = min(V, j0 + C);
+  const int j0 = (int)r * C, j1 = min(V, j0 + C), n = max(0, j1 - j0);
+  const uint16_t *x = logits + (int64_t)row * ldl + j0;  // this CTA's entries
+  // at the same position modulo 16 bytes as in global memory
+  const int shift = (int)(((uintptr_t)x & 15) >> 1);
+  uint16_t *x16 = reinterpret_cast<uint16_t *>(gs_smem + (size_t)C * 4) + shift;
+  {
+    const int head = min(n, (8 - shift) & 7);  // entries before the first 16-byte boundary
+    const int nvec = (n - head) >> 3;
+    for (int i = tid; i < head; i += kSampleThreads) x16[i] = x[i];
+    const uint4 *xv = reinterpret_cast<const uint4 *>(x + head);
+    uint4 *sv = reinterpret_cast<uint4 *>(x16 + head);
+#pragma unroll 8
+    for (int i = tid; i < nvec; i += kSampleThreads) sv[i] = __ldg(xv + i);
+    for (int i = head + nvec * 8 + tid; i < n; i += kSampleThreads) x16[i] = x[i];
+  }
+  __syncthreads();
   // 1. maximum of this CTA's entries, then of the row
   float mx = -INFINITY;
-  for (int j = j0 + tid; j < j1; j += kSampleThreads) mx = fmaxf(mx, bf2f(x[j]));
+#pragma unroll 4
+  for (int i = tid; i < n; i += kSampleThreads) mx = fmaxf(mx, bf2f(x16[i]));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if (lane == 0) s_red[warp] = mx;
@@ -127,59 +145,51 @@ __global__ void __launch_bounds__(kSampleThreads)
     s_cmax = m;
   }
   cluster_sync_all();
-  if (tid == 0) {
-    float m = ld_dsmem_f32(dsmem_addr(&s_cmax, 0));
-    for (int q = 1; q < kSampleCluster; ++q) m = fmaxf(m, ld_dsmem_f32(dsmem_addr(&s_cmax, q)));
-    s_red[0] = m;
-  }
+  if (tid < kSampleCluster) s_red[tid] = ld_dsmem_f32(dsmem_addr(&s_cmax, (uint32_t)tid));
   __syncthreads();
-  mx = s_red[0];
+  mx = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
   // 2. exponentials of this CTA's entries
-  for (int j = j0 + tid; j < j1; j += kSampleThreads) s_e[j - j0] = expf(bf2f(x[j]) - mx);
-  cluster_sync_all();
-  // 3. slot sums, in order, over the cluster's shared memory
-  if (warp == 0) {
-    const int t = 32 * (int)r + lane;
-    float acc = 0.0f;
-    constexpr int kBatch = 8;  // loads in flight before their additions
-    int q = 0, off = t;        // e_j lives in CTA q at offset off (C >= 256: q steps by <= 1)
-    for (int jb = t; jb < V; jb += 256 * kBatch) {
-      float e[kBatch];
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u) {
-        e[u] = 0.0f;
-        if (jb + 256 * u < V) {
-          e[u] = ld_dsmem_f32(dsmem_addr(&s_e[off], (uint32_t)q));
-          off += 256;
-          if (off >= C) {
-            off -= C;
-            ++q;
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kBatch; ++u)
-        if (jb + 256 * u < V) acc += e[u];
-    }
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dsmem_addr(&s_slots[t], 0)), "f"(acc)
-                 : "memory");
-  }
-  cluster_sync_all();
-  s_red[tid] = ld_dsmem_f32(dsmem_addr(&s_slots[tid], 0));
+#pragma unroll 4
+  for (int i = tid; i < n; i += kSampleThreads) s_e[i] = expf(bf2f(x16[i]) - mx);
   __syncthreads();
-  for (int s = 128; s > 0; s >>= 1) {
-    if (tid < s) s_red[tid] += s_red[tid + s];
-    __syncthreads();
+  // 3. slot t adds entries t, t + 256, ... in order, CTA by CTA
+  for (int q = 0; q < kSampleCluster; ++q) {
+    if ((int)r == q) {
+      float acc = q == 0 ? 0.0f : s_slots[tid];
+#pragma unroll 8
+      for (int i = tid; i < n; i += kSampleThreads) acc += s_e[i];
+      if (q + 1 < kSampleCluster) {
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dsmem_addr(&s_slots[tid], r + 1)),
+                     "f"(acc)
+                     : "memory");
+      } else {
+        s_red[tid] = acc;
+      }
+    }
+    cluster_sync_all();
   }
-  const float inv_sum = 1.0f / s_red[0];
+  if ((int)r == kSampleCluster - 1) {
+    for (int h = kSampleThreads / 2; h > 0; h >>= 1) {
+      if (tid < h) s_red[tid] += s_red[tid + h];
+      __syncthreads();
+    }
+    if (tid < kSampleCluster) {
+      const float inv = 1.0f / s_red[0];
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dsmem_addr(&s_inv, (uint32_t)tid)),
+                   "f"(inv)
+                   : "memory");
+    }
+  }
+  cluster_sync_all();
+  const float inv_sum = s_inv;
   // 4. probabilities and the first index of the maximum
   float best = -1.0f;
   int best_j = 0x7fffffff;
-  for (int j = j0 + tid; j < j1; j += kSampleThreads) {
-    const float p = bf2f(f2bf(bf2f(f2bf(s_e[j - j0])) * inv_sum));
-    if (p > best) {  // j increases within a thread: keeps the first index
+  for (int i = tid; i < n; i += kSampleThreads) {
+    const float p = bf2f(f2bf(bf2f(f2bf(s_e[i])) * inv_sum));
+    if (p > best) {  // i increases within a thread: keeps the first index
       best = p;
-      best_j = j;
+      best_j = j0 + i;
     }
   }
 #pragma unroll
@@ -192,7 +202,6 @@ __global__ void __launch_bounds__(kSampleThreads)
     }
   }
   __syncthreads();  // s_red is reused
-  __shared__ int s_wj[kSampleThreads / 32];
   if (lane == 0) {
     s_red[warp] = best;
     s_wj[warp] = best_j;
@@ -245,9 +254,10 @@ __global__ void advance_kernel(int32_t *dst, const int32_t *src, int n, int delt
 int launch_greedy_sample(const uint16_t *logits, int64_t ldl, int M, int V, int32_t *out,
                          int32_t *append_to, int64_t append_stride, int32_t *append_pos,
                          cudaStream_t s) {
-  const int C = (V + kSampleCluster - 1) / kSampleCluster;
-  const size_t smem = (size_t)C * sizeof(float);
-  if (M > 0 && V >= 256 * kSampleCluster && smem <= 200 * 1024) {
+  // each CTA a multiple of 256 entries: exponentials (fp32) + logits in shared memory
+  const int C = 256 * ((V + 256 * kSampleCluster - 1) / (256 * kSampleCluster));
+  const size_t smem = (size_t)C * 4 + ((size_t)(C + 8) * 2 + 15) / 16 * 16;
+  if (M > 0 && V >= 2048 && smem <= 200 * 1024) {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);

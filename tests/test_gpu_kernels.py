@@ -532,3 +532,15 @@ def test_prefill_gelu_every_bf16_input(cuda):
     # NaN out for the NaN inputs and for -inf (0.5 * -inf * (1 + -1))
     assert int(both_nan[0].sum()) == int(torch.isnan(bias).sum()) + 1
     assert ops.device_error(reset=True) == 0
+
+
+@pytest.mark.parametrize("V", [2048, 3001, 70000])
+def test_greedy_vocabulary_sizes(cuda, V):
+    """The cluster pick over vocabularies whose four 256-aligned slices end
+    short or empty-ish, with rows that start off a 16-byte boundary."""
+    rng = np.random.default_rng(V)
+    M = 5
+    lg = oracle.bf16_bits(rng.standard_normal((M, V + 3)).astype(np.float32) * 2.0)
+    d = to_dev_bf16(lg)[:, 3:]  # row stride V + 3: rows start at odd offsets
+    toks = ops.sample_greedy(d).cpu().numpy()
+    assert list(toks) == [oracle.greedy(lg[m, 3:]) for m in range(M)]
