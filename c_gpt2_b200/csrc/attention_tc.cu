@@ -275,13 +275,15 @@ __global__ void __launch_bounds__(kAThreads, 1)
     // ---- pass 1: row maximum ----
     uint32_t mx2 = 0xff80ff80u;  // (-inf, -inf)
     float m = -INFINITY;
+    // On the diagonal key tile (kt == qt) this warp's 32 keys lie past all
+    // of its rows' positions when cq > qd, before all of them when cq < qd.
     for (int kt = 0; kt < n_kt; ++kt) {
       uint32_t p[16];
       next_scores(p);
-      if (kt < qt) {  // below the diagonal: every key is visible
+      if (kt < qt || cq < qd) {  // every key visible
 #pragma unroll
         for (int c = 0; c < 16; ++c) mx2 = bf2_max(mx2, p[c]);
-      } else {
+      } else if (cq == qd) {
         const int lim = qpos - (kt * kAK + col0);  // columns c <= lim are causal
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
@@ -304,13 +306,13 @@ __global__ void __launch_bounds__(kAThreads, 1)
       for (int kt = par; kt < n_kt; kt += 2) {
         uint32_t p[16];
         next_scores(p);
-        if (kt < qt) {
+        if (kt < qt || cq < qd) {
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             sl[2 * c] = sl[2 * c] + expf(lo_f(p[c]) - m);
             sl[2 * c + 1] = sl[2 * c + 1] + expf(hi_f(p[c]) - m);
           }
-        } else {
+        } else if (cq == qd) {
           const int lim = qpos - (kt * kAK + col0);
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
@@ -370,12 +372,15 @@ __global__ void __launch_bounds__(kAThreads, 1)
       uint32_t p[16];
       next_scores(p);
       uint32_t pk[16];
-      if (kt < qt) {
+      if (kt < qt || cq < qd) {
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const uint32_t e2 = pack_bf2(expf(lo_f(p[c]) - m), expf(hi_f(p[c]) - m));
           pk[c] = pack_bf2(lo_f(e2) * inv, hi_f(e2) * inv);
         }
+      } else if (cq > qd) {  // every key masked: P = 0
+#pragma unroll
+        for (int c = 0; c < 16; ++c) pk[c] = 0u;
       } else {
         const int lim = qpos - (kt * kAK + col0);
 #pragma unroll
@@ -639,13 +644,15 @@ __global__ void __launch_bounds__(kAThreads, 1)
     // ---- pass 1: row maximum ----
     uint32_t mx2 = 0xff80ff80u;
     float m = -INFINITY;
+    // On the diagonal key tile (kt == qt) this warp's 32 keys lie past all
+    // of its rows' positions when cq > qd, before all of them when cq < qd.
     for (int kt = 0; kt < n_kt; ++kt) {
       uint32_t pp[16];
       next_scores(pp);
-      if (kt < qt) {
+      if (kt < qt || cq < qd) {
 #pragma unroll
         for (int c = 0; c < 16; ++c) mx2 = bf2_max(mx2, pp[c]);
-      } else {
+      } else if (cq == qd) {
         const int lim = qpos - (kt * kAK + col0);
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
@@ -676,8 +683,13 @@ __global__ void __launch_bounds__(kAThreads, 1)
         uint32_t pp[16];
         next_scores(pp);
         uint8_t *tile = sE + (size_t)kt * kAP;
+        if (kt == qt && cq > qd) {  // every key masked: e = 0
+#pragma unroll
+          for (int i = 0; i < 4; ++i) *p_unit(tile, r, cq, i) = make_uint4(0u, 0u, 0u, 0u);
+          continue;
+        }
         // keys past the row's own position (diagonal tile only) give e = 0
-        const int lim = kt < qt ? 31 : qpos - (kt * kAK + col0);
+        const int lim = (kt < qt || cq < qd) ? 31 : qpos - (kt * kAK + col0);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {  // one 16-byte unit (8 keys) at a time
           uint32_t e2[4];
@@ -769,14 +781,16 @@ __global__ void __launch_bounds__(kAThreads, 1)
     // ---- pass 3: P = bf16(bf16(e) * inv) in place ----
     for (int kt = 0; kt < n_kt; ++kt) {
       uint8_t *tile = sE + (size_t)kt * kAP;
+      if (!(kt == qt && cq > qd)) {  // (a masked quarter holds zeros already)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint4 *u = p_unit(tile, r, cq, i);
-        uint4 v = *u;
-        uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        for (int i = 0; i < 4; ++i) {
+          uint4 *u = p_unit(tile, r, cq, i);
+          uint4 v = *u;
+          uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) w[j] = pack_bf2(lo_f(w[j]) * inv, hi_f(w[j]) * inv);
-        *u = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int j = 0; j < 4; ++j) w[j] = pack_bf2(lo_f(w[j]) * inv, hi_f(w[j]) * inv);
+          *u = make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();
