@@ -322,8 +322,10 @@ TP_SEQ, TP_TOK = 32, 1024
 
 def tp_prefill_leg(args, rank: int, world: int, local: int, dev) -> dict | None:
     """GPT-2 large W8A8 prefill of 32 x 1024 tokens, tensor-parallel over the
-    run's ranks (W_qkv and W1 column-split, attn_proj and W2 row-split; int32
-    reduce-scatter + int8 all-gather + fp32 max all-reduce over NCCL), timed
+    run's ranks (W_qkv and W1 column-split; attn_proj and W2 over each rank's
+    own sequences with the whole K, their int8 inputs brought by one NCCL
+    all-to-all each; int8 all-gather of the LayerNorm rows, fp32 max
+    all-reduce of the row maxima), timed
     on the device (max over ranks), and its next tokens and logits compared
     bit for bit with the single-GPU engine's prefill of the same batch, which
     rank 0 also times. Every rank takes the same collective steps."""
@@ -392,7 +394,8 @@ def tp_prefill_leg(args, rank: int, world: int, local: int, dev) -> dict | None:
                "ms_1gpu_engine": round(ms1, 3), "vs_1gpu": round(ms1 / ms, 3),
                "bitexact": same_tok and same_logits, "tokens_equal": same_tok,
                "logits_equal": same_logits,
-               "exchange": "int32 reduce-scatter + int8 all-gather + fp32 max all-reduce (NCCL)"}
+               "exchange": "int8 all-to-all to the rows' owners + int8 all-gather + fp32 max "
+                           "all-reduce (NCCL)"}
     if world > 1:
         dist.barrier()
     return out

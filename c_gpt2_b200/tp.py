@@ -126,6 +126,7 @@ def shard_weights(w: dict[str, np.ndarray], plan: TPPlan, rank: int, device) -> 
             "W_qkv.scale": _dev(w[p + "W_qkv.scale"][rows], device),
             "b_qkv": _bf16(w[p + "b_qkv"][rows], device),
             "attn_proj": _dev(w[p + "attn_proj"][:, c0:c1], device),
+            "attn_proj.full": _dev(w[p + "attn_proj"], device),
             "attn_proj.scale": _dev(w[p + "attn_proj.scale"], device),
             "attn_proj_bias": _bf16(w[p + "attn_proj_bias"], device),
             "ln2_gamma": _bf16(w[p + "ln2_gamma"], device),
@@ -134,6 +135,7 @@ def shard_weights(w: dict[str, np.ndarray], plan: TPPlan, rank: int, device) -> 
             "W1.scale": _dev(w[p + "W1.scale"][f0:f1], device),
             "b1": _bf16(w[p + "b1"][f0:f1], device),
             "W2": _dev(w[p + "W2"][:, f0:f1], device),
+            "W2.full": _dev(w[p + "W2"], device),
             "W2.scale": _dev(w[p + "W2.scale"], device),
             "b2": _bf16(w[p + "b2"], device),
         })
@@ -171,6 +173,15 @@ class Collectives:
     def all_reduce_max(self, x: torch.Tensor) -> None:
         if self.world > 1:
             dist.all_reduce(x, op=dist.ReduceOp.MAX, group=self.group)
+
+    def all_to_all(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int],
+                   in_splits: list[int]) -> None:
+        """1-D tensors: block j of inp (in_splits[j] elements) goes to rank j;
+        block j of out comes from rank j."""
+        if self.world == 1:
+            out.copy_(inp)
+            return
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
 
 class Kernels:
@@ -230,6 +241,33 @@ class CollectiveExchange:
 
     def gather_tokens(self, nxt: torch.Tensor) -> None:
         self.c.all_gather_rows(nxt, self.rank, self.world)
+
+
+class AllToAllExchange(CollectiveExchange):
+    """Row-split GEMMs without partial sums: the int8 input columns each rank
+    holds for every row (its heads' attention output, its d_ff slice of the
+    GELU output) go to the rows' owners in one all-to-all, and each owner
+    runs attn_proj and W2 over its own rows with the whole K. The owner's
+    GEMM then computes exactly the one-GPU layer's rows (same int32 sums,
+    same fused epilogue), and the exchange moves int8 inputs instead of int32
+    partial sums: at G ranks each rank sends (G-1)/G of its column block."""
+
+    def __init__(self, kernels, collectives: Collectives, rank: int, world: int, M: int, d: int,
+                 device):
+        super().__init__(kernels, collectives, rank, world, M, d, device)
+        self.device = device
+
+    def to_owners(self, X: torch.Tensor, cols: list[int]) -> torch.Tensor:
+        """X [M, cols[rank]] int8 -> [Mo, sum(cols)] int8: this rank's rows with
+        every rank's columns, in rank order."""
+        Mo, c = self.Mo, X.shape[1]
+        recv = torch.empty((Mo * sum(cols),), dtype=X.dtype, device=self.device)
+        self.c.all_to_all(recv, X.reshape(-1), [Mo * cq for cq in cols], [Mo * c] * self.world)
+        blocks, off = [], 0
+        for cq in cols:
+            blocks.append(recv[off:off + Mo * cq].view(Mo, cq))
+            off += Mo * cq
+        return torch.cat(blocks, dim=1) if len(blocks) > 1 else blocks[0]
 
 
 class PeerExchange:
@@ -353,12 +391,14 @@ class TPPrefill:
     greedy next token of every sequence (on every rank) and the last-position
     logits of the sequences this rank owns.
 
-    exchange: "collective" (NCCL / gloo collectives) or "peer" (the library's
-    own kernels over NVLink peer memory; GPUs only)."""
+    exchange: "alltoall" (int8 inputs to the rows' owners in one all-to-all,
+    whole-K GEMMs there), "collective" (int32 partial sums reduce-scattered),
+    both over NCCL / gloo collectives, or "peer" (partial sums through the
+    library's own kernels over NVLink peer memory; GPUs only)."""
 
     def __init__(self, plan: TPPlan, shard: TPShard, rank: int, kernels=None,
                  collectives: Collectives | None = None, eps: float = 1e-5,
-                 exchange: str = "collective", group=None):
+                 exchange: str = "alltoall", group=None):
         self.plan, self.w, self.rank = plan, shard, rank
         self.k = kernels or Kernels()
         self.c = collectives or Collectives(group)
@@ -375,6 +415,8 @@ class TPPrefill:
             ex.close()
         if self.mode == "peer":
             ex = PeerExchange(self.rank, self.plan.world, M, d, self.group)
+        elif self.mode == "alltoall":
+            ex = AllToAllExchange(self.k, self.c, self.rank, self.plan.world, M, d, device)
         else:
             ex = CollectiveExchange(self.k, self.c, self.rank, self.plan.world, M, d, device)
         ex.M_key = (M, d)
@@ -385,6 +427,77 @@ class TPPrefill:
         if self._ex is not None and hasattr(self._ex, "close"):
             self._ex.close()
         self._ex = None
+
+    def _layers_alltoall(self, ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1) -> None:
+        """The blocks of TPPrefill.run for exchange "alltoall": QKV and W1 over the
+        rank's column slices for all rows; attn_proj and W2 over the rank's own
+        rows with the whole K, their inputs brought by AllToAllExchange.to_owners;
+        LayerNorm + quantization of the own rows, published to every rank."""
+        plan, w, k = self.plan, self.w, self.k
+        Xq, sX = ex.Xq, ex.sX
+        heads = [plan.d_heads(q) for q in range(plan.world)]
+        ffs = [f1 - f0 for f0, f1 in plan.ff]
+        R1 = torch.empty_like(H)
+        n_layer = len(w.layers)
+        for l, L in enumerate(w.layers):
+            k.linear_qkv_heads(Xq, sX, L["W_qkv"], L["W_qkv.scale"], L["b_qkv"], Q, Kc, Vc,
+                               T * dh, T)
+            O = k.attention_prefill(Q, Kc, Vc, T * dh, n_seq, T, hl)
+            Oq, sO = k.quant_rows_amax(O, ex.row_maxima(O, 0))
+            del O
+            Oq_own = ex.to_owners(Oq, heads)
+            # attn_proj + bias + residual (gpt2.c:1235-1245), then LN2 + quantization
+            k.linear(Oq_own, sO[m0:m1].contiguous(), L["attn_proj.full"], L["attn_proj.scale"],
+                     L["attn_proj_bias"], epilogue=2, R=H, out=R1)
+            xq, sxq = ex.own_rows()
+            _, q, sq = k.layernorm_quant(R1, L["ln2_gamma"], L["ln2_beta"], self.eps, want_y=False)
+            xq.copy_(q)
+            sxq.copy_(sq)
+            ex.publish_rows()
+            Gk = k.linear(Xq, sX, L["W1"], L["W1.scale"], L["b1"], epilogue=3)
+            Gq, sG = k.quant_rows_amax(Gk, ex.row_maxima(Gk, 1))
+            del Gk
+            Gq_own = ex.to_owners(Gq, ffs)
+            # W2 + bias + residual (gpt2.c:1302-1325), then the next layer's LN1
+            k.linear(Gq_own, sG[m0:m1].contiguous(), L["W2.full"], L["W2.scale"], L["b2"],
+                     epilogue=2, R=R1, out=H)
+            if l + 1 < n_layer:
+                N = w.layers[l + 1]
+                _, q, sq = k.layernorm_quant(H, N["ln1_gamma"], N["ln1_beta"], self.eps,
+                                             want_y=False)
+                xq.copy_(q)
+                sxq.copy_(sq)
+                ex.publish_rows()
+
+    def _layers_partial_sums(self, ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1) -> None:
+        """The blocks for exchanges "collective" and "peer": attn_proj and W2
+        over the rank's K slices for all rows, the int32 partial sums
+        reduce-scattered to the rows' owners, which add bias and residual and
+        form the LayerNorm + quantization of their rows."""
+        w, k = self.w, self.k
+        Xq, sX = ex.Xq, ex.sX
+        n_layer = len(w.layers)
+        for l, L in enumerate(w.layers):
+            # attention on the local heads
+            k.linear_qkv_heads(Xq, sX, L["W_qkv"], L["W_qkv.scale"], L["b_qkv"], Q, Kc, Vc,
+                               T * dh, T)
+            O = k.attention_prefill(Q, Kc, Vc, T * dh, n_seq, T, hl)
+            # attn_proj, row-split: whole-row scale, int32 partials to the row owners
+            Oq, sO = k.quant_rows_amax(O, ex.row_maxima(O, 0))
+            acc = ex.partial_sums(Oq, L["attn_proj"])
+            ex.reduce(acc, sO[m0:m1], L["attn_proj.scale"], L["attn_proj_bias"], H,
+                      L["ln2_gamma"], L["ln2_beta"], self.eps)
+            # MLP: W1 column-split with GELU, W2 row-split
+            Gk = k.linear(Xq, sX, L["W1"], L["W1.scale"], L["b1"], epilogue=3)
+            Gq, sG = k.quant_rows_amax(Gk, ex.row_maxima(Gk, 1))
+            del Gk
+            acc = ex.partial_sums(Gq, L["W2"])
+            if l + 1 < n_layer:
+                N = w.layers[l + 1]
+                ex.reduce(acc, sG[m0:m1], L["W2.scale"], L["b2"], H, N["ln1_gamma"],
+                          N["ln1_beta"], self.eps)
+            else:
+                ex.reduce(acc, sG[m0:m1], L["W2.scale"], L["b2"], H)
 
     def run(self, tokens: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         plan, w, k, r = self.plan, self.w, self.k, self.rank
@@ -409,28 +522,10 @@ class TPPrefill:
         Kc = torch.empty((n_seq, T, dh), dtype=torch.bfloat16, device=dev)
         Vc = torch.empty_like(Kc)
         Q = torch.empty((M, dh), dtype=torch.bfloat16, device=dev)
-        n_layer = len(w.layers)
-        for l, L in enumerate(w.layers):
-            # attention on the local heads
-            k.linear_qkv_heads(Xq, sX, L["W_qkv"], L["W_qkv.scale"], L["b_qkv"], Q, Kc, Vc,
-                               T * dh, T)
-            O = k.attention_prefill(Q, Kc, Vc, T * dh, n_seq, T, hl)
-            # attn_proj, row-split: whole-row scale, int32 partials to the row owners
-            Oq, sO = k.quant_rows_amax(O, ex.row_maxima(O, 0))
-            acc = ex.partial_sums(Oq, L["attn_proj"])
-            ex.reduce(acc, sO[m0:m1], L["attn_proj.scale"], L["attn_proj_bias"], H,
-                      L["ln2_gamma"], L["ln2_beta"], self.eps)
-            # MLP: W1 column-split with GELU, W2 row-split
-            Gk = k.linear(Xq, sX, L["W1"], L["W1.scale"], L["b1"], epilogue=3)
-            Gq, sG = k.quant_rows_amax(Gk, ex.row_maxima(Gk, 1))
-            del Gk
-            acc = ex.partial_sums(Gq, L["W2"])
-            if l + 1 < n_layer:
-                N = w.layers[l + 1]
-                ex.reduce(acc, sG[m0:m1], L["W2.scale"], L["b2"], H, N["ln1_gamma"],
-                          N["ln1_beta"], self.eps)
-            else:
-                ex.reduce(acc, sG[m0:m1], L["W2.scale"], L["b2"], H)
+        if self.mode == "alltoall":
+            self._layers_alltoall(ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1)
+        else:
+            self._layers_partial_sums(ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1)
         # final LayerNorm of each owned sequence's last position, LM head, greedy
         last = H.view(s1 - s0, T, d)[:, T - 1, :]
         Xf, _, _ = k.layernorm_quant(last, w.lnf_gamma, w.lnf_beta, self.eps, want_q=False)
@@ -439,6 +534,15 @@ class TPPrefill:
         nxt[s0:s1].copy_(k.sample_greedy(logits))
         ex.gather_tokens(nxt)
         return nxt, logits
+
+
+EXCHANGE_TEXT = {
+    "alltoall": "int8 inputs of attn_proj / W2 to the rows' owners by all-to-all + int8 "
+                "all-gather + fp32 max-allreduce (NCCL)",
+    "collective": "int32 reduce-scatter + int8 all-gather + fp32 max-allreduce (NCCL)",
+    "peer": "int32 partial sums stored into the owners' memory by the GEMM epilogue, int8 rows "
+            "broadcast by the LayerNorm kernel, fp32 row maxima, over NVLink peer memory",
+}
 
 
 def main(argv=None) -> None:
@@ -460,7 +564,7 @@ def main(argv=None) -> None:
     ap.add_argument("--layers", type=int, default=None, help="fewer layers (smoke runs only)")
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--exchange", choices=["collective", "peer"], default="collective")
+    ap.add_argument("--exchange", choices=["alltoall", "collective", "peer"], default="alltoall")
     a = ap.parse_args(argv)
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -501,11 +605,7 @@ def main(argv=None) -> None:
             "n_gpus": world, "ms_per_prefill": round(ms, 3),
             "tok_per_s": round(M / (ms / 1e3), 1),
             "gemm_tops_effective": round(gemm_ops / (ms / 1e3) / 1e12, 1),
-            "exchange": ("int32 partial sums stored into the owners' memory by the GEMM "
-                         "epilogue, int8 rows broadcast by the LayerNorm kernel, fp32 row "
-                         "maxima, over NVLink peer memory" if a.exchange == "peer" and world > 1
-                         else "int32 reduce-scatter + int8 all-gather + fp32 max-allreduce "
-                              "(NCCL)"),
+            "exchange": EXCHANGE_TEXT[a.exchange if world > 1 else "collective"],
             "steps": a.steps, "warmup": a.warmup,
             "first_tokens": nxt[:4].tolist()}))
     tp.close()

@@ -149,10 +149,18 @@ class CPUKernels:
     gemm_s32 = staticmethod(_acc)
 
     @staticmethod
-    def linear(Xq, sX, W, sW, b, epilogue):
-        assert epilogue == 3
-        y = _deq_bias(_acc(Xq, W), sX, sW, b).float()
-        return _bf(0.5 * y * (1.0 + torch.tanh(0.79788456 * (y + 0.044715 * y ** 3))))
+    def linear(Xq, sX, W, sW, b, epilogue, R=None, out=None):
+        y = _deq_bias(_acc(Xq, W), sX, sW, b)
+        if epilogue == 2:  # + residual
+            y = _bf(R.float() + y.float())
+        else:
+            assert epilogue == 3
+            y = y.float()
+            y = _bf(0.5 * y * (1.0 + torch.tanh(0.79788456 * (y + 0.044715 * y ** 3))))
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
     @staticmethod
     def reduce_residual_layernorm_quant(acc, sX, sW, b, R, H, g=None, beta=None, eps=1e-5,
@@ -166,8 +174,10 @@ class CPUKernels:
         return H
 
     @staticmethod
-    def layernorm_quant(X, g, b, eps, want_q=False):
-        return _ln(X, g, b, eps), None, None
+    def layernorm_quant(X, g, b, eps, want_y=True, want_q=True):
+        Y = _ln(X, g, b, eps)
+        q, s = _quant(Y, Y.float().abs().amax(1)) if want_q else (None, None)
+        return (Y if want_y else None), q, s
 
     @staticmethod
     def lm_head(Xf, wte):
@@ -183,7 +193,7 @@ def _tokens(n_seq, T):
                             ).to(torch.int32)
 
 
-def _run_rank(rank, world, port, out_dir):
+def _run_rank(rank, world, port, out_dir, exchange):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
@@ -191,19 +201,24 @@ def _run_rank(rank, world, port, out_dir):
     try:
         plan = TPPlan.make(TINY, world)
         shard = shard_weights(_weights(TINY), plan, rank, "cpu")
-        nxt, logits = TPPrefill(plan, shard, rank, CPUKernels(), Collectives()).run(_tokens(4, 16))
+        nxt, logits = TPPrefill(plan, shard, rank, CPUKernels(), Collectives(),
+                                exchange=exchange).run(_tokens(4, 16))
         torch.save({"next": nxt, "logits": logits}, os.path.join(out_dir, f"r{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
-def test_tp_prefill_two_gloo_ranks_equal_one_rank(tmp_path):
+@pytest.mark.parametrize("exchange", ["alltoall", "collective"])
+def test_tp_prefill_two_gloo_ranks_equal_one_rank(tmp_path, exchange):
+    """Two ranks, with the int8 inputs of the row-split GEMMs sent to the rows'
+    owners (alltoall) or their int32 partial sums reduce-scattered
+    (collective): the one-rank result bit for bit."""
     plan1 = TPPlan.make(TINY, 1)
     shard1 = shard_weights(_weights(TINY), plan1, 0, "cpu")
-    want_next, want_logits = TPPrefill(plan1, shard1, 0, CPUKernels(), Collectives()).run(
-        _tokens(4, 16))
-    port = 29500 + os.getpid() % 1000
-    mp.start_processes(_run_rank, args=(2, port, str(tmp_path)), nprocs=2, join=True,
+    want_next, want_logits = TPPrefill(plan1, shard1, 0, CPUKernels(), Collectives(),
+                                       exchange="collective").run(_tokens(4, 16))
+    port = 29500 + os.getpid() % 1000 + (500 if exchange == "alltoall" else 0)
+    mp.start_processes(_run_rank, args=(2, port, str(tmp_path), exchange), nprocs=2, join=True,
                        start_method="spawn")
     got = [torch.load(tmp_path / f"r{r}.pt") for r in range(2)]
     for g in got:

@@ -122,15 +122,16 @@ def _tp_rank(rank, world, port, img_path, p_path, out_dir, exchange="collective"
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("exchange", ["collective", "peer"])
+@pytest.mark.parametrize("exchange", ["alltoall", "collective", "peer"])
 def test_tp_two_ranks_match_engine(cuda, large2_image, tmp_path, exchange):
-    """Two ranks, exchange through NCCL or through the library's peer-memory
-    kernels over NVLink: the same logits and tokens as one GPU, bit for bit."""
+    """Two ranks, exchange through NCCL (int8 inputs to the rows' owners, or
+    int32 partial sums) or through the library's peer-memory kernels over
+    NVLink: the same logits and tokens as one GPU, bit for bit."""
     P = prompts(4, 128, seed=9)
     want_next, want_logits = _engine_prefill(large2_image, LARGE2, P)
     np.save(tmp_path / "img.npy", large2_image)
     np.save(tmp_path / "p.npy", P)
-    port = 29600 + os.getpid() % 500 + (500 if exchange == "peer" else 0)
+    port = 29600 + os.getpid() % 300 + {"collective": 0, "peer": 300, "alltoall": 600}[exchange]
     mp.start_processes(_tp_rank, args=(2, port, str(tmp_path / "img.npy"),
                                        str(tmp_path / "p.npy"), str(tmp_path), exchange),
                        nprocs=2, join=True, start_method="spawn")
