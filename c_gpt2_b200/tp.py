@@ -394,11 +394,19 @@ class TPPrefill:
     exchange: "alltoall" (int8 inputs to the rows' owners in one all-to-all,
     whole-K GEMMs there), "collective" (int32 partial sums reduce-scattered),
     both over NCCL / gloo collectives, or "peer" (partial sums through the
-    library's own kernels over NVLink peer memory; GPUs only)."""
+    library's own kernels over NVLink peer memory; GPUs only).
+
+    halves (exchange "alltoall", more than one rank): the batch runs as two
+    halves, each rank's first and second halves of its own sequences, each
+    half with its own process group and (on GPUs) its own CUDA stream; their
+    layers are issued alternately, so that one half's exchanges run while the
+    other half computes. Each sequence's arithmetic is unchanged. Off by
+    default: GPT-2 large 32 x 1024 on 2 GPUs took 50.4 ms in halves against
+    48.2 ms as one batch."""
 
     def __init__(self, plan: TPPlan, shard: TPShard, rank: int, kernels=None,
                  collectives: Collectives | None = None, eps: float = 1e-5,
-                 exchange: str = "alltoall", group=None):
+                 exchange: str = "alltoall", group=None, halves: bool = False):
         self.plan, self.w, self.rank = plan, shard, rank
         self.k = kernels or Kernels()
         self.c = collectives or Collectives(group)
@@ -406,6 +414,12 @@ class TPPrefill:
         self.mode = exchange
         self.group = group
         self._ex = None
+        self._halves = None
+        if halves and exchange == "alltoall" and plan.world > 1 and dist.is_initialized():
+            # one process group per half, created in the same order on every rank
+            ranks = list(range(plan.world))
+            self._halves = [{"c": Collectives(dist.new_group(ranks)), "ex": None}
+                            for _ in range(2)]
 
     def _exchange(self, M: int, d: int, device):
         ex = self._ex
@@ -427,8 +441,11 @@ class TPPrefill:
         if self._ex is not None and hasattr(self._ex, "close"):
             self._ex.close()
         self._ex = None
+        if self._halves:
+            for h in self._halves:
+                h["ex"] = None
 
-    def _layers_alltoall(self, ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1) -> None:
+    def _layers_alltoall(self, ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1):
         """The blocks of TPPrefill.run for exchange "alltoall": QKV and W1 over the
         rank's column slices for all rows; attn_proj and W2 over the rank's own
         rows with the whole K, their inputs brought by AllToAllExchange.to_owners;
@@ -445,7 +462,9 @@ class TPPrefill:
             O = k.attention_prefill(Q, Kc, Vc, T * dh, n_seq, T, hl)
             Oq, sO = k.quant_rows_amax(O, ex.row_maxima(O, 0))
             del O
+            yield
             Oq_own = ex.to_owners(Oq, heads)
+            yield
             # attn_proj + bias + residual (gpt2.c:1235-1245), then LN2 + quantization
             k.linear(Oq_own, sO[m0:m1].contiguous(), L["attn_proj.full"], L["attn_proj.scale"],
                      L["attn_proj_bias"], epilogue=2, R=H, out=R1)
@@ -454,10 +473,13 @@ class TPPrefill:
             xq.copy_(q)
             sxq.copy_(sq)
             ex.publish_rows()
+            yield
             Gk = k.linear(Xq, sX, L["W1"], L["W1.scale"], L["b1"], epilogue=3)
             Gq, sG = k.quant_rows_amax(Gk, ex.row_maxima(Gk, 1))
             del Gk
+            yield
             Gq_own = ex.to_owners(Gq, ffs)
+            yield
             # W2 + bias + residual (gpt2.c:1302-1325), then the next layer's LN1
             k.linear(Gq_own, sG[m0:m1].contiguous(), L["W2.full"], L["W2.scale"], L["b2"],
                      epilogue=2, R=R1, out=H)
@@ -468,6 +490,7 @@ class TPPrefill:
                 xq.copy_(q)
                 sxq.copy_(sq)
                 ex.publish_rows()
+                yield
 
     def _layers_partial_sums(self, ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1) -> None:
         """The blocks for exchanges "collective" and "peer": attn_proj and W2
@@ -499,7 +522,9 @@ class TPPrefill:
             else:
                 ex.reduce(acc, sG[m0:m1], L["W2.scale"], L["b2"], H)
 
-    def run(self, tokens: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    def _steps(self, tokens: torch.Tensor, ex, out: dict):
+        """The whole prefill of `tokens` as a generator that pauses after each
+        exchange step; leaves (next tokens, own logits) in out["result"]."""
         plan, w, k, r = self.plan, self.w, self.k, self.rank
         n_seq, T = tokens.shape
         d = plan.dims.d_model
@@ -510,7 +535,6 @@ class TPPrefill:
         m0, m1 = s0 * T, s1 * T
         dev = w.wte.device
         L0 = w.layers[0]
-        ex = self._exchange(M, d, dev)
         Xq, sX = ex.Xq, ex.sX
         # residual stream of the owned sequences; int8 LayerNorm output of all rows
         own_tok = tokens[s0:s1].contiguous().reshape(-1)
@@ -519,11 +543,12 @@ class TPPrefill:
         Xq[m0:m1].copy_(xq)
         sX[m0:m1].copy_(sx)
         ex.publish_rows()
+        yield
         Kc = torch.empty((n_seq, T, dh), dtype=torch.bfloat16, device=dev)
         Vc = torch.empty_like(Kc)
         Q = torch.empty((M, dh), dtype=torch.bfloat16, device=dev)
         if self.mode == "alltoall":
-            self._layers_alltoall(ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1)
+            yield from self._layers_alltoall(ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1)
         else:
             self._layers_partial_sums(ex, H, Q, Kc, Vc, n_seq, T, hl, dh, m0, m1)
         # final LayerNorm of each owned sequence's last position, LM head, greedy
@@ -533,6 +558,63 @@ class TPPrefill:
         nxt = torch.empty((n_seq,), dtype=torch.int32, device=dev)
         nxt[s0:s1].copy_(k.sample_greedy(logits))
         ex.gather_tokens(nxt)
+        out["result"] = (nxt, logits)
+
+    def run(self, tokens: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        n_seq, T = tokens.shape
+        world = self.plan.world
+        if self._halves and n_seq % (2 * world) == 0:
+            return self._run_halves(tokens)
+        ex = self._exchange(n_seq * T, self.plan.dims.d_model, self.w.wte.device)
+        out = {}
+        for _ in self._steps(tokens, ex, out):
+            pass
+        return out["result"]
+
+    def _run_halves(self, tokens: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        n_seq, T = tokens.shape
+        world, d, dev = self.plan.world, self.plan.dims.d_model, self.w.wte.device
+        per = n_seq // world
+        half = per // 2
+        cuda = dev.type == "cuda" if isinstance(dev, torch.device) else str(dev).startswith("cuda")
+        main = torch.cuda.current_stream(dev) if cuda else None
+        runs = []
+        for i, h in enumerate(self._halves):
+            # half i: the i-th half of every rank's own sequences, rank by rank
+            idx = torch.cat([torch.arange(q * per + i * half, q * per + (i + 1) * half)
+                             for q in range(world)]).to(tokens.device)
+            if h["ex"] is None or h["ex"].M_key != (world * half * T, d):
+                h["ex"] = AllToAllExchange(self.k, h["c"], self.rank, world, world * half * T, d,
+                                           dev)
+                h["ex"].M_key = (world * half * T, d)
+            if cuda and "stream" not in h:
+                h["stream"] = torch.cuda.Stream(dev)
+            stream = h.get("stream")
+            if stream is not None:
+                stream.wait_stream(main)
+            toks = tokens.index_select(0, idx)
+            out = {}
+            runs.append({"idx": idx, "out": out, "stream": stream,
+                         "gen": self._steps(toks, h["ex"], out)})
+        live = list(runs)
+        while live:
+            for run in list(live):
+                ctx = torch.cuda.stream(run["stream"]) if run["stream"] is not None else None
+                try:
+                    if ctx is not None:
+                        with ctx:
+                            next(run["gen"])
+                    else:
+                        next(run["gen"])
+                except StopIteration:
+                    live.remove(run)
+        if cuda:
+            for run in runs:
+                main.wait_stream(run["stream"])
+        nxt = torch.empty((n_seq,), dtype=torch.int32, device=dev)
+        for run in runs:
+            nxt.index_copy_(0, run["idx"], run["out"]["result"][0])
+        logits = torch.cat([run["out"]["result"][1] for run in runs])
         return nxt, logits
 
 
@@ -565,6 +647,8 @@ def main(argv=None) -> None:
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--exchange", choices=["alltoall", "collective", "peer"], default="alltoall")
+    ap.add_argument("--halves", action="store_true",
+                    help="alltoall: run the batch as two interleaved halves")
     a = ap.parse_args(argv)
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -581,7 +665,8 @@ def main(argv=None) -> None:
     shard = shard_weights(read_quant8(img, dims), plan, rank, dev)
     del img
     P = torch.from_numpy(prompts(a.n_seq, a.tokens, dims.vocab, seed=0)).to(dev)
-    tp = TPPrefill(plan, shard, rank, exchange=a.exchange if world > 1 else "collective")
+    tp = TPPrefill(plan, shard, rank, exchange=a.exchange if world > 1 else "collective",
+                   halves=a.halves)
     for _ in range(a.warmup):
         tp.run(P)
     torch.cuda.synchronize()

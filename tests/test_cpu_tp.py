@@ -193,7 +193,7 @@ def _tokens(n_seq, T):
                             ).to(torch.int32)
 
 
-def _run_rank(rank, world, port, out_dir, exchange):
+def _run_rank(rank, world, port, out_dir, exchange, halves):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
@@ -202,24 +202,26 @@ def _run_rank(rank, world, port, out_dir, exchange):
         plan = TPPlan.make(TINY, world)
         shard = shard_weights(_weights(TINY), plan, rank, "cpu")
         nxt, logits = TPPrefill(plan, shard, rank, CPUKernels(), Collectives(),
-                                exchange=exchange).run(_tokens(4, 16))
+                                exchange=exchange, halves=halves).run(_tokens(4, 16))
         torch.save({"next": nxt, "logits": logits}, os.path.join(out_dir, f"r{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["alltoall", "collective"])
-def test_tp_prefill_two_gloo_ranks_equal_one_rank(tmp_path, exchange):
+@pytest.mark.parametrize("exchange,halves", [("alltoall", True), ("alltoall", False),
+                                            ("collective", False)])
+def test_tp_prefill_two_gloo_ranks_equal_one_rank(tmp_path, exchange, halves):
     """Two ranks, with the int8 inputs of the row-split GEMMs sent to the rows'
-    owners (alltoall) or their int32 partial sums reduce-scattered
-    (collective): the one-rank result bit for bit."""
+    owners (alltoall; the batch in two interleaved halves or whole) or their
+    int32 partial sums reduce-scattered (collective): the one-rank result bit
+    for bit."""
     plan1 = TPPlan.make(TINY, 1)
     shard1 = shard_weights(_weights(TINY), plan1, 0, "cpu")
     want_next, want_logits = TPPrefill(plan1, shard1, 0, CPUKernels(), Collectives(),
                                        exchange="collective").run(_tokens(4, 16))
-    port = 29500 + os.getpid() % 1000 + (500 if exchange == "alltoall" else 0)
-    mp.start_processes(_run_rank, args=(2, port, str(tmp_path), exchange), nprocs=2, join=True,
-                       start_method="spawn")
+    port = 29500 + os.getpid() % 300 + {"collective": 0, "alltoall": 300}[exchange] + 300 * halves
+    mp.start_processes(_run_rank, args=(2, port, str(tmp_path), exchange, halves), nprocs=2,
+                       join=True, start_method="spawn")
     got = [torch.load(tmp_path / f"r{r}.pt") for r in range(2)]
     for g in got:
         assert torch.equal(g["next"], want_next)
