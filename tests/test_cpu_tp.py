@@ -193,7 +193,7 @@ def _tokens(n_seq, T):
                             ).to(torch.int32)
 
 
-def _run_rank(rank, world, port, out_dir, exchange, halves):
+def _run_rank(rank, world, port, out_dir, exchange, halves, n_seq=4):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
@@ -202,7 +202,7 @@ def _run_rank(rank, world, port, out_dir, exchange, halves):
         plan = TPPlan.make(TINY, world)
         shard = shard_weights(_weights(TINY), plan, rank, "cpu")
         nxt, logits = TPPrefill(plan, shard, rank, CPUKernels(), Collectives(),
-                                exchange=exchange, halves=halves).run(_tokens(4, 16))
+                                exchange=exchange, halves=halves).run(_tokens(n_seq, 16))
         torch.save({"next": nxt, "logits": logits}, os.path.join(out_dir, f"r{rank}.pt"))
     finally:
         dist.destroy_process_group()
@@ -227,3 +227,22 @@ def test_tp_prefill_two_gloo_ranks_equal_one_rank(tmp_path, exchange, halves):
         assert torch.equal(g["next"], want_next)
     logits = torch.cat([g["logits"] for g in got])
     assert torch.equal(logits, want_logits)
+
+
+def test_tp_prefill_three_gloo_ranks_uneven_heads(tmp_path):
+    """Three ranks: 4 heads as 2, 1, 1 and d_ff as 6, 5, 5 units of 64, so the
+    all-to-all moves column blocks of different widths (the shape of 20 heads
+    over 8 GPUs): the one-rank result bit for bit."""
+    plan1 = TPPlan.make(TINY, 1)
+    shard1 = shard_weights(_weights(TINY), plan1, 0, "cpu")
+    want_next, want_logits = TPPrefill(plan1, shard1, 0, CPUKernels(), Collectives(),
+                                       exchange="collective").run(_tokens(6, 16))
+    plan3 = TPPlan.make(TINY, 3)
+    assert [plan3.d_heads(r) for r in range(3)] == [128, 64, 64]
+    port = 28400 + os.getpid() % 500
+    mp.start_processes(_run_rank, args=(3, port, str(tmp_path), "alltoall", True, 6), nprocs=3,
+                       join=True, start_method="spawn")
+    got = [torch.load(tmp_path / f"r{r}.pt") for r in range(3)]
+    for g in got:
+        assert torch.equal(g["next"], want_next)
+    assert torch.equal(torch.cat([g["logits"] for g in got]), want_logits)
