@@ -28,8 +28,10 @@
 // The softmax warps first scale the Q tile by 0.125 in shared memory (exact:
 // a power of two), so S = bf16(acc) needs no multiply; scores stay packed as
 // bf16x2 until an exponential needs them, and only the diagonal key tile
-// (kt == query tile) pays for the causal mask. P is double-buffered when the
-// key tiles leave room for a second buffer (prompts up to 512 tokens).
+// (kt == query tile) pays for the causal mask (a warp whose 32 keys are all
+// masked there skips them). This three-pass kernel serves prompts of 513 to
+// 1024 tokens; up to 512 tokens attention_prefill_tc_e_kernel (below) keeps
+// the exponentials on chip instead of recomputing S a third time.
 // Every wait is bounded and records an error instead of hanging.
 #include "common.cuh"
 #include "runtime.cuh"
