@@ -50,6 +50,7 @@ struct ClusterGemmArgs : LinearArgs {
   int kb_per;   // K blocks per split
   int ksplit;   // CTAs per cluster
   int *err;
+  int early_dependents;  // let the next kernel launch once the partials are reduced
 };
 
 struct __align__(16) ClusterCtl {
@@ -180,10 +181,13 @@ __global__ void __launch_bounds__(kCThreads, 2)
   tc_fence_after();
   const uint32_t tmem_base = ctl->tmem_base;
   volatile int *abort_flag = &ctl->abort_flag;
-  // No early griddepcontrol.launch_dependents: the next kernel launches when
-  // this grid exits. Measured on a graphed decode step of GPT-2 large (64
-  // sequences), letting the next kernel's CTAs become resident during the GEMM
-  // made the step 15% slower, even when triggered after the MMAs.
+  // griddepcontrol.launch_dependents: at 64 tokens, none (the next kernel
+  // launches when this grid exits): letting its CTAs become resident during
+  // the GEMM made a graphed GPT-2 large decode step 15% slower, even when
+  // triggered after the MMAs. At <= 32 tokens, right after the cluster
+  // barrier that completes the partial tiles (a.early_dependents): steps of 8
+  // and 16 sequences 1616 -> 1585 and 1742 -> 1734 us, same box, two repeats
+  // (at the start of the kernel instead: slower than none).
 
   int issued = 0;
   const int pre = min(nkb, stages);
@@ -289,6 +293,7 @@ __global__ void __launch_bounds__(kCThreads, 2)
   (void)have_partial;
   tc_fence_before();
   cluster_sync_all();  // every partial tile of the cluster is in shared memory
+  if (a.early_dependents) pdl_launch_dependents();
 
   // ---------------- distributed reduction + epilogue ----------------
   // All DSMEM reads first; then the CTA tells the cluster it is done reading
@@ -411,6 +416,7 @@ static int launch_cluster(const int8_t *W, const int8_t *X, int64_t ldx, const L
   a.kb_per = (a.kblocks + ks - 1) / ks;
   a.ksplit = (a.kblocks + a.kb_per - 1) / a.kb_per;
   a.err = ctx->err;
+  a.early_dependents = la.M <= 32;
   const int stage_bytes = (kCBM + a.BN) * kCBox;
   const int budget = 227 * 1024 - 1024 - (int)sizeof(ClusterCtl) - 64;
   a.stages = a.kb_per < kCMaxStages ? a.kb_per : kCMaxStages;
