@@ -9,7 +9,7 @@ import torch
 from c_gpt2_b200 import _lib, ops
 from c_gpt2_b200.synthetic import outlier_activations
 from oracle import oracle
-from tests.gpu_util import bf16_ulp_diff, from_dev_bf16, to_dev, to_dev_bf16
+from tests.gpu_util import bf16_ulp_diff, from_dev_bf16, kernel_names_fresh, to_dev, to_dev_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -415,22 +415,6 @@ def test_embed_layernorm_warp_rows_equal_block_rows(cuda):
         assert torch.equal(Xq[r], q) and torch.equal(sX[r], sx)
 
 
-def _cuda_kernels(fn, tries=3):
-    """Names of the CUDA kernels fn launches (fn deterministic: a profiler
-    session that comes back with no activity records runs it again)."""
-    from torch.profiler import ProfilerActivity, profile
-    names = []
-    for _ in range(tries):
-        torch.cuda.synchronize()
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            fn()
-            torch.cuda.synchronize()
-        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
-        if names:
-            break
-    return names
-
-
 def _mlp_operands(rng, M, d):
     f = 4 * d
     x = oracle.bf16_bits(outlier_activations(M, d, seed=M + d))
@@ -462,24 +446,31 @@ def test_mlp_pair_fused_quantization(cuda, M, d):
     q2, s2 = ops.per_token_quant(X1)
     want = ops.linear(q2, s2, W2, sw2, b2, _lib.EPI_BIAS_RESID, R=R, workspace=ws)
 
-    out = {}
-
-    def fused():
-        X1f, rec = ops.linear_absmax(xq, sx, W1, sw1, b1, _lib.EPI_BIAS_GELU, workspace=ws)
-        out["X1"], out["rec"] = X1f, rec
-        out["Y"] = ops.linear_from_bf16(X1f, rec, W2, sw2, b2, _lib.EPI_BIAS_RESID, R=R,
-                                        workspace=ws)
-
-    names = _cuda_kernels(fused)
-    assert torch.equal(out["X1"].view(torch.int16), X1.view(torch.int16))
+    X1f, rec = ops.linear_absmax(xq, sx, W1, sw1, b1, _lib.EPI_BIAS_GELU, workspace=ws)
+    Y = ops.linear_from_bf16(X1f, rec, W2, sw2, b2, _lib.EPI_BIAS_RESID, R=R, workspace=ws)
+    assert torch.equal(X1f.view(torch.int16), X1.view(torch.int16))
     amax = X1.float().abs().amax(1)
-    assert torch.equal(out["rec"].amax(0), amax)
-    assert torch.equal(out["Y"].view(torch.int16), want.view(torch.int16))
-    quant = [n for n in names if "quant" in n or "amax" in n]
-    if M == 1:
-        assert not quant, names
-        assert len(names) == 2, names
+    assert torch.equal(rec.amax(0), amax)
+    assert torch.equal(Y.view(torch.int16), want.view(torch.int16))
     assert ops.device_error(reset=True) == 0
+    if M == 1:  # the fused GEMV pair: two launches, no quantization or maxima kernel
+        names = kernel_names_fresh("test_gpu_kernels", "mlp_pair_call", [[M, d]])[0]["names"]
+        assert len(names) == 2, names
+        assert not [n for n in names if "quant" in n or "amax" in n], names
+
+
+def mlp_pair_call(M, d):
+    """The fused W1 -> W2 pair on cuda:0 as the test above builds it, for
+    kernel_names_fresh."""
+    rng = np.random.default_rng(M * 5 + d)
+    xq, sx, W1, sw1, b1, W2, sw2, b2, R = _mlp_operands(rng, M, d)
+    ws = ops.linear_workspace(M, 4 * d, "cuda:0")
+
+    def call():
+        X1f, rec = ops.linear_absmax(xq, sx, W1, sw1, b1, _lib.EPI_BIAS_GELU, workspace=ws)
+        ops.linear_from_bf16(X1f, rec, W2, sw2, b2, _lib.EPI_BIAS_RESID, R=R, workspace=ws)
+        return 0
+    return call
 
 
 @pytest.mark.parametrize("M,K,n_part", [(1, 5120, 1), (1, 5120, 7), (3, 3072, 5), (64, 5120, 120),

@@ -8,8 +8,9 @@ the oracle's, call after call, since every call shares that array.
 The shapes below reach the split-K kernel: a few tokens whose output rows are
 not 16-byte aligned, or whose N is not a multiple of 4, which the cluster
 kernel does not take. The kernels each call launches are read back from the
-CUDA activity record (torch.profiler), which shows that these shapes really
-run the channel-major tcgen05 GEMM that reads the scratch.
+CUDA activity record (torch.profiler, in a fresh process), which shows that
+these shapes really run the channel-major tcgen05 GEMM that reads the
+scratch.
 
 This file is collected last so a run that stops at the first failure has
 already run every other test."""
@@ -18,12 +19,11 @@ import re
 import numpy as np
 import pytest
 import torch
-from torch.profiler import ProfilerActivity, profile
 
 from c_gpt2_b200 import _lib, ops
 from c_gpt2_b200.synthetic import outlier_activations
 from oracle import oracle
-from tests.gpu_util import bf16_ulp_diff, from_dev_bf16, to_dev, to_dev_bf16
+from tests.gpu_util import bf16_ulp_diff, from_dev_bf16, kernel_names_fresh, to_dev, to_dev_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -42,22 +42,6 @@ SCRATCH_BYTES = 4 << 20  # W8A8_NOALLOC_SCRATCH_BYTES of include/gpt2_w8a8.h
 SPLIT_K_KERNEL = re.compile(r"gemm_tc_kernel<0, \d+, true")
 
 
-def _kernels(fn, tries=3):
-    """Names of the CUDA kernels fn launches. After many profiler sessions in
-    one process a session can come back with no activity records at all; fn
-    (deterministic) then runs again, up to `tries` times."""
-    names = []
-    for _ in range(tries):
-        torch.cuda.synchronize()
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            fn()
-            torch.cuda.synchronize()
-        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
-        if names:
-            break
-    return names
-
-
 def _operands(M, N, K, epi, seed):
     rng = np.random.default_rng(seed)
     x = oracle.bf16_bits(outlier_activations(M, K, seed=7))
@@ -73,6 +57,20 @@ def _operands(M, N, K, epi, seed):
 def _out(M, N, pad, device):
     """[M, N] bf16 view with row pitch N + pad, filled with 7.0."""
     return torch.full((M, N + pad), 7.0, dtype=torch.bfloat16, device=device)[:, :N]
+
+
+def noalloc_call(M, N, K, epi, pad):
+    """One w8a8_linear_noalloc call of this shape on cuda:0 (operands as the
+    tests build them), for kernel_names_fresh."""
+    dev = torch.device("cuda", 0)
+    xq, sx, W, sw, b, r = _operands(M, N, K, epi, M + N + K)
+    args = (to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw), to_dev_bf16(b))
+    R = None
+    if r is not None:
+        R = torch.zeros((M, N + pad), dtype=torch.bfloat16, device=dev)[:, :N]
+        R.copy_(to_dev_bf16(r))
+    Y = _out(M, N, pad, dev)
+    return lambda: _noalloc(args, M, K, N, epi, R, Y)
 
 
 # (M, N, K, epilogue, extra elements per output row)
@@ -105,30 +103,34 @@ def test_noalloc_split_k_matches_linear_and_oracle(cuda, M, N, K, epi, pad):
     # two calls in a row: the shared scratch keeps the last call's contents
     for call in range(2):
         Y = _out(M, N, pad, cuda)
-        st = []
-        names = _kernels(lambda: st.append(_noalloc(args, M, K, N, epi, R, Y)))
-        assert st and all(x == _lib.W8A8_OK for x in st), st
+        assert _noalloc(args, M, K, N, epi, R, Y) == _lib.W8A8_OK
         np.testing.assert_array_equal(from_dev_bf16(Y), want)
-        if call == 0:
-            assert any(SPLIT_K_KERNEL.search(n) for n in names), names
     assert ops.device_error(reset=True) == 0
+    # the call runs the split-K kernel, which reads the scratch
+    rec = kernel_names_fresh("test_zz_no_alloc", "noalloc_call", [[M, N, K, epi, pad]])[0]
+    assert rec["status"] == _lib.W8A8_OK
+    assert any(SPLIT_K_KERNEL.search(n) for n in rec["names"]), rec["names"]
 
 
 def test_noalloc_shapes_without_split_k(cuda):
     """One token (GEMV), aligned decode rows (cluster kernel) and prefill rows
     (token-major kernel) read no workspace: they run as w8a8_linear, whatever
     their size, including shapes whose partial sums would not fit the scratch."""
-    for M, N, K in [(1, 2304, 768), (64, 5120, 1280), (1024, 2048, 64), (256, 5120, 1280)]:
-        xq, sx, W, sw, b, _ = _operands(M, N, K, _lib.EPI_BIAS, M + N)
+    shapes = [(1, 2304, 768), (64, 5120, 1280), (1024, 2048, 64), (256, 5120, 1280)]
+    for M, N, K in shapes:
+        xq, sx, W, sw, b, _ = _operands(M, N, K, _lib.EPI_BIAS, M + N + K)
         args = (to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw), to_dev_bf16(b))
         want = from_dev_bf16(ops.linear(*args, _lib.EPI_BIAS))
         np.testing.assert_array_equal(want, oracle.linear(xq, sx, W, sw, b, _lib.EPI_BIAS))
         Y = torch.full((M, N), 7.0, dtype=torch.bfloat16, device=cuda)
-        st = []
-        names = _kernels(lambda: st.append(_noalloc(args, M, K, N, _lib.EPI_BIAS, None, Y)))
-        assert st and all(x == _lib.W8A8_OK for x in st), st
+        assert _noalloc(args, M, K, N, _lib.EPI_BIAS, None, Y) == _lib.W8A8_OK
         np.testing.assert_array_equal(from_dev_bf16(Y), want)
-        assert names and not any(SPLIT_K_KERNEL.search(n) for n in names), names
+    recs = kernel_names_fresh("test_zz_no_alloc", "noalloc_call",
+                              [[M, N, K, _lib.EPI_BIAS, 0] for M, N, K in shapes])
+    for (M, N, K), rec in zip(shapes, recs):
+        names = rec["names"]
+        assert rec["status"] == _lib.W8A8_OK
+        assert names and not any(SPLIT_K_KERNEL.search(n) for n in names), (M, N, K, names)
         assert not any("emset" in n for n in names), names  # no clearing either
 
 
