@@ -28,7 +28,7 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
 constexpr int kWarpRows = 4;       // rows (warps) per block of the warp-per-row kernels
 constexpr int kWarpVec = 8;        // LayerNorm rows up to 8 * 256 = 2048 elements
 constexpr int kWarpQuantVec = 24;  // quantized rows up to 6144 elements
-// Kernels are instantiated for NV = 4, 5, 8 (LayerNorm) and 8, 16, 24 (quant)
+// Kernels are instantiated for NV = 4, 5, 8 (LayerNorm) and 5, 8, 16, 20, 24 (quant)
 // vectors per lane; a row of n elements uses the smallest NV >= n / 256.
 
 __device__ __forceinline__ float warp_fold1024(float (&s)[4][8]) {

@@ -6,6 +6,7 @@ size of the large model (d_model 1280, 20 heads, context 1024).
     python -m c_gpt2_b200.profcase attention-decode [--batch 64] [--n-ctx 768]
     python -m c_gpt2_b200.profcase attention-prefill [--seqs 64] [--tokens 512]
     python -m c_gpt2_b200.profcase layernorm-quant [--m 32768] [--d 1280]
+    python -m c_gpt2_b200.profcase quant-rows [--m 32768] [--k 5120]
     python -m c_gpt2_b200.profcase linear --m 32768 --n 5120 --k 1280 --epi gelu
     python -m c_gpt2_b200.profcase linear --m 64 --n 5120 --k 1280 --epi gelu
     python -m c_gpt2_b200.profcase decode [--model medium] [--batch 1] [--prompt 512] [--gen 256]
@@ -130,6 +131,22 @@ def layernorm_quant(a) -> None:
     us = _time(run, a.timed)
     byts = M * d * 2 + M * d + M * 4
     print(f"layernorm_quant M={M} d={d}: {us:.2f} us/launch, {byts / us / 1e3:.0f} GB/s")
+
+
+def quant_rows(a) -> None:
+    M, K = a.m, a.k
+    g = torch.Generator(device="cuda").manual_seed(0)
+    X = torch.randn((M, K), device="cuda", generator=g).to(torch.bfloat16)
+
+    def run():
+        ops.per_token_quant(X)
+
+    for _ in range(a.launches):
+        run()
+    torch.cuda.synchronize()
+    us = _time(run, a.timed)
+    byts = M * K * 2 + M * K + M * 4
+    print(f"quant_rows M={M} K={K}: {us:.2f} us/launch, {byts / us / 1e3:.0f} GB/s")
 
 
 def linear(a) -> None:
@@ -342,6 +359,9 @@ def main(argv=None) -> None:
     p = sub.add_parser("layernorm-quant")
     p.add_argument("--m", type=int, default=32768)
     p.add_argument("--d", type=int, default=1280)
+    p = sub.add_parser("quant-rows")
+    p.add_argument("--m", type=int, default=32768)
+    p.add_argument("--k", type=int, default=5120)
     p = sub.add_parser("decode")
     p.add_argument("--model", choices=["small", "medium", "large"], default="medium")
     p.add_argument("--batch", type=int, default=1)
@@ -374,7 +394,8 @@ def main(argv=None) -> None:
         _FLUSH = torch.ones((64 << 20,), dtype=torch.float32, device="cuda")
     {"attention-decode": attention_decode, "attention-prefill": attention_prefill,
      "layernorm-quant": layernorm_quant, "linear": linear, "decode": decode,
-     "gemv-chain": gemv_chain, "sample": sample, "mlp-pair": mlp_pair}[a.case](a)
+     "gemv-chain": gemv_chain, "sample": sample, "mlp-pair": mlp_pair,
+     "quant-rows": quant_rows}[a.case](a)
     st = ops.device_error()
     if st:
         raise SystemExit(f"device error word {st}")

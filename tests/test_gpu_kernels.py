@@ -19,7 +19,7 @@ def _rand_bf16(rng, shape, scale=1.0):
 
 
 @pytest.mark.parametrize("M,K", [(1, 768), (7, 3072), (64, 5120), (333, 1024), (5, 100),
-                                 (3, 8), (1024, 768)])
+                                 (3, 8), (1024, 768), (1024, 5120), (2048, 1280), (1024, 4104)])
 def test_quant_rows_bit_exact(cuda, M, K):
     rng = np.random.default_rng(M * 7 + K)
     x = outlier_activations(M, K, seed=M + K)
