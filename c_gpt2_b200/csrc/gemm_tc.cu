@@ -24,6 +24,11 @@
 // overlaps the main loop of the next. Every wait is bounded: a stalled
 // pipeline records an error code and the kernel returns.
 //
+// Token-major INT8 GEMMs with at least 256 output channels and K > 4608 run
+// on CTA pairs instead (gemm_tc_pair_kernel): one tcgen05.mma.cta_group::2
+// per K step covers 256 tokens x 256 channels, each CTA loading half of both
+// operands, with the same epilogue per CTA.
+//
 // Replaces the reference's cublasGemmEx INT8 call (gpt2.c:404-415), its
 // dequant kernel (cuda/activation_quant.cu:117-131) and the add_bias /
 // add_2d / gelu kernels that follow each GEMM (gpt2.c:1145-1325), and the
@@ -388,13 +393,43 @@ __device__ __forceinline__ void tm_issue_resid(const CUtensorMap *tmRb, uint64_t
       : "memory");
 }
 
-template <int EPI, bool RT>
+// Units of the epilogue loop. One CTA: unit = 128 x BN tile, CTAs stride the
+// grid. CTA pair: unit = 256-row x BN tile pair, clusters stride the grid, and
+// CTA `rank` of the pair finishes the 128-row tile 2 * (unit / b_tiles) + rank.
+template <bool PAIR>
+struct TmUnits {
+  int first, stride, total, rank;
+  __device__ __forceinline__ TmUnits(const GemmArgs &a) {
+    if (PAIR) {
+      rank = (int)cluster_ctarank();
+      first = (int)(blockIdx.x >> 1);
+      stride = (int)(gridDim.x >> 1);
+      total = ((a.a_tiles + 1) >> 1) * a.b_tiles;
+    } else {
+      rank = 0;
+      first = (int)blockIdx.x;
+      stride = (int)gridDim.x;
+      total = a.a_tiles * a.b_tiles;
+    }
+  }
+  __device__ __forceinline__ int tile(const GemmArgs &a, int u) const {
+    if (!PAIR) return u;
+    const int pm = u / a.b_tiles;
+    return (2 * pm + rank) * a.b_tiles + (u - pm * a.b_tiles);
+  }
+};
+
+template <int EPI, bool RT, bool PAIR = false>
 __device__ __forceinline__ void epilogue_tm(const GemmArgs &a, SmemCtl *ctl, uint32_t tmem_base,
                                             uint32_t wbase, int e, int lane,
                                             volatile int *abort_flag, bool vec_params,
                                             const CUtensorMap *tmRb) {
   const int quarter = (e + kEpiWarp0) & 3, group = e >> 2;
-  const int total_units = a.a_tiles * a.b_tiles;
+  const TmUnits<PAIR> units(a);
+  const int total_units = units.total;
+  // a pair's accumulators are handed back to the MMA issuer of the even CTA
+  const uint32_t empty_at[2] = {PAIR ? dsmem_addr(&ctl->tmem_empty[0], 0) : 0u,
+                                PAIR ? dsmem_addr(&ctl->tmem_empty[1], 0) : 0u};
   // output (and, without RT, residual) buffer; RT: the residual slots first
   const uint32_t stage = RT ? wbase + (uint32_t)(kRSlots * kWarpStageBytes) : wbase;
   const uint32_t params = stage + kWarpStageBytes;  // two buffers of kParamBytes
@@ -407,8 +442,8 @@ __device__ __forceinline__ void epilogue_tm(const GemmArgs &a, SmemCtl *ctl, uin
   float sx_next = 0.f;
   int64_t kv_next = 0;
   TmTile gn = {};
-  if ((int)blockIdx.x < total_units) {
-    gn = tm_tile(a, blockIdx.x, quarter, group, lane);
+  if (units.first < total_units) {
+    gn = tm_tile(a, units.tile(a, units.first), quarter, group, lane);
     tm_load_params<EPI>(a, gn, group, lane, params, vec_params);
     if (RT) {
       if (lane == 0)
@@ -423,10 +458,10 @@ __device__ __forceinline__ void epilogue_tm(const GemmArgs &a, SmemCtl *ctl, uin
     tm_row_info<EPI>(a, gn, quarter, lane, sx_next, kv_next);
   }
   int iter = 0;
-  for (int t = blockIdx.x; t < total_units; t += gridDim.x, ++iter) {
+  for (int u = units.first; u < total_units; u += units.stride, ++iter) {
     const TmTile g = gn;
-    const bool has_next = t + (int)gridDim.x < total_units;
-    if (has_next) gn = tm_tile(a, t + gridDim.x, quarter, group, lane);
+    const bool has_next = u + units.stride < total_units;
+    if (has_next) gn = tm_tile(a, units.tile(a, u + units.stride), quarter, group, lane);
     const uint32_t pbuf = params + (uint32_t)((iter & 1) * kParamBytes);
     int ok = 1;
     if (lane == 0) ok = mbar_wait(&ctl->tmem_full[acc], acc_phase, abort_flag, a.err, 0x1105);
@@ -512,7 +547,12 @@ __device__ __forceinline__ void epilogue_tm(const GemmArgs &a, SmemCtl *ctl, uin
       }
       if (j == 3) {  // the tile's accumulator is read: hand it back to the MMA warp
         tc_fence_before();
-        mbar_arrive(&ctl->tmem_empty[acc]);
+        if (PAIR) {  // one arrival per warp, on the even CTA's barrier
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(empty_at[acc]);
+        } else {
+          mbar_arrive(&ctl->tmem_empty[acc]);
+        }
       }
       uint4 rown[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
       if (RT) {  // this item's slot (its phase completes even for an item without columns)
@@ -897,6 +937,222 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Token-major INT8 GEMM on CTA pairs (tcgen05.mma.cta_group::2, M = 256).
+//
+// A cluster of two CTAs (one TPC) computes 256-token x 256-channel units:
+// CTA r loads tokens [m0 + 128 r, +128) and weight rows [n0 + 128 r, +128) of
+// every 128-byte K block, and the even CTA's MMA thread multiplies the pair's
+// 256 x 128 A and 256 x 128 B halves in one instruction per 32-byte K step.
+// Each CTA's TMEM receives its own 128 tokens x 256 channels, finished by the
+// same epilogue as the one-CTA kernel. Per SM and K block that is 32 KB of
+// operands for 128 x 256 outputs, against 48 KB with one CTA per tile: the
+// operand stream from L2, which sets the pace of the one-CTA kernel, shrinks
+// by a third.
+//
+// Barriers: the even CTA's full[s] counts both CTAs' bytes (its producer arms
+// it with both halves; the odd CTA's loads complete on it across the pair);
+// the MMA commits signal empty[s] and tmem_full[acc] in both CTAs; each
+// epilogue warp of either CTA releases tmem_empty[acc] of the even CTA. Every
+// wait is bounded; a CTA whose wait ran out stops issuing, lets its copies in
+// flight land, and both CTAs meet at a cluster barrier before TMEM is freed.
+// ---------------------------------------------------------------------------
+constexpr int kPairBN = 256;         // channels per unit (each CTA loads half)
+constexpr int kPairMinKBlocks = 36;  // pairs for reductions longer than 36 x 128 bytes
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmR, GemmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int stages = a.stages;
+  const uint32_t a_bytes = kBM * kBoxBytes;                // this CTA's 128 token rows
+  const uint32_t b_bytes = (kPairBN / 2) * kBoxBytes;      // this CTA's 128 weight rows
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+  uint8_t *epi_stage = smem + (size_t)stages * stage_bytes;
+  SmemCtl *ctl = reinterpret_cast<SmemCtl *>(epi_stage + kEpiStageBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const TmUnits<true> units(a);
+  constexpr uint32_t kCols = 2 * kPairBN;  // double-buffered 256-column accumulator
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->tmem_full[i], 1);
+      mbar_init(&ctl->tmem_empty[i], 2 * kEpiWarps);
+    }
+    mbar_init(&ctl->drain, 1);
+    ctl->abort_flag = 0;
+    ctl->consumed = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (EPI == EPI_RESID) prefetch_tmap(&tmR);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&ctl->tmem_base, kCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem_base = ctl->tmem_base;
+  volatile int *abort_flag = &ctl->abort_flag;
+
+  int issued = 0;
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    // Weight boxes of the first unit go out before waiting for the previous
+    // kernel (they do not depend on it).
+    const uint32_t full0 = dsmem_addr(&ctl->full[0], 0);  // the even CTA's full[0]
+    const uint32_t full_stride = (uint32_t)sizeof(uint64_t);
+    const uint32_t both = 2 * stage_bytes;
+    const int half = (int)rank * (kPairBN / 2);
+    int pre = 0;
+    if (units.first < units.total) {
+      const int b0 = (units.first % a.b_tiles) * kPairBN + half;
+      for (; pre < a.kblocks && pre < stages; ++pre) {
+        if (leader) mbar_arrive_expect_tx(&ctl->full[pre], both);
+        tma_load_2d_pair(smem + (size_t)pre * stage_bytes + a_bytes, &tmB,
+                         full0 + (uint32_t)pre * full_stride, pre * kBoxBytes, b0);
+      }
+    }
+    pdl_wait();
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    for (int u = units.first; u < units.total && !*abort_flag; u += units.stride) {
+      const int pm = u / a.b_tiles, pn = u - (u / a.b_tiles) * a.b_tiles;
+      const int a0 = pm * (2 * kBM) + (int)rank * kBM;
+      const int b0 = pn * kPairBN + half;
+      if (EPI == EPI_RESID && u + units.stride < units.total) {
+        // this CTA's residual rows of its next unit: into L2 now
+        const int un = u + units.stride;
+        const int pmn = un / a.b_tiles;
+        tma_prefetch_l2_2d(&tmR, (un - pmn * a.b_tiles) * kPairBN, pmn * (2 * kBM) + (int)rank * kBM);
+      }
+      for (int kb = 0; kb < a.kblocks; ++kb) {
+        if (!mbar_wait(&ctl->empty[stage], phase ^ 1, abort_flag, a.err, 0x1301)) break;
+        uint8_t *sa = smem + (size_t)stage * stage_bytes;
+        const uint32_t fb = full0 + (uint32_t)stage * full_stride;
+        if (it >= pre) {
+          if (leader) mbar_arrive_expect_tx(&ctl->full[stage], both);
+          tma_load_2d_pair(sa + a_bytes, &tmB, fb, kb * kBoxBytes, b0);
+        }
+        tma_load_2d_pair(sa, &tmA, fb, kb * kBoxBytes, a0);
+        ++it;
+        ++issued;
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    // Give every prefetched weight box its token box, so that each stage armed
+    // above can still complete.
+    if (units.first < units.total) {
+      const int a0 = (units.first / a.b_tiles) * (2 * kBM) + (int)rank * kBM;
+      for (; it < pre; ++it, ++issued)
+        tma_load_2d_pair(smem + (size_t)it * stage_bytes, &tmA, full0 + (uint32_t)it * full_stride,
+                         it * kBoxBytes, a0);
+    }
+    if (*abort_flag) {
+      // This CTA's copies complete on the even CTA's barriers: give the ones
+      // in flight time to land before the shared memory is released.
+      const uint64_t t0 = globaltimer_ns();
+      while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---------------- MMA issuer (even CTA) ----------------
+    pdl_wait();
+    const uint32_t idesc = make_idesc(2, 1, 2 * kBM, kPairBN);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int consumed = 0;
+    bool ok = true;
+    for (int u = units.first; u < units.total && ok; u += units.stride) {
+      if (!mbar_wait(&ctl->tmem_empty[acc], acc_phase ^ 1, abort_flag, a.err, 0x1302)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kPairBN);
+      for (int kb = 0; kb < a.kblocks; ++kb) {
+        if (!mbar_wait(&ctl->full[stage], phase, abort_flag, a.err, 0x1303)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + (size_t)stage * stage_bytes);
+        const uint32_t sb = sa + a_bytes;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)  // 4 x 32-byte K steps inside the 128-byte atom
+          tc_mma_i8_pair(d_tmem, make_sw128_desc(sa + 32 * k), make_sw128_desc(sb + 32 * k), idesc,
+                         (kb != 0 || k != 0) ? 1u : 0u);
+        tc_commit_pair_both(&ctl->empty[stage]);
+        ++consumed;
+        if (++stage == stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      tc_commit_pair_both(&ctl->tmem_full[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    ctl->consumed = consumed;
+    // No MMA may still write either CTA's TMEM or read shared memory when the
+    // pair meets at the final cluster barrier.
+    tc_commit_pair(&ctl->drain);
+    mbar_wait(&ctl->drain, 0, nullptr, a.err, 0x1304);
+  } else if (warp >= kEpiWarp0) {
+    // ---------------- epilogue (both CTAs) ----------------
+    pdl_wait();
+    const int e = warp - kEpiWarp0;
+    epilogue_tm<EPI, false, true>(a, ctl, tmem_base,
+                                  smem_u32(epi_stage) + (uint32_t)(e * kWarpEpiBytes), e, lane,
+                                  abort_flag, a.vec_params != 0, nullptr);
+  }
+
+  __syncthreads();
+  if (leader && warp == 0 && lane == 0 && *abort_flag) {
+    // Stages armed by this CTA but never consumed: wait (bounded) for their
+    // bytes, which include the odd CTA's.
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int i = 0; i < issued; ++i) {
+      // (a stage the odd CTA never filled does not complete: stop there)
+      if (i >= ctl->consumed && !mbar_wait(&ctl->full[stage], phase, nullptr, a.err, 0x1305))
+        break;
+      if (++stage == stages) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA frees TMEM or leaves while the pair still works
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host-side launcher
 // ---------------------------------------------------------------------------
 static int round_up32(int x) { return (x + 31) & ~31; }
@@ -1015,6 +1271,91 @@ static int launch_tc(const void *W, const void *X, int64_t ldx_elems, const Line
   return check_launch("gemm_tc");
 }
 
+// Token-major INT8 GEMM on CTA pairs: a persistent grid of as many 2-CTA
+// clusters as can be resident at once (at most one per TPC), each striding
+// over the 256 x 256 units.
+template <int EPI>
+static int launch_pair(const int8_t *W, const int8_t *X, int64_t ldx, const LinearArgs &la,
+                       cudaStream_t stream) {
+  int st;
+  DeviceCtx *ctx = device_ctx(&st);
+  if (!ctx) return st;
+  GemmArgs a;
+  static_cast<LinearArgs &>(a) = la;
+  const int M = la.M, N = la.N, K = la.K;
+  CUtensorMap tmA, tmB, tmR;
+  memset(&tmR, 0, sizeof(tmR));
+  a.BN = kPairBN;
+  st = make_tmap_2d(&tmA, X, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)M, (uint64_t)K,
+                    (uint64_t)ldx, kBoxBytes, kBM);
+  if (st) return st;
+  st = make_tmap_2d(&tmB, W, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)N, (uint64_t)K, (uint64_t)K,
+                    kBoxBytes, kPairBN / 2);
+  if (st) return st;
+  a.a_tiles = (M + kBM - 1) / kBM;
+  a.b_tiles = (N + kPairBN - 1) / kPairBN;
+  if (EPI == EPI_RESID) {  // L2 prefetch of the residual, one 128 x 256 box per CTA and unit
+    st = make_tmap_2d(&tmR, la.R, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)M, (uint64_t)N,
+                      (uint64_t)la.ldr * 2, (uint32_t)kPairBN, kBM, 0);
+    if (st) return st;
+  }
+  const int stage_bytes = (kBM + kPairBN / 2) * kBoxBytes;
+  const int epi_bytes = kEpiStageBytes;
+  const int budget = 227 * 1024 - 1024 - epi_bytes - (int)sizeof(SmemCtl) - 64;
+  a.stages = budget / stage_bytes;
+  if (a.stages > 8) a.stages = 8;
+  if (a.stages < 2) return W8A8_ERR_UNSUPPORTED;
+  const size_t smem = 1024 + (size_t)a.stages * stage_bytes + epi_bytes + sizeof(SmemCtl);
+  a.vec_params = aligned16(la.sW) && (la.bias == nullptr || aligned16(la.bias));
+  a.kblocks = (K + kBoxBytes - 1) / kBoxBytes;
+  a.err = ctx->err;
+  a.ksplit = 1;
+  a.kb_per = a.kblocks;
+  a.ws = nullptr;
+  a.tickets = nullptr;
+
+  static int max_clusters[64] = {};  // per template instantiation and device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return W8A8_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  if (max_clusters[dev] == 0) {
+    if (cudaFuncSetAttribute(gemm_tc_pair_kernel<EPI>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+      return W8A8_ERR_CUDA;
+    cfg.gridDim = dim3(2 * (ctx->sm_count / 2));
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_pair_kernel<EPI>, &cfg) != cudaSuccess ||
+        n < 1) {
+      cudaGetLastError();
+      return W8A8_ERR_UNSUPPORTED;
+    }
+    max_clusters[dev] = n;
+  }
+  const int units = ((a.a_tiles + 1) / 2) * a.b_tiles;
+  const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.numAttrs = 2;
+  if (cudaLaunchKernelEx(&cfg, gemm_tc_pair_kernel<EPI>, tmA, tmB, tmR, a) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return W8A8_ERR_CUDA;
+  }
+  return check_launch("gemm_tc_pair");
+}
+
 size_t linear_workspace_bytes(int M, int N) {
   const size_t tiles = (size_t)((N + kBM - 1) / kBM) * (size_t)((M + 31) / 32);
   return (((size_t)M * N * 4 + 255) & ~(size_t)255) + tiles * 4;
@@ -1044,9 +1385,23 @@ static int launch_i8(const int8_t *W, const int8_t *X, int64_t ldx, const Linear
                      cudaStream_t s) {
   if (token_major_ok(a)) {
     // Residual GEMMs with short K (attn_proj): residual blocks by TMA into
-    // per-warp slots; the slots leave room for three pipeline stages, enough
+    // per-warp slots; the slots leave room for fewer pipeline stages, enough
     // where the residual loads, not the operand loads, set the pace.
-    if (EPI == EPI_RESID && (a.K + kBoxBytes - 1) / kBoxBytes <= 16)
+    const int kblocks = (a.K + kBoxBytes - 1) / kBoxBytes;
+    if constexpr (EPI != EPI_S32) {
+      // The longest reductions on CTA pairs, where the main loop sets the
+      // pace: W2 of GPT-2 large (K 5120) at 32768 tokens 178 -> 162 us,
+      // tensor pipe 65 -> 74% busy. Shorter ones gain nothing or lose, each
+      // unit's time being set by the epilogue (~18 us per 128 x 256 residual
+      // tile) or the operand round trip: W2 K 4096 122 -> 123 us, K 3072
+      // 89 -> 97; K 1280: W_qkv 147 -> 149, attn_proj 75 -> 78, W1 + GELU
+      // 267 -> 270.
+      if (a.N >= kPairBN && kblocks > kPairMinKBlocks) {
+        const int st = launch_pair<EPI>(W, X, ldx, a, s);
+        if (st != W8A8_ERR_UNSUPPORTED) return st;
+      }
+    }
+    if (EPI == EPI_RESID && kblocks <= 16)
       return launch_tc<0, EPI, false, EPI == EPI_RESID>(W, X, ldx, a, s);
     return launch_tc<0, EPI, false>(W, X, ldx, a, s);
   }

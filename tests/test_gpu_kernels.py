@@ -62,7 +62,8 @@ def test_gemm_s32_extreme_values(cuda):
 @pytest.mark.parametrize("M,N,K", [(1, 2304, 768), (9, 768, 3072), (16, 2304, 768),
                                    (128, 3072, 768), (300, 768, 3072), (1024, 2304, 768),
                                    (300, 320, 768), (129, 96, 256), (1, 1280, 5120),
-                                   (1, 200, 3072), (1, 5120, 1280)])
+                                   (1, 200, 3072), (1, 5120, 1280), (257, 288, 4736),
+                                   (600, 1280, 5120), (256, 256, 64)])
 @pytest.mark.parametrize("epi", [_lib.EPI_DEQUANT, _lib.EPI_BIAS, _lib.EPI_BIAS_RESID])
 def test_linear_epilogues_bit_exact(cuda, M, N, K, epi):
     rng = np.random.default_rng(M + N + K + epi)
@@ -132,15 +133,15 @@ def test_linear_qkv_scatter_split_k(cuda, B):
 
 
 @pytest.mark.parametrize("zero_acc", [True, False])
-@pytest.mark.parametrize("M", [256, 64])
-def test_linear_resid_bf16_edge_values(cuda, zero_acc, M):
+@pytest.mark.parametrize("M,K", [(256, 128), (256, 5120), (64, 128)])
+def test_linear_resid_bf16_edge_values(cuda, zero_acc, M, K):
     """Bias and residual additions at the edges of bf16: subnormals, signed
     zeros, the largest finite values and infinities (token-major tiles at 256
-    tokens, the cluster split-K path at 64). With zero weights every
-    dequantized product is +0, so the sums see the edge values themselves;
-    with random weights tiny biases meet normal values."""
+    tokens, on CTA pairs with K = 5120, the cluster split-K path at 64). With
+    zero weights every dequantized product is +0, so the sums see the edge
+    values themselves; with random weights tiny biases meet normal values."""
     rng = np.random.default_rng(21 + zero_acc)
-    N, K = 512, 128
+    N = 512
     x = oracle.bf16_bits(outlier_activations(M, K, seed=9))
     xq, sx = oracle.quant_rows(x)
     W = (np.zeros((N, K), np.int8) if zero_acc
@@ -189,7 +190,7 @@ def test_linear_qkv_scatter_prefill(cuda):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 3072, 768), (64, 5120, 1280), (512, 3072, 768),
-                                   (333, 320, 768)])
+                                   (333, 320, 768), (300, 512, 4864)])
 def test_linear_gelu_within_one_ulp(cuda, M, N, K):
     """GELU uses CUDA's tanhf on the GPU and the C library's on the CPU:
     at most 1 bf16 ulp apart, almost always identical."""
