@@ -44,6 +44,10 @@ SIGNATURES = {
     "w8a8_linear_from_bf16": (_i, [_p, _i64, _p, _i, _i, _i, _p, _p, _p, _i, _i, _p, _i64, _p,
                                    _i64, _p, _p, _p, _sz, _p]),
     "w8a8_linear_noalloc": (_i, [_p, _p, _i, _i, _p, _p, _p, _i, _i, _p, _i64, _p, _i64, _p]),
+    "w8a8_layernorm_linear_qkv": (_i, [_p, _i64, _p, _p, _f, _p, _p, _i, _i, _p, _p, _p, _p, _i64,
+                                       _p, _p, _i64, _i, _p, _p, _sz, _p]),
+    "w8a8_layernorm_linear_absmax": (_i, [_p, _i64, _p, _p, _f, _p, _p, _i, _i, _p, _p, _p, _i, _i,
+                                          _p, _i64, _p, _i64, _p, _sz, _p, _p, _sz, _p]),
     "w8a8_linear_qkv": (_i, [_p, _p, _i, _i, _p, _p, _p, _p, _i64, _p, _p, _i64, _i, _p, _p,
                              _sz, _p]),
     "w8a8_linear_qkv_heads": (_i, [_p, _p, _i, _i, _i, _p, _p, _p, _p, _i64, _p, _p, _i64, _i,

@@ -293,6 +293,77 @@ extern "C" int w8a8_linear_qkv_heads(const int8_t *Xq, const float *sX, int M, i
                          pos0, workspace, workspace_bytes, stream);
 }
 
+// LayerNorm folded into the single-token GEMV (gemv_layernorm), else the
+// LayerNorm kernel followed by the linear layer on its quantized rows.
+extern "C" int w8a8_layernorm_linear_qkv(const gpt2_bf16_t *X, int64_t ldx,
+                                         const gpt2_bf16_t *gamma, const gpt2_bf16_t *beta,
+                                         float eps, int8_t *Xq, float *sX, int M, int d,
+                                         const int8_t *Wqkv, const float *sWqkv,
+                                         const gpt2_bf16_t *bqkv, gpt2_bf16_t *Q, int64_t ldq,
+                                         gpt2_bf16_t *Kc, gpt2_bf16_t *Vc, int64_t seq_stride,
+                                         int T, const int32_t *pos0, void *workspace,
+                                         size_t workspace_bytes, void *stream) {
+  if (M == 0) return W8A8_OK;
+  if (!X || !gamma || !beta || !Xq || !sX || !Wqkv || !sWqkv || !bqkv || !Q || !Kc || !Vc ||
+      M < 0 || d <= 0 || d > 8192 || ldx < d || T <= 0 || M % T != 0 || ldq < d)
+    return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  if (M == 1) {
+    LinearArgs a = make_args(EPI_QKV, M, 3 * d, d, sX, sWqkv, bqkv, nullptr, 0, Q, ldq);
+    a.Kc = Kc;
+    a.Vc = Vc;
+    a.seq_stride = seq_stride;
+    a.T = T;
+    a.pos0 = pos0;
+    a.dseg = d;
+    const GemvLnArgs ln = {X, gamma, beta, eps, Xq, sX};
+    st = gemv_layernorm(Wqkv, a, ln, nullptr, (cudaStream_t)stream);
+    if (st != W8A8_ERR_UNSUPPORTED) return st;
+  }
+  st = w8a8_layernorm_quant(X, ldx, M, d, gamma, beta, eps, nullptr, 0, Xq, sX, stream);
+  if (st) return st;
+  return w8a8_linear_qkv(Xq, sX, M, d, Wqkv, sWqkv, bqkv, Q, ldq, Kc, Vc, seq_stride, T, pos0,
+                         workspace, workspace_bytes, stream);
+}
+
+extern "C" int w8a8_layernorm_linear_absmax(const gpt2_bf16_t *X, int64_t ldx,
+                                            const gpt2_bf16_t *gamma, const gpt2_bf16_t *beta,
+                                            float eps, int8_t *Xq, float *sX, int M, int K,
+                                            const int8_t *W, const float *sW,
+                                            const gpt2_bf16_t *bias, int N, int epilogue,
+                                            const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y,
+                                            int64_t ldy, float *absmax, size_t absmax_floats,
+                                            int *n_part, void *workspace,
+                                            size_t workspace_bytes, void *stream) {
+  if (!n_part) return W8A8_ERR_INVALID;
+  *n_part = 0;
+  if (M == 0 || N == 0) return W8A8_OK;
+  if (!X || !gamma || !beta || !Xq || !sX || !W || !sW || !Y || !absmax || M < 0 || N < 0 ||
+      K <= 0 || K > 8192 || ldx < K || ldy < N)
+    return W8A8_ERR_INVALID;
+  int epi;
+  if (epi_code(epilogue, &epi)) return W8A8_ERR_INVALID;
+  if (epi != EPI_DEQUANT && !bias) return W8A8_ERR_INVALID;
+  if (epi == EPI_RESID && (!R || ldr < N)) return W8A8_ERR_INVALID;
+  if (absmax_floats < w8a8_absmax_record_floats(M, N)) return W8A8_ERR_INVALID;
+  int st = ready();
+  if (st) return st;
+  if (M == 1) {
+    LinearArgs a = make_args(epi, M, N, K, sX, sW, bias, R, ldr, Y, ldy);
+    a.amax_out = absmax;
+    const GemvLnArgs ln = {X, gamma, beta, eps, Xq, sX};
+    int parts = 0;
+    st = gemv_layernorm(W, a, ln, &parts, (cudaStream_t)stream);
+    if (st == W8A8_OK) *n_part = parts;
+    if (st != W8A8_ERR_UNSUPPORTED) return st;
+  }
+  st = w8a8_layernorm_quant(X, ldx, M, K, gamma, beta, eps, nullptr, 0, Xq, sX, stream);
+  if (st) return st;
+  return w8a8_linear_absmax(Xq, sX, M, K, W, sW, bias, N, epilogue, R, ldr, Y, ldy, absmax,
+                            absmax_floats, n_part, workspace, workspace_bytes, stream);
+}
+
 extern "C" int w8a8_row_amax(const gpt2_bf16_t *X, int64_t ldx, int M, int K, float *amax,
                              void *stream) {
   if (M == 0) return W8A8_OK;

@@ -13,6 +13,7 @@
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "kernels.cuh"
+#include "rowblock.cuh"
 #include "runtime.cuh"
 
 namespace w8a8 {
@@ -132,6 +133,94 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     __syncthreads();
     if ((int)threadIdx.x < a.M)
       a.amax_out[(int64_t)blockIdx.x * a.M + threadIdx.x] = __uint_as_float(s_amax[threadIdx.x]);
+  }
+}
+
+// Batch-1 decode with the LayerNorm folded in: every 4-warp block (128
+// threads, the block-per-row LayerNorm's width) forms the token's LayerNorm
+// and per-token quantization itself, from the bf16 row, with the reference's
+// 1024-slot sums and fold (rowblock.cuh: the arithmetic of
+// layernorm_block_kernel, bit for bit), keeps the int8 row in shared memory
+// and runs the GEMV of gemv_i8_vec_kernel on it, two output channels a warp
+// (half the blocks, so half the repeated LayerNorms, and one wave of blocks
+// for GPT-2 large's W1: 640 blocks of 91 registers a thread, 5 per SM). Block 0 also writes the
+// quantized row and its scale out. The weights and the LayerNorm's gain and
+// bias do not depend on the previous kernel: they are requested before
+// waiting for it. Replaces a LayerNorm launch and the quantized row's round
+// trip through memory in every layer of a single-sequence decode step.
+constexpr int kLnVec = 2;   // rows up to 128 threads x 2 vectors x 8 = 2048 elements
+constexpr int kLnRows = 2;  // output channels a warp
+
+template <int NVL, bool AMAX>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    gemv_ln_i8_kernel(const int8_t *__restrict__ W, GemvArgs a, GemvLnArgs ln) {
+  static_assert(kGemvWarps * 32 == kRowThreads, "one LayerNorm block per GEMV block");
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int n0 = (blockIdx.x * kGemvWarps + warp) * kLnRows;  // channels n0, n0 + 1
+  const int kv = a.K >> 4, nv = a.K >> 3;
+  __shared__ RowShared sh;
+  __shared__ __align__(16) int8_t xq[kLnVec * kRowThreads * 8];
+  __shared__ float sx;
+  __shared__ unsigned s_amax;
+  if (AMAX && t == 0) s_amax = 0u;  // published by the LayerNorm's barriers
+  int4 w[kLnRows][NVL];
+#pragma unroll
+  for (int j = 0; j < kLnRows; ++j) {
+    const int n = n0 + j;
+    const int4 *wrow = reinterpret_cast<const int4 *>(W + (int64_t)n * a.K);
+#pragma unroll
+    for (int u = 0; u < NVL; ++u) {
+      const int v = lane + 32 * u;
+      w[j][u] = (n < a.N && v < kv) ? __ldg(wrow + v) : make_int4(0, 0, 0, 0);
+    }
+  }
+  uint4 g[kLnVec], bt[kLnVec];
+  load_row_vec(ln.gamma, nv, t, g);
+  load_row_vec(ln.beta, nv, t, bt);
+  pdl_wait();
+  pdl_launch_dependents();
+  uint4 x[kLnVec];
+  load_row_vec(ln.X, nv, t, x);
+  ln_quant_tail(sh, x, g, bt, nv, t, a.K, ln.eps, nullptr, xq, &sx);
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    if (t < kv) reinterpret_cast<int4 *>(ln.Xq)[t] = reinterpret_cast<const int4 *>(xq)[t];
+    if (t == 0) *ln.sX = sx;
+  }
+  int acc[kLnRows];
+#pragma unroll
+  for (int j = 0; j < kLnRows; ++j) acc[j] = 0;
+  const int4 *xr = reinterpret_cast<const int4 *>(xq);
+#pragma unroll
+  for (int u = 0; u < NVL; ++u) {
+    const int v = lane + 32 * u;
+    if (v < kv) {
+      const int4 q = xr[v];
+#pragma unroll
+      for (int j = 0; j < kLnRows; ++j) {
+        acc[j] = __dp4a(w[j][u].x, q.x, acc[j]);
+        acc[j] = __dp4a(w[j][u].y, q.y, acc[j]);
+        acc[j] = __dp4a(w[j][u].z, q.z, acc[j]);
+        acc[j] = __dp4a(w[j][u].w, q.w, acc[j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kLnRows; ++j) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+  }
+  // lane j stores channel n0 + j
+#pragma unroll
+  for (int j = 0; j < kLnRows; ++j) {
+    if (lane == j && n0 + j < a.N) {
+      const float y = gemv_store(a, &sx, 0, n0 + j, acc[j]);
+      if (AMAX) atomicMax(&s_amax, __float_as_uint(fabsf(y)));
+    }
+  }
+  if (AMAX) {
+    __syncthreads();
+    if (t == 0) a.amax_out[blockIdx.x] = __uint_as_float(s_amax);
   }
 }
 
@@ -340,6 +429,28 @@ int gemv_absmax(const int8_t *X, int64_t ldx, const int8_t *W, const GemvArgs &a
   *n_part = (a.N + kGemvWarps - 1) / kGemvWarps;
   if (nvl <= 2) return launch_vec<1, 2, true>(X, ldx, W, a, s);
   return launch_vec<1, 4, true>(X, ldx, W, a, s);
+}
+
+// One token whose LayerNorm the GEMV forms itself (gemv_ln_i8_kernel); with
+// a.amax_out, also the row absmax record (*n_part parts). K <= 2048, K % 16 == 0.
+// W8A8_ERR_UNSUPPORTED where the operands do not allow it.
+int gemv_layernorm(const int8_t *W, const GemvArgs &a, const GemvLnArgs &ln, int *n_part,
+                   cudaStream_t s) {
+  if (a.M != 1 || a.K % 16 || a.K > kLnVec * kRowThreads * 8 || a.epi == EPI_S32 || !ln.X ||
+      !ln.gamma || !ln.beta || !ln.Xq || !ln.sX || !aligned16(W) || !aligned16(ln.X) ||
+      !aligned16(ln.gamma) || !aligned16(ln.beta) || !aligned16(ln.Xq))
+    return W8A8_ERR_UNSUPPORTED;
+  const int grid = (a.N + kGemvWarps * kLnRows - 1) / (kGemvWarps * kLnRows);
+  const int nvl = ((a.K >> 4) + 31) / 32;  // <= 4
+  if (a.amax_out) {
+    if (n_part) *n_part = grid;
+    if (nvl <= 2) launch_pdl(gemv_ln_i8_kernel<2, true>, dim3(grid), dim3(kGemvWarps * 32), 0, s, W, a, ln);
+    else launch_pdl(gemv_ln_i8_kernel<4, true>, dim3(grid), dim3(kGemvWarps * 32), 0, s, W, a, ln);
+  } else {
+    if (nvl <= 2) launch_pdl(gemv_ln_i8_kernel<2, false>, dim3(grid), dim3(kGemvWarps * 32), 0, s, W, a, ln);
+    else launch_pdl(gemv_ln_i8_kernel<4, false>, dim3(grid), dim3(kGemvWarps * 32), 0, s, W, a, ln);
+  }
+  return check_launch("gemv_ln_i8");
 }
 
 // One token with a long bf16 row (K > 2048) through the 16-warp GEMV that

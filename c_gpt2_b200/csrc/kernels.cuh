@@ -148,6 +148,18 @@ int launch_gemv_i8(const int8_t *X, int64_t ldx, const int8_t *W, const LinearAr
 int gemv_absmax(const int8_t *X, int64_t ldx, const int8_t *W, const LinearArgs &a, int *n_part,
                 cudaStream_t s);
 int gemv_from_bf16(const int8_t *W, const LinearArgs &a, cudaStream_t s);
+// The batch-1 GEMV that forms its input row's LayerNorm and quantization
+// itself (from the bf16 row X with gain / bias), also writing the quantized
+// row to Xq / sX: W8A8_ERR_UNSUPPORTED where the operands do not allow it.
+struct GemvLnArgs {
+  const uint16_t *X;
+  const uint16_t *gamma, *beta;
+  float eps;
+  int8_t *Xq;
+  float *sX;
+};
+int gemv_layernorm(const int8_t *W, const LinearArgs &a, const GemvLnArgs &ln, int *n_part,
+                   cudaStream_t s);
 // norm_quant.cu
 int launch_quant_rows(const uint16_t *X, int64_t ldx, int M, int K, int8_t *Xq, float *sX,
                       cudaStream_t s);

@@ -631,10 +631,20 @@ static int block_forward(gpt2_engine *e, const act_view *v, int l, int slot0, in
   gpt2_bf16_t *Vl = e->Vc + (int64_t)slot0 * seq_stride + (int64_t)l * c->ctx * d;
   void *s = v->s;
   const size_t lwb = e->lin_ws_bytes;
-  if (!first)
+  /* one decoding sequence: the LayerNorms run inside the GEMVs that follow them */
+  const int one_row = pos0 != NULL && M == 1;
+  if (first)
+    W8_TRY(e, w8a8_linear_qkv(v->Xq, v->sX, M, d, w->Wqkv, w->sWqkv, w->bqkv, v->Q, d, Kl, Vl,
+                              seq_stride, T, pos0, v->lin_ws, lwb, s));
+  else if (one_row)
+    W8_TRY(e, w8a8_layernorm_linear_qkv(v->H, d, w->ln1_g, w->ln1_b, eps, v->Xq, v->sX, M, d,
+                                        w->Wqkv, w->sWqkv, w->bqkv, v->Q, d, Kl, Vl, seq_stride,
+                                        T, pos0, v->lin_ws, lwb, s));
+  else {
     W8_TRY(e, w8a8_layernorm_quant(v->H, d, M, d, w->ln1_g, w->ln1_b, eps, NULL, 0, v->Xq, v->sX, s));
-  W8_TRY(e, w8a8_linear_qkv(v->Xq, v->sX, M, d, w->Wqkv, w->sWqkv, w->bqkv, v->Q, d, Kl, Vl,
-                            seq_stride, T, pos0, v->lin_ws, lwb, s));
+    W8_TRY(e, w8a8_linear_qkv(v->Xq, v->sX, M, d, w->Wqkv, w->sWqkv, w->bqkv, v->Q, d, Kl, Vl,
+                              seq_stride, T, pos0, v->lin_ws, lwb, s));
+  }
   if (pos0 == NULL)
     W8_TRY(e, w8a8_attention_prefill(v->Q, d, Kl, Vl, seq_stride, B, T, Hh, 64, v->ATT, d, s));
   else  /* decode: the attention kernel also quantizes its output rows */
@@ -644,19 +654,21 @@ static int block_forward(gpt2_engine *e, const act_view *v, int l, int slot0, in
   if (pos0 == NULL) W8_TRY(e, w8a8_quant_rows(v->ATT, d, M, d, v->Xq, v->sX, s));
   W8_TRY(e, w8a8_linear(v->Xq, v->sX, M, d, w->Wproj, w->sWproj, w->bproj, d, W8A8_EPI_BIAS_RESID,
                         v->H, d, v->R1, d, v->lin_ws, lwb, s));
-  W8_TRY(e, w8a8_layernorm_quant(v->R1, d, M, d, w->ln2_g, w->ln2_b, eps, NULL, 0, v->Xq, v->sX, s));
-  if (pos0 != NULL && M == 1) {
-    /* batch-1 decode: W1's epilogue records the row maxima of its GELU output
-     * and W2 quantizes the row itself (no separate quantization launch) */
+  if (one_row) {
+    /* batch-1 decode: W1 forms LN2 itself, its epilogue records the row
+     * maxima of its GELU output and W2 quantizes the row itself (no
+     * LayerNorm or quantization launch) */
     int n_part = 0;
-    W8_TRY(e, w8a8_linear_absmax(v->Xq, v->sX, M, d, w->W1, w->sW1, w->b1, f, W8A8_EPI_BIAS_GELU,
-                                 NULL, 0, v->X1, f, v->amax, e->amax_rec_floats, &n_part,
-                                 v->lin_ws, lwb, s));
+    W8_TRY(e, w8a8_layernorm_linear_absmax(v->R1, d, w->ln2_g, w->ln2_b, eps, v->Xq, v->sX, M,
+                                           d, w->W1, w->sW1, w->b1, f, W8A8_EPI_BIAS_GELU, NULL,
+                                           0, v->X1, f, v->amax, e->amax_rec_floats, &n_part,
+                                           v->lin_ws, lwb, s));
     W8_TRY(e, w8a8_linear_from_bf16(v->X1, f, v->amax, n_part, M, f, w->W2, w->sW2, w->b2, d,
                                     W8A8_EPI_BIAS_RESID, v->R1, d, v->H, d, v->Xq, v->sX,
                                     v->lin_ws, lwb, s));
     return W8A8_OK;
   }
+  W8_TRY(e, w8a8_layernorm_quant(v->R1, d, M, d, w->ln2_g, w->ln2_b, eps, NULL, 0, v->Xq, v->sX, s));
   W8_TRY(e, w8a8_linear(v->Xq, v->sX, M, d, w->W1, w->sW1, w->b1, f, W8A8_EPI_BIAS_GELU, NULL, 0,
                         v->X1, f, v->lin_ws, lwb, s));
   W8_TRY(e, w8a8_quant_rows(v->X1, f, M, f, v->Xq, v->sX, s));

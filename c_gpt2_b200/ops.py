@@ -165,6 +165,47 @@ def linear_qkv(Xq, sX, Wqkv, sWqkv, bqkv, Q, Kc, Vc, seq_stride, T, pos0=None, w
           "w8a8_linear_qkv")
 
 
+def layernorm_linear_qkv(X, gamma, beta, Wqkv, sWqkv, bqkv, Q, Kc, Vc, seq_stride, T, pos0=None,
+                         eps=1e-5, workspace=None):
+    """layernorm_quant(X) then linear_qkv on its rows, as one kernel for a
+    single token; returns the quantized rows (Xq, sX) it also writes."""
+    _need(X, torch.bfloat16, "X")
+    M, d = X.shape
+    Xq = torch.empty((M, d), dtype=torch.int8, device=X.device)
+    sX = torch.empty(M, dtype=torch.float32, device=X.device)
+    ws_bytes = workspace.numel() if workspace is not None else 0
+    check(core().w8a8_layernorm_linear_qkv(_ptr(X), X.stride(0), _ptr(gamma), _ptr(beta), eps,
+                                           _ptr(Xq), _ptr(sX), M, d, _ptr(Wqkv), _ptr(sWqkv),
+                                           _ptr(bqkv), _ptr(Q), Q.stride(0), _ptr(Kc), _ptr(Vc),
+                                           seq_stride, T, _ptr(pos0), _ptr(workspace), ws_bytes,
+                                           _stream()), "w8a8_layernorm_linear_qkv")
+    return Xq, sX
+
+
+def layernorm_linear_absmax(X, gamma, beta, W, sW, bias, epilogue=_lib.EPI_BIAS_GELU, R=None,
+                            eps=1e-5, out=None, workspace=None):
+    """layernorm_quant(X) then linear_absmax on its rows, as one kernel for a
+    single token: (Y, record [n_part, M], Xq, sX)."""
+    _need(X, torch.bfloat16, "X")
+    M, K = X.shape
+    N = W.shape[0]
+    Y = out if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=X.device)
+    Xq = torch.empty((M, K), dtype=torch.int8, device=X.device)
+    sX = torch.empty(M, dtype=torch.float32, device=X.device)
+    ldr = R.stride(0) if R is not None else 0
+    ws_bytes = workspace.numel() if workspace is not None else 0
+    cap = core().w8a8_absmax_record_floats(M, N)
+    rec = torch.empty(cap, dtype=torch.float32, device=X.device)
+    n_part = ctypes.c_int(0)
+    check(core().w8a8_layernorm_linear_absmax(_ptr(X), X.stride(0), _ptr(gamma), _ptr(beta), eps,
+                                              _ptr(Xq), _ptr(sX), M, K, _ptr(W), _ptr(sW),
+                                              _ptr(bias), N, epilogue, _ptr(R), ldr, _ptr(Y),
+                                              Y.stride(0), _ptr(rec), cap, ctypes.byref(n_part),
+                                              _ptr(workspace), ws_bytes, _stream()),
+          "w8a8_layernorm_linear_absmax")
+    return Y, rec[: n_part.value * M].view(n_part.value, M), Xq, sX
+
+
 def linear_qkv_heads(Xq, sX, Wqkv, sWqkv, bqkv, Q, Kc, Vc, seq_stride, T, pos0=None,
                      workspace=None):
     """QKV projection of a subset of heads: Wqkv [3*d_heads, K]."""

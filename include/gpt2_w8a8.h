@@ -140,6 +140,33 @@ int w8a8_linear_from_bf16(const gpt2_bf16_t *X, int64_t ldx, const float *absmax
                           int64_t ldr, gpt2_bf16_t *Y, int64_t ldy, int8_t *Xq, float *sX,
                           void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- LayerNorm folded into the GEMV of a single token ----
+ * The reference runs LayerNorm (layernorm_cuda, cuda/layernorm.cu) and then
+ * quantizes its output per token inside dot_2d_gpu_int8 (gpt2.c:1138-1145,
+ * 1293-1296) before the QKV and W1 GEMMs. Each call below is
+ * w8a8_layernorm_quant(X, ldx, M, K, gamma, beta, eps, NULL, 0, Xq, sX)
+ * followed by w8a8_linear_qkv / w8a8_linear_absmax on Xq, sX, with the same
+ * results (Xq and sX are written in both forms). For one token (M == 1,
+ * K % 16 == 0, K <= 2048, 16-byte aligned X, gain, bias, Xq and weights)
+ * the two run as one kernel: every block of the GEMV forms the row's
+ * LayerNorm and quantization itself, so the LayerNorm launch and the
+ * quantized row's trip through memory leave the batch-1 decode chain. Other
+ * shapes run the two kernels. */
+int w8a8_layernorm_linear_qkv(const gpt2_bf16_t *X, int64_t ldx, const gpt2_bf16_t *gamma,
+                              const gpt2_bf16_t *beta, float eps, int8_t *Xq, float *sX, int M,
+                              int d, const int8_t *Wqkv, const float *sWqkv,
+                              const gpt2_bf16_t *bqkv, gpt2_bf16_t *Q, int64_t ldq,
+                              gpt2_bf16_t *Kc, gpt2_bf16_t *Vc, int64_t seq_stride, int T,
+                              const int32_t *pos0, void *workspace, size_t workspace_bytes,
+                              void *stream);
+int w8a8_layernorm_linear_absmax(const gpt2_bf16_t *X, int64_t ldx, const gpt2_bf16_t *gamma,
+                                 const gpt2_bf16_t *beta, float eps, int8_t *Xq, float *sX,
+                                 int M, int K, const int8_t *W, const float *sW,
+                                 const gpt2_bf16_t *bias, int N, int epilogue,
+                                 const gpt2_bf16_t *R, int64_t ldr, gpt2_bf16_t *Y, int64_t ldy,
+                                 float *absmax, size_t absmax_floats, int *n_part,
+                                 void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- w8a8_linear without a caller-provided workspace ----
  * No counterpart in the reference. For callers that cannot allocate device
  * memory (a host that sizes all device memory once at start-up, a plugin whose

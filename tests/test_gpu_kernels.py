@@ -499,6 +499,79 @@ def test_linear_from_bf16_matches_quant_rows(cuda, M, K, n_part):
     assert ops.device_error(reset=True) == 0
 
 
+def _ln_operands(rng, M, d, N):
+    X = _rand_bf16(rng, (M, d), 2.0)
+    X[:, rng.choice(d, max(1, d // 100), replace=False)] = _rand_bf16(rng, (M, max(1, d // 100)), 40.0)
+    g = _rand_bf16(rng, (d,), 1.0)
+    b = _rand_bf16(rng, (d,), 0.1)
+    W = rng.integers(-127, 128, (N, d), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    bias = _rand_bf16(rng, (N,), 0.02)
+    return (to_dev_bf16(X), to_dev_bf16(g), to_dev_bf16(b), to_dev(W), to_dev(sw),
+            to_dev_bf16(bias))
+
+
+@pytest.mark.parametrize("M,d", [(1, 768), (1, 1024), (1, 1280), (1, 1600), (3, 1280)])
+def test_layernorm_folded_into_qkv_gemv(cuda, M, d):
+    """The QKV GEMV that forms the token's LayerNorm itself equals the
+    LayerNorm kernel followed by the QKV GEMM, bit for bit: Q, the K/V cache
+    rows and the quantized row it also writes (M = 3: the two kernels)."""
+    rng = np.random.default_rng(d + M)
+    X, g, b, W, sw, bias = _ln_operands(rng, M, d, 3 * d)
+    C = 40
+    pos = torch.tensor([17], dtype=torch.int32, device=cuda)
+    T = M
+    outs = []
+    for fused in (False, True):
+        Q = torch.zeros((M, d), dtype=torch.bfloat16, device=cuda)
+        Kc = torch.zeros((1, C, d), dtype=torch.bfloat16, device=cuda)
+        Vc = torch.zeros((1, C, d), dtype=torch.bfloat16, device=cuda)
+        if fused:
+            Xq, sX = ops.layernorm_linear_qkv(X, g, b, W, sw, bias, Q, Kc, Vc, C * d, T, pos)
+        else:
+            _, Xq, sX = ops.layernorm_quant(X, g, b, want_y=False)
+            ops.linear_qkv(Xq, sX, W, sw, bias, Q, Kc, Vc, C * d, T, pos)
+        outs.append([Q, Kc, Vc, Xq, sX])
+    for a, f in zip(*outs):
+        assert torch.equal(a.view(torch.uint8), f.view(torch.uint8))
+    assert ops.device_error(reset=True) == 0
+    if M == 1:
+        names = kernel_names_fresh("test_gpu_kernels", "ln_qkv_call", [[d]])[0]["names"]
+        assert len(names) == 1 and "gemv_ln" in names[0], names
+
+
+def ln_qkv_call(d):
+    """The fused LayerNorm + QKV GEMV of the test above on cuda:0."""
+    rng = np.random.default_rng(d + 1)
+    X, g, b, W, sw, bias = _ln_operands(rng, 1, d, 3 * d)
+    Q = torch.zeros((1, d), dtype=torch.bfloat16, device="cuda:0")
+    Kc = torch.zeros((1, 40, d), dtype=torch.bfloat16, device="cuda:0")
+    Vc = torch.zeros((1, 40, d), dtype=torch.bfloat16, device="cuda:0")
+    pos = torch.tensor([3], dtype=torch.int32, device="cuda:0")
+
+    def call():
+        ops.layernorm_linear_qkv(X, g, b, W, sw, bias, Q, Kc, Vc, 40 * d, 1, pos)
+        return 0
+    return call
+
+
+@pytest.mark.parametrize("M,d", [(1, 768), (1, 1280), (1, 1600), (2, 1024)])
+def test_layernorm_folded_into_w1_gemv(cuda, M, d):
+    """W1 with the LayerNorm formed in the GEMV and the row absmax record
+    equals the LayerNorm kernel followed by linear_absmax, bit for bit (the
+    record's row maxima, the GELU output and the quantized row)."""
+    rng = np.random.default_rng(3 * d + M)
+    X, g, b, W, sw, bias = _ln_operands(rng, M, d, 4 * d)
+    Y, rec, Xq, sX = ops.layernorm_linear_absmax(X, g, b, W, sw, bias, _lib.EPI_BIAS_GELU)
+    _, Xq0, sX0 = ops.layernorm_quant(X, g, b, want_y=False)
+    Y0, rec0 = ops.linear_absmax(Xq0, sX0, W, sw, bias, _lib.EPI_BIAS_GELU)
+    assert torch.equal(Xq, Xq0) and torch.equal(sX.view(torch.int32), sX0.view(torch.int32))
+    assert torch.equal(Y.view(torch.int16), Y0.view(torch.int16))
+    assert torch.equal(rec.max(0).values, rec0.max(0).values)
+    assert torch.equal(rec.max(0).values, Y.float().abs().max(1).values)
+    assert ops.device_error(reset=True) == 0
+
+
 def test_prefill_gelu_every_bf16_input(cuda):
     """The GELU of the prefill GEMM's fused epilogue against the reference-
     shaped element-wise GELU kernel (cuda/gelu.cu:10-15) for every one of the
