@@ -189,6 +189,36 @@ def test_linear_qkv_scatter_prefill(cuda):
         assert not k[i, other].any() and not v[i, other].any()
 
 
+def test_linear_qkv_heads_scatter_long_k(cuda):
+    """QKV scatter of a head subset with a long reduction (K 4736), which
+    takes the CTA-pair GEMM: 2 sequences of 150 tokens into Q and K/V cache
+    rows pos0[b] + t, 128-column segments (one 256-channel unit straddles
+    the Q/K boundary)."""
+    rng = np.random.default_rng(31)
+    B, T, K, dh, C = 2, 150, 4736, 128, 400
+    x = oracle.bf16_bits(outlier_activations(B * T, K, seed=6))
+    xq, sx = oracle.quant_rows(x)
+    W = rng.integers(-127, 128, (3 * dh, K), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, 3 * dh).astype(np.float32)
+    b = _rand_bf16(rng, (3 * dh,), 0.02)
+    want = oracle.linear(xq, sx, W, sw, b, oracle.EPI_BIAS)
+    pos = np.array([7, 230], np.int32)
+    Q = torch.zeros((B * T, dh), dtype=torch.bfloat16, device=cuda)
+    Kc = torch.zeros((B, C, dh), dtype=torch.bfloat16, device=cuda)
+    Vc = torch.zeros((B, C, dh), dtype=torch.bfloat16, device=cuda)
+    ops.linear_qkv_heads(to_dev(xq), to_dev(sx), to_dev(W), to_dev(sw), to_dev_bf16(b), Q, Kc, Vc,
+                         C * dh, T, to_dev(pos))
+    q, k, v = from_dev_bf16(Q), from_dev_bf16(Kc), from_dev_bf16(Vc)
+    np.testing.assert_array_equal(q, want[:, :dh])
+    for i in range(B):
+        rows = slice(i * T, (i + 1) * T)
+        np.testing.assert_array_equal(k[i, pos[i]:pos[i] + T], want[rows, dh:2 * dh])
+        np.testing.assert_array_equal(v[i, pos[i]:pos[i] + T], want[rows, 2 * dh:])
+        other = np.r_[0:pos[i], pos[i] + T:C]
+        assert not k[i, other].any() and not v[i, other].any()
+    assert ops.device_error(reset=True) == 0
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 3072, 768), (64, 5120, 1280), (512, 3072, 768),
                                    (333, 320, 768), (300, 512, 4864)])
 def test_linear_gelu_within_one_ulp(cuda, M, N, K):
