@@ -163,6 +163,23 @@ def test_host_validation_without_gpu():
     assert lib.w8a8_linear(None, None, 4, 16, None, None, None, 8, 1, None, 0, None, 8,
                            None, 0, None) == _lib.W8A8_ERR_INVALID
     assert lib.w8a8_quant_rows(None, 8, 0, 8, None, None, None) == _lib.W8A8_OK  # empty
+    # the LayerNorm-forming entry points: missing rows / gain, and an empty call
+    assert lib.w8a8_layernorm_linear_qkv(None, 768, None, None, 1e-5, None, None, 1, 768, None,
+                                         None, None, None, 768, None, None, 0, 1, None, None, 0,
+                                         None) == _lib.W8A8_ERR_INVALID
+    assert lib.w8a8_layernorm_linear_qkv(None, 768, None, None, 1e-5, None, None, 0, 768, None,
+                                         None, None, None, 768, None, None, 0, 1, None, None, 0,
+                                         None) == _lib.W8A8_OK
+    n_part = C.c_int(7)
+    assert lib.w8a8_layernorm_linear_absmax(None, 768, None, None, 1e-5, None, None, 1, 768, None,
+                                            None, None, 3072, _lib.EPI_BIAS_GELU, None, 0, None,
+                                            3072, None, 0, C.byref(n_part), None, 0,
+                                            None) == _lib.W8A8_ERR_INVALID
+    assert n_part.value == 0
+    assert lib.w8a8_layernorm_linear_absmax(None, 768, None, None, 1e-5, None, None, 1, 768, None,
+                                            None, None, 3072, _lib.EPI_BIAS_GELU, None, 0, None,
+                                            3072, None, 0, None, None, 0,
+                                            None) == _lib.W8A8_ERR_INVALID  # no n_part
     assert _lib.status_string(_lib.W8A8_ERR_DEVICE).startswith("a kernel")
     cfg = _lib.EngineConfig(768, 12, 10, 50257, 1024, 4, 4096)  # head_dim != 64
     h = C.c_void_p()
